@@ -1,0 +1,156 @@
+"""Generate golden attention/KV fixtures by running the reference's own NumPy oracle.
+
+Run in the build container, where tampajohn/fpga-qwen is checked out (default
+``/root/reference``, override with ``FPGA_QWEN_REF``)::
+
+    python tests/golden/make_golden.py
+
+It imports ``NumpyQwen`` from the reference's ``tests/test_full_model.py`` (lines 14-80)
+unchanged and runs ``NumpyQwen.token`` on a synthetic checkpoint written in the
+safetensors layout its constructor reads (:20-34): BF16 tensors, the real 28 layers,
+16 query heads, 8 KV heads and head_dim 128, with a small hidden size (64), MLP width (8)
+and vocabulary (16), since only the attention inputs matter here and no Qwen3-0.6B
+checkpoint is available. ``kv_precision='f16'`` selects the FP16 current-K/V rounding of
+:60-63.
+
+While it runs, two probes record what the reference computes:
+
+* an ``ndarray`` subclass on the q/k/v projection weights records each projection
+  result, i.e. the pre-norm q ``[16,128]`` and k, v ``[8,128]`` of every (token, layer);
+* a wrapper on ``np.einsum`` records the normed+roped query (first operand of the
+  ``'hd,thd->ht'`` call) and the attention output (result of ``'ht,thd->hd'``).
+
+The FP16 K/V rows come from the oracle's own cache payload. The recorded arrays for a few
+layers are written to ``tests/golden/numpyqwen_t{T}.npz``; the tests feed the pre-norm
+inputs to the C++ restatement and to the CUDA library and compare.
+"""
+from __future__ import annotations
+
+import json
+import os
+import struct
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("FPGA_QWEN_REF", "/root/reference"))
+TOKENS = 40                 # covers causal lengths 1..40, incl. the 31/32/33 edges
+KEEP_LAYERS = (0, 27)       # layers written to the fixture
+H, F, V = 64, 8, 16
+SEED = 20261201
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> bfloat16 bits, round to nearest even."""
+    u = x.astype(np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
+def write_checkpoint(path: Path, rng: np.random.Generator) -> None:
+    tensors = {}
+    tensors["model.embed_tokens.weight"] = rng.standard_normal((V, H))
+    tensors["model.norm.weight"] = np.ones(H)
+    for layer in range(28):
+        p = f"model.layers.{layer}."
+        tensors[p + "input_layernorm.weight"] = np.ones(H)
+        tensors[p + "post_attention_layernorm.weight"] = np.ones(H)
+        tensors[p + "self_attn.q_norm.weight"] = rng.normal(1.0, 0.05, 128)
+        tensors[p + "self_attn.k_norm.weight"] = rng.normal(1.0, 0.05, 128)
+        # rows ~ N(0, 1/H) so that projections of the unit-RMS hidden state are ~N(0,1)
+        tensors[p + "self_attn.q_proj.weight"] = rng.standard_normal((2048, H)) / np.sqrt(H)
+        tensors[p + "self_attn.k_proj.weight"] = rng.standard_normal((1024, H)) / np.sqrt(H)
+        tensors[p + "self_attn.v_proj.weight"] = rng.standard_normal((1024, H)) / np.sqrt(H)
+        tensors[p + "self_attn.o_proj.weight"] = rng.standard_normal((H, 2048)) * 0.02
+        tensors[p + "mlp.gate_proj.weight"] = rng.standard_normal((F, H)) * 0.1
+        tensors[p + "mlp.up_proj.weight"] = rng.standard_normal((F, H)) * 0.1
+        tensors[p + "mlp.down_proj.weight"] = rng.standard_normal((H, F)) * 0.1
+    header, blobs, offset = {}, [], 0
+    for name, value in tensors.items():
+        raw = bf16_bits(np.asarray(value, np.float32)).tobytes()
+        header[name] = {"dtype": "BF16", "shape": list(np.shape(value)),
+                        "data_offsets": [offset, offset + len(raw)]}
+        blobs.append(raw)
+        offset += len(raw)
+    head = json.dumps(header).encode()
+    head += b" " * (-len(head) % 8)
+    with path.open("wb") as f:
+        f.write(struct.pack("<Q", len(head)))
+        f.write(head)
+        for raw in blobs:
+            f.write(raw)
+
+
+def main() -> None:
+    sys.path.insert(0, str(REF))
+    from tests.test_full_model import NumpyQwen  # the reference's oracle, unchanged
+
+    rng = np.random.default_rng(SEED)
+    with tempfile.TemporaryDirectory() as tmp:
+        model = Path(tmp)
+        write_checkpoint(model / "model.safetensors", rng)
+        oracle = NumpyQwen(model, weight_precision="bf16", kv_precision="f16")
+
+    log = {}
+    current = {"token": -1}
+
+    class Recorded(np.ndarray):
+        def __array_ufunc__(self, ufunc, method, *inputs, **kwargs):
+            args = [np.asarray(a) if isinstance(a, Recorded) else a for a in inputs]
+            out = getattr(ufunc, method)(*args, **kwargs)
+            if ufunc is np.matmul:
+                log[(current["token"], self.layer, self.kind)] = np.array(out, np.float32)
+            return out
+
+    for layer in range(28):
+        for kind in ("q", "k", "v"):
+            name = f"model.layers.{layer}.self_attn.{kind}_proj.weight"
+            w = oracle.weights[name].view(Recorded)
+            w.layer, w.kind = layer, kind
+            oracle.weights[name] = w
+
+    real_einsum = np.einsum
+    einsum_layer = {"qk": 0, "pv": 0}
+
+    def einsum(subscripts, *operands, **kwargs):
+        out = real_einsum(subscripts, *operands, **kwargs)
+        if subscripts == "hd,thd->ht":
+            log[(current["token"], einsum_layer["qk"], "q_rot")] = np.array(operands[0], np.float32)
+            einsum_layer["qk"] += 1
+        elif subscripts == "ht,thd->hd":
+            log[(current["token"], einsum_layer["pv"], "out")] = np.array(out, np.float32)
+            einsum_layer["pv"] += 1
+        return out
+
+    np.einsum = einsum
+    try:
+        ids = rng.integers(0, V, TOKENS)
+        for t, token in enumerate(ids):
+            current["token"] = t
+            einsum_layer["qk"] = einsum_layer["pv"] = 0
+            oracle.token(int(token), logits=False)
+    finally:
+        np.einsum = real_einsum
+
+    arrays = {"layers": np.array(KEEP_LAYERS, np.int32)}
+    for layer in KEEP_LAYERS:
+        p = f"model.layers.{layer}.self_attn."
+        arrays[f"L{layer}_q_pre"] = np.stack([log[(t, layer, "q")].reshape(16, 128) for t in range(TOKENS)])
+        arrays[f"L{layer}_k_pre"] = np.stack([log[(t, layer, "k")].reshape(8, 128) for t in range(TOKENS)])
+        arrays[f"L{layer}_v_pre"] = np.stack([log[(t, layer, "v")].reshape(8, 128) for t in range(TOKENS)])
+        arrays[f"L{layer}_q_rot"] = np.stack([log[(t, layer, "q_rot")] for t in range(TOKENS)])
+        arrays[f"L{layer}_k16"] = np.stack([oracle.cache[t][layer][0] for t in range(TOKENS)]).astype(np.float32)
+        arrays[f"L{layer}_v16"] = np.stack([oracle.cache[t][layer][1] for t in range(TOKENS)]).astype(np.float32)
+        arrays[f"L{layer}_out"] = np.stack([log[(t, layer, "out")] for t in range(TOKENS)])
+        arrays[f"L{layer}_q_norm"] = np.asarray(oracle.weights[p + "q_norm.weight"], np.float32)
+        arrays[f"L{layer}_k_norm"] = np.asarray(oracle.weights[p + "k_norm.weight"], np.float32)
+    out = HERE / f"numpyqwen_t{TOKENS}.npz"
+    np.savez_compressed(out, **arrays)
+    print(f"wrote {out} ({out.stat().st_size} bytes)")
+
+
+if __name__ == "__main__":
+    main()
