@@ -1,0 +1,419 @@
+#!/usr/bin/env python
+"""Benchmark of the attention + KV-cache hot path (BASELINE metric: decode-attn HBM GB/s &
+prefill-attn TFLOP/s, Qwen3-0.6B GQA, 4K context).
+
+Workload (one "step"): a 3968-token batched prefill — fused KV append
+(QK-RMSNorm + RoPE + FP16 write) and causal GQA prefill attention over all 28 layers —
+followed by 128 single-token decode steps (append + split-context decode attention over all
+28 layers) at contexts 3969..4096. Inputs are seeded synthetic q/k/v generated on the GPU
+(N(0,1); norm weights N(1,0.05)); the Qwen3-0.6B checkpoint is not available.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``value`` is decode-attention GB/s (algorithmic KV+q+out bytes over the device time of the
+decode phase, appends included); ``prefill`` reports TFLOP/s of the prefill phase. With
+N > 1 (torchrun), the 8 KV heads are sharded over the ranks (each keeps its 2 GQA query
+heads) and rank 0 prints the max-over-ranks timing. ``--impl reference`` times the CPU
+restatement of the reference's attention path on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode-attn HBM GB/s & prefill-attn TFLOP/s, Qwen3-0.6B GQA, 4K ctx"
+L, HQ, HKV, D = 28, 16, 8, 128
+PREFILL, DECODE = 3968, 128
+KV_BYTES_PER_POS = L * HKV * D * 2 * 2          # 114,688 B: K and V rows of one position, all layers
+FLOPS_PER_KEY = 4 * D * HQ * L                  # 229,376 FLOP per (query row, visible key), all layers
+
+
+def prefill_flops(pos0: int, n: int, layers: int = L, heads: int = HQ) -> float:
+    keys = n * pos0 + n * (n + 1) // 2           # Σ_{p=pos0}^{pos0+n-1} (p+1)
+    return 4.0 * D * heads * layers * keys
+
+
+def decode_bytes(ctx_len: int, layers: int = L, hkv: int = HKV) -> float:
+    hq = 2 * hkv
+    return layers * hkv * ctx_len * D * 2 * 2 + 2 * layers * hq * D * 4
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------------------------
+class CpuBaseline:
+    """The CPU restatement of the reference's attention path (oracle/, a portable C++ port of
+    engine/core.cpp; the reference's NEON/Accelerate build is Apple-only) on the host cores,
+    over a bounded sample of config 4: decode steps over all 28 layers at contexts 3969..,
+    and layers of the 3968-row causal prefill."""
+
+    def __init__(self, threads: int, max_decode: int = 8, seed: int = 7):
+        from oracle import oracle as O
+        self.O, self.threads = O, threads
+        rng = np.random.default_rng(seed)
+        tables = O.rope_tables(4096)
+        n_total = PREFILL + max_decode
+        self.kvs, self.q = [], []
+        w = np.ones(D, np.float32)
+        for _ in range(L):
+            kv = O.LayerKV(HKV, 4096)
+            q = rng.standard_normal((n_total, HQ, D), dtype=np.float32)
+            k = rng.standard_normal((n_total, HKV, D), dtype=np.float32)
+            v = rng.standard_normal((n_total, HKV, D), dtype=np.float32)
+            self.q.append(O.append(kv, 0, q, k, v, w, w, tables))
+            self.kvs.append(kv)
+        self.max_decode = max_decode
+
+    def decode(self, steps: int):
+        """Returns (algorithmic bytes, seconds) of `steps` decode steps x 28 layers."""
+        t0 = time.perf_counter()
+        moved = 0.0
+        for s in range(steps):
+            pos = PREFILL + (s % self.max_decode)
+            for layer in range(L):
+                self.O.attention(self.kvs[layer], pos, self.q[layer][pos:pos + 1], threads=self.threads)
+            moved += decode_bytes(pos + 1)
+        return moved, time.perf_counter() - t0
+
+    def prefill(self, layers: int = 1):
+        """Returns (algorithmic FLOPs, seconds) of `layers` layers of the 3968-row prefill."""
+        t0 = time.perf_counter()
+        for layer in range(layers):
+            self.O.attention(self.kvs[layer], 0, self.q[layer][:PREFILL], threads=self.threads)
+        return prefill_flops(0, PREFILL, layers=layers), time.perf_counter() - t0
+
+
+def cpu_baseline(threads: int, decode_steps: int = 8, prefill_layers: int = 1):
+    cb = CpuBaseline(threads, max_decode=min(decode_steps, 8))
+    nbytes, td = cb.decode(decode_steps)
+    flops, tp = cb.prefill(prefill_layers)
+    return {"decode_gbs": nbytes / td / 1e9, "decode_s": td,
+            "decode_sample": f"{decode_steps} decode steps x 28 layers at contexts {PREFILL + 1}..{PREFILL + decode_steps}",
+            "prefill_tflops": flops / tp / 1e12, "prefill_s": tp,
+            "prefill_sample": f"{prefill_layers} layer(s) of the {PREFILL}-row causal prefill"}
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement (the reference's Apple-only NEON/Accelerate build
+    cannot compile on x86) with all host threads, rank 0 only. One step = 2 decode steps over
+    all 28 layers at config-4 contexts."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    cb = CpuBaseline(threads, max_decode=2)
+    rates, secs = [], []
+    for i in range(args.warmup + args.steps):
+        nbytes, t = cb.decode(2)
+        if i >= args.warmup:
+            rates.append(nbytes / t / 1e9)
+            secs.append(t)
+    flops, tp = cb.prefill(1)
+    dec = statistics.median(rates)
+    line = {
+        "metric": METRIC, "value": round(dec, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(statistics.median(secs) * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16 KV)", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config4 decode-attention sample: 2 decode steps x 28 layers at ctx 3969-3970",
+                   "layers": L, "q_heads": HQ, "kv_heads": HKV, "head_dim": D},
+        "prefill": {"metric": "prefill-attn TFLOP/s", "value": round(flops / tp / 1e12, 5), "unit": "TFLOP/s",
+                    "sample": f"1 layer of the {PREFILL}-row causal prefill"},
+        "cpu_baseline": {"value": round(dec, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "2 decode steps x 28 layers per step (config 4 contexts); portable C++ "
+                                   "restatement of engine/core.cpp (glibc expf for Accelerate vvexpf)"},
+        "e2e": {"value": round(dec, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from fpga_qwen_b200 import qattn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    if HKV % world:
+        raise SystemExit(f"{HKV} KV heads do not split over {world} ranks")
+    hkv = HKV // world
+    hq = 2 * hkv
+    head0 = rank * hkv
+    seed = 4
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+
+    ctx = qattn.Context(n_layers=L, context=4096, max_seqs=1, kv_head_begin=head0, kv_head_count=hkv, device=local)
+    ctx.set_stream(stream.cuda_stream)
+
+    def synth(kind, pos0, n, heads, h0, mean=0.0, std=1.0):
+        t = torch.empty((L, n, heads, D), dtype=torch.float32, device=dev)
+        qattn.synth_fill(t.data_ptr(), seed, kind, 0, L, pos0, n, h0, heads, mean, std, stream.cuda_stream)
+        return t
+
+    qn_w = synth(3, 0, 1, 1, 0, 1.0, 0.05).reshape(L, D).cpu().numpy()
+    kn_w = synth(4, 0, 1, 1, 0, 1.0, 0.05).reshape(L, D).cpu().numpy()
+    for layer in range(L):
+        a, b = np.ascontiguousarray(qn_w[layer]), np.ascontiguousarray(kn_w[layer])
+        ctx.set_norms(layer, a.ctypes.data, b.ctypes.data)
+    # prefill inputs [L][3968][h][128]; decode inputs per step [L][1][h][128] (layer-major)
+    pq, pk, pv = synth(0, 0, PREFILL, hq, 2 * head0), synth(1, 0, PREFILL, hkv, head0), synth(2, 0, PREFILL, hkv, head0)
+    dq = [synth(0, PREFILL + s, 1, hq, 2 * head0) for s in range(DECODE)]
+    dk = [synth(1, PREFILL + s, 1, hkv, head0) for s in range(DECODE)]
+    dv = [synth(2, PREFILL + s, 1, hkv, head0) for s in range(DECODE)]
+    pqn, pout = torch.empty_like(pq), torch.empty_like(pq)
+    dqn, dout = torch.empty_like(dq[0]), torch.empty_like(dq[0])
+
+    launches_per_step = 0
+
+    def step(evs=None):
+        nonlocal launches_per_step
+        launches = 0
+        ctx.reset(0)
+        if evs:
+            evs["p0"].record(stream)
+        ctx.append(0, 0, L, 0, PREFILL, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), pqn.data_ptr())
+        if evs:
+            evs["pa0"].record(stream)
+        ctx.attn_prefill(0, 0, L, 0, PREFILL, pqn.data_ptr(), pout.data_ptr())
+        if evs:
+            evs["pa1"].record(stream)
+        launches += 2
+        ctx.commit(0, PREFILL)
+        for s in range(DECODE):
+            pos = PREFILL + s
+            ctx.append(0, 0, L, pos, 1, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), dqn.data_ptr())
+            if evs:
+                evs["d0"][s].record(stream)
+            ctx.attn_decode(0, 0, L, pos, 1, dqn.data_ptr(), dout.data_ptr())
+            if evs:
+                evs["d1"][s].record(stream)
+            ctx.commit(0, 1)
+            launches += 2
+        if evs:
+            evs["e"].record(stream)
+        launches_per_step = launches
+
+    def mkev():
+        return torch.cuda.Event(enable_timing=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    records = []
+    sampler = ClockSampler(local)
+    with sampler:
+        start, end = mkev(), mkev()
+        start.record(stream)
+        for _ in range(args.steps):
+            evs = {"p0": mkev(), "pa0": mkev(), "pa1": mkev(), "e": mkev(),
+                   "d0": [mkev() for _ in range(DECODE)], "d1": [mkev() for _ in range(DECODE)]}
+            step(evs)
+            records.append(evs)
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.summary()
+
+    total_ms = start.elapsed_time(end)
+    prefill_ms = [r["p0"].elapsed_time(r["d0"][0]) for r in records]   # prefill phase incl. append
+    decode_ms = [r["pa1"].elapsed_time(r["e"]) for r in records]       # 128 decode steps incl. appends
+    pattn_ms = [r["pa0"].elapsed_time(r["pa1"]) for r in records]
+    dattn_ms = [sum(r["d0"][s].elapsed_time(r["d1"][s]) for s in range(DECODE)) for r in records]
+
+    t = torch.tensor([total_ms, statistics.mean(prefill_ms), statistics.mean(decode_ms),
+                      statistics.mean(pattn_ms), statistics.mean(dattn_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, prefill_phase, decode_phase, pattn, dattn = t.tolist()
+
+    dec_bytes = sum(decode_bytes(PREFILL + s + 1) for s in range(DECODE))      # whole job (all heads)
+    pre_flops = prefill_flops(0, PREFILL)
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    value = dec_bytes / (decode_phase * 1e-3) / 1e9
+    line = None
+    if rank == 0:
+        dec_kernel_gbs = dec_bytes / world / (dattn * 1e-3) / 1e9     # this GPU's kernel bytes / kernel time
+        pre_kernel_tfs = pre_flops / world / (pattn * 1e-3) / 1e12
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32 (fp16 KV)",
+            "data": "synthetic",
+            "config": {"workload": "config4: 3968-token prefill + 128 decode steps, 28 layers, 16 q / 8 kv heads, "
+                                   "head_dim 128, FP16 KV",
+                       "prefill_tokens": PREFILL, "decode_steps": DECODE, "layers": L,
+                       "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (470 MB KV read per decode step, 1.8 GB prefill inputs)"},
+            "decode_phase_ms": round(decode_phase, 3),
+            "prefill": {"metric": "prefill-attn TFLOP/s", "value": round(pre_flops / (prefill_phase * 1e-3) / 1e12, 3),
+                        "unit": "TFLOP/s", "phase_ms": round(prefill_phase, 3),
+                        "roofline": {"bound": "tensor", "achieved": round(pre_kernel_tfs, 3), "peak": tf_peak,
+                                     "unit": "TFLOP/s", "frac": round(pre_kernel_tfs / tf_peak, 4), "traffic": None,
+                                     "peak_kind": f"{peak_kind} bf16 burst (fp16 same dense rate)",
+                                     "kernel_ms": round(pattn, 3)}},
+            "roofline": {"bound": "hbm", "achieved": round(dec_kernel_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(dec_kernel_gbs / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "attn_decode (28 layers per launch)",
+                         "kernel_us": round(dattn / DECODE * 1e3, 2)},
+            "clocks": clocks,
+            "gpu_launches": launches_per_step * args.steps,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    ctx.close()
+    if rank == 0:
+        if world == 1 and not args.no_e2e:
+            line["e2e"] = e2e_decode(args, seed)
+        if world == 1 and not args.no_cpu:
+            cb = cpu_baseline(os.cpu_count() or 1, decode_steps=64)
+            line["cpu_baseline"] = {"value": round(cb["decode_gbs"], 3), "unit": "GB/s", "cores": os.cpu_count(),
+                                    "kind": "port", "sample": cb["decode_sample"],
+                                    "prefill_tflops": round(cb["prefill_tflops"], 5),
+                                    "prefill_sample": cb["prefill_sample"]}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def e2e_decode(args, seed):
+    """Decode GB/s through the C ABI with HOST buffers (io_host=1): per step the host->device
+    copy of that step's q/k/v and the device->host read of the attention output are inside
+    the timed region."""
+    import torch
+    from fpga_qwen_b200 import qattn
+    ctx = qattn.Context(n_layers=L, context=4096, max_seqs=1, io_host=1)
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    def host(kind, pos0, n, heads):
+        t = torch.empty((L, n, heads, D), dtype=torch.float32, device=dev)
+        qattn.synth_fill(t.data_ptr(), seed, kind, 0, L, pos0, n, 0, heads, 0.0, 1.0, None)
+        return t.cpu().pin_memory()
+
+    pq, pk, pv = host(0, 0, PREFILL, HQ), host(1, 0, PREFILL, HKV), host(2, 0, PREFILL, HKV)
+    dq = [host(0, PREFILL + s, 1, HQ) for s in range(DECODE)]
+    dk = [host(1, PREFILL + s, 1, HKV) for s in range(DECODE)]
+    dv = [host(2, PREFILL + s, 1, HKV) for s in range(DECODE)]
+    pqn, pout = torch.empty_like(pq).pin_memory(), torch.empty_like(pq).pin_memory()
+    dqn, dout = torch.empty_like(dq[0]).pin_memory(), torch.empty_like(dq[0]).pin_memory()
+    times = []
+    for it in range(args.warmup + args.steps):
+        ctx.reset(0)
+        ctx.append(0, 0, L, 0, PREFILL, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), pqn.data_ptr())
+        ctx.attn_prefill(0, 0, L, 0, PREFILL, pqn.data_ptr(), pout.data_ptr())
+        ctx.commit(0, PREFILL)
+        t0 = time.perf_counter()
+        for s in range(DECODE):
+            pos = PREFILL + s
+            ctx.append(0, 0, L, pos, 1, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), dqn.data_ptr())
+            ctx.attn_decode(0, 0, L, pos, 1, dqn.data_ptr(), dout.data_ptr())
+            ctx.commit(0, 1)
+        t1 = time.perf_counter()
+        if it >= args.warmup:
+            times.append(t1 - t0)
+    ctx.close()
+    dec_bytes = sum(decode_bytes(PREFILL + s + 1) for s in range(DECODE))
+    t = statistics.median(times)
+    per_step_in = (HQ + 2 * HKV) * D * 4 * L + HQ * D * 4 * L     # q/k/v in + q_out back in
+    per_step_out = 2 * HQ * D * 4 * L                               # q_out and attention out
+    return {"value": round(dec_bytes / t / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": per_step_in * DECODE,
+            "d2h_bytes_per_step": per_step_out * DECODE,
+            "note": "128 decode steps per step, host wall clock around C-ABI calls with host buffers"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

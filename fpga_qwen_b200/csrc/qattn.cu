@@ -1,0 +1,433 @@
+// qattn.cu — context, validation and the C ABI of libqattn.so (declared in include/qattn.h).
+//
+// The context owns everything the reference's Model::Impl owns for this path
+// (engine/core.cpp:223-232, :277, :287-288): the FP16 KV history (here in HBM, one slot per
+// sequence), the RoPE tables, the per-layer q_norm/k_norm weights and the logical position
+// `pos` of each sequence. All validation happens on the host before any launch, so a call
+// that fails validation leaves the state unchanged (core.hpp:32-33, :41).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/qattn.h"
+#include "../../include/qattn_synth.h"
+#include "qattn_common.cuh"
+
+using namespace qattn;
+
+struct qa_ctx {
+    qa_config cfg{};
+    int hq = 0, hkv = 0;                   // local heads
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    KVLayout kv{};
+    float* norms = nullptr;                // [L][2][128]
+    float* cosines = nullptr;              // [ctx][64]
+    float* sines = nullptr;
+    std::vector<int> pos;                  // committed position per sequence
+    std::vector<std::vector<int>> appended;  // per sequence, per layer: rows written through
+    float* partial = nullptr;              // split-context records
+    size_t partial_floats = 0;
+    int* counters = nullptr;
+    int max_units = 0;
+    float* staging = nullptr;              // device staging for io_host calls
+    size_t staging_floats = 0;
+    std::string err;
+};
+
+namespace {
+
+int fail(qa_ctx* c, int status, const char* fmt, ...) {
+    if (c) {
+        char buf[512];
+        va_list ap; va_start(ap, fmt); vsnprintf(buf, sizeof buf, fmt, ap); va_end(ap);
+        c->err = buf;
+    }
+    return status;
+}
+
+int cuda_fail(qa_ctx* c, cudaError_t e, const char* what) {
+    return fail(c, e == cudaErrorMemoryAllocation ? QA_ERR_OOM : QA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define QA_CUDA(call)                                                  \
+    do {                                                               \
+        cudaError_t e_ = (call);                                       \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call);       \
+    } while (0)
+
+// After a launch or device error the affected sequence restarts from position 0, like the
+// engine's "Errors ... reset all model ... state" (engine/INTERFACE.md error contract).
+int after_launch(qa_ctx* ctx, int seq, const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return QA_OK;
+    if (seq >= 0 && seq < (int)ctx->pos.size()) {
+        ctx->pos[seq] = 0;
+        std::fill(ctx->appended[seq].begin(), ctx->appended[seq].end(), 0);
+    }
+    return cuda_fail(ctx, e, what);
+}
+
+int check_seq(qa_ctx* ctx, int seq) {
+    if (seq < 0 || seq >= ctx->cfg.max_seqs) return fail(ctx, QA_ERR_INVALID, "sequence %d out of range [0,%d)", seq, ctx->cfg.max_seqs);
+    return QA_OK;
+}
+
+int check_layers(qa_ctx* ctx, int layer, int n_layers) {
+    if (layer < 0 || n_layers < 1 || layer + n_layers > ctx->cfg.n_layers)
+        return fail(ctx, QA_ERR_INVALID, "layer range [%d,%d) outside [0,%d)", layer, layer + n_layers, ctx->cfg.n_layers);
+    return QA_OK;
+}
+
+// Common validation of the hot-path calls: rows [pos0, pos0+n) at the committed position.
+int check_rows(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n) {
+    int st;
+    if ((st = check_seq(ctx, seq))) return st;
+    if ((st = check_layers(ctx, layer, n_layers))) return st;
+    if (n < 1) return fail(ctx, QA_ERR_INVALID, "empty input (n=%d)", n);
+    if (pos0 != ctx->pos[seq])
+        return fail(ctx, QA_ERR_STATE, "pos0 %d differs from the sequence position %d", pos0, ctx->pos[seq]);
+    if (n > ctx->cfg.context - pos0)
+        return fail(ctx, QA_ERR_CAPACITY, "context capacity exceeded: %d + %d > %d", pos0, n, ctx->cfg.context);
+    return QA_OK;
+}
+
+int check_appended(qa_ctx* ctx, int seq, int layer, int n_layers, int end) {
+    for (int l = layer; l < layer + n_layers; ++l)
+        if (ctx->appended[seq][l] < end)
+            return fail(ctx, QA_ERR_STATE, "layer %d holds rows through %d, attention needs %d", l, ctx->appended[seq][l], end);
+    return QA_OK;
+}
+
+// Device staging for io_host calls: grows on demand (the only allocation after create).
+int ensure_staging(qa_ctx* ctx, size_t floats) {
+    if (floats <= ctx->staging_floats) return QA_OK;
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (ctx->staging) cudaFree(ctx->staging);
+    ctx->staging = nullptr; ctx->staging_floats = 0;
+    QA_CUDA(cudaMalloc(&ctx->staging, floats * sizeof(float)));
+    ctx->staging_floats = floats;
+    return QA_OK;
+}
+
+// Chooses the split count for split-context attention over `units` (layer, row, head)
+// work items whose longest context is max_len keys: enough CTAs to cover the SMs several
+// times over, at least 64 keys per split, record space permitting.
+void choose_splits(const qa_ctx* ctx, long long units, int max_len, int& splits, int& kps) {
+    const long long target = (long long)NUM_SMS_B200 * 8;
+    long long s = std::max<long long>(1, (target + units - 1) / units);
+    s = std::min<long long>(s, (max_len + 63) / 64);
+    const long long cap = (long long)(ctx->partial_floats / PARTIAL_FLOATS) / std::max<long long>(1, units);
+    s = std::max<long long>(1, std::min(s, cap));
+    kps = (int)(((max_len + s - 1) / s + 31) / 32 * 32);
+    splits = (max_len + kps - 1) / kps;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* qa_version(void) { return "qattn 0.1 sm_100a"; }
+
+const char* qa_status_string(int status) {
+    switch (status) {
+        case QA_OK: return "ok";
+        case QA_ERR_INVALID: return "invalid argument";
+        case QA_ERR_CAPACITY: return "context capacity exceeded";
+        case QA_ERR_STATE: return "invalid state";
+        case QA_ERR_CUDA: return "CUDA error";
+        case QA_ERR_NCCL: return "NCCL error";
+        case QA_ERR_TIMEOUT: return "device wait timed out";
+        case QA_ERR_OOM: return "out of device memory";
+        case QA_ERR_UNSUPPORTED: return "unsupported";
+        default: return "unknown status";
+    }
+}
+
+void qa_default_config(qa_config* c) {
+    if (!c) return;
+    std::memset(c, 0, sizeof *c);
+    c->n_layers = 28; c->n_q_heads = 16; c->n_kv_heads = 8; c->head_dim = 128;
+    c->context = QA_MAX_CONTEXT; c->max_seqs = 1; c->kv_head_begin = 0; c->kv_head_count = 0;
+    c->rope_theta = 1000000.0; c->norm_eps = 1e-6f; c->device = 0; c->io_host = 0;
+}
+
+const char* qa_last_error(const qa_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int qa_create(const qa_config* cfg, qa_ctx** out) {
+    if (!cfg || !out) return QA_ERR_INVALID;
+    *out = nullptr;
+    qa_config c = *cfg;
+    if (c.kv_head_count == 0) c.kv_head_count = c.n_kv_heads;
+    // Shape limits: Qwen3-0.6B attention (core.cpp:28, :236-237).
+    if (c.head_dim != D) return QA_ERR_UNSUPPORTED;
+    if (c.n_kv_heads < 1 || c.n_q_heads != GROUP * c.n_kv_heads) return QA_ERR_UNSUPPORTED;
+    if (c.n_layers < 1 || c.n_layers > 64) return QA_ERR_INVALID;
+    if (c.context < 1 || c.context > QA_MAX_CONTEXT) return QA_ERR_INVALID;
+    if (c.max_seqs < 1 || c.max_seqs > 4096) return QA_ERR_INVALID;
+    if (c.kv_head_begin < 0 || c.kv_head_count < 1 || c.kv_head_begin + c.kv_head_count > c.n_kv_heads) return QA_ERR_INVALID;
+    if (!(c.rope_theta > 1.0) || !(c.norm_eps > 0.f)) return QA_ERR_INVALID;
+
+    qa_ctx* ctx = new (std::nothrow) qa_ctx();
+    if (!ctx) return QA_ERR_OOM;
+    ctx->cfg = c;
+    ctx->hkv = c.kv_head_count;
+    ctx->hq = GROUP * c.kv_head_count;
+    auto cleanup = [&](int st) { qa_destroy(ctx); return st; };
+
+    if (cudaSetDevice(c.device) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+    if (cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+    ctx->stream = ctx->own_stream;
+
+    ctx->kv.layers = c.n_layers; ctx->kv.hkv = ctx->hkv; ctx->kv.ctx = c.context;
+    const size_t kv_bytes = ctx->kv.slot_elems() * sizeof(__half) * c.max_seqs;
+    if (cudaMalloc(&ctx->kv.base, kv_bytes) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMemset(ctx->kv.base, 0, kv_bytes) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+
+    // RoPE tables exactly as core.cpp:288 computes them (FP64 angle, FP64 cos/sin, FP32 store).
+    std::vector<float> cs((size_t)c.context * 64), sn(cs.size());
+    for (int p = 0; p < c.context; ++p)
+        for (int j = 0; j < 64; ++j) {
+            const double angle = p / std::pow(c.rope_theta, 2.0 * j / D);
+            cs[(size_t)p * 64 + j] = (float)std::cos(angle);
+            sn[(size_t)p * 64 + j] = (float)std::sin(angle);
+        }
+    if (cudaMalloc(&ctx->cosines, cs.size() * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMalloc(&ctx->sines, sn.size() * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMemcpy(ctx->cosines, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+    if (cudaMemcpy(ctx->sines, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+
+    std::vector<float> ones((size_t)c.n_layers * 2 * D, 1.0f);
+    if (cudaMalloc(&ctx->norms, ones.size() * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMemcpy(ctx->norms, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+
+    // Split-context records: every (layer, decode row, head) unit with up to 32 splits.
+    ctx->max_units = c.n_layers * QA_MAX_DECODE_ROWS * ctx->hkv;
+    ctx->partial_floats = (size_t)ctx->max_units * 32 * PARTIAL_FLOATS;
+    if (cudaMalloc(&ctx->partial, ctx->partial_floats * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMalloc(&ctx->counters, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMemset(ctx->counters, 0, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+
+    ctx->pos.assign(c.max_seqs, 0);
+    ctx->appended.assign(c.max_seqs, std::vector<int>(c.n_layers, 0));
+    if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(QA_ERR_CUDA);
+    *out = ctx;
+    return QA_OK;
+}
+
+void qa_destroy(qa_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->cfg.device);
+    if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
+    if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
+    cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->staging);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+}
+
+int qa_set_stream(qa_ctx* ctx, void* s) {
+    if (!ctx) return QA_ERR_INVALID;
+    ctx->stream = s ? static_cast<cudaStream_t>(s) : ctx->own_stream;
+    return QA_OK;
+}
+
+int qa_sync(qa_ctx* ctx) {
+    if (!ctx) return QA_ERR_INVALID;
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    return QA_OK;
+}
+
+int qa_set_norms(qa_ctx* ctx, int layer, const float* q_norm, const float* k_norm) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_layers(ctx, layer, 1))) return st;
+    if (!q_norm || !k_norm) return fail(ctx, QA_ERR_INVALID, "null norm weights");
+    for (int j = 0; j < D; ++j)
+        if (!std::isfinite(q_norm[j]) || !std::isfinite(k_norm[j]))
+            return fail(ctx, QA_ERR_INVALID, "nonfinite norm weight in layer %d", layer);  // core.cpp:271
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    float* dst = ctx->norms + (size_t)layer * 2 * D;
+    QA_CUDA(cudaMemcpyAsync(dst, q_norm, D * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+    QA_CUDA(cudaMemcpyAsync(dst + D, k_norm, D * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    return QA_OK;
+}
+
+int qa_position(const qa_ctx* ctx, int seq, int* pos) {
+    if (!ctx || !pos) return QA_ERR_INVALID;
+    if (seq < 0 || seq >= ctx->cfg.max_seqs) return QA_ERR_INVALID;
+    *pos = ctx->pos[seq];
+    return QA_OK;
+}
+
+int qa_reset(qa_ctx* ctx, int seq) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_seq(ctx, seq))) return st;
+    ctx->pos[seq] = 0;
+    std::fill(ctx->appended[seq].begin(), ctx->appended[seq].end(), 0);
+    return QA_OK;
+}
+
+int qa_truncate(qa_ctx* ctx, int seq, int pos) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_seq(ctx, seq))) return st;
+    if (pos < 0 || pos > ctx->pos[seq])
+        return fail(ctx, QA_ERR_STATE, "Rewind position out of range: %d not in [0,%d]", pos, ctx->pos[seq]);  // core.cpp:723
+    ctx->pos[seq] = pos;
+    for (int& a : ctx->appended[seq]) a = std::min(a, pos);
+    return QA_OK;
+}
+
+int qa_commit(qa_ctx* ctx, int seq, int n) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_seq(ctx, seq))) return st;
+    if (n < 1) return fail(ctx, QA_ERR_INVALID, "commit count %d < 1", n);
+    if (n > ctx->cfg.context - ctx->pos[seq]) return fail(ctx, QA_ERR_CAPACITY, "commit past context capacity");
+    if ((st = check_appended(ctx, seq, 0, ctx->cfg.n_layers, ctx->pos[seq] + n))) return st;
+    ctx->pos[seq] += n;
+    return QA_OK;
+}
+
+int qa_append(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n,
+              const float* q_pre, const float* k_pre, const float* v, float* q_out) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_rows(ctx, seq, layer, n_layers, pos0, n))) return st;
+    if (!q_pre || !k_pre || !v || !q_out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const size_t qn = (size_t)n_layers * n * ctx->hq * D, kn = (size_t)n_layers * n * ctx->hkv * D;
+    AppendArgs a{};
+    a.q_pre = q_pre; a.k_pre = k_pre; a.v_pre = v; a.q_out = q_out;
+    if (ctx->cfg.io_host) {
+        if ((st = ensure_staging(ctx, 2 * qn + 2 * kn))) return st;
+        float* s = ctx->staging;
+        QA_CUDA(cudaMemcpyAsync(s, q_pre, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        QA_CUDA(cudaMemcpyAsync(s + qn, k_pre, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        QA_CUDA(cudaMemcpyAsync(s + qn + kn, v, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        a.q_pre = s; a.k_pre = s + qn; a.v_pre = s + qn + kn; a.q_out = s + qn + 2 * kn;
+    }
+    a.kv = ctx->kv; a.seq = seq; a.layer0 = layer; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
+    a.hq = ctx->hq; a.hkv = ctx->hkv; a.norms = ctx->norms; a.cosines = ctx->cosines; a.sines = ctx->sines;
+    a.eps = ctx->cfg.norm_eps;
+    launch_kv_append(a, ctx->stream);
+    if ((st = after_launch(ctx, seq, "kv_append"))) return st;
+    for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seq][l] = pos0 + n;
+    if (ctx->cfg.io_host) {
+        QA_CUDA(cudaMemcpyAsync(q_out, a.q_out, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
+    return QA_OK;
+}
+
+static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q, float* out,
+                  bool decode) {
+    int st;
+    if ((st = check_rows(ctx, seq, layer, n_layers, pos0, n))) return st;
+    if (decode && n > QA_MAX_DECODE_ROWS)
+        return fail(ctx, QA_ERR_INVALID, "decode takes at most %d rows, got %d", QA_MAX_DECODE_ROWS, n);
+    if (!q || !out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
+    if ((st = check_appended(ctx, seq, layer, n_layers, pos0 + n))) return st;
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const size_t qn = (size_t)n_layers * n * ctx->hq * D;
+    const float* qd = q; float* od = out;
+    if (ctx->cfg.io_host) {
+        if ((st = ensure_staging(ctx, 2 * qn))) return st;
+        QA_CUDA(cudaMemcpyAsync(ctx->staging, q, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        qd = ctx->staging; od = ctx->staging + qn;
+    }
+    RowsArgs r{};
+    r.q = qd; r.out = od; r.kv = ctx->kv; r.seq = seq; r.layer0 = layer; r.n_layers = n_layers;
+    r.pos0 = pos0; r.n = n; r.hq = ctx->hq; r.hkv = ctx->hkv; r.row_begin = 0; r.row_end = n;
+    r.partial = ctx->partial; r.counters = ctx->counters;
+    if (decode) {
+        choose_splits(ctx, (long long)n_layers * n * ctx->hkv, pos0 + n, r.splits, r.keys_per_split);
+    } else {
+        r.splits = 1; r.keys_per_split = ((pos0 + n) + 31) / 32 * 32;
+    }
+    launch_attn_rows(r, ctx->stream);
+    if ((st = after_launch(ctx, seq, decode ? "attn_decode" : "attn_prefill"))) return st;
+    if (ctx->cfg.io_host) {
+        QA_CUDA(cudaMemcpyAsync(out, od, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
+    return QA_OK;
+}
+
+int qa_attn_prefill(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q, float* out) {
+    if (!ctx) return QA_ERR_INVALID;
+    return attend(ctx, seq, layer, n_layers, pos0, n, q, out, false);
+}
+
+int qa_attn_decode(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q, float* out) {
+    if (!ctx) return QA_ERR_INVALID;
+    return attend(ctx, seq, layer, n_layers, pos0, n, q, out, true);
+}
+
+int qa_copy_prefix(qa_ctx* ctx, int src, int dst, int ntok) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_seq(ctx, src)) || (st = check_seq(ctx, dst))) return st;
+    if (src == dst) return fail(ctx, QA_ERR_INVALID, "prefix copy onto itself");
+    if (ntok < QA_PREFIX_CHUNK || ntok % QA_PREFIX_CHUNK)
+        return fail(ctx, QA_ERR_INVALID, "prefix length %d is not a positive multiple of %d", ntok, QA_PREFIX_CHUNK);
+    if (ntok > ctx->pos[src]) return fail(ctx, QA_ERR_STATE, "source holds %d committed rows, copy wants %d", ctx->pos[src], ntok);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    launch_kv_copy(ctx->kv, src, dst, ntok, ctx->stream);
+    if ((st = after_launch(ctx, dst, "kv_copy"))) return st;
+    ctx->pos[dst] = ntok;
+    std::fill(ctx->appended[dst].begin(), ctx->appended[dst].end(), ntok);
+    return QA_OK;
+}
+
+int qa_read_kv(qa_ctx* ctx, int seq, int layer, int kv, int head, int pos0, int n, uint16_t* dst) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_seq(ctx, seq)) || (st = check_layers(ctx, layer, 1))) return st;
+    if (kv < 0 || kv > 1 || head < 0 || head >= ctx->hkv) return fail(ctx, QA_ERR_INVALID, "bad kv/head selector");
+    if (pos0 < 0 || n < 0 || pos0 + n > ctx->cfg.context) return fail(ctx, QA_ERR_INVALID, "rows outside the context");
+    if (!dst && n) return fail(ctx, QA_ERR_INVALID, "null destination");
+    if (!n) return QA_OK;
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const __half* src = ctx->kv.plane(seq, layer, kv, head) + (size_t)pos0 * D;
+    QA_CUDA(cudaMemcpyAsync(dst, src, (size_t)n * D * sizeof(__half), cudaMemcpyDeviceToHost, ctx->stream));
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    return QA_OK;
+}
+
+int qa_kv_pointer(qa_ctx* ctx, int seq, int layer, int kv, int head, void** ptr) {
+    if (!ctx || !ptr) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_seq(ctx, seq)) || (st = check_layers(ctx, layer, 1))) return st;
+    if (kv < 0 || kv > 1 || head < 0 || head >= ctx->hkv) return fail(ctx, QA_ERR_INVALID, "bad kv/head selector");
+    *ptr = ctx->kv.plane(seq, layer, kv, head);
+    return QA_OK;
+}
+
+int qa_kv_slot_bytes(const qa_ctx* ctx, size_t* bytes) {
+    if (!ctx || !bytes) return QA_ERR_INVALID;
+    *bytes = ctx->kv.slot_elems() * sizeof(__half);
+    return QA_OK;
+}
+
+int qa_synth_fill(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n, int head0,
+                  int heads, float mean, float stdev, void* stream) {
+    if (!dst || kind < 0 || kind > 4 || layer0 < 0 || layer0 + n_layers > 64 || n_layers < 1 || pos0 < 0 || n < 1 ||
+        pos0 + n > 8192 || head0 < 0 || heads < 1 || head0 + heads > 64)
+        return QA_ERR_INVALID;
+    launch_synth(dst, seed, kind, layer0, n_layers, pos0, n, head0, heads, mean, stdev, static_cast<cudaStream_t>(stream));
+    return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_CUDA;
+}
+
+}  // extern "C"

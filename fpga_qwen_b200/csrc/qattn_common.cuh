@@ -1,0 +1,57 @@
+// Shared definitions of the qattn CUDA library: KV layout, launch argument blocks and
+// the kernel launchers implemented in the per-kernel .cu files.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace qattn {
+
+constexpr int D = 128;          // head_dim
+constexpr int GROUP = 2;        // query heads per KV head (Qwen3-0.6B: 16 / 8)
+constexpr int NUM_SMS_B200 = 148;
+
+// HBM KV store: [seq][layer][K|V][kv_head][pos][128] FP16 (256-byte rows).
+struct KVLayout {
+    __half* base = nullptr;
+    int layers = 0, hkv = 0, ctx = 0;
+    __host__ __device__ size_t plane_elems() const { return size_t(ctx) * D; }
+    __host__ __device__ size_t slot_elems() const { return size_t(layers) * 2 * hkv * plane_elems(); }
+    __host__ __device__ __half* plane(int seq, int layer, int kv, int head) const {
+        return base + ((((size_t(seq) * layers + layer) * 2 + kv) * hkv + head) * size_t(ctx)) * D;
+    }
+};
+
+struct AppendArgs {
+    const float* q_pre; const float* k_pre; const float* v_pre; float* q_out;
+    KVLayout kv; int seq; int layer0; int n_layers; int pos0; int n; int hq; int hkv;
+    const float* norms;      // [layers][2][128]: q_norm, k_norm
+    const float* cosines;    // [ctx][64]
+    const float* sines;      // [ctx][64]
+    float eps;
+};
+
+// Split-context attention over explicit rows. Row b of the call sits at absolute position
+// pos0+b and attends to keys [0, pos0+b]. Rows [row_begin, row_end) are computed.
+struct RowsArgs {
+    const float* q; float* out;     // [n_layers][n][hq][128]
+    KVLayout kv; int seq; int layer0; int n_layers; int pos0; int n; int hq; int hkv;
+    int row_begin, row_end;
+    int splits, keys_per_split;
+    float* partial;                 // [units][splits][4 + 2*128] when splits > 1
+    int* counters;                  // [units], zero between calls
+};
+
+void launch_kv_append(const AppendArgs& a, cudaStream_t s);
+void launch_attn_rows(const RowsArgs& a, cudaStream_t s);
+void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cudaStream_t s);
+void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n,
+                  int head0, int heads, float mean, float stdev, cudaStream_t s);
+
+// Partial record size (floats) of one split in RowsArgs::partial.
+constexpr int PARTIAL_FLOATS = 4 + GROUP * D;
+
+}  // namespace qattn

@@ -1,0 +1,207 @@
+"""ctypes binding of libqattn.so (the C ABI in include/qattn.h).
+
+This is a thin, 1:1 binding: every function returns the C status and raises ``QAttnError``
+with ``qa_last_error`` on failure. Tensor arguments are raw addresses (``int``): device
+addresses for contexts created with ``io_host=0`` (e.g. ``torch.Tensor.data_ptr()``), host
+addresses for ``io_host=1`` (e.g. ``numpy.ndarray.ctypes.data``).
+
+The library must exist: there is no fallback. Build it with ``python -m fpga_qwen_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libqattn.so"
+
+QA_OK = 0
+STATUS = {1: "invalid argument", 2: "context capacity exceeded", 3: "invalid state", 4: "CUDA error",
+          5: "NCCL error", 6: "device wait timed out", 7: "out of device memory", 8: "unsupported"}
+QA_ERR_INVALID, QA_ERR_CAPACITY, QA_ERR_STATE, QA_ERR_CUDA = 1, 2, 3, 4
+QA_ERR_NCCL, QA_ERR_TIMEOUT, QA_ERR_OOM, QA_ERR_UNSUPPORTED = 5, 6, 7, 8
+PREFIX_CHUNK = 512
+MAX_DECODE_ROWS = 4
+HEAD_DIM = 128
+
+
+class QAttnError(RuntimeError):
+    """A non-zero status from the C ABI (the C++ engine maps these to std::runtime_error)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS.get(status, 'error')} ({status}): {message}")
+        self.status = status
+
+
+class Config(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int), ("n_q_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("context", ctypes.c_int), ("max_seqs", ctypes.c_int),
+                ("kv_head_begin", ctypes.c_int), ("kv_head_count", ctypes.c_int),
+                ("rope_theta", ctypes.c_double), ("norm_eps", ctypes.c_float), ("device", ctypes.c_int),
+                ("io_host", ctypes.c_int)]
+
+
+_lib = None
+
+_SIGNATURES = {
+    "qa_default_config": (None, [ctypes.POINTER(Config)]),
+    "qa_create": (ctypes.c_int, [ctypes.POINTER(Config), ctypes.POINTER(ctypes.c_void_p)]),
+    "qa_destroy": (None, [ctypes.c_void_p]),
+    "qa_last_error": (ctypes.c_char_p, [ctypes.c_void_p]),
+    "qa_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "qa_version": (ctypes.c_char_p, []),
+    "qa_set_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "qa_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_set_norms": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "qa_position": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "qa_reset": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "qa_truncate": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
+    "qa_commit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
+    "qa_append": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                 ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                 ctypes.c_void_p]),
+    "qa_attn_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "qa_attn_decode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "qa_copy_prefix": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "qa_read_kv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "qa_kv_pointer": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.POINTER(ctypes.c_void_p)]),
+    "qa_kv_slot_bytes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "qa_synth_fill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                     ctypes.c_float, ctypes.c_void_p]),
+}
+
+EXPORTS = tuple(_SIGNATURES)
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libqattn.so (raises if it was not built: there is no fallback path)."""
+    global _lib
+    if _lib is None:
+        path = Path(os.environ.get("QATTN_LIB", LIB_PATH))
+        if not path.exists():
+            raise RuntimeError(f"{path} is missing; build it with `python -m fpga_qwen_b200.build`")
+        handle = ctypes.CDLL(str(path))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = handle
+    return _lib
+
+
+def default_config(**overrides) -> Config:
+    cfg = Config()
+    lib().qa_default_config(ctypes.byref(cfg))
+    for key, value in overrides.items():
+        if not hasattr(cfg, key):
+            raise TypeError(f"unknown config field {key}")
+        setattr(cfg, key, value)
+    return cfg
+
+
+class Context:
+    """Owns one ``qa_ctx``: the HBM KV store of ``max_seqs`` sequence slots and its state."""
+
+    def __init__(self, **config):
+        self.config = default_config(**config)
+        handle = ctypes.c_void_p()
+        st = lib().qa_create(ctypes.byref(self.config), ctypes.byref(handle))
+        if st != QA_OK:
+            raise QAttnError(st, "qa_create failed")
+        self._h = handle
+        heads = self.config.kv_head_count or self.config.n_kv_heads
+        self.hkv = heads
+        self.hq = heads * (self.config.n_q_heads // self.config.n_kv_heads)
+
+    # -- helpers ---------------------------------------------------------------------------
+    def _check(self, st: int):
+        if st != QA_OK:
+            raise QAttnError(st, lib().qa_last_error(self._h).decode())
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().qa_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def handle(self):
+        return self._h
+
+    # -- ABI -------------------------------------------------------------------------------
+    def set_stream(self, stream_ptr: int | None):
+        """Run on a cudaStream_t. 0 is the legacy default stream (torch's default stream
+        reports 0; it is passed as cudaStreamLegacy); None restores the context's own stream."""
+        if stream_ptr == 0:
+            stream_ptr = 1          # cudaStreamLegacy
+        self._check(lib().qa_set_stream(self._h, stream_ptr))
+
+    def sync(self):
+        self._check(lib().qa_sync(self._h))
+
+    def set_norms(self, layer: int, q_norm_ptr: int, k_norm_ptr: int):
+        self._check(lib().qa_set_norms(self._h, layer, q_norm_ptr, k_norm_ptr))
+
+    def position(self, seq: int = 0) -> int:
+        out = ctypes.c_int()
+        st = lib().qa_position(self._h, seq, ctypes.byref(out))
+        if st != QA_OK:
+            raise QAttnError(st, "bad sequence")
+        return out.value
+
+    def reset(self, seq: int = 0):
+        self._check(lib().qa_reset(self._h, seq))
+
+    def truncate(self, seq: int, pos: int):
+        self._check(lib().qa_truncate(self._h, seq, pos))
+
+    def commit(self, seq: int, n: int):
+        self._check(lib().qa_commit(self._h, seq, n))
+
+    def append(self, seq, layer, n_layers, pos0, n, q_pre, k_pre, v, q_out):
+        self._check(lib().qa_append(self._h, seq, layer, n_layers, pos0, n, q_pre, k_pre, v, q_out))
+
+    def attn_prefill(self, seq, layer, n_layers, pos0, n, q, out):
+        self._check(lib().qa_attn_prefill(self._h, seq, layer, n_layers, pos0, n, q, out))
+
+    def attn_decode(self, seq, layer, n_layers, pos0, n, q, out):
+        self._check(lib().qa_attn_decode(self._h, seq, layer, n_layers, pos0, n, q, out))
+
+    def copy_prefix(self, src: int, dst: int, ntok: int):
+        self._check(lib().qa_copy_prefix(self._h, src, dst, ntok))
+
+    def read_kv(self, seq, layer, kv, head, pos0, n, dst_ptr):
+        self._check(lib().qa_read_kv(self._h, seq, layer, kv, head, pos0, n, dst_ptr))
+
+    def kv_pointer(self, seq, layer, kv, head) -> int:
+        out = ctypes.c_void_p()
+        self._check(lib().qa_kv_pointer(self._h, seq, layer, kv, head, ctypes.byref(out)))
+        return out.value
+
+    def kv_slot_bytes(self) -> int:
+        out = ctypes.c_size_t()
+        self._check(lib().qa_kv_slot_bytes(self._h, ctypes.byref(out)))
+        return out.value
+
+
+def synth_fill(dst_ptr: int, seed: int, kind: int, layer0: int, n_layers: int, pos0: int, n: int,
+               head0: int, heads: int, mean: float = 0.0, std: float = 1.0, stream: int | None = None):
+    st = lib().qa_synth_fill(dst_ptr, seed & 0xFFFFFFFFFFFFFFFF, kind, layer0, n_layers, pos0, n, head0, heads,
+                             mean, std, stream or None)
+    if st != QA_OK:
+        raise QAttnError(st, "qa_synth_fill failed")

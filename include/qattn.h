@@ -1,0 +1,148 @@
+/* qattn.h — C ABI of the B200 attention + KV-cache library (libqattn.so).
+ *
+ * Drop-in boundary for the attention and KV-cache hot path of tampajohn/fpga-qwen's C++
+ * Qwen3-0.6B engine. The engine's Model::Impl (engine/core.cpp) keeps its projections,
+ * MLP, sampler and protocol; the lines that own the FP16 KV history and compute
+ * QK-RMSNorm, RoPE, the FP16 KV write and causal GQA attention become calls below.
+ * Each declaration names the reference code it replaces.
+ *
+ * Conventions
+ *   - Every entry point returns int status (QA_OK == 0). Validation happens before any
+ *     state change or launch: a call that fails validation leaves the context unchanged
+ *     (engine/core.hpp:32-33, :41; core.cpp:708-710, :723). qa_last_error() describes
+ *     the most recent failure.
+ *   - One host thread per context at a time ("One caller at a time", core.hpp:23).
+ *   - Tensor arguments are FP32, row-major, heads innermost-but-one:
+ *        q      [n_layers][n][hq_local][128]
+ *        k, v   [n_layers][n][hkv_local][128]
+ *        out    [n_layers][n][hq_local][128]
+ *     where hkv_local = kv_head_count and hq_local = kv_head_count * (n_q_heads/n_kv_heads).
+ *     Device pointers when the context was created with io_host = 0 (calls are
+ *     asynchronous on the context's stream); host pointers when io_host = 1 (the call
+ *     stages through device buffers and returns after the results are in host memory).
+ *   - KV history lives in HBM, one slot per sequence, laid out
+ *        [seq][layer][K|V][kv_head][pos][128] FP16, 256-byte rows
+ *     (reference: two arrays [layer][head][pos][128], core.cpp:223, :277, :350-352).
+ */
+#ifndef QATTN_H
+#define QATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    QA_OK = 0,
+    QA_ERR_INVALID = 1,     /* bad argument; nothing changed                         */
+    QA_ERR_CAPACITY = 2,    /* context capacity exceeded (core.cpp:709); nothing changed */
+    QA_ERR_STATE = 3,       /* not valid in the sequence's current state; nothing changed */
+    QA_ERR_CUDA = 4,        /* CUDA error; the sequence is reset to position 0        */
+    QA_ERR_NCCL = 5,        /* NCCL error                                             */
+    QA_ERR_TIMEOUT = 6,     /* a bounded device-side wait expired                     */
+    QA_ERR_OOM = 7,         /* device allocation failed                               */
+    QA_ERR_UNSUPPORTED = 8  /* shape or feature this build does not support           */
+};
+
+#define QA_HEAD_DIM 128
+#define QA_MAX_CONTEXT 4096
+#define QA_PREFIX_CHUNK 512       /* canonical prefix-reuse granule, core.hpp:10 */
+#define QA_MAX_DECODE_ROWS 4      /* rows per qa_attn_decode call (1 = step, 2 = B2 verify) */
+
+typedef struct qa_config {
+    int n_layers;        /* 28                                                       */
+    int n_q_heads;       /* 16 (global)                                              */
+    int n_kv_heads;      /* 8 (global); GQA group = n_q_heads / n_kv_heads           */
+    int head_dim;        /* must be 128                                              */
+    int context;         /* 1..4096 positions per sequence (core.cpp:237)            */
+    int max_seqs;        /* sequence slots held in HBM                               */
+    int kv_head_begin;   /* first global KV head this context holds (head sharding)  */
+    int kv_head_count;   /* KV heads held; 0 means all n_kv_heads                    */
+    double rope_theta;   /* 1e6 (core.cpp:288)                                       */
+    float norm_eps;      /* 1e-6 (core.cpp:213)                                      */
+    int device;          /* CUDA device ordinal                                      */
+    int io_host;         /* 0: tensor pointers are device memory; 1: host memory     */
+} qa_config;
+
+typedef struct qa_ctx qa_ctx;
+
+/* Fills the Qwen3-0.6B defaults: 28 layers, 16/8 heads, 128, context 4096, 1 slot. */
+void qa_default_config(qa_config* cfg);
+
+/* Allocates the HBM KV store, RoPE tables and norm weights.
+ * Replaces Model::Impl's KV allocation and table set-up, core.cpp:236-237, :277, :287-288. */
+int qa_create(const qa_config* cfg, qa_ctx** out);
+void qa_destroy(qa_ctx* ctx);
+
+const char* qa_last_error(const qa_ctx* ctx);
+const char* qa_status_string(int status);
+/* Library build identification, e.g. "qattn sm_100a". */
+const char* qa_version(void);
+
+/* Runs subsequent work on an external cudaStream_t (NULL restores the context's own). */
+int qa_set_stream(qa_ctx* ctx, void* cuda_stream);
+/* Blocks until all work issued on the context's stream has finished. */
+int qa_sync(qa_ctx* ctx);
+
+/* Per-layer q_norm / k_norm weights [128] FP32, host pointers (pack tensors
+ * self_attn.q_norm / k_norm, core.cpp:244, :395). Default: all ones. */
+int qa_set_norms(qa_ctx* ctx, int layer, const float* q_norm, const float* k_norm);
+
+/* Logical KV state: `pos` is the only validity state (core.cpp:232).
+ * qa_position  -> Model::position, core.cpp:758
+ * qa_reset     -> Model::reset, core.cpp:718-721 (O(1), no KV work)
+ * qa_truncate  -> Model::truncate, core.cpp:722-726 (0 <= pos <= current, else QA_ERR_STATE)
+ * qa_commit    -> the `pos += batch` after all layers, core.cpp:643, and
+ *                 Model::commit_verified's `pos += count`, core.cpp:749. Every layer must
+ *                 have been appended through pos+n. */
+int qa_position(const qa_ctx* ctx, int seq, int* pos);
+int qa_reset(qa_ctx* ctx, int seq);
+int qa_truncate(qa_ctx* ctx, int seq, int pos);
+int qa_commit(qa_ctx* ctx, int seq, int n);
+
+/* Fused KV append: per-head QK-RMSNorm (eps 1e-6, FP64 sum of FP32 squares), RoPE at
+ * absolute positions pos0..pos0+n-1, FP32->FP16 round-to-nearest-even K/V write into
+ * rows [pos0, pos0+n) of layers [layer, layer+n_layers). Writes the normed, roped
+ * query to q_out. pos0 must equal the sequence's committed position.
+ * Replaces core.cpp:395-406 (and the B2 copy :659-670). Bit-exact with that arithmetic. */
+int qa_append(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n,
+              const float* q_pre, const float* k_pre, const float* v, float* q_out);
+
+/* Causal GQA attention of n new rows: row b (position pos0+b) of query head h attends to
+ * keys [0, pos0+b] of KV head h/group, softmax(q.k/sqrt(128)) . V, FP32 out.
+ * Rows [pos0, pos0+n) of every layer in range must have been appended.
+ * Replaces the batched-prefill attention, core.cpp:357-381 and :407-605.
+ * Within max-abs 1e-3 / RMS 1e-4 of that arithmetic. */
+int qa_attn_prefill(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n,
+                    const float* q, float* out);
+
+/* Same contract for 1 <= n <= QA_MAX_DECODE_ROWS rows with split-context
+ * (flash-decoding) parallelism. n == 1 replaces the decode attention, core.cpp:606-624;
+ * n == 2 replaces the B2 verify attention, core.cpp:671-689. */
+int qa_attn_decode(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n,
+                   const float* q, float* out);
+
+/* Canonical prefix reuse by device block copy: copies KV rows [0, ntok) of every layer,
+ * K/V and head from slot src_seq to slot dst_seq and sets dst's position to ntok.
+ * ntok must be a positive multiple of QA_PREFIX_CHUNK and <= src's position.
+ * Replaces the adapter's `rewind` of a retained prefix (tools/native_cpu_chat.py:189-216,
+ * engine/INTERFACE.md:151-168) for a prefix held by another sequence slot. */
+int qa_copy_prefix(qa_ctx* ctx, int src_seq, int dst_seq, int ntok);
+
+/* Reads FP16 KV rows [pos0, pos0+n) of (layer, kv = 0 for K / 1 for V, local head) into
+ * dst (host memory, n*128 uint16). Synchronous. Diagnostic / parity access to the store. */
+int qa_read_kv(qa_ctx* ctx, int seq, int layer, int kv, int head, int pos0, int n,
+               uint16_t* dst);
+
+/* Device address of the KV rows of (seq, layer, kv, local head) at position 0, and the
+ * byte size of one whole sequence slot. For peer copies and external consumers. */
+int qa_kv_pointer(qa_ctx* ctx, int seq, int layer, int kv, int head, void** ptr);
+int qa_kv_slot_bytes(const qa_ctx* ctx, size_t* bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QATTN_H */
