@@ -1,0 +1,367 @@
+// attn_prefill_sm100.cu — causal GQA prefill attention on the 5th-generation tensor cores.
+//
+// Replaces the reference's batched-prefill attention (tampajohn/fpga-qwen engine/core.cpp
+// :357-381, :407-605): for each new row b (position pos0+b) and query head h,
+// out = softmax(q.K^T / sqrt(128)) V over keys [0, pos0+b] of KV head h/2.
+//
+// One CTA = (layer, KV head, 128-row query tile). Both query heads of the GQA pair live in
+// the CTA and share every K/V tile (the reference pairs heads for the same reason,
+// core.cpp:150-159). Rows whose absolute position is below 128 are not handled here: they
+// attend to few keys, where FP16 probabilities are not accurate enough, and go to the
+// FP32 CUDA-core kernel (attn_rows.cu).
+//
+// Warp roles (320 threads):
+//   warps 0-3  softmax group for query head 0 (thread t owns query row t of the tile)
+//   warps 4-7  softmax group for query head 1
+//   warp  8    MMA issuer (one elected thread issues tcgen05.mma, the warp zeroes stale V rows)
+//   warp  9    TMA producer (one thread)
+// Per 128-key tile j:
+//   S_h = Q_h K_j^T         tcgen05.mma kind::f16, M=128 N=128 K=128, FP32 accumulate in TMEM
+//   softmax group h: tcgen05.ld S_h row, causal mask, running max (log2 domain, lazy
+//   rescale when the max grows by more than 8), P = 2^(s - m) -> FP16 into shared memory
+//   O_h += P_h V_j          tcgen05.mma, A = P (K-major), B = V (MN-major), accumulate in TMEM
+// The MMA thread issues PV_h(j) then S_h(j+1) for h = 0, 1, so the tensor pipe works on one
+// head while the other head's softmax runs (ping-pong). Key tiles above the diagonal of the
+// query tile are skipped; tiles crossing it are masked per element.
+//
+// Memory: Q_0, Q_1 (FP16, 32 KB each), K (2 stages x 32 KB), V (32 KB), P_0, P_1 (32 KB each)
+// = 224 KB shared; TMEM 512 columns = S_0, S_1, O_0, O_1 (128 FP32 columns each).
+// K/V tiles come from the HBM KV store through one 3-D tensor map
+// {128 channels, ctx positions, planes} with 64x128 boxes and 128-byte swizzle.
+//
+// Every wait is bounded (globaltimer, 2 s): on expiry the CTA raises an abort flag, writes
+// an error code to the host-visible flag, drains what it issued and frees its TMEM.
+#include "qattn_common.cuh"
+#include "sm100.cuh"
+
+namespace qattn {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 128;
+constexpr int THREADS = 320;
+constexpr uint32_t TILE_BYTES = BN * D * 2;               // 32 KB FP16 K or V tile
+constexpr int OFF_Q = 0, OFF_K = 65536, OFF_V = 131072, OFF_P = 163840, OFF_BAR = 229376;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;          // + barriers + alignment slack
+constexpr float RESCALE_THRESHOLD = 8.0f;                 // log2 units
+
+enum {
+    B_Q0, B_Q1, B_KF0, B_KF1, B_KE0, B_KE1, B_VF, B_VE, B_SF0, B_SF1, B_SE0, B_SE1, B_PF0, B_PF1, B_OD0, B_OD1,
+    B_DRAIN, B_COUNT
+};
+
+struct PrefillArgs {
+    const float* q; float* out;       // [n_layers][n][hq][128]
+    int seq, layer0, n_layers, pos0, n, hq, hkv, layers_total;
+    int row_begin, n_qtiles;
+    int* error;
+};
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk16) {   // K-major, 128B swizzle, 2 atom columns
+    return (uint32_t)((chunk16 >> 3) * 16384 + (row >> 3) * 1024 + (row & 7) * 128 + (((chunk16 & 7) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + B_COUNT * 8);
+    __shared__ int abort_flag;
+    __shared__ int never_abort;                              // for drains that must not give up early
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // ---- work item: heaviest query tiles first ----
+    const int per_tile = a.hkv * a.n_layers;
+    const int tile = a.n_qtiles - 1 - (int)(blockIdx.x / per_tile);
+    const int rest = blockIdx.x % per_tile;
+    const int kh = rest % a.hkv, l = rest / a.hkv;
+    const int layer = a.layer0 + l;
+    const int r0 = a.row_begin + tile * BM;                  // first query row of the tile
+    const int r_last = min(r0 + BM, a.n) - 1;
+    const int nk = (a.pos0 + r_last + 1 + BN - 1) / BN;      // causal key tiles
+    const int valid_keys = a.pos0 + r_last + 1;
+    const int plane_k = ((a.seq * a.layers_total + layer) * 2 + 0) * a.hkv + kh;
+    const int plane_v = plane_k + a.hkv;
+
+    if (tid == 0) {
+        abort_flag = 0;
+        never_abort = 0;
+        mbar_init(&bar[B_Q0], 128); mbar_init(&bar[B_Q1], 128);
+        mbar_init(&bar[B_KF0], 1); mbar_init(&bar[B_KF1], 1); mbar_init(&bar[B_KE0], 1); mbar_init(&bar[B_KE1], 1);
+        mbar_init(&bar[B_VF], 1); mbar_init(&bar[B_VE], 1);
+        mbar_init(&bar[B_SF0], 1); mbar_init(&bar[B_SF1], 1); mbar_init(&bar[B_SE0], 128); mbar_init(&bar[B_SE1], 128);
+        mbar_init(&bar[B_PF0], 128); mbar_init(&bar[B_PF1], 128); mbar_init(&bar[B_OD0], 1); mbar_init(&bar[B_OD1], 1);
+        mbar_init(&bar[B_DRAIN], 1);
+        fence_mbar_init();
+    }
+    if (warp == 8) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+    if (warp == 9 && lane == 0) prefetch_tmap(&kv_map);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    volatile int* abortp = &abort_flag;
+    auto fail = [&](int code) { *abortp = 1; atomicCAS(a.error, 0, code); };
+
+    if (warp < 8) {
+        // ================================ softmax groups ================================
+        const int h = warp >> 2;                             // query head within the pair
+        const int t = tid & 127;                             // row within the tile
+        const int r = r0 + t;
+        const bool row_ok = r < a.n;
+        const int row_pos = a.pos0 + r;
+        const size_t qoff = (((size_t)l * a.n + r) * a.hq + (size_t)kh * 2 + h) * D;
+        uint8_t* Qs = smem + OFF_Q + h * 32768;
+        uint8_t* Ps = smem + OFF_P + h * 32768;
+        // Q row -> FP16 in the swizzled K-major layout
+        #pragma unroll 4
+        for (int c = 0; c < 16; ++c) {
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (row_ok) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(a.q + qoff) + 2 * c);
+                const float4 y = __ldg(reinterpret_cast<const float4*>(a.q + qoff) + 2 * c + 1);
+                v = make_uint4(pack_half2(x.x, x.y), pack_half2(x.z, x.w), pack_half2(y.x, y.y), pack_half2(y.z, y.w));
+            }
+            *reinterpret_cast<uint4*>(Qs + swz(t, c)) = v;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bar[B_Q0 + h]);
+
+        const float scale = 1.4426950408889634f * 0.08838834764831845f;   // log2(e)/sqrt(128)
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t s_col = tmem + lane_base + h * 128;
+        const uint32_t o_col = tmem + lane_base + 256 + h * 128;
+        float m = -INFINITY, lsum = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nk && ok; ++j) {
+            if (!mbar_wait(&bar[B_SF0 + h], j & 1, abortp)) { fail(11); ok = false; break; }
+            tc_fence_after();
+            float s[BN];
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t rr[32];
+                tmem_ld32(s_col + c * 32, rr);
+                tmem_wait_ld();
+                #pragma unroll
+                for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(rr[i]);
+            }
+            tc_fence_before();
+            mbar_arrive(&bar[B_SE0 + h]);
+            const int k0 = j * BN;
+            if (k0 + BN - 1 > row_pos) {
+                #pragma unroll
+                for (int c = 0; c < BN; ++c) if (k0 + c > row_pos) s[c] = -INFINITY;
+            }
+            float mt = -INFINITY;
+            #pragma unroll
+            for (int c = 0; c < BN; ++c) mt = fmaxf(mt, s[c]);
+            mt *= scale;
+            float alpha = 1.f;
+            bool rescale = false;
+            if (j == 0) m = mt;
+            else if (mt > m + RESCALE_THRESHOLD) { alpha = exp2f(m - mt); m = mt; rescale = true; }
+            // P buffer and O_h are free once PV_h(j-1) has completed
+            if (j > 0 && !mbar_wait(&bar[B_OD0 + h], (j - 1) & 1, abortp)) { fail(12); ok = false; break; }
+            if (rescale) {
+                tc_fence_after();
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t rr[32];
+                    tmem_ld32(o_col + c * 32, rr);
+                    tmem_wait_ld();
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
+                    tmem_st32(o_col + c * 32, rr);
+                }
+                tmem_wait_st();
+                lsum *= alpha;
+            }
+            const float mneg = -m;
+            float psum = 0.f;
+            #pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                float p[8];
+                #pragma unroll
+                for (int i = 0; i < 8; ++i) { p[i] = exp2f(fmaf(s[c * 8 + i], scale, mneg)); psum += p[i]; }
+                const uint4 v = make_uint4(pack_half2(p[0], p[1]), pack_half2(p[2], p[3]), pack_half2(p[4], p[5]),
+                                           pack_half2(p[6], p[7]));
+                *reinterpret_cast<uint4*>(Ps + swz(t, c)) = v;
+            }
+            lsum += psum;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&bar[B_PF0 + h]);
+        }
+        if (ok && mbar_wait(&bar[B_OD0 + h], (nk - 1) & 1, abortp)) {
+            tc_fence_after();
+            const float inv = 1.f / lsum;
+            float* dst = a.out + qoff;
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t rr[32];
+                tmem_ld32(o_col + c * 32, rr);
+                tmem_wait_ld();
+                if (row_ok) {
+                    #pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(dst + c * 32 + i) =
+                            make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
+                                        __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
+                }
+            }
+        } else if (ok) {
+            fail(13);
+        }
+    } else if (warp == 8) {
+        // ================================== MMA issuer ==================================
+        const uint32_t idesc_qk = idesc_f16_f32(BM, BN, false);
+        const uint32_t idesc_pv = idesc_f16_f32(BM, D, true);
+        const uint32_t q_addr = smem_u32(smem + OFF_Q), k_addr = smem_u32(smem + OFF_K);
+        const uint32_t v_addr = smem_u32(smem + OFF_V), p_addr = smem_u32(smem + OFF_P);
+        uint8_t* Vs = smem + OFF_V;
+        bool ok = true;
+        auto issue_qk = [&](int j, int h) {
+            const uint32_t kb = k_addr + (j & 1) * TILE_BYTES, qb = q_addr + h * 32768;
+            if (lane == 0) {
+                #pragma unroll
+                for (int s = 0; s < 8; ++s) {
+                    const uint32_t off = (s >> 2) * 16384 + (s & 3) * 32;
+                    mma_f16_ss(tmem + h * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024), idesc_qk, s > 0);
+                }
+                mma_commit(&bar[B_SF0 + h]);
+            }
+            __syncwarp();
+        };
+        auto issue_pv = [&](int j, int h) {
+            const uint32_t pb = p_addr + h * 32768;
+            if (lane == 0) {
+                #pragma unroll
+                for (int s = 0; s < 8; ++s) {
+                    const uint32_t offa = (s >> 2) * 16384 + (s & 3) * 32;
+                    mma_f16_ss(tmem + 256 + h * 128, sw128_desc(pb + offa, 16, 1024),
+                               sw128_desc(v_addr + s * 2048, 16384, 1024), idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
+                }
+                mma_commit(&bar[B_OD0 + h]);
+            }
+            __syncwarp();
+        };
+        // prologue: S_0(0), S_1(0)
+        if (!mbar_wait(&bar[B_Q0], 0, abortp) || !mbar_wait(&bar[B_Q1], 0, abortp) || !mbar_wait(&bar[B_KF0], 0, abortp)) {
+            fail(21); ok = false;
+        }
+        if (ok) {
+            tc_fence_after();
+            issue_qk(0, 0);
+            issue_qk(0, 1);
+            if (lane == 0) mma_commit(&bar[B_KE0]);
+            __syncwarp();
+        }
+        for (int j = 0; j < nk && ok; ++j) {
+            if (!mbar_wait(&bar[B_VF], j & 1, abortp)) { fail(22); ok = false; break; }
+            if (j == nk - 1 && valid_keys < (j + 1) * BN) {
+                // Rows of the last V tile past the causal end hold stale data: zero them so
+                // that a zero probability never meets a non-finite value.
+                const int first = valid_keys - j * BN;
+                for (int idx = first * 16 + lane; idx < BN * 16; idx += 32) {
+                    const int row = idx >> 4, c = idx & 15;        // c: 16-byte chunk of the 256-byte row
+                    const int half_sel = c >> 3, cc = c & 7;
+                    *reinterpret_cast<uint4*>(Vs + half_sel * 16384 + (row >> 3) * 1024 + (row & 7) * 128 +
+                                              ((cc ^ (row & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+            }
+            tc_fence_after();
+            for (int h = 0; h < 2 && ok; ++h) {
+                if (!mbar_wait(&bar[B_PF0 + h], j & 1, abortp)) { fail(23); ok = false; break; }
+                tc_fence_after();
+                issue_pv(j, h);
+                if (j + 1 < nk) {
+                    const int jn = j + 1;
+                    if (h == 0 && !mbar_wait(&bar[B_KF0 + (jn & 1)], (jn >> 1) & 1, abortp)) { fail(24); ok = false; break; }
+                    if (!mbar_wait(&bar[B_SE0 + h], j & 1, abortp)) { fail(25); ok = false; break; }
+                    tc_fence_after();
+                    issue_qk(jn, h);
+                    if (h == 1) {
+                        if (lane == 0) mma_commit(&bar[B_KE0 + (jn & 1)]);
+                        __syncwarp();
+                    }
+                }
+            }
+            if (ok) {
+                if (lane == 0) mma_commit(&bar[B_VE]);
+                __syncwarp();
+            }
+        }
+        // drain: every MMA this thread issued has completed before TMEM is released
+        if (lane == 0) {
+            mma_commit(&bar[B_DRAIN]);
+            if (!mbar_wait(&bar[B_DRAIN], 0, &never_abort)) atomicCAS(a.error, 0, 29);
+        }
+        __syncwarp();
+    } else if (warp == 9 && lane == 0) {
+        // ================================== TMA producer ==================================
+        int issued_k = 0, issued_v = 0;
+        bool ok = true;
+        for (int j = 0; j < nk && ok; ++j) {
+            const int st = j & 1;
+            if (j >= 2 && !mbar_wait(&bar[B_KE0 + st], ((j >> 1) - 1) & 1, abortp)) { fail(31); ok = false; break; }
+            uint8_t* kd = smem + OFF_K + st * TILE_BYTES;
+            mbar_arrive_expect_tx(&bar[B_KF0 + st], TILE_BYTES);
+            tma_load_3d(kd, &kv_map, 0, j * BN, plane_k, &bar[B_KF0 + st]);
+            tma_load_3d(kd + 16384, &kv_map, 64, j * BN, plane_k, &bar[B_KF0 + st]);
+            ++issued_k;
+            if (j >= 1 && !mbar_wait(&bar[B_VE], (j - 1) & 1, abortp)) { fail(32); ok = false; break; }
+            uint8_t* vd = smem + OFF_V;
+            mbar_arrive_expect_tx(&bar[B_VF], TILE_BYTES);
+            tma_load_3d(vd, &kv_map, 0, j * BN, plane_v, &bar[B_VF]);
+            tma_load_3d(vd + 16384, &kv_map, 64, j * BN, plane_v, &bar[B_VF]);
+            ++issued_v;
+        }
+        if (!ok) {
+            // drain the loads this thread issued (bounded, ignoring the abort flag)
+            if (issued_k > 0) {
+                const int jl = issued_k - 1;
+                mbar_wait(&bar[B_KF0 + (jl & 1)], (jl >> 1) & 1, &never_abort, 500000000ull);
+            }
+            if (issued_v > 0) mbar_wait(&bar[B_VF], (issued_v - 1) & 1, &never_abort, 500000000ull);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace
+
+// Host side --------------------------------------------------------------------------------------
+void launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
+                               int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
+                               cudaStream_t s) {
+    if (row_begin >= n) return;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(attn_prefill_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        attr_set = true;
+    }
+    PrefillArgs a{};
+    a.q = q; a.out = out; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
+    a.hq = hq; a.hkv = hkv; a.layers_total = layers_total; a.row_begin = row_begin;
+    a.n_qtiles = (n - row_begin + BM - 1) / BM; a.error = error;
+    const unsigned blocks = (unsigned)(a.n_qtiles * hkv * n_layers);
+    attn_prefill_sm100_kernel<<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
+}
+
+}  // namespace qattn

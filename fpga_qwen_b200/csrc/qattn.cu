@@ -39,6 +39,8 @@ struct qa_ctx {
     int max_units = 0;
     float* staging = nullptr;              // device staging for io_host calls
     size_t staging_floats = 0;
+    CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
+    int* error = nullptr;                  // device-side error code of bounded waits (0 = none)
     std::string err;
 };
 
@@ -114,6 +116,40 @@ int ensure_staging(qa_ctx* ctx, size_t floats) {
     ctx->staging = nullptr; ctx->staging_floats = 0;
     QA_CUDA(cudaMalloc(&ctx->staging, floats * sizeof(float)));
     ctx->staging_floats = floats;
+    return QA_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// TMA descriptor of the KV store: planes of [ctx][128] FP16 rows; rows past ctx read as zero.
+int make_kv_map(qa_ctx* ctx) {
+    EncodeTiledFn encode = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault, &q) !=
+            cudaSuccess || !encode)
+        return fail(ctx, QA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t planes = (cuuint64_t)ctx->cfg.max_seqs * ctx->cfg.n_layers * 2 * ctx->hkv;
+    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->cfg.context, planes};
+    cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->cfg.context * D * 2};
+    cuuint32_t box[3] = {64, 128, 1}, elem[3] = {1, 1, 1};
+    CUresult r = encode(&ctx->kv_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->kv.base, dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ctx, QA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return QA_OK;
+}
+
+// Reads and clears the device error flag of the bounded waits.
+int check_device_error(qa_ctx* ctx) {
+    int code = 0;
+    QA_CUDA(cudaMemcpyAsync(&code, ctx->error, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (code) {
+        QA_CUDA(cudaMemsetAsync(ctx->error, 0, sizeof(int), ctx->stream));
+        return fail(ctx, QA_ERR_TIMEOUT, "a device-side wait expired (code %d); results of the last calls are invalid", code);
+    }
     return QA_OK;
 }
 
@@ -215,6 +251,10 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     if (cudaMalloc(&ctx->counters, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMemset(ctx->counters, 0, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
 
+    if (cudaMalloc(&ctx->error, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMemset(ctx->error, 0, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+    if (make_kv_map(ctx) != QA_OK) return cleanup(QA_ERR_CUDA);
+
     ctx->pos.assign(c.max_seqs, 0);
     ctx->appended.assign(c.max_seqs, std::vector<int>(c.n_layers, 0));
     if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(QA_ERR_CUDA);
@@ -228,7 +268,7 @@ void qa_destroy(qa_ctx* ctx) {
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
-    cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->staging);
+    cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->staging); cudaFree(ctx->error);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }
@@ -243,7 +283,7 @@ int qa_sync(qa_ctx* ctx) {
     if (!ctx) return QA_ERR_INVALID;
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
     QA_CUDA(cudaStreamSynchronize(ctx->stream));
-    return QA_OK;
+    return check_device_error(ctx);
 }
 
 int qa_set_norms(qa_ctx* ctx, int layer, const float* q_norm, const float* k_norm) {
@@ -353,14 +393,23 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
     r.partial = ctx->partial; r.counters = ctx->counters;
     if (decode) {
         choose_splits(ctx, (long long)n_layers * n * ctx->hkv, pos0 + n, r.splits, r.keys_per_split);
+        launch_attn_rows(r, ctx->stream);
     } else {
-        r.splits = 1; r.keys_per_split = ((pos0 + n) + 31) / 32 * 32;
+        // rows below position TC_MIN_POSITION: FP32 CUDA cores; the rest: tcgen05 tensor cores
+        const int tc_begin = std::min(n, std::max(0, TC_MIN_POSITION - pos0));
+        if (tc_begin > 0) {
+            r.row_end = tc_begin;
+            r.splits = 1; r.keys_per_split = ((pos0 + tc_begin) + 31) / 32 * 32;
+            launch_attn_rows(r, ctx->stream);
+        }
+        launch_attn_prefill_sm100(ctx->kv_map, qd, od, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv,
+                                  ctx->cfg.n_layers, tc_begin, ctx->error, ctx->stream);
     }
-    launch_attn_rows(r, ctx->stream);
     if ((st = after_launch(ctx, seq, decode ? "attn_decode" : "attn_prefill"))) return st;
     if (ctx->cfg.io_host) {
         QA_CUDA(cudaMemcpyAsync(out, od, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
         QA_CUDA(cudaStreamSynchronize(ctx->stream));
+        if (!decode) return check_device_error(ctx);
     }
     return QA_OK;
 }

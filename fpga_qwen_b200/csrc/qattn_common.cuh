@@ -2,6 +2,7 @@
 // the kernel launchers implemented in the per-kernel .cu files.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -48,6 +49,12 @@ struct RowsArgs {
 void launch_kv_append(const AppendArgs& a, cudaStream_t s);
 void launch_attn_rows(const RowsArgs& a, cudaStream_t s);
 void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cudaStream_t s);
+// Tensor-core prefill for rows [row_begin, n) (all with absolute position >= 128).
+void launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
+                               int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
+                               cudaStream_t s);
+// Rows at absolute positions below this go to the FP32 CUDA-core kernel.
+constexpr int TC_MIN_POSITION = 128;
 void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n,
                   int head0, int heads, float mean, float stdev, cudaStream_t s);
 
