@@ -401,6 +401,58 @@ def e2e_decode(args, seed):
             "note": "128 decode steps per step, host wall clock around C-ABI calls with host buffers"}
 
 
+def run_profile_case(args):
+    """Small, self-contained launches of one kernel for ncu captures (few GB on the device,
+    few launches before the captured ones):
+      decode   28 layers with a 3968-row KV history built chunk by chunk, then 3 decode steps
+               (each attn_decode launch reads 470 MB of KV, more than L2)
+      prefill  4 layers, 3968-row prefill (append + attention) repeated 3 times
+      append   28 layers x 1024-row append repeated 3 times"""
+    import torch
+    from fpga_qwen_b200 import qattn
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    layers = 4 if args.profile_case == "prefill" else L
+    ctx = qattn.Context(n_layers=layers, context=4096, max_seqs=1)
+    ctx.set_stream(stream.cuda_stream)
+
+    def synth(kind, pos0, n, heads):
+        t = torch.empty((layers, n, heads, D), dtype=torch.float32, device=dev)
+        qattn.synth_fill(t.data_ptr(), 4, kind, 0, layers, pos0, n, 0, heads, 0.0, 1.0, stream.cuda_stream)
+        return t
+
+    if args.profile_case == "decode":
+        chunk = 512
+        for b0 in range(0, PREFILL, chunk):
+            nb = min(chunk, PREFILL - b0)
+            q, k, v = synth(0, b0, nb, HQ), synth(1, b0, nb, HKV), synth(2, b0, nb, HKV)
+            qn = torch.empty_like(q)
+            ctx.append(0, 0, layers, b0, nb, q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr())
+            ctx.commit(0, nb)
+            del q, k, v, qn
+        for s in range(3):
+            pos = PREFILL + s
+            q, k, v = synth(0, pos, 1, HQ), synth(1, pos, 1, HKV), synth(2, pos, 1, HKV)
+            qn, out = torch.empty_like(q), torch.empty_like(q)
+            ctx.append(0, 0, layers, pos, 1, q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr())
+            ctx.attn_decode(0, 0, layers, pos, 1, qn.data_ptr(), out.data_ptr())
+            ctx.commit(0, 1)
+    else:
+        n = PREFILL if args.profile_case == "prefill" else 1024
+        q, k, v = synth(0, 0, n, HQ), synth(1, 0, n, HKV), synth(2, 0, n, HKV)
+        qn, out = torch.empty_like(q), torch.empty_like(q)
+        for _ in range(3):
+            ctx.reset(0)
+            ctx.append(0, 0, layers, 0, n, q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr())
+            if args.profile_case == "prefill":
+                ctx.attn_prefill(0, 0, layers, 0, n, qn.data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    ctx.sync()
+    ctx.close()
+    print(json.dumps({"profile_case": args.profile_case, "ok": True}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -409,7 +461,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-case", choices=["decode", "prefill", "append"], default=None,
+                    help="run a small single-kernel case for ncu instead of the benchmark")
     args = ap.parse_args()
+    if args.profile_case:
+        return run_profile_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -22,7 +22,8 @@ namespace {
 
 constexpr int THREADS = 128;
 constexpr int HALF_WARPS = THREADS / 16;   // 8 key rows in flight per step
-constexpr int UNROLL = 4;                  // key rows per half-warp per step
+constexpr int UNROLL = 4;                  // key rows per half-warp per step (transpose-reduce needs 4)
+static_assert(UNROLL * GROUP == 8, "transpose-reduce is written for 8 values per lane");
 
 __device__ __forceinline__ void unpack8(const uint4 u, float f[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&u);
@@ -73,7 +74,11 @@ __global__ void __launch_bounds__(THREADS) attn_rows_kernel(const RowsArgs a) {
     float mloc[GROUP];
     #pragma unroll
     for (int g = 0; g < GROUP; ++g) mloc[g] = -INFINITY;
-    for (int base = hw; base < cnt; base += HALF_WARPS * UNROLL) {
+    // The loop bound is warp-uniform (both half-warps of a warp run the same iterations):
+    // the shuffles below use the full mask. Keys past cnt load as zero and are not stored.
+    const int warp_first = hw & ~1;
+    for (int it = warp_first; it < cnt; it += HALF_WARPS * UNROLL) {
+        const int base = it + (hw & 1);
         uint4 kr[UNROLL];
         #pragma unroll
         for (int u = 0; u < UNROLL; ++u) {
@@ -81,30 +86,49 @@ __global__ void __launch_bounds__(THREADS) attn_rows_kernel(const RowsArgs a) {
             if (t < cnt) kr[u] = __ldg(reinterpret_cast<const uint4*>(Kp + (size_t)(k0 + t) * D) + sl);
             else kr[u] = make_uint4(0, 0, 0, 0);
         }
+        // partial dot products: value i = u * GROUP + g (key u of this step, query head g)
+        float v[UNROLL * GROUP];
         #pragma unroll
         for (int u = 0; u < UNROLL; ++u) {
             float kf[8]; unpack8(kr[u], kf);
-            float s[GROUP];
             #pragma unroll
             for (int g = 0; g < GROUP; ++g) {
                 float acc = 0.f;
                 #pragma unroll
                 for (int e = 0; e < 8; ++e) acc = fmaf(q[g][e], kf[e], acc);
-                s[g] = acc;
+                v[u * GROUP + g] = acc;
             }
-            #pragma unroll
-            for (int off = 8; off >= 1; off >>= 1) {
-                #pragma unroll
-                for (int g = 0; g < GROUP; ++g) s[g] += __shfl_xor_sync(0xffffffffu, s[g], off);
-            }
-            const int t = base + u * HALF_WARPS;
-            if (t < cnt) {
-                #pragma unroll
-                for (int g = 0; g < GROUP; ++g) {
-                    mloc[g] = fmaxf(mloc[g], s[g]);
-                    if (sl == 0) scores[g * a.keys_per_split + t] = s[g];
-                }
-            }
+        }
+        // transpose-reduce over the 16 lanes of the half-warp: each exchange halves the
+        // number of values a lane carries (4 + 2 + 1 + 1 shuffles for 8 sums instead of 32)
+        const bool b3 = sl & 8, b2 = sl & 4, b1 = sl & 2;
+        float w4[4];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float send = b3 ? v[i] : v[i + 4];
+            const float keep = b3 ? v[i + 4] : v[i];
+            w4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+        }
+        float w2[2];
+        #pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float send = b2 ? w4[i] : w4[i + 2];
+            const float keep = b2 ? w4[i + 2] : w4[i];
+            w2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+        float y;
+        {
+            const float send = b1 ? w2[0] : w2[1];
+            const float keep = b1 ? w2[1] : w2[0];
+            y = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+        }
+        y += __shfl_xor_sync(0xffffffffu, y, 1);
+        // this lane now holds key my_u, head my_g
+        const int my_u = (b3 ? 2 : 0) + (b2 ? 1 : 0), my_g = b1 ? 1 : 0;
+        const int t = base + my_u * HALF_WARPS;
+        if (t < cnt) {
+            if (my_g == 0) mloc[0] = fmaxf(mloc[0], y); else mloc[1] = fmaxf(mloc[1], y);
+            if ((sl & 1) == 0) scores[my_g * a.keys_per_split + t] = y;
         }
     }
     // block max per head
@@ -158,7 +182,8 @@ __global__ void __launch_bounds__(THREADS) attn_rows_kernel(const RowsArgs a) {
     for (int g = 0; g < GROUP; ++g)
         #pragma unroll
         for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
-    for (int base = hw; base < cnt; base += HALF_WARPS * UNROLL) {
+    for (int it = warp_first; it < cnt; it += HALF_WARPS * UNROLL) {
+        const int base = it + (hw & 1);
         uint4 vr[UNROLL];
         #pragma unroll
         for (int u = 0; u < UNROLL; ++u) {

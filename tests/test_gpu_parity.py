@@ -265,3 +265,63 @@ def test_engine_mirror_state_machine():
     assert torch.allclose(ov[:, :1], o2, atol=1e-6, rtol=0)
     assert out.shape == (L, 10, 16, 128) and o1.shape == (L, 1, 16, 128)
     ctx.close()
+
+
+def test_config4_full_size_sampled_rows():
+    """BASELINE config 4 at full size on one GPU: 3968-row prefill over 28 layers, then 4
+    decode steps. KV bytes of sampled layers are bit-exact with the oracle's append; sampled
+    rows (tile edges, the position-128 boundary between the FP32 and tensor-core paths,
+    random rows) and the decode outputs are within tolerance of the oracle."""
+    L, n, steps = 28, 3968, 4
+    ctx = make_ctx(L, context=4096)
+    qw, kw = H.norms(21, L)
+    H.set_norms(ctx, qw, kw)
+    q, k, v = H.inputs(21, L, 0, n + steps)
+    qn = gpu_append(ctx, 0, 0, q[:, :n].contiguous(), k[:, :n].contiguous(), v[:, :n].contiguous())
+    out = gpu_attend(ctx, 0, 0, qn)
+    ctx.commit(0, n)
+    dec = []
+    for s in range(steps):
+        p = n + s
+        qs = gpu_append(ctx, 0, p, q[:, p:p + 1].contiguous(), k[:, p:p + 1].contiguous(), v[:, p:p + 1].contiguous())
+        dec.append(gpu_attend(ctx, 0, p, qs, decode=True))
+        ctx.commit(0, 1)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(0)
+    rows = sorted(set([0, 1, 2, 63, 126, 127, 128, 129, 130, 255, 256, 257, 1000, 2047, 2048, 3839, 3840, 3967]
+                      + rng.integers(0, n, 24).tolist()))
+    outh = out.cpu().numpy()
+    dech = np.concatenate([d.cpu().numpy() for d in dec], axis=1)
+    for layer in (0, 13, 27):
+        qh, kh, vh = (t[layer].cpu().numpy() for t in (q, k, v))
+        kv, qref = oracle_layer(qh, kh, vh, qw[layer], kw[layer], 0, ctx_len=4096)
+        gk = np.stack([H.read_plane(ctx, 0, layer, 0, h, 0, n + steps) for h in range(8)])
+        gv = np.stack([H.read_plane(ctx, 0, layer, 1, h, 0, n + steps) for h in range(8)])
+        assert np.array_equal(gk, kv.k[:, :n + steps]) and np.array_equal(gv, kv.v[:, :n + steps])
+        ref = np.stack([O.attention(kv, r, qref[r:r + 1], threads=8)[0] for r in rows])
+        mx, rms = H.err_stats(outh[layer][rows], ref)
+        assert mx < H.MAX_ABS and rms < H.RMS, (layer, mx, rms)
+        refd = np.stack([O.attention(kv, n + s, qref[n + s:n + s + 1], threads=8)[0] for s in range(steps)])
+        mx, rms = H.err_stats(dech[layer], refd)
+        assert mx < H.MAX_ABS and rms < H.RMS, (layer, mx, rms)
+    ctx.close()
+
+
+def test_prefill_is_deterministic_and_matches_single_layer_calls():
+    """Layer-batched and per-layer calls give identical bits; repeated calls are deterministic."""
+    L, n = 3, 700
+    ctx = make_ctx(L, max_seqs=2, context=1024)
+    q, k, v = H.inputs(8, L, 0, n)
+    qn = gpu_append(ctx, 0, 0, q, k, v)
+    out_all = gpu_attend(ctx, 0, 0, qn)
+    out_again = gpu_attend(ctx, 0, 0, qn)
+    per_layer = torch.empty_like(qn)
+    for layer in range(L):
+        qn1 = torch.empty_like(q[layer:layer + 1])
+        ctx.append(1, layer, 1, 0, n, q[layer].data_ptr(), k[layer].data_ptr(), v[layer].data_ptr(), qn1.data_ptr())
+        ctx.attn_prefill(1, layer, 1, 0, n, qn1.data_ptr(), per_layer[layer].data_ptr())
+    torch.cuda.synchronize()
+    ctx.sync()
+    assert torch.equal(out_all, out_again)
+    assert torch.equal(out_all, per_layer)
+    ctx.close()
