@@ -252,7 +252,7 @@ def run_ours(args):
         ctx.attn_prefill(0, 0, L, 0, PREFILL, pqn.data_ptr(), pout.data_ptr())
         if evs:
             evs["pa1"].record(stream)
-        launches += 2
+        launches += 3          # append, FP32 rows below position 128, tcgen05 prefill
         ctx.commit(0, PREFILL)
         for s in range(DECODE):
             pos = PREFILL + s
