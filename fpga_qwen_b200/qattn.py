@@ -70,6 +70,9 @@ _SIGNATURES = {
     "qa_kv_pointer": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.POINTER(ctypes.c_void_p)]),
     "qa_kv_slot_bytes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "qa_attn_decode_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                              ctypes.c_void_p, ctypes.c_void_p]),
     "qa_synth_fill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                      ctypes.c_float, ctypes.c_void_p]),
@@ -197,6 +200,19 @@ class Context:
         out = ctypes.c_size_t()
         self._check(lib().qa_kv_slot_bytes(self._h, ctypes.byref(out)))
         return out.value
+
+
+NOALLOC_SCRATCH_BYTES = 4 << 20
+
+
+def attn_decode_noalloc(kv_slot_ptr: int, n_layers_total: int, n_kv_heads: int, context: int, layer: int,
+                        n_layers: int, pos0: int, n: int, q_ptr: int, out_ptr: int, stream: int | None = None) -> int:
+    """Split-context decode that allocates nothing (scratch in a fixed device array).
+    Returns the C status; 0 is success. stream 0 means the legacy default stream."""
+    if stream == 0:
+        stream = 1          # cudaStreamLegacy
+    return lib().qa_attn_decode_noalloc(kv_slot_ptr, n_layers_total, n_kv_heads, context, layer, n_layers, pos0, n,
+                                        q_ptr, out_ptr, stream or None)
 
 
 def synth_fill(dst_ptr: int, seed: int, kind: int, layer0: int, n_layers: int, pos0: int, n: int,

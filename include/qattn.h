@@ -141,6 +141,29 @@ int qa_read_kv(qa_ctx* ctx, int seq, int layer, int kv, int head, int pos0, int 
 int qa_kv_pointer(qa_ctx* ctx, int seq, int layer, int kv, int head, void** ptr);
 int qa_kv_slot_bytes(const qa_ctx* ctx, size_t* bytes);
 
+/* Size of the fixed device array behind qa_attn_decode_noalloc: 4 MiB per GPU, held by
+ * every GPU that loads the library until the process exits. */
+#define QA_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* Split-context decode attention that allocates nothing. It has no counterpart in the
+ * reference: it exists for hosts that own all device memory themselves (a serving
+ * runtime's pre-reserved arena, an engine with a fixed HBM budget) and do not let this
+ * library call cudaMalloc, which would fail there or synchronise the whole device.
+ * Same arithmetic and tolerance as qa_attn_decode, on caller-owned memory:
+ *   kv_slot  one sequence slot of the KV store, [n_layers_total][K|V][n_kv_heads][context][128]
+ *            FP16 (what qa_kv_pointer(ctx, seq, 0, 0, 0, &p) returns), device memory
+ *   q, out   [n_layers][n][2*n_kv_heads][128] FP32, device memory; rows at positions
+ *            pos0..pos0+n-1 of layers [layer, layer+n_layers), 1 <= n <= QA_MAX_DECODE_ROWS
+ *   stream   cudaStream_t (NULL: the legacy default stream)
+ * Scratch lives in one static device array of QA_NOALLOC_SCRATCH_BYTES; requests whose
+ * (layer, row, head) records do not fit return QA_ERR_CAPACITY before anything runs. The
+ * first call on a device looks up that array's address (make it before any stream capture).
+ * Every call shares the array: calls that overlap on the GPU race, so issue them on one
+ * stream or order them. Asynchronous on `stream`. */
+int qa_attn_decode_noalloc(const void* kv_slot, int n_layers_total, int n_kv_heads, int context,
+                           int layer, int n_layers, int pos0, int n, const float* q, float* out,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif
