@@ -1,0 +1,374 @@
+// attn_decode_sm100.cu — decode / verify attention streamed from HBM by the TMA engine.
+//
+// Replaces the reference's single-token decode attention (tampajohn/fpga-qwen
+// engine/core.cpp:606-624) and the B2 verify attention (:671-689): for each of the n new
+// rows b (position pos0+b, context pos0+b+1) and query head h,
+// out = softmax(q.K^T / sqrt(128)) V over the KV head h/2 of every requested layer.
+//
+// Decode is bound by HBM bandwidth: at 4K context one step reads 470 MB of FP16 K/V for
+// 57 KFLOP-per-row of arithmetic. The kernel is built to keep HBM busy:
+//   * Even work split (stream-K style). The keys of all (layer, row, KV head) units are laid
+//     end to end and cut into C equal ranges, C a multiple of the SM count; CTA c takes range
+//     c. A range can end inside one unit and continue in the next, so every CTA gets the
+//     same number of keys and there is no tail wave.
+//   * TMA bulk copies. K and V rows of one (layer, head) are contiguous, so a 64-key chunk
+//     is one 16 KB cp.async.bulk. One thread keeps a 4-stage ring of chunks in flight
+//     (64 KB per CTA, 2 CTAs per SM), so the CTA never waits on individual loads.
+//   * Both GQA query heads share every K and V chunk (the reference pairs heads the same
+//     way, core.cpp:150-159). Scores of the range stay in shared memory; the max and sum
+//     over the range are exact; V is streamed after K.
+// A range that covers a whole unit writes that unit's output directly. A unit split over
+// several CTAs gets one (max, sum, 2x128 partial output) record per CTA; the last CTA to
+// finish (one atomic counter, no waiting) merges them.
+// Every wait is bounded (globaltimer): on expiry the CTA records an error code for the
+// host, stops consuming, drains its outstanding copies and exits.
+#include <algorithm>
+
+#include "qattn_common.cuh"
+#include "sm100.cuh"
+
+namespace qattn {
+namespace {
+
+using namespace sm100;
+
+constexpr int THREADS = 128;
+constexpr int HALF_WARPS = THREADS / 16;
+constexpr int CH = 64;                        // keys per chunk
+constexpr int NST = 4;                        // ring stages
+constexpr uint32_t CHUNK_BYTES = CH * D * 2;  // 16 KB
+
+struct DecodeArgs {
+    const float* q; float* out;               // [n_layers][n][hq][128]
+    KVLayout kv; int seq, layer0, n_layers, pos0, n, hq, hkv;
+    long long total_keys;                     // T = Σ over units of their context length
+    int ctas;                                 // C
+    int max_keys;                             // max keys of one CTA range (scores capacity)
+    int max_records;                          // records reserved per unit
+    float* partial;                           // [units][max_records][PARTIAL_FLOATS]
+    int* counters;                            // [units], zero between calls
+    int* error;
+};
+
+struct Unit { int l, b, kh, len; long long off; };
+
+// Unit containing global key g; units ordered (layer, row, KV head).
+__device__ __forceinline__ Unit unit_of(const DecodeArgs& a, long long g) {
+    const long long per_row0 = a.pos0 + 1;
+    const long long layer_keys = (long long)a.hkv * ((long long)a.n * a.pos0 + (long long)a.n * (a.n + 1) / 2);
+    Unit u;
+    u.l = (int)(g / layer_keys);
+    long long r = g - (long long)u.l * layer_keys;
+    long long off = (long long)u.l * layer_keys;
+    int b = 0;
+    for (; b < a.n - 1; ++b) {
+        const long long row_keys = (long long)a.hkv * (per_row0 + b);
+        if (r < row_keys) break;
+        r -= row_keys; off += row_keys;
+    }
+    u.b = b;
+    u.len = a.pos0 + b + 1;
+    u.kh = (int)(r / u.len);
+    u.off = off + (long long)u.kh * u.len;
+    return u;
+}
+
+// CTA whose range holds global key g: the largest c with floor(c*T/C) <= g.
+__device__ __forceinline__ int cta_of(long long g, long long T, int C) { return (int)(((g + 1) * C - 1) / T); }
+
+__device__ __forceinline__ void unpack8(const uint4 u, float f[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) { const float2 t = __half22float2(h[i]); f[2 * i] = t.x; f[2 * i + 1] = t.y; }
+}
+
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const DecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* ring = smem;                                              // NST x 16 KB
+    float* scores = reinterpret_cast<float*>(smem + NST * CHUNK_BYTES);   // [GROUP][max_keys]
+    __shared__ __align__(8) uint64_t full[NST];
+    __shared__ float red[GROUP][THREADS / 32];
+    __shared__ float stat[2 * GROUP];
+    __shared__ float accbuf[HALF_WARPS][GROUP][D];
+    __shared__ int is_last, abort_flag, never_abort;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hw = tid >> 4, sl = tid & 15;
+    const long long T = a.total_keys;
+    const int C = a.ctas, c = blockIdx.x;
+    const long long g_begin = (long long)c * T / C, g_end = (long long)(c + 1) * T / C;
+
+    if (tid == 0) {
+        abort_flag = 0; never_abort = 0;
+        for (int s = 0; s < NST; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    uint32_t issued = 0, consumed = 0;                 // ring sequence numbers (thread 0 issues)
+    const float qscale = 1.4426950408889634f * 0.08838834764831845f;   // log2(e)/sqrt(128)
+
+    for (long long g = g_begin; g < g_end;) {
+        const Unit u = unit_of(a, g);
+        const int k0 = (int)(g - u.off);
+        const int k1 = (int)min((long long)u.len, g_end - u.off);
+        const int cnt = k1 - k0;
+        g = u.off + k1;
+        const int layer = a.layer0 + u.l;
+        const __half* Kp = a.kv.plane(a.seq, layer, 0, u.kh) + (size_t)k0 * D;
+        const __half* Vp = a.kv.plane(a.seq, layer, 1, u.kh) + (size_t)k0 * D;
+        const int nch = (cnt + CH - 1) / CH;
+        const int total_chunks = 2 * nch;                // K chunks then V chunks
+        const size_t qrow = ((size_t)u.l * a.n + u.b) * a.hq + (size_t)u.kh * GROUP;
+
+        auto issue = [&](int j) {                        // chunk j of this segment -> ring
+            const int stage = issued % NST;
+            const bool is_v = j >= nch;
+            const int jj = is_v ? j - nch : j;
+            const int keys = min(CH, cnt - jj * CH);
+            const __half* src = (is_v ? Vp : Kp) + (size_t)jj * CH * D;
+            mbar_arrive_expect_tx(&full[stage], keys * D * 2);
+            bulk_copy(ring + stage * CHUNK_BYTES, src, keys * D * 2, &full[stage]);
+            ++issued;
+        };
+        if (tid == 0)
+            for (int j = 0; j < min(NST, total_chunks); ++j) issue(j);
+        int next_issue = min(NST, total_chunks);
+
+        float q[GROUP][8];
+        #pragma unroll
+        for (int gq = 0; gq < GROUP; ++gq) {
+            const float4* src = reinterpret_cast<const float4*>(a.q + (qrow + gq) * D + sl * 8);
+            const float4 x = __ldg(src), y = __ldg(src + 1);
+            q[gq][0] = x.x * qscale; q[gq][1] = x.y * qscale; q[gq][2] = x.z * qscale; q[gq][3] = x.w * qscale;
+            q[gq][4] = y.x * qscale; q[gq][5] = y.y * qscale; q[gq][6] = y.z * qscale; q[gq][7] = y.w * qscale;
+        }
+        float mloc0 = -INFINITY, mloc1 = -INFINITY;
+        float acc[GROUP][8];
+        #pragma unroll
+        for (int gq = 0; gq < GROUP; ++gq)
+            #pragma unroll
+            for (int e = 0; e < 8; ++e) acc[gq][e] = 0.f;
+
+        bool aborted = false;
+        for (int j = 0; j < total_chunks; ++j) {
+            const int stage = consumed % NST;
+            const uint32_t parity = (consumed / NST) & 1;
+            bool got = mbar_wait(&full[stage], parity, &abort_flag);
+            if (!got) { abort_flag = 1; atomicCAS(a.error, 0, 41); }
+            got = __all_sync(0xffffffffu, got);           // warp-uniform: the shuffles below need all lanes
+            const uint8_t* buf = ring + stage * CHUNK_BYTES;
+            const bool is_v = j >= nch;
+            const int jj = is_v ? j - nch : j;
+            const int keys = min(CH, cnt - jj * CH);
+            if (got) {
+                if (!is_v) {
+                    // ---- scores: half-warp hw takes keys hw, hw+8, hw+16, hw+24 (+32) ----
+                    #pragma unroll
+                    for (int half = 0; half < CH / (HALF_WARPS * 4); ++half) {
+                        float v[8];
+                        #pragma unroll
+                        for (int uu = 0; uu < 4; ++uu) {
+                            const int t = half * 32 + uu * HALF_WARPS + hw;
+                            uint4 kr = make_uint4(0, 0, 0, 0);
+                            if (t < keys) kr = *reinterpret_cast<const uint4*>(buf + t * 256 + sl * 16);
+                            float kf[8]; unpack8(kr, kf);
+                            #pragma unroll
+                            for (int gq = 0; gq < GROUP; ++gq) {
+                                float s = 0.f;
+                                #pragma unroll
+                                for (int e = 0; e < 8; ++e) s = fmaf(q[gq][e], kf[e], s);
+                                v[uu * GROUP + gq] = s;
+                            }
+                        }
+                        // transpose-reduce over the 16 lanes of the half-warp (8 shuffles for 8 sums)
+                        const bool b3 = sl & 8, b2 = sl & 4, b1 = sl & 2;
+                        float w4[4], w2[2], y;
+                        #pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            w4[i] = (b3 ? v[i + 4] : v[i]) + __shfl_xor_sync(0xffffffffu, b3 ? v[i] : v[i + 4], 8);
+                        #pragma unroll
+                        for (int i = 0; i < 2; ++i)
+                            w2[i] = (b2 ? w4[i + 2] : w4[i]) + __shfl_xor_sync(0xffffffffu, b2 ? w4[i] : w4[i + 2], 4);
+                        y = (b1 ? w2[1] : w2[0]) + __shfl_xor_sync(0xffffffffu, b1 ? w2[0] : w2[1], 2);
+                        y += __shfl_xor_sync(0xffffffffu, y, 1);
+                        const int my_u = (b3 ? 2 : 0) + (b2 ? 1 : 0), my_g = b1 ? 1 : 0;
+                        const int t = half * 32 + my_u * HALF_WARPS + hw;
+                        if (t < keys) {
+                            if (my_g == 0) mloc0 = fmaxf(mloc0, y); else mloc1 = fmaxf(mloc1, y);
+                            if ((sl & 1) == 0) scores[my_g * a.max_keys + jj * CH + t] = y;
+                        }
+                    }
+                } else {
+                    // ---- PV: half-warp hw takes value rows hw, hw+8, ... of the chunk ----
+                    #pragma unroll 4
+                    for (int t = hw; t < keys; t += HALF_WARPS) {
+                        float vf[8];
+                        unpack8(*reinterpret_cast<const uint4*>(buf + t * 256 + sl * 16), vf);
+                        const float p0 = scores[jj * CH + t], p1 = scores[a.max_keys + jj * CH + t];
+                        #pragma unroll
+                        for (int e = 0; e < 8; ++e) { acc[0][e] = fmaf(p0, vf[e], acc[0][e]); acc[1][e] = fmaf(p1, vf[e], acc[1][e]); }
+                    }
+                }
+            }
+            ++consumed;
+            __syncthreads();                       // everyone is done with this stage
+            if (abort_flag) { aborted = true; break; }
+            if (tid == 0 && next_issue < total_chunks) { issue(next_issue); }
+            ++next_issue;
+            if (j == nch - 1) {
+                // ---- end of the K pass: exact max and exp-sum over this range ----
+                float m0 = mloc0, m1 = mloc1;
+                #pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) {
+                    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+                    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+                }
+                if (lane == 0) { red[0][warp] = m0; red[1][warp] = m1; }
+                __syncthreads();
+                if (tid < GROUP) {
+                    float m = red[tid][0];
+                    #pragma unroll
+                    for (int w = 1; w < THREADS / 32; ++w) m = fmaxf(m, red[tid][w]);
+                    stat[tid] = m;
+                }
+                __syncthreads();
+                float s0 = 0.f, s1 = 0.f;
+                const float mm0 = stat[0], mm1 = stat[1];
+                for (int t = tid; t < cnt; t += THREADS) {
+                    const float p0 = exp2f(scores[t] - mm0), p1 = exp2f(scores[a.max_keys + t] - mm1);
+                    scores[t] = p0; scores[a.max_keys + t] = p1;
+                    s0 += p0; s1 += p1;
+                }
+                #pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) {
+                    s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+                    s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+                }
+                __syncthreads();                   // red reuse
+                if (lane == 0) { red[0][warp] = s0; red[1][warp] = s1; }
+                __syncthreads();
+                if (tid < GROUP) {
+                    float s = 0.f;
+                    #pragma unroll
+                    for (int w = 0; w < THREADS / 32; ++w) s += red[tid][w];
+                    stat[GROUP + tid] = s;
+                }
+                __syncthreads();
+            }
+        }
+        if (aborted) break;
+
+        // ---- combine the 8 half-warps' partial PV sums ----
+        #pragma unroll
+        for (int gq = 0; gq < GROUP; ++gq)
+            #pragma unroll
+            for (int e = 0; e < 8; ++e) accbuf[hw][gq][sl * 8 + e] = acc[gq][e];
+        __syncthreads();
+        float o[GROUP * D / THREADS];
+        #pragma unroll
+        for (int i = 0; i < GROUP * D / THREADS; ++i) {
+            const int idx = tid + i * THREADS, gq = idx / D, jc = idx % D;
+            float s = 0.f;
+            #pragma unroll
+            for (int h = 0; h < HALF_WARPS; ++h) s += accbuf[h][gq][jc];
+            o[i] = s;
+        }
+
+        const int c_first = cta_of(u.off, T, C), c_last = cta_of(u.off + u.len - 1, T, C);
+        if (c_first == c_last) {
+            // this CTA holds the whole unit: normalise and store
+            #pragma unroll
+            for (int i = 0; i < GROUP * D / THREADS; ++i) {
+                const int idx = tid + i * THREADS, gq = idx / D, jc = idx % D;
+                a.out[(qrow + gq) * D + jc] = o[i] / stat[GROUP + gq];
+            }
+        } else {
+            const int unit = (u.l * a.n + u.b) * a.hkv + u.kh;
+            const int nrec = c_last - c_first + 1;
+            float* rec = a.partial + ((size_t)unit * a.max_records + (c - c_first)) * PARTIAL_FLOATS;
+            if (tid < 2 * GROUP) rec[tid] = stat[tid];
+            #pragma unroll
+            for (int i = 0; i < GROUP * D / THREADS; ++i) rec[4 + tid + i * THREADS] = o[i];
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) is_last = (atomicAdd(&a.counters[unit], 1) == nrec - 1);
+            __syncthreads();
+            if (is_last) {
+                __threadfence();
+                const float* recs = a.partial + (size_t)unit * a.max_records * PARTIAL_FLOATS;
+                float mall[GROUP], lall[GROUP];
+                #pragma unroll
+                for (int gq = 0; gq < GROUP; ++gq) {
+                    float m = -INFINITY;
+                    for (int s = 0; s < nrec; ++s) m = fmaxf(m, __ldcg(recs + (size_t)s * PARTIAL_FLOATS + gq));
+                    mall[gq] = m;
+                    float lv = 0.f;
+                    for (int s = 0; s < nrec; ++s)
+                        lv += exp2f(__ldcg(recs + (size_t)s * PARTIAL_FLOATS + gq) - m) *
+                              __ldcg(recs + (size_t)s * PARTIAL_FLOATS + GROUP + gq);
+                    lall[gq] = lv;
+                }
+                #pragma unroll
+                for (int i = 0; i < GROUP * D / THREADS; ++i) {
+                    const int idx = tid + i * THREADS, gq = idx / D, jc = idx % D;
+                    float v = 0.f;
+                    for (int s = 0; s < nrec; ++s)
+                        v += exp2f(__ldcg(recs + (size_t)s * PARTIAL_FLOATS + gq) - mall[gq]) *
+                             __ldcg(recs + (size_t)s * PARTIAL_FLOATS + 4 + idx);
+                    a.out[(qrow + gq) * D + jc] = v / lall[gq];
+                }
+                if (tid == 0) a.counters[unit] = 0;    // ready for the next call on this stream
+            }
+        }
+        __syncthreads();                               // accbuf / stat reuse by the next segment
+    }
+
+    // drain: copies issued but never consumed (abort path) must land before the CTA exits
+    if (tid == 0) {
+        while (consumed < issued) {
+            mbar_wait(&full[consumed % NST], (consumed / NST) & 1, &never_abort, 500000000ull);
+            ++consumed;
+        }
+    }
+}
+
+}  // namespace
+
+int decode_max_records(int max_len) { return max_len / 64 + 3; }
+
+// Even split: C ranges of T/C keys, C a multiple of the SM count with 2 CTAs per SM, each
+// range between 64 and 2048 keys.
+void launch_attn_decode_sm100(const KVLayout& kv, const float* q, float* out, int seq, int layer0, int n_layers,
+                              int pos0, int n, int hq, int hkv, float* partial, int max_records, int* counters,
+                              int* error, cudaStream_t s) {
+    DecodeArgs a{};
+    a.q = q; a.out = out; a.kv = kv; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0;
+    a.n = n; a.hq = hq; a.hkv = hkv;
+    a.total_keys = (long long)n_layers * hkv * ((long long)n * pos0 + (long long)n * (n + 1) / 2);
+    long long ctas = (long long)NUM_SMS_B200 * 2;
+    ctas = std::min<long long>(ctas, std::max<long long>(1, a.total_keys / 64));
+    ctas = std::max<long long>(ctas, (a.total_keys + 2047) / 2048);
+    // records per unit are bounded: a unit of len keys meets at most len/(T/C)+2 CTAs
+    const long long max_len = pos0 + n;
+    while (ctas > 1 && (max_len * ctas) / a.total_keys + 2 > max_records) --ctas;
+    a.ctas = (int)ctas;
+    a.max_keys = (int)((a.total_keys + ctas - 1) / ctas) + 1;
+    a.max_records = max_records;
+    a.partial = partial; a.counters = counters; a.error = error;
+    const size_t smem = (size_t)NST * CHUNK_BYTES + (size_t)GROUP * a.max_keys * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(attn_decode_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             NST * CHUNK_BYTES + GROUP * 2050 * (int)sizeof(float));
+        attr = true;
+    }
+    attn_decode_sm100_kernel<<<a.ctas, THREADS, smem, s>>>(a);
+}
+
+}  // namespace qattn

@@ -37,6 +37,7 @@ struct qa_ctx {
     size_t partial_floats = 0;
     int* counters = nullptr;
     int max_units = 0;
+    int max_records = 0;                   // split records per unit
     float* staging = nullptr;              // device staging for io_host calls
     size_t staging_floats = 0;
     CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
@@ -153,19 +154,6 @@ int check_device_error(qa_ctx* ctx) {
     return QA_OK;
 }
 
-// Chooses the split count for split-context attention over `units` (layer, row, head)
-// work items whose longest context is max_len keys: enough CTAs to cover the SMs several
-// times over, at least 64 keys per split, record space permitting.
-void choose_splits(const qa_ctx* ctx, long long units, int max_len, int& splits, int& kps) {
-    const long long target = (long long)NUM_SMS_B200 * 8;
-    long long s = std::max<long long>(1, (target + units - 1) / units);
-    s = std::min<long long>(s, (max_len + 63) / 64);
-    const long long cap = (long long)(ctx->partial_floats / PARTIAL_FLOATS) / std::max<long long>(1, units);
-    s = std::max<long long>(1, std::min(s, cap));
-    kps = (int)(((max_len + s - 1) / s + 31) / 32 * 32);
-    splits = (max_len + kps - 1) / kps;
-}
-
 }  // namespace
 
 extern "C" {
@@ -244,9 +232,11 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     if (cudaMalloc(&ctx->norms, ones.size() * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMemcpy(ctx->norms, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) return cleanup(QA_ERR_CUDA);
 
-    // Split-context records: every (layer, decode row, head) unit with up to 32 splits.
+    // Split-context records: every (layer, decode row, head) unit, as many records as the
+    // decode partition can give one unit at this context length.
     ctx->max_units = c.n_layers * QA_MAX_DECODE_ROWS * ctx->hkv;
-    ctx->partial_floats = (size_t)ctx->max_units * 32 * PARTIAL_FLOATS;
+    ctx->max_records = decode_max_records(c.context);
+    ctx->partial_floats = (size_t)ctx->max_units * ctx->max_records * PARTIAL_FLOATS;
     if (cudaMalloc(&ctx->partial, ctx->partial_floats * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMalloc(&ctx->counters, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMemset(ctx->counters, 0, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
@@ -392,8 +382,8 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
     r.pos0 = pos0; r.n = n; r.hq = ctx->hq; r.hkv = ctx->hkv; r.row_begin = 0; r.row_end = n;
     r.partial = ctx->partial; r.counters = ctx->counters;
     if (decode) {
-        choose_splits(ctx, (long long)n_layers * n * ctx->hkv, pos0 + n, r.splits, r.keys_per_split);
-        launch_attn_rows(r, ctx->stream);
+        launch_attn_decode_sm100(ctx->kv, qd, od, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv, ctx->partial,
+                                 ctx->max_records, ctx->counters, ctx->error, ctx->stream);
     } else {
         // rows below position TC_MIN_POSITION: FP32 CUDA cores; the rest: tcgen05 tensor cores
         const int tc_begin = std::min(n, std::max(0, TC_MIN_POSITION - pos0));

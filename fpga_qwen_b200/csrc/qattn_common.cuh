@@ -53,6 +53,12 @@ void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cuda
 void launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
                                int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
                                cudaStream_t s);
+// TMA-streamed split-context decode (rows pos0..pos0+n-1, n <= QA_MAX_DECODE_ROWS).
+void launch_attn_decode_sm100(const KVLayout& kv, const float* q, float* out, int seq, int layer0, int n_layers,
+                              int pos0, int n, int hq, int hkv, float* partial, int max_records, int* counters,
+                              int* error, cudaStream_t s);
+// Partial records reserved per (layer, row, head) unit for contexts up to max_len keys.
+int decode_max_records(int max_len);
 // Rows at absolute positions below this go to the FP32 CUDA-core kernel.
 constexpr int TC_MIN_POSITION = 128;
 void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n,

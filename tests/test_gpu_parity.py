@@ -325,3 +325,31 @@ def test_prefill_is_deterministic_and_matches_single_layer_calls():
     assert torch.equal(out_all, out_again)
     assert torch.equal(out_all, per_layer)
     ctx.close()
+
+
+@pytest.mark.parametrize("layers,pos0,n", [(28, 0, 1), (28, 0, 4), (3, 63, 1), (1, 4094, 2), (28, 3000, 3),
+                                           (5, 129, 4), (2, 1, 1), (28, 4092, 4)])
+def test_decode_partitions(layers, pos0, n):
+    """Decode / verify rows over the even key partition: ranges that split units, ranges that
+    hold several whole units, 1..4 rows, tiny and full contexts — all within tolerance of the
+    oracle, and repeat calls are bitwise deterministic."""
+    ctx = make_ctx(layers, context=4096)
+    qw, kw = H.norms(40 + n, layers)
+    H.set_norms(ctx, qw, kw)
+    q, k, v = H.inputs(40 + pos0, layers, 0, pos0 + n)
+    if pos0:
+        gpu_append(ctx, 0, 0, q[:, :pos0].contiguous(), k[:, :pos0].contiguous(), v[:, :pos0].contiguous())
+        ctx.commit(0, pos0)
+    qn = gpu_append(ctx, 0, pos0, q[:, pos0:].contiguous(), k[:, pos0:].contiguous(), v[:, pos0:].contiguous())
+    out = gpu_attend(ctx, 0, pos0, qn, decode=True)
+    again = gpu_attend(ctx, 0, pos0, qn, decode=True)
+    torch.cuda.synchronize()
+    ctx.sync()
+    assert torch.equal(out, again)
+    outh, qnh = out.cpu().numpy(), qn.cpu().numpy()
+    for layer in sorted({0, layers // 2, layers - 1}):
+        kv = H.read_layer_kv(ctx, 0, layer, pos0 + n, 4096)
+        ref = O.attention(kv, pos0, qnh[layer], threads=8)
+        mx, rms = H.err_stats(outh[layer], ref)
+        assert mx < H.MAX_ABS and rms < H.RMS, (layer, mx, rms)
+    ctx.close()
