@@ -62,6 +62,29 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk16) {   // K-major, 12
     return (uint32_t)((chunk16 >> 3) * 16384 + (row >> 3) * 1024 + (row & 7) * 128 + (((chunk16 & 7) ^ (row & 7)) << 4));
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+// 2^x on the MUFU unit (PTX ex2.approx.ftz: relative error ~2^-22, inputs here are <= 8)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long r, ua = *reinterpret_cast<unsigned long long*>(&a), ub = *reinterpret_cast<unsigned long long*>(&b),
+                          uc = *reinterpret_cast<unsigned long long*>(&c);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(ua), "l"(ub), "l"(uc));
+    return *reinterpret_cast<float2*>(&r);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    unsigned long long r, ua = *reinterpret_cast<unsigned long long*>(&a), ub = *reinterpret_cast<unsigned long long*>(&b);
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(ua), "l"(ub));
+    return *reinterpret_cast<float2*>(&r);
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -144,30 +167,35 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         for (int j = 0; j < nk && ok; ++j) {
             if (!mbar_wait(&bar[B_SF0 + h], j & 1, abortp)) { fail(11); ok = false; break; }
             tc_fence_after();
-            float s[BN];
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t rr[32];
-                tmem_ld32(s_col + c * 32, rr);
-                tmem_wait_ld();
-                #pragma unroll
-                for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(rr[i]);
-            }
-            tc_fence_before();
-            mbar_arrive(&bar[B_SE0 + h]);
+            // Pass A: masked row maximum, reading S from TMEM 64 columns at a time (the row is
+            // read again in pass B rather than held in 128 registers).
             const int k0 = j * BN;
-            if (k0 + BN - 1 > row_pos) {
-                #pragma unroll
-                for (int c = 0; c < BN; ++c) if (k0 + c > row_pos) s[c] = -INFINITY;
-            }
+            const int lim = row_pos - k0;                       // keys c > lim are in the future
+            const bool diag = lim < BN - 1;                     // tile crosses the diagonal
             float mt = -INFINITY;
             #pragma unroll
-            for (int c = 0; c < BN; ++c) mt = fmaxf(mt, s[c]);
+            for (int half = 0; half < 2; ++half) {
+                uint32_t sr[2][32];
+                tmem_ld32(s_col + half * 64, sr[0]);
+                tmem_ld32(s_col + half * 64 + 32, sr[1]);
+                tmem_wait_ld();
+                #pragma unroll
+                for (int c = 0; c < 2; ++c)
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
+                float* v = reinterpret_cast<float*>(&sr[0][0]);
+                if (diag) {
+                    #pragma unroll
+                    for (int c = 0; c < 64; ++c) v[c] = (half * 64 + c > lim) ? -INFINITY : v[c];
+                }
+                #pragma unroll
+                for (int c = 0; c < 64; c += 2) mt = fmax3(mt, v[c], v[c + 1]);
+            }
             mt *= scale;
             float alpha = 1.f;
             bool rescale = false;
             if (j == 0) m = mt;
-            else if (mt > m + RESCALE_THRESHOLD) { alpha = exp2f(m - mt); m = mt; rescale = true; }
+            else if (mt > m + RESCALE_THRESHOLD) { alpha = ex2_approx(m - mt); m = mt; rescale = true; }
             // P buffer and O_h are free once PV_h(j-1) has completed
             if (j > 0 && !mbar_wait(&bar[B_OD0 + h], (j - 1) & 1, abortp)) { fail(12); ok = false; break; }
             if (rescale) {
@@ -184,17 +212,41 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 tmem_wait_st();
                 lsum *= alpha;
             }
-            const float mneg = -m;
-            float psum = 0.f;
+            // Pass B: p = 2^(s*scale - m) with packed FMA pairs and MUFU ex2, FP16 P into the
+            // swizzled shared-memory operand, 4 independent packed partial sums.
+            const float2 sc2 = make_float2(scale, scale), mn2 = make_float2(-m, -m);
+            float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                float p[8];
+            for (int half = 0; half < 2; ++half) {
+                uint32_t sr[2][32];
+                tmem_ld32(s_col + half * 64, sr[0]);
+                tmem_ld32(s_col + half * 64 + 32, sr[1]);
+                tmem_wait_ld();
                 #pragma unroll
-                for (int i = 0; i < 8; ++i) { p[i] = exp2f(fmaf(s[c * 8 + i], scale, mneg)); psum += p[i]; }
-                const uint4 v = make_uint4(pack_half2(p[0], p[1]), pack_half2(p[2], p[3]), pack_half2(p[4], p[5]),
-                                           pack_half2(p[6], p[7]));
-                *reinterpret_cast<uint4*>(Ps + swz(t, c)) = v;
+                for (int c = 0; c < 2; ++c)
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
+                float* v = reinterpret_cast<float*>(&sr[0][0]);
+                if (diag) {
+                    #pragma unroll
+                    for (int c = 0; c < 64; ++c) v[c] = (half * 64 + c > lim) ? -INFINITY : v[c];
+                }
+                #pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t packed[4];
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 x = ffma2(make_float2(v[c * 8 + 2 * i], v[c * 8 + 2 * i + 1]), sc2, mn2);
+                        const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                        ps[i] = fadd2(ps[i], e);
+                        packed[i] = pack_half2(e.x, e.y);
+                    }
+                    *reinterpret_cast<uint4*>(Ps + swz(t, half * 8 + c)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                }
             }
+            tc_fence_before();
+            mbar_arrive(&bar[B_SE0 + h]);                       // S_h may now be overwritten
+            const float psum = (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) + (ps[3].x + ps[3].y);
             lsum += psum;
             fence_proxy_async_smem();
             tc_fence_before();
