@@ -37,6 +37,7 @@ constexpr int HALF_WARPS = THREADS / 16;
 constexpr int CH = 64;                        // keys per chunk
 constexpr int NST = 4;                        // ring stages
 constexpr uint32_t CHUNK_BYTES = CH * D * 2;  // 16 KB
+constexpr int MAX_RANGE = 6144;               // keys per CTA range (scores: 2 x 24 KB of shared memory)
 
 struct DecodeArgs {
     const float* q; float* out;               // [n_layers][n][hq][128]
@@ -80,6 +81,13 @@ __device__ __forceinline__ void unpack8(const uint4 u, float f[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&u);
     #pragma unroll
     for (int i = 0; i < 4; ++i) { const float2 t = __half22float2(h[i]); f[2 * i] = t.x; f[2 * i + 1] = t.y; }
+}
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long r, ua = *reinterpret_cast<unsigned long long*>(&a), ub = *reinterpret_cast<unsigned long long*>(&b),
+                          uc = *reinterpret_cast<unsigned long long*>(&c);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(ua), "l"(ub), "l"(uc));
+    return *reinterpret_cast<float2*>(&r);
 }
 
 __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -180,10 +188,12 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
                             float kf[8]; unpack8(kr, kf);
                             #pragma unroll
                             for (int gq = 0; gq < GROUP; ++gq) {
-                                float s = 0.f;
+                                // even/odd channel partial sums with packed FP32 FMA
+                                float2 s2 = make_float2(0.f, 0.f);
                                 #pragma unroll
-                                for (int e = 0; e < 8; ++e) s = fmaf(q[gq][e], kf[e], s);
-                                v[uu * GROUP + gq] = s;
+                                for (int e = 0; e < 8; e += 2)
+                                    s2 = ffma2(make_float2(q[gq][e], q[gq][e + 1]), make_float2(kf[e], kf[e + 1]), s2);
+                                v[uu * GROUP + gq] = s2.x + s2.y;
                             }
                         }
                         // transpose-reduce over the 16 lanes of the half-warp (8 shuffles for 8 sums)
@@ -211,8 +221,14 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
                         float vf[8];
                         unpack8(*reinterpret_cast<const uint4*>(buf + t * 256 + sl * 16), vf);
                         const float p0 = scores[jj * CH + t], p1 = scores[a.max_keys + jj * CH + t];
+                        const float2 pp0 = make_float2(p0, p0), pp1 = make_float2(p1, p1);
                         #pragma unroll
-                        for (int e = 0; e < 8; ++e) { acc[0][e] = fmaf(p0, vf[e], acc[0][e]); acc[1][e] = fmaf(p1, vf[e], acc[1][e]); }
+                        for (int e = 0; e < 8; e += 2) {
+                            const float2 v2 = make_float2(vf[e], vf[e + 1]);
+                            float2 a0 = ffma2(pp0, v2, make_float2(acc[0][e], acc[0][e + 1]));
+                            float2 a1 = ffma2(pp1, v2, make_float2(acc[1][e], acc[1][e + 1]));
+                            acc[0][e] = a0.x; acc[0][e + 1] = a0.y; acc[1][e] = a1.x; acc[1][e + 1] = a1.y;
+                        }
                     }
                 }
             }
@@ -343,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
 int decode_max_records(int max_len) { return max_len / 64 + 3; }
 
 // Even split: C ranges of T/C keys, C a multiple of the SM count with 2 CTAs per SM, each
-// range between 64 and 2048 keys.
+// range between 64 and MAX_RANGE keys (one wave at 4K context: 889K keys over 296 CTAs).
 void launch_attn_decode_sm100(const KVLayout& kv, const float* q, float* out, int seq, int layer0, int n_layers,
                               int pos0, int n, int hq, int hkv, float* partial, int max_records, int* counters,
                               int* error, cudaStream_t s) {
@@ -353,7 +369,7 @@ void launch_attn_decode_sm100(const KVLayout& kv, const float* q, float* out, in
     a.total_keys = (long long)n_layers * hkv * ((long long)n * pos0 + (long long)n * (n + 1) / 2);
     long long ctas = (long long)NUM_SMS_B200 * 2;
     ctas = std::min<long long>(ctas, std::max<long long>(1, a.total_keys / 64));
-    ctas = std::max<long long>(ctas, (a.total_keys + 2047) / 2048);
+    ctas = std::max<long long>(ctas, (a.total_keys + MAX_RANGE - 1) / MAX_RANGE);
     // records per unit are bounded: a unit of len keys meets at most len/(T/C)+2 CTAs
     const long long max_len = pos0 + n;
     while (ctas > 1 && (max_len * ctas) / a.total_keys + 2 > max_records) --ctas;
@@ -365,7 +381,7 @@ void launch_attn_decode_sm100(const KVLayout& kv, const float* q, float* out, in
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(attn_decode_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             NST * CHUNK_BYTES + GROUP * 2050 * (int)sizeof(float));
+                             NST * CHUNK_BYTES + GROUP * (MAX_RANGE + 2) * (int)sizeof(float));
         attr = true;
     }
     attn_decode_sm100_kernel<<<a.ctas, THREADS, smem, s>>>(a);

@@ -10,11 +10,13 @@
 // attend to few keys, where FP16 probabilities are not accurate enough, and go to the
 // FP32 CUDA-core kernel (attn_rows.cu).
 //
-// Warp roles (320 threads):
+// Warp roles (384 threads, three warpgroups):
 //   warps 0-3  softmax group for query head 0 (thread t owns query row t of the tile)
 //   warps 4-7  softmax group for query head 1
 //   warp  8    MMA issuer (one elected thread issues tcgen05.mma, the warp zeroes stale V rows)
-//   warp  9    TMA producer (one thread)
+//   warp  9    TMA producer (one thread); warps 10-11 idle
+// setmaxnreg moves registers from the control warpgroup to the softmax warpgroups so each
+// softmax thread holds its 128-column S row in registers.
 // Per 128-key tile j:
 //   S_h = Q_h K_j^T         tcgen05.mma kind::f16, M=128 N=128 K=128, FP32 accumulate in TMEM
 //   softmax group h: tcgen05.ld S_h row, causal mask, running max (log2 domain, lazy
@@ -40,7 +42,12 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128, BN = 128;
-constexpr int THREADS = 320;
+constexpr int THREADS = 384;                              // 12 warps = 3 warpgroups
+// Register split: launched at 168 per thread (384 x 168 = 64,512); the control warpgroup
+// (MMA + TMA warps) drops to 56 and the two softmax warpgroups rise to 224:
+// 2 x 128 x 224 + 128 x 56 = 64,512, the launch total.
+constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 224, REGS_CONTROL = 56;
+static_assert(2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL == THREADS * REGS_LAUNCH, "register split must match launch");
 constexpr uint32_t TILE_BYTES = BN * D * 2;               // 32 KB FP16 K or V tile
 constexpr int OFF_Q = 0, OFF_K = 65536, OFF_V = 131072, OFF_P = 163840, OFF_BAR = 229376;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;          // + barriers + alignment slack
@@ -132,6 +139,8 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     volatile int* abortp = &abort_flag;
+    if (warp < 8) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
+    else asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CONTROL));
     auto fail = [&](int code) { *abortp = 1; atomicCAS(a.error, 0, code); };
 
     if (warp < 8) {
@@ -167,30 +176,29 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         for (int j = 0; j < nk && ok; ++j) {
             if (!mbar_wait(&bar[B_SF0 + h], j & 1, abortp)) { fail(11); ok = false; break; }
             tc_fence_after();
-            // Pass A: masked row maximum, reading S from TMEM 64 columns at a time (the row is
-            // read again in pass B rather than held in 128 registers).
+            // S row -> registers: four 32-column loads in flight, one wait; the empty asm pins
+            // every use of the loaded registers after the wait
+            uint32_t sr[4][32];
+            #pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, sr[c]);
+            tmem_wait_ld();
+            #pragma unroll
+            for (int c = 0; c < 4; ++c)
+                #pragma unroll
+                for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
+            tc_fence_before();
+            mbar_arrive(&bar[B_SE0 + h]);                       // S_h may now be overwritten
+            float* v = reinterpret_cast<float*>(&sr[0][0]);
             const int k0 = j * BN;
             const int lim = row_pos - k0;                       // keys c > lim are in the future
-            const bool diag = lim < BN - 1;                     // tile crosses the diagonal
-            float mt = -INFINITY;
-            #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t sr[2][32];
-                tmem_ld32(s_col + half * 64, sr[0]);
-                tmem_ld32(s_col + half * 64 + 32, sr[1]);
-                tmem_wait_ld();
+            if (lim < BN - 1) {                                 // tile crosses the diagonal
                 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
-                float* v = reinterpret_cast<float*>(&sr[0][0]);
-                if (diag) {
-                    #pragma unroll
-                    for (int c = 0; c < 64; ++c) v[c] = (half * 64 + c > lim) ? -INFINITY : v[c];
-                }
-                #pragma unroll
-                for (int c = 0; c < 64; c += 2) mt = fmax3(mt, v[c], v[c + 1]);
+                for (int c = 0; c < BN; ++c) v[c] = (c > lim) ? -INFINITY : v[c];
             }
+            float mt = fmax3(v[0], v[1], v[2]);
+            #pragma unroll
+            for (int c = 3; c < BN - 1; c += 2) mt = fmax3(mt, v[c], v[c + 1]);
+            mt = fmaxf(mt, v[BN - 1]);
             mt *= scale;
             float alpha = 1.f;
             bool rescale = false;
@@ -212,40 +220,22 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 tmem_wait_st();
                 lsum *= alpha;
             }
-            // Pass B: p = 2^(s*scale - m) with packed FMA pairs and MUFU ex2, FP16 P into the
-            // swizzled shared-memory operand, 4 independent packed partial sums.
+            // p = 2^(s*scale - m): packed FMA pairs, MUFU ex2, FP16 P into the swizzled
+            // shared-memory operand, 4 independent packed partial sums
             const float2 sc2 = make_float2(scale, scale), mn2 = make_float2(-m, -m);
             float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t sr[2][32];
-                tmem_ld32(s_col + half * 64, sr[0]);
-                tmem_ld32(s_col + half * 64 + 32, sr[1]);
-                tmem_wait_ld();
+            for (int c = 0; c < 16; ++c) {
+                uint32_t packed[4];
                 #pragma unroll
-                for (int c = 0; c < 2; ++c)
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
-                float* v = reinterpret_cast<float*>(&sr[0][0]);
-                if (diag) {
-                    #pragma unroll
-                    for (int c = 0; c < 64; ++c) v[c] = (half * 64 + c > lim) ? -INFINITY : v[c];
+                for (int i = 0; i < 4; ++i) {
+                    const float2 x = ffma2(make_float2(v[c * 8 + 2 * i], v[c * 8 + 2 * i + 1]), sc2, mn2);
+                    const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                    ps[i] = fadd2(ps[i], e);
+                    packed[i] = pack_half2(e.x, e.y);
                 }
-                #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t packed[4];
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 x = ffma2(make_float2(v[c * 8 + 2 * i], v[c * 8 + 2 * i + 1]), sc2, mn2);
-                        const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                        ps[i] = fadd2(ps[i], e);
-                        packed[i] = pack_half2(e.x, e.y);
-                    }
-                    *reinterpret_cast<uint4*>(Ps + swz(t, half * 8 + c)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                }
+                *reinterpret_cast<uint4*>(Ps + swz(t, c)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
             }
-            tc_fence_before();
-            mbar_arrive(&bar[B_SE0 + h]);                       // S_h may now be overwritten
             const float psum = (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) + (ps[3].x + ps[3].y);
             lsum += psum;
             fence_proxy_async_smem();
@@ -399,21 +389,30 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
 }  // namespace
 
 // Host side --------------------------------------------------------------------------------------
-void launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
-                               int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
-                               cudaStream_t s) {
-    if (row_begin >= n) return;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(attn_prefill_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        attr_set = true;
+int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
+                              int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
+                              cudaStream_t s) {
+    if (row_begin >= n) return 0;
+    static int checked = 0;                      // 1: ready, -1: refused
+    if (!checked) {
+        // setmaxnreg.inc waits for registers the control warpgroup releases; the split is
+        // only consistent with a launch at exactly REGS_LAUNCH registers per thread.
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, attn_prefill_sm100_kernel) != cudaSuccess || fa.numRegs != REGS_LAUNCH ||
+            cudaFuncSetAttribute(attn_prefill_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+                cudaSuccess)
+            checked = -1;
+        else
+            checked = 1;
     }
+    if (checked < 0) return -1;
     PrefillArgs a{};
     a.q = q; a.out = out; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
     a.hq = hq; a.hkv = hkv; a.layers_total = layers_total; a.row_begin = row_begin;
     a.n_qtiles = (n - row_begin + BM - 1) / BM; a.error = error;
     const unsigned blocks = (unsigned)(a.n_qtiles * hkv * n_layers);
     attn_prefill_sm100_kernel<<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
+    return 0;
 }
 
 }  // namespace qattn

@@ -392,8 +392,9 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
             r.splits = 1; r.keys_per_split = ((pos0 + tc_begin) + 31) / 32 * 32;
             launch_attn_rows(r, ctx->stream);
         }
-        launch_attn_prefill_sm100(ctx->kv_map, qd, od, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv,
-                                  ctx->cfg.n_layers, tc_begin, ctx->error, ctx->stream);
+        if (launch_attn_prefill_sm100(ctx->kv_map, qd, od, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv,
+                                      ctx->cfg.n_layers, tc_begin, ctx->error, ctx->stream))
+            return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel has an unexpected register allocation");
     }
     if ((st = after_launch(ctx, seq, decode ? "attn_decode" : "attn_prefill"))) return st;
     if (ctx->cfg.io_host) {

@@ -50,7 +50,8 @@ void launch_kv_append(const AppendArgs& a, cudaStream_t s);
 void launch_attn_rows(const RowsArgs& a, cudaStream_t s);
 void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cudaStream_t s);
 // Tensor-core prefill for rows [row_begin, n) (all with absolute position >= 128).
-void launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
+// Returns non-zero (and launches nothing) if the kernel was not built with the expected registers.
+int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
                                int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
                                cudaStream_t s);
 // TMA-streamed split-context decode (rows pos0..pos0+n-1, n <= QA_MAX_DECODE_ROWS).
