@@ -26,13 +26,15 @@
 // head while the other head's softmax runs (ping-pong). Key tiles above the diagonal of the
 // query tile are skipped; tiles crossing it are masked per element.
 //
-// Memory: Q_0, Q_1 (FP16, 32 KB each), K (2 stages x 32 KB), V (32 KB), P_0, P_1 (32 KB each)
+// Memory: Q_0, Q_1 (FP16, 32 KB each), a 3-stage K/V ring (32 KB stages), P_0, P_1 (32 KB each)
 // = 224 KB shared; TMEM 512 columns = S_0, S_1, O_0, O_1 (128 FP32 columns each).
 // K/V tiles come from the HBM KV store through one 3-D tensor map
 // {128 channels, ctx positions, planes} with 64x128 boxes and 128-byte swizzle.
 //
 // Every wait is bounded (globaltimer, 2 s): on expiry the CTA raises an abort flag, writes
 // an error code to the host-visible flag, drains what it issued and frees its TMEM.
+#include <algorithm>
+
 #include "qattn_common.cuh"
 #include "sm100.cuh"
 
@@ -49,12 +51,16 @@ constexpr int THREADS = 384;                              // 12 warps = 3 warpgr
 constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 224, REGS_CONTROL = 56;
 static_assert(2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL == THREADS * REGS_LAUNCH, "register split must match launch");
 constexpr uint32_t TILE_BYTES = BN * D * 2;               // 32 KB FP16 K or V tile
-constexpr int OFF_Q = 0, OFF_K = 65536, OFF_V = 131072, OFF_P = 163840, OFF_BAR = 229376;
+// K and V tiles share one 3-stage ring in load order K0, V0, K1, V1, ...: item i = 2j (K_j)
+// or 2j+1 (V_j) lives in stage i % 3, so every load is issued about 1.5 tiles before use.
+constexpr int RING = 3;
+constexpr int OFF_Q = 0, OFF_RING = 65536, OFF_P = OFF_RING + RING * 32768, OFF_BAR = OFF_P + 65536;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;          // + barriers + alignment slack
 constexpr float RESCALE_THRESHOLD = 8.0f;                 // log2 units
 
 enum {
-    B_Q0, B_Q1, B_KF0, B_KF1, B_KE0, B_KE1, B_VF, B_VE, B_SF0, B_SF1, B_SE0, B_SE1, B_PF0, B_PF1, B_OD0, B_OD1,
+    B_Q0, B_Q1, B_FULL0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_SF0, B_SF1, B_SE0, B_SE1, B_PF0, B_PF1,
+    B_OD0, B_OD1,
     B_DRAIN, B_COUNT
 };
 
@@ -125,8 +131,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         abort_flag = 0;
         never_abort = 0;
         mbar_init(&bar[B_Q0], 128); mbar_init(&bar[B_Q1], 128);
-        mbar_init(&bar[B_KF0], 1); mbar_init(&bar[B_KF1], 1); mbar_init(&bar[B_KE0], 1); mbar_init(&bar[B_KE1], 1);
-        mbar_init(&bar[B_VF], 1); mbar_init(&bar[B_VE], 1);
+        for (int i = 0; i < RING; ++i) { mbar_init(&bar[B_FULL0 + i], 1); mbar_init(&bar[B_EMPTY0 + i], 1); }
         mbar_init(&bar[B_SF0], 1); mbar_init(&bar[B_SF1], 1); mbar_init(&bar[B_SE0], 128); mbar_init(&bar[B_SE1], 128);
         mbar_init(&bar[B_PF0], 128); mbar_init(&bar[B_PF1], 128); mbar_init(&bar[B_OD0], 1); mbar_init(&bar[B_OD1], 1);
         mbar_init(&bar[B_DRAIN], 1);
@@ -266,12 +271,18 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         // ================================== MMA issuer ==================================
         const uint32_t idesc_qk = idesc_f16_f32(BM, BN, false);
         const uint32_t idesc_pv = idesc_f16_f32(BM, D, true);
-        const uint32_t q_addr = smem_u32(smem + OFF_Q), k_addr = smem_u32(smem + OFF_K);
-        const uint32_t v_addr = smem_u32(smem + OFF_V), p_addr = smem_u32(smem + OFF_P);
-        uint8_t* Vs = smem + OFF_V;
+        const uint32_t q_addr = smem_u32(smem + OFF_Q), ring_addr = smem_u32(smem + OFF_RING);
+        const uint32_t p_addr = smem_u32(smem + OFF_P);
         bool ok = true;
+        auto wait_item = [&](int i) {                    // ring item i has landed
+            return mbar_wait(&bar[B_FULL0 + i % RING], (i / RING) & 1, abortp);
+        };
+        auto release_item = [&](int i) {                 // stage of item i free once prior MMAs finish
+            if (lane == 0) mma_commit(&bar[B_EMPTY0 + i % RING]);
+            __syncwarp();
+        };
         auto issue_qk = [&](int j, int h) {
-            const uint32_t kb = k_addr + (j & 1) * TILE_BYTES, qb = q_addr + h * 32768;
+            const uint32_t kb = ring_addr + ((2 * j) % RING) * TILE_BYTES, qb = q_addr + h * 32768;
             if (lane == 0) {
                 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
@@ -283,34 +294,34 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             __syncwarp();
         };
         auto issue_pv = [&](int j, int h) {
-            const uint32_t pb = p_addr + h * 32768;
+            const uint32_t pb = p_addr + h * 32768, vb = ring_addr + ((2 * j + 1) % RING) * TILE_BYTES;
             if (lane == 0) {
                 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
                     const uint32_t offa = (s >> 2) * 16384 + (s & 3) * 32;
                     mma_f16_ss(tmem + 256 + h * 128, sw128_desc(pb + offa, 16, 1024),
-                               sw128_desc(v_addr + s * 2048, 16384, 1024), idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
+                               sw128_desc(vb + s * 2048, 16384, 1024), idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
                 }
                 mma_commit(&bar[B_OD0 + h]);
             }
             __syncwarp();
         };
         // prologue: S_0(0), S_1(0)
-        if (!mbar_wait(&bar[B_Q0], 0, abortp) || !mbar_wait(&bar[B_Q1], 0, abortp) || !mbar_wait(&bar[B_KF0], 0, abortp)) {
+        if (!mbar_wait(&bar[B_Q0], 0, abortp) || !mbar_wait(&bar[B_Q1], 0, abortp) || !wait_item(0)) {
             fail(21); ok = false;
         }
         if (ok) {
             tc_fence_after();
             issue_qk(0, 0);
             issue_qk(0, 1);
-            if (lane == 0) mma_commit(&bar[B_KE0]);
-            __syncwarp();
+            release_item(0);
         }
         for (int j = 0; j < nk && ok; ++j) {
-            if (!mbar_wait(&bar[B_VF], j & 1, abortp)) { fail(22); ok = false; break; }
+            if (!wait_item(2 * j + 1)) { fail(22); ok = false; break; }
             if (j == nk - 1 && valid_keys < (j + 1) * BN) {
                 // Rows of the last V tile past the causal end hold stale data: zero them so
                 // that a zero probability never meets a non-finite value.
+                uint8_t* Vs = smem + OFF_RING + ((2 * j + 1) % RING) * TILE_BYTES;
                 const int first = valid_keys - j * BN;
                 for (int idx = first * 16 + lane; idx < BN * 16; idx += 32) {
                     const int row = idx >> 4, c = idx & 15;        // c: 16-byte chunk of the 256-byte row
@@ -326,21 +337,15 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 if (!mbar_wait(&bar[B_PF0 + h], j & 1, abortp)) { fail(23); ok = false; break; }
                 tc_fence_after();
                 issue_pv(j, h);
+                if (h == 1) release_item(2 * j + 1);         // V_j free when PV_1(j) completes
                 if (j + 1 < nk) {
                     const int jn = j + 1;
-                    if (h == 0 && !mbar_wait(&bar[B_KF0 + (jn & 1)], (jn >> 1) & 1, abortp)) { fail(24); ok = false; break; }
+                    if (h == 0 && !wait_item(2 * jn)) { fail(24); ok = false; break; }
                     if (!mbar_wait(&bar[B_SE0 + h], j & 1, abortp)) { fail(25); ok = false; break; }
                     tc_fence_after();
                     issue_qk(jn, h);
-                    if (h == 1) {
-                        if (lane == 0) mma_commit(&bar[B_KE0 + (jn & 1)]);
-                        __syncwarp();
-                    }
+                    if (h == 1) release_item(2 * jn);        // K_{j+1} free when QK_1(j+1) completes
                 }
-            }
-            if (ok) {
-                if (lane == 0) mma_commit(&bar[B_VE]);
-                __syncwarp();
             }
         }
         // drain: every MMA this thread issued has completed before TMEM is released
@@ -351,30 +356,22 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         __syncwarp();
     } else if (warp == 9 && lane == 0) {
         // ================================== TMA producer ==================================
-        int issued_k = 0, issued_v = 0;
+        int issued = 0;
         bool ok = true;
-        for (int j = 0; j < nk && ok; ++j) {
-            const int st = j & 1;
-            if (j >= 2 && !mbar_wait(&bar[B_KE0 + st], ((j >> 1) - 1) & 1, abortp)) { fail(31); ok = false; break; }
-            uint8_t* kd = smem + OFF_K + st * TILE_BYTES;
-            mbar_arrive_expect_tx(&bar[B_KF0 + st], TILE_BYTES);
-            tma_load_3d(kd, &kv_map, 0, j * BN, plane_k, &bar[B_KF0 + st]);
-            tma_load_3d(kd + 16384, &kv_map, 64, j * BN, plane_k, &bar[B_KF0 + st]);
-            ++issued_k;
-            if (j >= 1 && !mbar_wait(&bar[B_VE], (j - 1) & 1, abortp)) { fail(32); ok = false; break; }
-            uint8_t* vd = smem + OFF_V;
-            mbar_arrive_expect_tx(&bar[B_VF], TILE_BYTES);
-            tma_load_3d(vd, &kv_map, 0, j * BN, plane_v, &bar[B_VF]);
-            tma_load_3d(vd + 16384, &kv_map, 64, j * BN, plane_v, &bar[B_VF]);
-            ++issued_v;
+        for (int i = 0; i < 2 * nk && ok; ++i) {
+            const int st = i % RING;
+            if (i >= RING && !mbar_wait(&bar[B_EMPTY0 + st], ((i / RING) - 1) & 1, abortp)) { fail(31); ok = false; break; }
+            uint8_t* dst = smem + OFF_RING + st * TILE_BYTES;
+            const int plane = (i & 1) ? plane_v : plane_k, key0 = (i >> 1) * BN;
+            mbar_arrive_expect_tx(&bar[B_FULL0 + st], TILE_BYTES);
+            tma_load_3d(dst, &kv_map, 0, key0, plane, &bar[B_FULL0 + st]);
+            tma_load_3d(dst + 16384, &kv_map, 64, key0, plane, &bar[B_FULL0 + st]);
+            ++issued;
         }
         if (!ok) {
             // drain the loads this thread issued (bounded, ignoring the abort flag)
-            if (issued_k > 0) {
-                const int jl = issued_k - 1;
-                mbar_wait(&bar[B_KF0 + (jl & 1)], (jl >> 1) & 1, &never_abort, 500000000ull);
-            }
-            if (issued_v > 0) mbar_wait(&bar[B_VF], (issued_v - 1) & 1, &never_abort, 500000000ull);
+            for (int i = std::max(0, issued - RING); i < issued; ++i)
+                mbar_wait(&bar[B_FULL0 + i % RING], (i / RING) & 1, &never_abort, 500000000ull);
         }
     }
 
