@@ -9,12 +9,15 @@
 // contraction can change a result.
 //
 // Layout: one "row" is one head vector of 128 FP32 values. Per token there are hq query
-// rows, hkv key rows and hkv value rows. A block of ROWS threads owns ROWS consecutive
-// rows: it stages them in shared memory with coalesced 16-byte loads (one warp reads one
-// 512-byte row), then each thread runs the sequential FP64 sum of its own row (the order
-// the reference fixes), normalises and rotates in place, and the block writes back with
-// coalesced stores: FP32 query rows to q_out, FP16 K/V rows into the HBM KV store.
-// The kernel is HBM-bound: 28,672 algorithmic bytes per (token, layer) at hq=16, hkv=8.
+// rows, hkv key rows and hkv value rows. A block of ROWS threads owns ROWS consecutive rows.
+// It stages them in shared memory with 16-byte cp.async copies (no registers held, all
+// copies in flight at once). It also stages the RoPE cos/sin rows and the q_norm/k_norm
+// weights of every token it touches, so the per-row arithmetic reads only shared memory.
+// Each thread then runs the reference's sequential FP64 sum of squares for its own row
+// (the squares and their FP64 conversions are independent; only the 128 additions form a
+// chain), normalises and rotates in place. The block writes back with coalesced stores:
+// FP32 query rows to q_out, FP16 K/V rows into the HBM KV store.
+// HBM-bound: 28,672 algorithmic bytes per (token, layer) at hq=16, hkv=8.
 #include "qattn_common.cuh"
 
 namespace qattn {
@@ -22,79 +25,88 @@ namespace {
 
 constexpr int ROWS = 64;          // rows (threads) per block
 constexpr int STRIDE = 132;       // padded row stride in floats: conflict-free float4 access
+constexpr int SLOT = 384;         // staged floats per token: cos[64] sin[64] q_norm[128] k_norm[128]
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __global__ void __launch_bounds__(ROWS) kv_append_kernel(const AppendArgs a) {
-    __shared__ __align__(16) float tile[ROWS * STRIDE];
+    extern __shared__ __align__(16) float smem[];
+    float* tile = smem;                                   // [ROWS][STRIDE]
+    float* slots = smem + ROWS * STRIDE;                  // [tokens of this block][SLOT]
     const int R = a.hq + 2 * a.hkv;                       // rows per token
-    const int per_layer = a.n * R;                        // <= 4096 * 32
-    const int total = per_layer * a.n_layers;             // <= 28 * 4096 * 32 < 2^31
+    const int total = a.n_layers * a.n * R;               // <= 28 * 4096 * 32 < 2^31
     const int g0 = blockIdx.x * ROWS;
+    const int tok0 = g0 / R;                              // first (layer, token) index of the block
+    const int tok1 = min(g0 + ROWS, total) - 1;
+    const int ntok = tok1 / R - tok0 + 1;
 
-    auto src_row = [&](int g, int& kind, int& l, int& b, int& head) -> const float* {
-        l = (unsigned)g / (unsigned)per_layer;
-        const int rem = g - l * per_layer;
-        b = (unsigned)rem / (unsigned)R;
-        const int r = rem - b * R;
-        const size_t tok = (size_t)l * a.n + b;
-        if (r < a.hq) { kind = 0; head = r; return a.q_pre + (tok * a.hq + head) * D; }
-        if (r < a.hq + a.hkv) { kind = 1; head = r - a.hq; return a.k_pre + (tok * a.hkv + head) * D; }
-        kind = 2; head = r - a.hq - a.hkv; return a.v_pre + (tok * a.hkv + head) * D;
-    };
-
-    // ---- stage: warp w reads rows w, w+warps, ... ; lane c reads 16-byte chunk c ----
+    // ---- stage rows: warp w reads rows w, w+2, ...; lane c reads 16-byte chunk c ----
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int WARPS = ROWS / 32;
-    float4 staged[ROWS / WARPS];
-    #pragma unroll
-    for (int i = 0; i < ROWS / WARPS; ++i) {
-        const int g = g0 + warp + i * WARPS;
-        if (g < total) {
-            int kind, l, b, head;
-            const float* src = src_row(g, kind, l, b, head);
-            staged[i] = __ldg(reinterpret_cast<const float4*>(src) + lane);
-        }
+    for (int row = warp; row < ROWS; row += WARPS) {
+        const int g = g0 + row;
+        if (g >= total) break;
+        const int tk = g / R, r = g - tk * R;
+        const int l = tk / a.n, b = tk - l * a.n;
+        const size_t tok = (size_t)l * a.n + b;
+        const float* src = r < a.hq ? a.q_pre + (tok * a.hq + r) * D
+                         : r < a.hq + a.hkv ? a.k_pre + (tok * a.hkv + (r - a.hq)) * D
+                                            : a.v_pre + (tok * a.hkv + (r - a.hq - a.hkv)) * D;
+        cp_async16(&tile[row * STRIDE + lane * 4], src + lane * 4);
     }
-    #pragma unroll
-    for (int i = 0; i < ROWS / WARPS; ++i) {
-        const int row = warp + i * WARPS;
-        if (g0 + row < total) *reinterpret_cast<float4*>(&tile[row * STRIDE + lane * 4]) = staged[i];
+    // ---- stage per-token tables: cos, sin of the position; q_norm, k_norm of the layer ----
+    for (int i = threadIdx.x; i < ntok * (SLOT / 4); i += ROWS) {
+        const int s = i / (SLOT / 4), c = i - s * (SLOT / 4);   // 96 chunks of 16 bytes per slot
+        const int tk = tok0 + s, l = tk / a.n, b = tk - l * a.n;
+        const int pos = a.pos0 + b;
+        const float* src = c < 16 ? a.cosines + (size_t)pos * 64 + c * 4
+                         : c < 32 ? a.sines + (size_t)pos * 64 + (c - 16) * 4
+                                  : a.norms + (size_t)(a.layer0 + l) * 2 * D + (c - 32) * 4;
+        cp_async16(&slots[s * SLOT + c * 4], src);
     }
+    cp_async_wait_all();
     __syncthreads();
 
     // ---- per-row arithmetic: thread t owns row t ----
     const int g = g0 + threadIdx.x;
     if (g < total) {
-        int kind, l, b, head;
-        (void)src_row(g, kind, l, b, head);
+        const int tk = g / R, r = g - tk * R;
+        const int kind = r < a.hq ? 0 : (r < a.hq + a.hkv ? 1 : 2);
         if (kind < 2) {
             float* x = &tile[threadIdx.x * STRIDE];
-            double precise_sum = 0.0;
-            #pragma unroll 4
+            const float* slot = &slots[(tk - tok0) * SLOT];
+            const float* cs = slot;
+            const float* sn = slot + 64;
+            const float* w = slot + 128 + kind * D;
+            // FP32 squares and their FP64 values are independent; only the adds chain
+            double sq[D];
+            #pragma unroll
             for (int j = 0; j < D; j += 4) {
                 const float4 v = *reinterpret_cast<const float4*>(x + j);
-                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.x, v.x));
-                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.y, v.y));
-                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.z, v.z));
-                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.w, v.w));
+                sq[j] = (double)__fmul_rn(v.x, v.x); sq[j + 1] = (double)__fmul_rn(v.y, v.y);
+                sq[j + 2] = (double)__fmul_rn(v.z, v.z); sq[j + 3] = (double)__fmul_rn(v.w, v.w);
             }
+            double precise_sum = 0.0;
+            #pragma unroll
+            for (int j = 0; j < D; ++j) precise_sum = __dadd_rn(precise_sum, sq[j]);
             const float sum = __double2float_rn(precise_sum);
             const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), a.eps)));
-            const float* w = a.norms + ((size_t)(a.layer0 + l) * 2 + kind) * D;
-            const int pos = a.pos0 + b;
-            const float* cs = a.cosines + (size_t)pos * 64;
-            const float* sn = a.sines + (size_t)pos * 64;
-            #pragma unroll 2
+            #pragma unroll 4
             for (int j = 0; j < 64; j += 4) {
                 const float4 xa = *reinterpret_cast<const float4*>(x + j);
                 const float4 xb = *reinterpret_cast<const float4*>(x + j + 64);
-                const float4 wa = __ldg(reinterpret_cast<const float4*>(w + j));
-                const float4 wb = __ldg(reinterpret_cast<const float4*>(w + j + 64));
-                const float4 c = __ldg(reinterpret_cast<const float4*>(cs + j));
-                const float4 s = __ldg(reinterpret_cast<const float4*>(sn + j));
-                float na[4] = {__fmul_rn(__fmul_rn(xa.x, inv), wa.x), __fmul_rn(__fmul_rn(xa.y, inv), wa.y),
-                               __fmul_rn(__fmul_rn(xa.z, inv), wa.z), __fmul_rn(__fmul_rn(xa.w, inv), wa.w)};
-                float nb[4] = {__fmul_rn(__fmul_rn(xb.x, inv), wb.x), __fmul_rn(__fmul_rn(xb.y, inv), wb.y),
-                               __fmul_rn(__fmul_rn(xb.z, inv), wb.z), __fmul_rn(__fmul_rn(xb.w, inv), wb.w)};
+                const float4 wa = *reinterpret_cast<const float4*>(w + j);
+                const float4 wb = *reinterpret_cast<const float4*>(w + j + 64);
+                const float4 c = *reinterpret_cast<const float4*>(cs + j);
+                const float4 s = *reinterpret_cast<const float4*>(sn + j);
+                const float na[4] = {__fmul_rn(__fmul_rn(xa.x, inv), wa.x), __fmul_rn(__fmul_rn(xa.y, inv), wa.y),
+                                     __fmul_rn(__fmul_rn(xa.z, inv), wa.z), __fmul_rn(__fmul_rn(xa.w, inv), wa.w)};
+                const float nb[4] = {__fmul_rn(__fmul_rn(xb.x, inv), wb.x), __fmul_rn(__fmul_rn(xb.y, inv), wb.y),
+                                     __fmul_rn(__fmul_rn(xb.z, inv), wb.z), __fmul_rn(__fmul_rn(xb.w, inv), wb.w)};
                 const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
                 float ra[4], rb[4];
                 #pragma unroll
@@ -113,13 +125,15 @@ __global__ void __launch_bounds__(ROWS) kv_append_kernel(const AppendArgs a) {
     for (int row = warp; row < ROWS; row += WARPS) {
         const int gr = g0 + row;
         if (gr >= total) break;
-        int kind, l, b, head;
-        (void)src_row(gr, kind, l, b, head);
+        const int tk = gr / R, r = gr - tk * R;
+        const int l = tk / a.n, b = tk - l * a.n;
         const float* x = &tile[row * STRIDE];
-        if (kind == 0) {
-            float* dst = a.q_out + (((size_t)l * a.n + b) * a.hq + head) * D;
+        if (r < a.hq) {
+            float* dst = a.q_out + (((size_t)l * a.n + b) * a.hq + r) * D;
             reinterpret_cast<float4*>(dst)[lane] = *reinterpret_cast<const float4*>(x + lane * 4);
         } else if (lane < 16) {
+            const int kind = r < a.hq + a.hkv ? 1 : 2;
+            const int head = kind == 1 ? r - a.hq : r - a.hq - a.hkv;
             const float4 lo = *reinterpret_cast<const float4*>(x + lane * 8);
             const float4 hi = *reinterpret_cast<const float4*>(x + lane * 8 + 4);
             __half2 h0 = __floats2half2_rn(lo.x, lo.y), h1 = __floats2half2_rn(lo.z, lo.w);
@@ -136,9 +150,17 @@ __global__ void __launch_bounds__(ROWS) kv_append_kernel(const AppendArgs a) {
 }  // namespace
 
 void launch_kv_append(const AppendArgs& a, cudaStream_t s) {
-    const int total = a.n_layers * a.n * (a.hq + 2 * a.hkv);
+    const int R = a.hq + 2 * a.hkv;
+    const int total = a.n_layers * a.n * R;
     const unsigned blocks = (unsigned)((total + ROWS - 1) / ROWS);
-    kv_append_kernel<<<blocks, ROWS, 0, s>>>(a);
+    const int max_tokens = (ROWS + R - 2) / R + 1;           // tokens one block of ROWS rows can touch
+    const size_t smem = ((size_t)ROWS * STRIDE + (size_t)max_tokens * SLOT) * sizeof(float);
+    static size_t attr = 0;
+    if (smem > attr) {
+        cudaFuncSetAttribute(kv_append_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
+    }
+    kv_append_kernel<<<blocks, ROWS, smem, s>>>(a);
 }
 
 }  // namespace qattn

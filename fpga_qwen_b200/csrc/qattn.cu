@@ -389,8 +389,7 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
         const int tc_begin = std::min(n, std::max(0, TC_MIN_POSITION - pos0));
         if (tc_begin > 0) {
             r.row_end = tc_begin;
-            r.splits = 1; r.keys_per_split = ((pos0 + tc_begin) + 31) / 32 * 32;
-            launch_attn_rows(r, ctx->stream);
+            launch_attn_head_rows(r, ctx->stream);
         }
         if (launch_attn_prefill_sm100(ctx->kv_map, qd, od, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv,
                                       ctx->cfg.n_layers, tc_begin, ctx->error, ctx->stream))

@@ -48,6 +48,8 @@ struct RowsArgs {
 
 void launch_kv_append(const AppendArgs& a, cudaStream_t s);
 void launch_attn_rows(const RowsArgs& a, cudaStream_t s);
+// FP32 attention of prefill rows [0, row_end) whose positions are all below 128.
+void launch_attn_head_rows(const RowsArgs& a, cudaStream_t s);
 void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cudaStream_t s);
 // Tensor-core prefill for rows [row_begin, n) (all with absolute position >= 128).
 // Returns non-zero (and launches nothing) if the kernel was not built with the expected registers.
