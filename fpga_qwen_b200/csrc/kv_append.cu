@@ -9,10 +9,10 @@
 // contraction can change a result.
 //
 // Layout: one "row" is one head vector of 128 FP32 values. Per token there are hq query
-// rows, hkv key rows and hkv value rows. A block of ROWS threads owns ROWS consecutive rows.
-// It stages them in shared memory with 16-byte cp.async copies (no registers held, all
-// copies in flight at once). It also stages the RoPE cos/sin rows and the q_norm/k_norm
-// weights of every token it touches, so the per-row arithmetic reads only shared memory.
+// rows, hkv key rows and hkv value rows. A block owns TPB consecutive tokens of one layer,
+// one thread per row. It stages the rows in shared memory with 16-byte cp.async copies (no
+// registers held, all copies in flight at once), together with the RoPE cos/sin rows and
+// the layer's q_norm/k_norm weights, so the per-row arithmetic reads only shared memory.
 // Each thread then runs the reference's sequential FP64 sum of squares for its own row
 // (the squares and their FP64 conversions are independent; only the 128 additions form a
 // chain), normalises and rotates in place. The block writes back with coalesced stores:
@@ -23,7 +23,6 @@
 namespace qattn {
 namespace {
 
-constexpr int ROWS = 64;          // rows (threads) per block
 constexpr int STRIDE = 132;       // padded row stride in floats: conflict-free float4 access
 constexpr int SLOT = 384;         // staged floats per token: cos[64] sin[64] q_norm[128] k_norm[128]
 
@@ -33,66 +32,63 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-__global__ void __launch_bounds__(ROWS) kv_append_kernel(const AppendArgs a) {
+// One block = TPB consecutive tokens of one layer; R = 4*HKV rows per token (2*HKV query
+// rows, HKV key rows, HKV value rows); one thread per row. HKV is a template parameter so
+// every row/token index below divides by a constant.
+template <int HKV, int TPB>
+__global__ void __launch_bounds__(TPB * 4 * HKV) kv_append_kernel(const AppendArgs a) {
+    constexpr int HQ = GROUP * HKV, R = HQ + 2 * HKV, ROWS = TPB * R, WARPS = (ROWS + 31) / 32;
     extern __shared__ __align__(16) float smem[];
     float* tile = smem;                                   // [ROWS][STRIDE]
-    float* slots = smem + ROWS * STRIDE;                  // [tokens of this block][SLOT]
-    const int R = a.hq + 2 * a.hkv;                       // rows per token
-    const int total = a.n_layers * a.n * R;               // <= 28 * 4096 * 32 < 2^31
-    const int g0 = blockIdx.x * ROWS;
-    const int tok0 = g0 / R;                              // first (layer, token) index of the block
-    const int tok1 = min(g0 + ROWS, total) - 1;
-    const int ntok = tok1 / R - tok0 + 1;
-
-    // ---- stage rows: warp w reads rows w, w+2, ...; lane c reads 16-byte chunk c ----
+    float* slots = smem + ROWS * STRIDE;                  // [TPB][SLOT]
+    const int l = blockIdx.y;
+    const int b0 = blockIdx.x * TPB;
+    const int ntok = min(TPB, a.n - b0);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int WARPS = ROWS / 32;
-    for (int row = warp; row < ROWS; row += WARPS) {
-        const int g = g0 + row;
-        if (g >= total) break;
-        const int tk = g / R, r = g - tk * R;
-        const int l = tk / a.n, b = tk - l * a.n;
-        const size_t tok = (size_t)l * a.n + b;
-        const float* src = r < a.hq ? a.q_pre + (tok * a.hq + r) * D
-                         : r < a.hq + a.hkv ? a.k_pre + (tok * a.hkv + (r - a.hq)) * D
-                                            : a.v_pre + (tok * a.hkv + (r - a.hq - a.hkv)) * D;
+    const size_t tok_base = (size_t)l * a.n + b0;
+
+    // ---- stage rows: warp w copies rows w, w+WARPS, ...; lane c copies 16-byte chunk c ----
+    for (int row = warp; row < ntok * R; row += WARPS) {
+        const int tb = row / R, r = row - tb * R;
+        const size_t tok = tok_base + tb;
+        const float* src = r < HQ ? a.q_pre + (tok * HQ + r) * D
+                         : r < HQ + HKV ? a.k_pre + (tok * HKV + (r - HQ)) * D
+                                        : a.v_pre + (tok * HKV + (r - HQ - HKV)) * D;
         cp_async16(&tile[row * STRIDE + lane * 4], src + lane * 4);
     }
     // ---- stage per-token tables: cos, sin of the position; q_norm, k_norm of the layer ----
     for (int i = threadIdx.x; i < ntok * (SLOT / 4); i += ROWS) {
-        const int s = i / (SLOT / 4), c = i - s * (SLOT / 4);   // 96 chunks of 16 bytes per slot
-        const int tk = tok0 + s, l = tk / a.n, b = tk - l * a.n;
-        const int pos = a.pos0 + b;
+        const int tb = i / (SLOT / 4), c = i - tb * (SLOT / 4);   // 96 chunks of 16 bytes per token
+        const int pos = a.pos0 + b0 + tb;
         const float* src = c < 16 ? a.cosines + (size_t)pos * 64 + c * 4
                          : c < 32 ? a.sines + (size_t)pos * 64 + (c - 16) * 4
                                   : a.norms + (size_t)(a.layer0 + l) * 2 * D + (c - 32) * 4;
-        cp_async16(&slots[s * SLOT + c * 4], src);
+        cp_async16(&slots[tb * SLOT + c * 4], src);
     }
     cp_async_wait_all();
     __syncthreads();
 
     // ---- per-row arithmetic: thread t owns row t ----
-    const int g = g0 + threadIdx.x;
-    if (g < total) {
-        const int tk = g / R, r = g - tk * R;
-        const int kind = r < a.hq ? 0 : (r < a.hq + a.hkv ? 1 : 2);
-        if (kind < 2) {
-            float* x = &tile[threadIdx.x * STRIDE];
-            const float* slot = &slots[(tk - tok0) * SLOT];
+    {
+        const int row = threadIdx.x;
+        const int tb = row / R, r = row - tb * R;
+        const int kind = r < HQ ? 0 : (r < HQ + HKV ? 1 : 2);
+        if (tb < ntok && kind < 2) {
+            float* x = &tile[row * STRIDE];
+            const float* slot = &slots[tb * SLOT];
             const float* cs = slot;
             const float* sn = slot + 64;
             const float* w = slot + 128 + kind * D;
             // FP32 squares and their FP64 values are independent; only the adds chain
-            double sq[D];
-            #pragma unroll
+            double precise_sum = 0.0;
+            #pragma unroll 8
             for (int j = 0; j < D; j += 4) {
                 const float4 v = *reinterpret_cast<const float4*>(x + j);
-                sq[j] = (double)__fmul_rn(v.x, v.x); sq[j + 1] = (double)__fmul_rn(v.y, v.y);
-                sq[j + 2] = (double)__fmul_rn(v.z, v.z); sq[j + 3] = (double)__fmul_rn(v.w, v.w);
+                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.x, v.x));
+                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.y, v.y));
+                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.z, v.z));
+                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.w, v.w));
             }
-            double precise_sum = 0.0;
-            #pragma unroll
-            for (int j = 0; j < D; ++j) precise_sum = __dadd_rn(precise_sum, sq[j]);
             const float sum = __double2float_rn(precise_sum);
             const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), a.eps)));
             #pragma unroll 4
@@ -122,18 +118,15 @@ __global__ void __launch_bounds__(ROWS) kv_append_kernel(const AppendArgs a) {
     __syncthreads();
 
     // ---- write back: query rows as FP32 (32 chunks), K/V rows as FP16 (16 chunks) ----
-    for (int row = warp; row < ROWS; row += WARPS) {
-        const int gr = g0 + row;
-        if (gr >= total) break;
-        const int tk = gr / R, r = gr - tk * R;
-        const int l = tk / a.n, b = tk - l * a.n;
+    for (int row = warp; row < ntok * R; row += WARPS) {
+        const int tb = row / R, r = row - tb * R;
         const float* x = &tile[row * STRIDE];
-        if (r < a.hq) {
-            float* dst = a.q_out + (((size_t)l * a.n + b) * a.hq + r) * D;
+        if (r < HQ) {
+            float* dst = a.q_out + ((tok_base + tb) * HQ + r) * D;
             reinterpret_cast<float4*>(dst)[lane] = *reinterpret_cast<const float4*>(x + lane * 4);
         } else if (lane < 16) {
-            const int kind = r < a.hq + a.hkv ? 1 : 2;
-            const int head = kind == 1 ? r - a.hq : r - a.hq - a.hkv;
+            const int kind = r < HQ + HKV ? 1 : 2;
+            const int head = kind == 1 ? r - HQ : r - HQ - HKV;
             const float4 lo = *reinterpret_cast<const float4*>(x + lane * 8);
             const float4 hi = *reinterpret_cast<const float4*>(x + lane * 8 + 4);
             __half2 h0 = __floats2half2_rn(lo.x, lo.y), h1 = __floats2half2_rn(lo.z, lo.w);
@@ -141,26 +134,37 @@ __global__ void __launch_bounds__(ROWS) kv_append_kernel(const AppendArgs a) {
             uint4 packed;
             packed.x = *reinterpret_cast<uint32_t*>(&h0); packed.y = *reinterpret_cast<uint32_t*>(&h1);
             packed.z = *reinterpret_cast<uint32_t*>(&h2); packed.w = *reinterpret_cast<uint32_t*>(&h3);
-            __half* dst = a.kv.plane(a.seq, a.layer0 + l, kind - 1, head) + (size_t)(a.pos0 + b) * D;
+            __half* dst = a.kv.plane(a.seq, a.layer0 + l, kind - 1, head) + (size_t)(a.pos0 + b0 + tb) * D;
             reinterpret_cast<uint4*>(dst)[lane] = packed;
         }
     }
 }
 
+template <int HKV, int TPB>
+void launch_append_t(const AppendArgs& a, cudaStream_t s) {
+    constexpr int ROWS = TPB * 4 * HKV;
+    const size_t smem = ((size_t)ROWS * STRIDE + (size_t)TPB * SLOT) * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(kv_append_kernel<HKV, TPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = true;
+    }
+    const dim3 grid((a.n + TPB - 1) / TPB, a.n_layers);
+    kv_append_kernel<HKV, TPB><<<grid, ROWS, smem, s>>>(a);
+}
+
 }  // namespace
 
 void launch_kv_append(const AppendArgs& a, cudaStream_t s) {
-    const int R = a.hq + 2 * a.hkv;
-    const int total = a.n_layers * a.n * R;
-    const unsigned blocks = (unsigned)((total + ROWS - 1) / ROWS);
-    const int max_tokens = (ROWS + R - 2) / R + 1;           // tokens one block of ROWS rows can touch
-    const size_t smem = ((size_t)ROWS * STRIDE + (size_t)max_tokens * SLOT) * sizeof(float);
-    static size_t attr = 0;
-    if (smem > attr) {
-        cudaFuncSetAttribute(kv_append_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
+    // 64 rows per block for decode-sized calls; 128 for long prefills
+    const bool big = (long long)a.n * a.n_layers >= 4096;
+    switch (a.hkv) {
+        case 8: big ? launch_append_t<8, 4>(a, s) : launch_append_t<8, 2>(a, s); break;
+        case 4: big ? launch_append_t<4, 8>(a, s) : launch_append_t<4, 4>(a, s); break;
+        case 2: big ? launch_append_t<2, 16>(a, s) : launch_append_t<2, 8>(a, s); break;
+        case 1: big ? launch_append_t<1, 32>(a, s) : launch_append_t<1, 16>(a, s); break;
+        default: break;   // rejected at context creation
     }
-    kv_append_kernel<<<blocks, ROWS, smem, s>>>(a);
 }
 
 }  // namespace qattn

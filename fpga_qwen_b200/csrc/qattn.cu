@@ -197,6 +197,9 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     if (c.context < 1 || c.context > QA_MAX_CONTEXT) return QA_ERR_INVALID;
     if (c.max_seqs < 1 || c.max_seqs > 4096) return QA_ERR_INVALID;
     if (c.kv_head_begin < 0 || c.kv_head_count < 1 || c.kv_head_begin + c.kv_head_count > c.n_kv_heads) return QA_ERR_INVALID;
+    // kernels are specialised for 1, 2, 4 or 8 KV heads per context (Qwen3-0.6B: 8 over 1/2/4/8 GPUs)
+    if (c.kv_head_count != 1 && c.kv_head_count != 2 && c.kv_head_count != 4 && c.kv_head_count != 8)
+        return QA_ERR_UNSUPPORTED;
     if (!(c.rope_theta > 1.0) || !(c.norm_eps > 0.f)) return QA_ERR_INVALID;
 
     qa_ctx* ctx = new (std::nothrow) qa_ctx();
