@@ -22,8 +22,8 @@
 //   softmax group h: tcgen05.ld S_h row, causal mask, running max (log2 domain, lazy
 //   rescale when the max grows by more than 8), P = 2^(s - m) -> FP16 into shared memory
 //   O_h += P_h V_j          tcgen05.mma, A = P (K-major), B = V (MN-major), accumulate in TMEM
-// The MMA thread issues S_h(j+1) as soon as softmax group h has read S_h(j) into registers
-// (the scores for the next tile are computed while the softmax runs), then O_h += P_h(j) V_j. Key tiles above the diagonal of the
+// The MMA thread issues PV_h(j) then S_h(j+1) for h = 0, 1, so the tensor pipe works on one
+// head while the other head's softmax runs. Key tiles above the diagonal of the
 // query tile are skipped; tiles crossing it are masked per element.
 //
 // Memory: Q_0, Q_1 (FP16, 32 KB each), a 3-stage K/V ring (32 KB stages), P_0, P_1 (32 KB each)
@@ -46,9 +46,9 @@ using namespace sm100;
 constexpr int BM = 128, BN = 128;
 constexpr int THREADS = 384;                              // 12 warps = 3 warpgroups
 // Register split: launched at 168 per thread (384 x 168 = 64,512); the control warpgroup
-// (MMA + TMA warps) drops to 88 and the two softmax warpgroups rise to 208:
-// 2 x 128 x 208 + 128 x 88 = 64,512, the launch total.
-constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 208, REGS_CONTROL = 88;
+// (MMA + TMA warps) drops to 56 and the two softmax warpgroups rise to 224:
+// 2 x 128 x 224 + 128 x 56 = 64,512, the launch total.
+constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 224, REGS_CONTROL = 56;
 static_assert(2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL == THREADS * REGS_LAUNCH, "register split must match launch");
 constexpr uint32_t TILE_BYTES = BN * D * 2;               // 32 KB FP16 K or V tile
 // K and V tiles share one 3-stage ring in load order K0, V0, K1, V1, ...: item i = 2j (K_j)
@@ -283,32 +283,27 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             if (lane == 0) mma_commit(&bar[B_EMPTY0 + i % RING]);
             __syncwarp();
         };
-        // Descriptors: the start-address field is the low 14 bits (address >> 4), so stepping
-        // K by 16 elements inside a 128-byte swizzle atom (+32 B) or to the next atom column
-        // (+16 KB) is an addition to the descriptor.
-        const uint64_t dq0 = sw128_desc(q_addr, 16, 1024);
-        const uint64_t dring = sw128_desc(ring_addr, 16, 1024);
-        const uint64_t dp0 = sw128_desc(p_addr, 16, 1024);
-        const uint64_t dv0 = sw128_desc(ring_addr, 16384, 1024);
-        auto kstep = [](int s) -> uint64_t { return (uint64_t)(((s >> 2) * 16384 + (s & 3) * 32) >> 4); };
         auto issue_qk = [&](int j, int h) {
-            const uint64_t a0 = dq0 + (uint64_t)((h * 32768) >> 4);
-            const uint64_t b0 = dring + (uint64_t)((((2 * j) % RING) * TILE_BYTES) >> 4);
+            const uint32_t kb = ring_addr + ((2 * j) % RING) * TILE_BYTES, qb = q_addr + h * 32768;
             if (lane == 0) {
                 #pragma unroll
-                for (int s = 0; s < 8; ++s) mma_f16_ss(tmem + h * 128, a0 + kstep(s), b0 + kstep(s), idesc_qk, s > 0);
+                for (int s = 0; s < 8; ++s) {
+                    const uint32_t off = (s >> 2) * 16384 + (s & 3) * 32;
+                    mma_f16_ss(tmem + h * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024), idesc_qk, s > 0);
+                }
                 mma_commit(&bar[B_SF0 + h]);
             }
             __syncwarp();
         };
         auto issue_pv = [&](int j, int h) {
-            const uint64_t a0 = dp0 + (uint64_t)((h * 32768) >> 4);
-            const uint64_t b0 = dv0 + (uint64_t)((((2 * j + 1) % RING) * TILE_BYTES) >> 4);
+            const uint32_t pb = p_addr + h * 32768, vb = ring_addr + ((2 * j + 1) % RING) * TILE_BYTES;
             if (lane == 0) {
                 #pragma unroll
-                for (int s = 0; s < 8; ++s)
-                    mma_f16_ss(tmem + 256 + h * 128, a0 + kstep(s), b0 + (uint64_t)((s * 2048) >> 4), idesc_pv,
-                               (j > 0 || s > 0) ? 1u : 0u);
+                for (int s = 0; s < 8; ++s) {
+                    const uint32_t offa = (s >> 2) * 16384 + (s & 3) * 32;
+                    mma_f16_ss(tmem + 256 + h * 128, sw128_desc(pb + offa, 16, 1024),
+                               sw128_desc(vb + s * 2048, 16384, 1024), idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
+                }
                 mma_commit(&bar[B_OD0 + h]);
             }
             __syncwarp();
@@ -323,20 +318,10 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             issue_qk(0, 1);
             release_item(0);
         }
-        // Per tile j: S_h(j+1) = Q_h K_{j+1}^T is issued as soon as the softmax group h has read
-        // S_h(j) into registers, so the next scores are ready when the softmax finishes; then
-        // O_h += P_h(j) V_j once P_h(j) is written.
+        // Per tile j and head h: O_h += P_h(j) V_j as soon as P_h(j) is written, then
+        // S_h(j+1) = Q_h K_{j+1}^T; the tensor pipe works on one head while the other head's
+        // softmax runs.
         for (int j = 0; j < nk && ok; ++j) {
-            if (j + 1 < nk) {
-                if (!wait_item(2 * j + 2)) { fail(24); ok = false; break; }
-                for (int h = 0; h < 2 && ok; ++h) {
-                    if (!mbar_wait(&bar[B_SE0 + h], j & 1, abortp)) { fail(25); ok = false; break; }
-                    tc_fence_after();
-                    issue_qk(j + 1, h);
-                }
-                if (!ok) break;
-                release_item(2 * j + 2);                     // K_{j+1} free when QK_1(j+1) completes
-            }
             if (!wait_item(2 * j + 1)) { fail(22); ok = false; break; }
             if (j == nk - 1 && valid_keys < (j + 1) * BN) {
                 // Rows of the last V tile past the causal end hold stale data: zero them so
@@ -352,13 +337,21 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 fence_proxy_async_smem();
                 __syncwarp();
             }
+            tc_fence_after();
             for (int h = 0; h < 2 && ok; ++h) {
                 if (!mbar_wait(&bar[B_PF0 + h], j & 1, abortp)) { fail(23); ok = false; break; }
                 tc_fence_after();
                 issue_pv(j, h);
+                if (h == 1) release_item(2 * j + 1);         // V_j free when PV_1(j) completes
+                if (j + 1 < nk) {
+                    const int jn = j + 1;
+                    if (h == 0 && !wait_item(2 * jn)) { fail(24); ok = false; break; }
+                    if (!mbar_wait(&bar[B_SE0 + h], j & 1, abortp)) { fail(25); ok = false; break; }
+                    tc_fence_after();
+                    issue_qk(jn, h);
+                    if (h == 1) release_item(2 * jn);        // K_{j+1} free when QK_1(j+1) completes
+                }
             }
-            if (!ok) break;
-            release_item(2 * j + 1);                         // V_j free when PV_1(j) completes
         }
         // drain: every MMA this thread issued has completed before TMEM is released
         if (lane == 0) {
