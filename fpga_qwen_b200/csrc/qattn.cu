@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <string>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -21,6 +22,14 @@
 #include "qattn_common.cuh"
 
 using namespace qattn;
+
+namespace qattn {
+int nccl_unique_id(char out[128]);
+int nccl_comm_init(void** comm, int nranks, int rank, const char id_bytes[128], std::string& err);
+void nccl_comm_destroy(void* comm);
+int nccl_all_gather_f32(void* comm, const float* send, float* recv, size_t count, cudaStream_t s, std::string& err);
+int nccl_send_recv_bytes(void* comm, void* buf, size_t bytes, int peer, bool send, cudaStream_t s, std::string& err);
+}  // namespace qattn
 
 struct qa_ctx {
     qa_config cfg{};
@@ -42,6 +51,12 @@ struct qa_ctx {
     size_t staging_floats = 0;
     CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
     int* error = nullptr;                  // device-side error code of bounded waits (0 = none)
+    void* comm = nullptr;                  // NCCL communicator (multi-GPU)
+    int nranks = 1, rank = 0;
+    float* gather_buf = nullptr;           // all-gather landing buffer
+    size_t gather_floats = 0;
+    void* kv_buf = nullptr;                // packed KV rows for the handoff
+    size_t kv_buf_bytes = 0;
     std::string err;
 };
 
@@ -262,6 +277,8 @@ void qa_destroy(qa_ctx* ctx) {
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
     cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->staging); cudaFree(ctx->error);
+    cudaFree(ctx->gather_buf); cudaFree(ctx->kv_buf);
+    nccl_comm_destroy(ctx->comm);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }
@@ -471,5 +488,110 @@ int qa_synth_fill(float* dst, uint64_t seed, int kind, int layer0, int n_layers,
     launch_synth(dst, seed, kind, layer0, n_layers, pos0, n, head0, heads, mean, stdev, static_cast<cudaStream_t>(stream));
     return cudaGetLastError() == cudaSuccess ? QA_OK : QA_ERR_CUDA;
 }
+
+}  // extern "C"
+
+// ---- multi-GPU ---------------------------------------------------------------------------------
+namespace {
+int grow(qa_ctx* ctx, void** buf, size_t& have, size_t need) {
+    if (need <= have) return QA_OK;
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    cudaFree(*buf);
+    *buf = nullptr; have = 0;
+    QA_CUDA(cudaMalloc(buf, need));
+    have = need;
+    return QA_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qa_comm_unique_id(char id[128]) {
+    if (!id) return QA_ERR_INVALID;
+    return nccl_unique_id(id);
+}
+
+int qa_comm_init(qa_ctx* ctx, int nranks, int rank, const char id[128]) {
+    if (!ctx || !id) return QA_ERR_INVALID;
+    if (nranks < 1 || rank < 0 || rank >= nranks) return fail(ctx, QA_ERR_INVALID, "rank %d of %d", rank, nranks);
+    if (ctx->comm) return fail(ctx, QA_ERR_STATE, "communicator already initialised");
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    std::string err;
+    const int st = nccl_comm_init(&ctx->comm, nranks, rank, id, err);
+    if (st) return fail(ctx, st, "ncclCommInitRank: %s", err.c_str());
+    ctx->nranks = nranks; ctx->rank = rank;
+    return QA_OK;
+}
+
+int qa_comm_destroy(qa_ctx* ctx) {
+    if (!ctx) return QA_ERR_INVALID;
+    if (ctx->comm) {
+        cudaSetDevice(ctx->cfg.device);
+        cudaStreamSynchronize(ctx->stream);
+        nccl_comm_destroy(ctx->comm);
+        ctx->comm = nullptr;
+    }
+    ctx->nranks = 1; ctx->rank = 0;
+    return QA_OK;
+}
+
+int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float* full) {
+    if (!ctx) return QA_ERR_INVALID;
+    if (!ctx->comm) return fail(ctx, QA_ERR_STATE, "no communicator (qa_comm_init)");
+    if (ctx->cfg.io_host) return fail(ctx, QA_ERR_UNSUPPORTED, "qa_gather_heads takes device pointers");
+    if (!local || !full) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
+    if (n_layers < 1 || n < 1 || n_layers > ctx->cfg.n_layers || n > ctx->cfg.context)
+        return fail(ctx, QA_ERR_INVALID, "bad shape %d x %d", n_layers, n);
+    if (ctx->cfg.kv_head_begin != ctx->rank * ctx->hkv || ctx->nranks * ctx->hkv != ctx->cfg.n_kv_heads)
+        return fail(ctx, QA_ERR_STATE, "rank %d holds KV heads [%d,%d): not the head shard the gather expects",
+                    ctx->rank, ctx->cfg.kv_head_begin, ctx->cfg.kv_head_begin + ctx->hkv);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const size_t count = (size_t)n_layers * n * ctx->hq * D;
+    int st;
+    {
+        void* buf = ctx->gather_buf;
+        size_t have = ctx->gather_floats * sizeof(float);
+        if ((st = grow(ctx, &buf, have, count * ctx->nranks * sizeof(float)))) return st;
+        ctx->gather_buf = static_cast<float*>(buf);
+        ctx->gather_floats = have / sizeof(float);
+    }
+    std::string err;
+    if ((st = nccl_all_gather_f32(ctx->comm, local, ctx->gather_buf, count, ctx->stream, err)))
+        return fail(ctx, st, "ncclAllGather: %s", err.c_str());
+    launch_permute_heads(ctx->gather_buf, full, ctx->nranks, n_layers, n, ctx->hq, ctx->stream);
+    return after_launch(ctx, -1, "permute_heads");
+}
+
+static int kv_transfer(qa_ctx* ctx, int seq, int ntok, int peer, bool send) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_seq(ctx, seq))) return st;
+    if (!ctx->comm) return fail(ctx, QA_ERR_STATE, "no communicator (qa_comm_init)");
+    if (peer < 0 || peer >= ctx->nranks || peer == ctx->rank) return fail(ctx, QA_ERR_INVALID, "bad peer %d", peer);
+    if (ntok < 1 || ntok > ctx->cfg.context) return fail(ctx, QA_ERR_INVALID, "bad row count %d", ntok);
+    if (send && ntok > ctx->pos[seq])
+        return fail(ctx, QA_ERR_STATE, "sequence holds %d committed rows, send wants %d", ctx->pos[seq], ntok);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const size_t bytes = (size_t)ctx->cfg.n_layers * 2 * ctx->hkv * ntok * D * sizeof(__half);
+    if ((st = grow(ctx, &ctx->kv_buf, ctx->kv_buf_bytes, bytes))) return st;
+    std::string err;
+    if (send) {
+        launch_pack_kv(ctx->kv, seq, ntok, ctx->kv_buf, false, ctx->stream);
+        if ((st = after_launch(ctx, -1, "pack_kv"))) return st;
+        if ((st = nccl_send_recv_bytes(ctx->comm, ctx->kv_buf, bytes, peer, true, ctx->stream, err)))
+            return fail(ctx, st, "ncclSend: %s", err.c_str());
+    } else {
+        if ((st = nccl_send_recv_bytes(ctx->comm, ctx->kv_buf, bytes, peer, false, ctx->stream, err)))
+            return fail(ctx, st, "ncclRecv: %s", err.c_str());
+        launch_pack_kv(ctx->kv, seq, ntok, ctx->kv_buf, true, ctx->stream);
+        if ((st = after_launch(ctx, seq, "unpack_kv"))) return st;
+        ctx->pos[seq] = ntok;
+        std::fill(ctx->appended[seq].begin(), ctx->appended[seq].end(), ntok);
+    }
+    return QA_OK;
+}
+
+int qa_kv_send(qa_ctx* ctx, int seq, int ntok, int peer) { return kv_transfer(ctx, seq, ntok, peer, true); }
+int qa_kv_recv(qa_ctx* ctx, int seq, int ntok, int peer) { return kv_transfer(ctx, seq, ntok, peer, false); }
 
 }  // extern "C"

@@ -67,6 +67,11 @@ constexpr int TC_MIN_POSITION = 128;
 void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n,
                   int head0, int heads, float mean, float stdev, cudaStream_t s);
 
+// Multi-GPU helpers (qattn_dist.cu).
+void launch_permute_heads(const float* gathered, float* full, int nranks, int n_layers, int n, int hq_local,
+                          cudaStream_t s);
+void launch_pack_kv(const KVLayout& kv, int seq, int ntok, void* buf, bool unpack, cudaStream_t s);
+
 // Partial record size (floats) of one split in RowsArgs::partial.
 constexpr int PARTIAL_FLOATS = 4 + GROUP * D;
 

@@ -1,0 +1,144 @@
+// qattn_dist.cu — multi-GPU entry points: KV-head sharding with an all-gather of the
+// attention outputs, and the prefill -> decode KV-block handoff, over NCCL on NVLink.
+//
+// The reference runs on one host (no distributed backend); BASELINE's multi-GPU plan splits
+// the 8 KV heads over 1/2/4/8 GPUs (each GPU keeps the 2 query heads of its KV heads and
+// the outputs [pos, 16, 128] are gathered over NVLink), shards independent requests over
+// GPUs (no collective), and hands prefilled KV blocks from prefill GPUs to decode GPUs.
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2 — the copy a PyTorch process has
+// already loaded, or the system one), so the library links neither NCCL nor PyTorch.
+// One communicator per context; every call runs on the context's stream.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/qattn.h"
+#include "qattn_common.cuh"
+
+namespace qattn {
+namespace {
+
+struct NcclApi {
+    bool ok = false;
+    std::string err;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) { api.err = std::string("cannot load libnccl.so.2: ") + dlerror(); return; }
+        auto sym = [&](const char* name) { return dlsym(h, name); };
+        api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(sym("ncclGetUniqueId"));
+        api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(sym("ncclCommInitRank"));
+        api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(sym("ncclCommDestroy"));
+        api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
+        api.Send = reinterpret_cast<decltype(api.Send)>(sym("ncclSend"));
+        api.Recv = reinterpret_cast<decltype(api.Recv)>(sym("ncclRecv"));
+        api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(sym("ncclGroupStart"));
+        api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
+        api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
+        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather && api.Send && api.Recv &&
+                 api.GroupStart && api.GroupEnd && api.GetErrorString;
+        if (!api.ok) api.err = "libnccl.so.2 lacks a required symbol";
+    });
+    return api;
+}
+
+// full[l][b][r*hq_local + h][:] = gathered[r][l][b][h][:]
+__global__ void permute_heads_kernel(const float4* gathered, float4* full, int nranks, int n_layers, int n, int hq_local) {
+    const size_t per_rank = (size_t)n_layers * n * hq_local * (D / 4);
+    const size_t total = per_rank * nranks;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % (D / 4));
+        size_t rr = i / (D / 4);
+        const int h = (int)(rr % hq_local); rr /= hq_local;
+        const int b = (int)(rr % n); rr /= n;
+        const int l = (int)(rr % n_layers);
+        const int r = (int)(rr / n_layers);
+        const size_t dst = (((size_t)l * n + b) * (hq_local * nranks) + (size_t)r * hq_local + h) * (D / 4) + c;
+        full[dst] = gathered[i];
+    }
+}
+
+// Slot rows [0, ntok) of every (layer, K|V, head) plane <-> contiguous [planes][ntok][128].
+__global__ void pack_kv_kernel(const KVLayout kv, int seq, int ntok, uint4* buf, int unpack) {
+    const size_t chunks_per_plane = (size_t)ntok * (D * sizeof(__half) / 16);
+    const size_t planes = (size_t)kv.layers * 2 * kv.hkv;
+    const size_t total = chunks_per_plane * planes;
+    uint4* slot = reinterpret_cast<uint4*>(kv.base + kv.slot_elems() * seq);
+    const size_t plane_chunks = kv.plane_elems() * sizeof(__half) / 16;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t plane = i / chunks_per_plane, c = i - plane * chunks_per_plane;
+        if (unpack) slot[plane * plane_chunks + c] = buf[i];
+        else buf[i] = slot[plane * plane_chunks + c];
+    }
+}
+
+}  // namespace
+
+void launch_permute_heads(const float* gathered, float* full, int nranks, int n_layers, int n, int hq_local,
+                          cudaStream_t s) {
+    permute_heads_kernel<<<NUM_SMS_B200 * 4, 256, 0, s>>>(reinterpret_cast<const float4*>(gathered),
+                                                         reinterpret_cast<float4*>(full), nranks, n_layers, n,
+                                                         hq_local);
+}
+void launch_pack_kv(const KVLayout& kv, int seq, int ntok, void* buf, bool unpack, cudaStream_t s) {
+    pack_kv_kernel<<<NUM_SMS_B200 * 4, 512, 0, s>>>(kv, seq, ntok, reinterpret_cast<uint4*>(buf), unpack ? 1 : 0);
+}
+
+const char* nccl_load_error() { return nccl().ok ? nullptr : nccl().err.c_str(); }
+
+int nccl_unique_id(char out[128]) {
+    if (!nccl().ok) return QA_ERR_NCCL;
+    ncclUniqueId id;
+    if (nccl().GetUniqueId(&id) != ncclSuccess) return QA_ERR_NCCL;
+    std::memcpy(out, id.internal, 128);
+    return QA_OK;
+}
+
+int nccl_comm_init(void** comm, int nranks, int rank, const char id_bytes[128], std::string& err) {
+    if (!nccl().ok) { err = nccl().err; return QA_ERR_NCCL; }
+    ncclUniqueId id;
+    std::memcpy(id.internal, id_bytes, 128);
+    ncclComm_t c = nullptr;
+    const ncclResult_t r = nccl().CommInitRank(&c, nranks, id, rank);
+    if (r != ncclSuccess) { err = nccl().GetErrorString(r); return QA_ERR_NCCL; }
+    *comm = c;
+    return QA_OK;
+}
+
+void nccl_comm_destroy(void* comm) {
+    if (comm && nccl().ok) nccl().CommDestroy(static_cast<ncclComm_t>(comm));
+}
+
+int nccl_all_gather_f32(void* comm, const float* send, float* recv, size_t count, cudaStream_t s, std::string& err) {
+    const ncclResult_t r = nccl().AllGather(send, recv, count, ncclFloat32, static_cast<ncclComm_t>(comm), s);
+    if (r != ncclSuccess) { err = nccl().GetErrorString(r); return QA_ERR_NCCL; }
+    return QA_OK;
+}
+
+int nccl_send_recv_bytes(void* comm, void* buf, size_t bytes, int peer, bool send, cudaStream_t s, std::string& err) {
+    const ncclResult_t r = send ? nccl().Send(buf, bytes, ncclUint8, peer, static_cast<ncclComm_t>(comm), s)
+                                : nccl().Recv(buf, bytes, ncclUint8, peer, static_cast<ncclComm_t>(comm), s);
+    if (r != ncclSuccess) { err = nccl().GetErrorString(r); return QA_ERR_NCCL; }
+    return QA_OK;
+}
+
+}  // namespace qattn

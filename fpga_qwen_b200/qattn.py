@@ -70,6 +70,12 @@ _SIGNATURES = {
     "qa_kv_pointer": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.POINTER(ctypes.c_void_p)]),
     "qa_kv_slot_bytes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "qa_comm_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
+    "qa_comm_init": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p]),
+    "qa_comm_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_gather_heads": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "qa_kv_send": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "qa_kv_recv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_attn_decode_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                               ctypes.c_void_p, ctypes.c_void_p]),
@@ -196,10 +202,37 @@ class Context:
         self._check(lib().qa_kv_pointer(self._h, seq, layer, kv, head, ctypes.byref(out)))
         return out.value
 
+    # -- multi-GPU ------------------------------------------------------------------------
+    def comm_init(self, nranks: int, rank: int, unique_id: bytes):
+        if len(unique_id) != 128:
+            raise ValueError("NCCL unique id must be 128 bytes")
+        self._check(lib().qa_comm_init(self._h, nranks, rank, unique_id))
+
+    def comm_destroy(self):
+        self._check(lib().qa_comm_destroy(self._h))
+
+    def gather_heads(self, n_layers: int, n: int, local_ptr: int, full_ptr: int):
+        self._check(lib().qa_gather_heads(self._h, n_layers, n, local_ptr, full_ptr))
+
+    def kv_send(self, seq: int, ntok: int, peer: int):
+        self._check(lib().qa_kv_send(self._h, seq, ntok, peer))
+
+    def kv_recv(self, seq: int, ntok: int, peer: int):
+        self._check(lib().qa_kv_recv(self._h, seq, ntok, peer))
+
     def kv_slot_bytes(self) -> int:
         out = ctypes.c_size_t()
         self._check(lib().qa_kv_slot_bytes(self._h, ctypes.byref(out)))
         return out.value
+
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for Context.comm_init."""
+    buf = ctypes.create_string_buffer(128)
+    st = lib().qa_comm_unique_id(buf)
+    if st != QA_OK:
+        raise QAttnError(st, "qa_comm_unique_id failed (is libnccl.so.2 available?)")
+    return buf.raw
 
 
 NOALLOC_SCRATCH_BYTES = 4 << 20

@@ -141,6 +141,29 @@ int qa_read_kv(qa_ctx* ctx, int seq, int layer, int kv, int head, int pos0, int 
 int qa_kv_pointer(qa_ctx* ctx, int seq, int layer, int kv, int head, void** ptr);
 int qa_kv_slot_bytes(const qa_ctx* ctx, size_t* bytes);
 
+/* ---- Multi-GPU: KV-head sharding and prefill -> decode handoff (NCCL over NVLink) -------
+ * No counterpart in the reference, a single-host CPU engine. One process per GPU; each
+ * context holds KV heads [kv_head_begin, kv_head_begin + kv_head_count) with their GQA
+ * query heads. NCCL is loaded at run time (libnccl.so.2). */
+
+/* Writes a new NCCL unique id (128 bytes) for qa_comm_init; call on one rank, share it. */
+int qa_comm_unique_id(char id[128]);
+/* Joins the communicator of nranks contexts (collective: every rank must call it). */
+int qa_comm_init(qa_ctx* ctx, int nranks, int rank, const char id[128]);
+int qa_comm_destroy(qa_ctx* ctx);
+/* All-gather of head-sharded attention outputs. Rank r must hold KV heads
+ * [r*kv_head_count, (r+1)*kv_head_count) and nranks*kv_head_count == n_kv_heads.
+ * local: [n_layers][n][hq_local][128] device FP32; full: [n_layers][n][n_q_heads][128]
+ * device FP32 with heads in global order (the layout the reference's o_proj reads,
+ * core.cpp:625). Collective; asynchronous on the context's stream. */
+int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float* full);
+/* Prefill -> decode KV handoff. qa_kv_send ships KV rows [0, ntok) of every layer, K|V and
+ * local head of sequence `seq` to rank `peer`; the peer's matching qa_kv_recv stores them in
+ * its slot `seq` and sets that sequence's position to ntok. Both contexts must hold the
+ * same heads. 114,688*ntok bytes at 28 layers and 8 KV heads. Asynchronous on the stream. */
+int qa_kv_send(qa_ctx* ctx, int seq, int ntok, int peer);
+int qa_kv_recv(qa_ctx* ctx, int seq, int ntok, int peer);
+
 /* Size of the fixed device array behind qa_attn_decode_noalloc: 4 MiB per GPU, held by
  * every GPU that loads the library until the process exits. */
 #define QA_NOALLOC_SCRATCH_BYTES (4u << 20)

@@ -1,0 +1,138 @@
+"""Two-GPU tests of the multi-GPU entry points (run on a box with >= 2 GPUs; skipped otherwise).
+
+* KV-head sharding: each rank holds 4 of the 8 KV heads; prefill + decode outputs gathered
+  with qa_gather_heads equal a single-GPU context holding all heads (within the attention
+  tolerance), and each rank's KV bytes equal the matching heads of the single-GPU store.
+* Prefill -> decode handoff: rank 0 prefills, ships the KV rows to rank 1 with
+  qa_kv_send/qa_kv_recv; rank 1's KV bytes equal rank 0's bit for bit and its decode
+  output equals rank 0's.
+NVLS is switched off (NCCL_NVLS_ENABLE=0) and ranks leave only between steps.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tests import helpers as H
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs two GPUs")]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from fpga_qwen_b200 import dist as qd
+    from fpga_qwen_b200 import qattn
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=qd.short_timeout(120))
+    L, n, steps = 4, 300, 3
+    begin, count = qd.head_shard(rank, world)
+    stream = torch.cuda.current_stream().cuda_stream
+    shard = qattn.Context(n_layers=L, context=1024, max_seqs=2, kv_head_begin=begin, kv_head_count=count,
+                          device=rank)
+    shard.set_stream(stream)
+    full = qattn.Context(n_layers=L, context=1024, max_seqs=2, device=rank)
+    full.set_stream(stream)
+    qd.init_comm(shard)
+    qw, kw = H.norms(77, L)
+    H.set_norms(shard, qw, kw)
+    H.set_norms(full, qw, kw)
+    # all-head inputs, and this rank's slice of them
+    q, k, v = H.inputs(77, L, 0, n + steps)
+    hq = 2 * count
+    qs, ks, vs = (q[:, :, 2 * begin:2 * begin + hq].contiguous(), k[:, :, begin:begin + count].contiguous(),
+                  v[:, :, begin:begin + count].contiguous())
+    report = {}
+
+    def run(ctx, qq, kk, vv, gather):
+        outs = []
+        qn = torch.empty_like(qq[:, :n])
+        ctx.append(0, 0, L, 0, n, qq[:, :n].contiguous().data_ptr(), kk[:, :n].contiguous().data_ptr(),
+                   vv[:, :n].contiguous().data_ptr(), qn.data_ptr())
+        out = torch.empty_like(qn)
+        ctx.attn_prefill(0, 0, L, 0, n, qn.data_ptr(), out.data_ptr())
+        ctx.commit(0, n)
+        outs.append(out)
+        for s in range(steps):
+            p = n + s
+            qn1 = torch.empty_like(qq[:, p:p + 1])
+            ctx.append(0, 0, L, p, 1, qq[:, p:p + 1].contiguous().data_ptr(), kk[:, p:p + 1].contiguous().data_ptr(),
+                       vv[:, p:p + 1].contiguous().data_ptr(), qn1.data_ptr())
+            o = torch.empty_like(qn1)
+            ctx.attn_decode(0, 0, L, p, 1, qn1.data_ptr(), o.data_ptr())
+            ctx.commit(0, 1)
+            outs.append(o)
+        local = torch.cat(outs, dim=1).contiguous()
+        if not gather:
+            return local
+        g = torch.empty((L, n + steps, 16, 128), dtype=torch.float32, device="cuda")
+        ctx.gather_heads(L, n + steps, local.data_ptr(), g.data_ptr())
+        return g
+
+    gathered = run(shard, qs, ks, vs, gather=True)
+    reference = run(full, q, k, v, gather=False)
+    torch.cuda.synchronize()
+    mx, rms = H.err_stats(gathered.cpu().numpy(), reference.cpu().numpy())
+    report["gather_max"], report["gather_rms"] = mx, rms
+    kv_equal = True
+    for layer in range(L):
+        for h in range(count):
+            for kvsel in (0, 1):
+                a = H.read_plane(shard, 0, layer, kvsel, h, 0, n + steps)
+                b = H.read_plane(full, 0, layer, kvsel, begin + h, 0, n + steps)
+                kv_equal &= bool(np.array_equal(a, b))
+    report["kv_equal"] = kv_equal
+
+    # prefill -> decode handoff of the full-head sequence: rank 0 sends slot 0, rank 1 receives into slot 1
+    dist.barrier()
+    full_comm = qattn.Context(n_layers=L, context=1024, max_seqs=2, device=rank)
+    full_comm.set_stream(stream)
+    H.set_norms(full_comm, qw, kw)
+    qd.init_comm(full_comm)
+    if rank == 0:
+        qn = torch.empty_like(q[:, :n])
+        full_comm.append(0, 0, L, 0, n, q[:, :n].contiguous().data_ptr(), k[:, :n].contiguous().data_ptr(),
+                         v[:, :n].contiguous().data_ptr(), qn.data_ptr())
+        full_comm.commit(0, n)
+        full_comm.kv_send(0, n, 1)
+    else:
+        full_comm.kv_recv(1, n, 0)
+    full_comm.sync()
+    if rank == 1:
+        same = True
+        for layer in range(L):
+            for h in range(8):
+                for kvsel in (0, 1):
+                    same &= bool(np.array_equal(H.read_plane(full_comm, 1, layer, kvsel, h, 0, n),
+                                                H.read_plane(full, 0, layer, kvsel, h, 0, n)))
+        report["handoff_equal"] = same
+        report["handoff_pos"] = full_comm.position(1)
+    dist.barrier()
+    full_comm.comm_destroy()
+    shard.comm_destroy()
+    np.save(os.path.join(out_dir, f"report{rank}.npy"), report, allow_pickle=True)
+    dist.destroy_process_group()
+
+
+def test_head_sharded_gather_and_kv_handoff(tmp_path):
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    for rank in range(world):
+        rep = np.load(tmp_path / f"report{rank}.npy", allow_pickle=True).item()
+        assert rep["kv_equal"], rep
+        assert rep["gather_max"] < H.MAX_ABS and rep["gather_rms"] < H.RMS, rep
+        if rank == 1:
+            assert rep["handoff_equal"] and rep["handoff_pos"] == 300, rep
