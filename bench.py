@@ -219,6 +219,9 @@ def run_ours(args):
 
     ctx = qattn.Context(n_layers=L, context=4096, max_seqs=1, kv_head_begin=head0, kv_head_count=hkv, device=local)
     ctx.set_stream(stream.cuda_stream)
+    if world > 1:
+        from fpga_qwen_b200 import dist as qd
+        qd.init_comm(ctx)           # NCCL communicator of the library (outputs gathered over NVLink)
 
     def synth(kind, pos0, n, heads, h0, mean=0.0, std=1.0):
         t = torch.empty((L, n, heads, D), dtype=torch.float32, device=dev)
@@ -237,6 +240,9 @@ def run_ours(args):
     dv = [synth(2, PREFILL + s, 1, hkv, head0) for s in range(DECODE)]
     pqn, pout = torch.empty_like(pq), torch.empty_like(pq)
     dqn, dout = torch.empty_like(dq[0]), torch.empty_like(dq[0])
+    if world > 1:    # gathered outputs: all 16 query heads on every rank
+        pfull = torch.empty((L, PREFILL, HQ, D), dtype=torch.float32, device=dev)
+        dfull = torch.empty((L, 1, HQ, D), dtype=torch.float32, device=dev)
 
     launches_per_step = 0
 
@@ -250,6 +256,9 @@ def run_ours(args):
         if evs:
             evs["pa0"].record(stream)
         ctx.attn_prefill(0, 0, L, 0, PREFILL, pqn.data_ptr(), pout.data_ptr())
+        if world > 1:
+            ctx.gather_heads(L, PREFILL, pout.data_ptr(), pfull.data_ptr())
+            launches += 1      # permute (the all-gather itself is NCCL's kernel)
         if evs:
             evs["pa1"].record(stream)
         launches += 3          # append, FP32 rows below position 128, tcgen05 prefill
@@ -260,6 +269,9 @@ def run_ours(args):
             if evs:
                 evs["d0"][s].record(stream)
             ctx.attn_decode(0, 0, L, pos, 1, dqn.data_ptr(), dout.data_ptr())
+            if world > 1:
+                ctx.gather_heads(L, 1, dout.data_ptr(), dfull.data_ptr())
+                launches += 1
             if evs:
                 evs["d1"][s].record(stream)
             ctx.commit(0, 1)
@@ -341,6 +353,7 @@ def run_ours(args):
         }
     if world > 1:
         dist.barrier()
+        ctx.comm_destroy()
         dist.destroy_process_group()
     ctx.close()
     if rank == 0:
