@@ -52,6 +52,8 @@ struct qa_ctx {
     CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
     int* error = nullptr;                  // device-side error code of bounded waits (0 = none)
     void* comm = nullptr;                  // NCCL communicator (multi-GPU)
+    cudaStream_t comm_stream = nullptr;    // NCCL work runs here, ordered after/before the context stream
+    cudaEvent_t comm_ev[2] = {nullptr, nullptr};
     int nranks = 1, rank = 0;
     float* gather_buf = nullptr;           // all-gather landing buffer
     size_t gather_floats = 0;
@@ -279,6 +281,8 @@ void qa_destroy(qa_ctx* ctx) {
     cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->staging); cudaFree(ctx->error);
     cudaFree(ctx->gather_buf); cudaFree(ctx->kv_buf);
     nccl_comm_destroy(ctx->comm);
+    if (ctx->comm_stream) cudaStreamDestroy(ctx->comm_stream);
+    for (cudaEvent_t e : ctx->comm_ev) if (e) cudaEventDestroy(e);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
 }
@@ -504,6 +508,20 @@ int grow(qa_ctx* ctx, void** buf, size_t& have, size_t need) {
 }
 }  // namespace
 
+// NCCL runs on the context's own communication stream: it waits for the work already on the
+// context stream, and the context stream waits for it (any stream handle works, including
+// the legacy default stream).
+int comm_enter(qa_ctx* ctx) {
+    QA_CUDA(cudaEventRecord(ctx->comm_ev[0], ctx->stream));
+    QA_CUDA(cudaStreamWaitEvent(ctx->comm_stream, ctx->comm_ev[0], 0));
+    return QA_OK;
+}
+int comm_leave(qa_ctx* ctx) {
+    QA_CUDA(cudaEventRecord(ctx->comm_ev[1], ctx->comm_stream));
+    QA_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->comm_ev[1], 0));
+    return QA_OK;
+}
+
 extern "C" {
 
 int qa_comm_unique_id(char id[128]) {
@@ -516,6 +534,11 @@ int qa_comm_init(qa_ctx* ctx, int nranks, int rank, const char id[128]) {
     if (nranks < 1 || rank < 0 || rank >= nranks) return fail(ctx, QA_ERR_INVALID, "rank %d of %d", rank, nranks);
     if (ctx->comm) return fail(ctx, QA_ERR_STATE, "communicator already initialised");
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    if (!ctx->comm_stream) {
+        QA_CUDA(cudaStreamCreateWithFlags(&ctx->comm_stream, cudaStreamNonBlocking));
+        QA_CUDA(cudaEventCreateWithFlags(&ctx->comm_ev[0], cudaEventDisableTiming));
+        QA_CUDA(cudaEventCreateWithFlags(&ctx->comm_ev[1], cudaEventDisableTiming));
+    }
     std::string err;
     const int st = nccl_comm_init(&ctx->comm, nranks, rank, id, err);
     if (st) return fail(ctx, st, "ncclCommInitRank: %s", err.c_str());
@@ -556,8 +579,10 @@ int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float*
         ctx->gather_floats = have / sizeof(float);
     }
     std::string err;
-    if ((st = nccl_all_gather_f32(ctx->comm, local, ctx->gather_buf, count, ctx->stream, err)))
+    if ((st = comm_enter(ctx))) return st;
+    if ((st = nccl_all_gather_f32(ctx->comm, local, ctx->gather_buf, count, ctx->comm_stream, err)))
         return fail(ctx, st, "ncclAllGather: %s", err.c_str());
+    if ((st = comm_leave(ctx))) return st;
     launch_permute_heads(ctx->gather_buf, full, ctx->nranks, n_layers, n, ctx->hq, ctx->stream);
     return after_launch(ctx, -1, "permute_heads");
 }
@@ -578,11 +603,15 @@ static int kv_transfer(qa_ctx* ctx, int seq, int ntok, int peer, bool send) {
     if (send) {
         launch_pack_kv(ctx->kv, seq, ntok, ctx->kv_buf, false, ctx->stream);
         if ((st = after_launch(ctx, -1, "pack_kv"))) return st;
-        if ((st = nccl_send_recv_bytes(ctx->comm, ctx->kv_buf, bytes, peer, true, ctx->stream, err)))
+        if ((st = comm_enter(ctx))) return st;
+        if ((st = nccl_send_recv_bytes(ctx->comm, ctx->kv_buf, bytes, peer, true, ctx->comm_stream, err)))
             return fail(ctx, st, "ncclSend: %s", err.c_str());
+        if ((st = comm_leave(ctx))) return st;
     } else {
-        if ((st = nccl_send_recv_bytes(ctx->comm, ctx->kv_buf, bytes, peer, false, ctx->stream, err)))
+        if ((st = comm_enter(ctx))) return st;
+        if ((st = nccl_send_recv_bytes(ctx->comm, ctx->kv_buf, bytes, peer, false, ctx->comm_stream, err)))
             return fail(ctx, st, "ncclRecv: %s", err.c_str());
+        if ((st = comm_leave(ctx))) return st;
         launch_pack_kv(ctx->kv, seq, ntok, ctx->kv_buf, true, ctx->stream);
         if ((st = after_launch(ctx, seq, "unpack_kv"))) return st;
         ctx->pos[seq] = ntok;
