@@ -56,12 +56,15 @@ def _worker(rank, world, port, out_dir):
     qs, ks, vs = (q[:, :, 2 * begin:2 * begin + hq].contiguous(), k[:, :, begin:begin + count].contiguous(),
                   v[:, :, begin:begin + count].contiguous())
     report = {}
+    keep = []
 
     def run(ctx, qq, kk, vv, gather):
         outs = []
         qn = torch.empty_like(qq[:, :n])
-        ctx.append(0, 0, L, 0, n, qq[:, :n].contiguous().data_ptr(), kk[:, :n].contiguous().data_ptr(),
-                   vv[:, :n].contiguous().data_ptr(), qn.data_ptr())
+        # keep the contiguous copies alive until the queued kernels have read them
+        qp, kp, vp = qq[:, :n].contiguous(), kk[:, :n].contiguous(), vv[:, :n].contiguous()
+        keep.extend((qp, kp, vp))
+        ctx.append(0, 0, L, 0, n, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), qn.data_ptr())
         out = torch.empty_like(qn)
         ctx.attn_prefill(0, 0, L, 0, n, qn.data_ptr(), out.data_ptr())
         ctx.commit(0, n)
@@ -69,13 +72,15 @@ def _worker(rank, world, port, out_dir):
         for s in range(steps):
             p = n + s
             qn1 = torch.empty_like(qq[:, p:p + 1])
-            ctx.append(0, 0, L, p, 1, qq[:, p:p + 1].contiguous().data_ptr(), kk[:, p:p + 1].contiguous().data_ptr(),
-                       vv[:, p:p + 1].contiguous().data_ptr(), qn1.data_ptr())
+            q1, k1, v1 = qq[:, p:p + 1].contiguous(), kk[:, p:p + 1].contiguous(), vv[:, p:p + 1].contiguous()
+            keep.extend((q1, k1, v1))
+            ctx.append(0, 0, L, p, 1, q1.data_ptr(), k1.data_ptr(), v1.data_ptr(), qn1.data_ptr())
             o = torch.empty_like(qn1)
             ctx.attn_decode(0, 0, L, p, 1, qn1.data_ptr(), o.data_ptr())
             ctx.commit(0, 1)
             outs.append(o)
         local = torch.cat(outs, dim=1).contiguous()
+        report["local_" + ("shard" if gather else "full")] = local.cpu().numpy()
         if not gather:
             return local
         g = torch.empty((L, n + steps, 16, 128), dtype=torch.float32, device="cuda")
@@ -87,6 +92,8 @@ def _worker(rank, world, port, out_dir):
     torch.cuda.synchronize()
     mx, rms = H.err_stats(gathered.cpu().numpy(), reference.cpu().numpy())
     report["gather_max"], report["gather_rms"] = mx, rms
+    lmx, lrms = H.err_stats(report.pop("local_shard"), report.pop("local_full")[:, :, 2 * begin:2 * begin + hq])
+    report["local_max"], report["local_rms"] = lmx, lrms
     kv_equal = True
     for layer in range(L):
         for h in range(count):
@@ -104,8 +111,9 @@ def _worker(rank, world, port, out_dir):
     qd.init_comm(full_comm)
     if rank == 0:
         qn = torch.empty_like(q[:, :n])
-        full_comm.append(0, 0, L, 0, n, q[:, :n].contiguous().data_ptr(), k[:, :n].contiguous().data_ptr(),
-                         v[:, :n].contiguous().data_ptr(), qn.data_ptr())
+        qp, kp, vp = q[:, :n].contiguous(), k[:, :n].contiguous(), v[:, :n].contiguous()
+        keep.extend((qp, kp, vp))
+        full_comm.append(0, 0, L, 0, n, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), qn.data_ptr())
         full_comm.commit(0, n)
         full_comm.kv_send(0, n, 1)
     else:

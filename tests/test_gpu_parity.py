@@ -353,3 +353,30 @@ def test_decode_partitions(layers, pos0, n):
         mx, rms = H.err_stats(outh[layer], ref)
         assert mx < H.MAX_ABS and rms < H.RMS, (layer, mx, rms)
     ctx.close()
+
+
+@pytest.mark.parametrize("begin,count", [(4, 4), (6, 2), (3, 1)])
+def test_head_sharded_context_single_gpu(begin, count):
+    """A context holding KV heads [begin, begin+count) (one GPU's shard) computes exactly the
+    slice of a full context: KV bytes equal, attention within tolerance of the oracle."""
+    L, n, steps = 3, 260, 2
+    ctx = make_ctx(L, context=512, kv_head_begin=begin, kv_head_count=count)
+    qw, kw = H.norms(61, L)
+    H.set_norms(ctx, qw, kw)
+    q, k, v = H.inputs(61, L, 0, n + steps, hkv=count, head0=begin)
+    qn = gpu_append(ctx, 0, 0, q[:, :n].contiguous(), k[:, :n].contiguous(), v[:, :n].contiguous())
+    out = gpu_attend(ctx, 0, 0, qn)
+    ctx.commit(0, n)
+    qd = gpu_append(ctx, 0, n, q[:, n:].contiguous(), k[:, n:].contiguous(), v[:, n:].contiguous())
+    outd = gpu_attend(ctx, 0, n, qd, decode=True)
+    torch.cuda.synchronize()
+    got = np.concatenate([out.cpu().numpy(), outd.cpu().numpy()], axis=1)
+    qh, kh, vh = q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
+    for layer in range(L):
+        kv, qref = oracle_layer(qh[layer], kh[layer], vh[layer], qw[layer], kw[layer], 0, ctx_len=512)
+        gk = np.stack([H.read_plane(ctx, 0, layer, 0, h, 0, n + steps) for h in range(count)])
+        assert np.array_equal(gk, kv.k[:, :n + steps])
+        ref = O.attention(kv, 0, qref, threads=8)
+        mx, rms = H.err_stats(got[layer], ref)
+        assert mx < H.MAX_ABS and rms < H.RMS, (layer, mx, rms)
+    ctx.close()

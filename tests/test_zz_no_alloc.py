@@ -35,12 +35,13 @@ def test_noalloc_decode_matches_the_regular_entry_point_on_two_calls():
     H.set_norms(ctx, qw, kw)
     q, k, v = H.inputs(31, L, 0, P + 2)
     qn_p = torch.empty_like(q[:, :P])
-    ctx.append(0, 0, L, 0, P, q[:, :P].contiguous().data_ptr(), k[:, :P].contiguous().data_ptr(),
-               v[:, :P].contiguous().data_ptr(), qn_p.data_ptr())
+    # the contiguous copies stay referenced until the queued kernels have read them
+    qp, kp, vp = q[:, :P].contiguous(), k[:, :P].contiguous(), v[:, :P].contiguous()
+    ctx.append(0, 0, L, 0, P, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), qn_p.data_ptr())
     ctx.commit(0, P)
     qn = torch.empty_like(q[:, P:])
-    ctx.append(0, 0, L, P, 2, q[:, P:].contiguous().data_ptr(), k[:, P:].contiguous().data_ptr(),
-               v[:, P:].contiguous().data_ptr(), qn.data_ptr())
+    qt, kt, vt = q[:, P:].contiguous(), k[:, P:].contiguous(), v[:, P:].contiguous()
+    ctx.append(0, 0, L, P, 2, qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), qn.data_ptr())
     kv_slot = ctx.kv_pointer(0, 0, 0, 0)
 
     # call 1: two rows (B2 verify shape), all 28 layers
