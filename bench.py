@@ -50,6 +50,15 @@ def decode_bytes(ctx_len: int, layers: int = L, hkv: int = HKV) -> float:
     return layers * hkv * ctx_len * D * 2 * 2 + 2 * layers * hq * D * 4
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture per kernel
+# (commands: `bench.py --profile-case decode|prefill` under ncu --set full):
+#   decode: 461.3 MB for a 28-layer launch at context 3971 whose algorithmic bytes are 455.9 MB,
+#           applied as a ratio to the average launch of the timed region;
+#   prefill: 279.3 MB for a 4-layer, 3968-row launch; traffic grows with the layer count.
+DECODE_TRAFFIC_RATIO = 461.27e6 / 455.90e6
+PREFILL_TRAFFIC_PER_LAYER = 279.28e6 / 4
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -341,11 +350,14 @@ def run_ours(args):
             "prefill": {"metric": "prefill-attn TFLOP/s", "value": round(pre_flops / (prefill_phase * 1e-3) / 1e12, 3),
                         "unit": "TFLOP/s", "phase_ms": round(prefill_phase, 3),
                         "roofline": {"bound": "tensor", "achieved": round(pre_kernel_tfs, 3), "peak": tf_peak,
-                                     "unit": "TFLOP/s", "frac": round(pre_kernel_tfs / tf_peak, 4), "traffic": None,
+                                     "unit": "TFLOP/s", "frac": round(pre_kernel_tfs / tf_peak, 4),
+                                     "traffic": round(PREFILL_TRAFFIC_PER_LAYER * L / world),
                                      "peak_kind": f"{peak_kind} bf16 burst (fp16 same dense rate)",
                                      "kernel_ms": round(pattn, 3)}},
             "roofline": {"bound": "hbm", "achieved": round(dec_kernel_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(dec_kernel_gbs / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "frac": round(dec_kernel_gbs / hbm_peak, 4),
+                         "traffic": round(DECODE_TRAFFIC_RATIO * dec_bytes / DECODE / world),
+                         "algorithmic_bytes": round(dec_bytes / DECODE / world), "peak_kind": peak_kind,
                          "kernel": "attn_decode (28 layers per launch)",
                          "kernel_us": round(dattn / DECODE * 1e3, 2)},
             "clocks": clocks,
