@@ -41,7 +41,10 @@ constexpr int MAX_RANGE = 6144;               // keys per CTA range (scores: 2 x
 
 struct DecodeArgs {
     const float* q; float* out;               // [n_layers][n][hq][128]
-    KVLayout kv; int seq, layer0, n_layers, pos0, n, hq, hkv;
+    KVLayout kv; int layer0, n_layers, n, hq, hkv;
+    int seq[MAX_BATCH];                       // sequence slot of row b
+    int pos[MAX_BATCH];                       // absolute position of row b (context pos+1)
+    int start[MAX_BATCH + 1];                 // prefix sums of row context lengths
     long long total_keys;                     // T = Σ over units of their context length
     int ctas;                                 // C
     int max_keys;                             // max keys of one CTA range (scores capacity)
@@ -53,24 +56,20 @@ struct DecodeArgs {
 
 struct Unit { int l, b, kh, len; long long off; };
 
-// Unit containing global key g; units ordered (layer, row, KV head).
+// Unit containing global key g; units ordered (layer, row, KV head), unit (l, b, kh) holding
+// keys [0, pos[b]] of row b's sequence.
 __device__ __forceinline__ Unit unit_of(const DecodeArgs& a, long long g) {
-    const long long per_row0 = a.pos0 + 1;
-    const long long layer_keys = (long long)a.hkv * ((long long)a.n * a.pos0 + (long long)a.n * (a.n + 1) / 2);
+    const long long layer_keys = (long long)a.hkv * a.start[a.n];
     Unit u;
     u.l = (int)(g / layer_keys);
-    long long r = g - (long long)u.l * layer_keys;
-    long long off = (long long)u.l * layer_keys;
+    const long long r = g - (long long)u.l * layer_keys;
     int b = 0;
-    for (; b < a.n - 1; ++b) {
-        const long long row_keys = (long long)a.hkv * (per_row0 + b);
-        if (r < row_keys) break;
-        r -= row_keys; off += row_keys;
-    }
+    while (b < a.n - 1 && (long long)a.hkv * a.start[b + 1] <= r) ++b;
     u.b = b;
-    u.len = a.pos0 + b + 1;
-    u.kh = (int)(r / u.len);
-    u.off = off + (long long)u.kh * u.len;
+    u.len = a.pos[b] + 1;
+    const long long rr = r - (long long)a.hkv * a.start[b];
+    u.kh = (int)(rr / u.len);
+    u.off = (long long)u.l * layer_keys + (long long)a.hkv * a.start[b] + (long long)u.kh * u.len;
     return u;
 }
 
@@ -128,8 +127,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         const int cnt = k1 - k0;
         g = u.off + k1;
         const int layer = a.layer0 + u.l;
-        const __half* Kp = a.kv.plane(a.seq, layer, 0, u.kh) + (size_t)k0 * D;
-        const __half* Vp = a.kv.plane(a.seq, layer, 1, u.kh) + (size_t)k0 * D;
+        const __half* Kp = a.kv.plane(a.seq[u.b], layer, 0, u.kh) + (size_t)k0 * D;
+        const __half* Vp = a.kv.plane(a.seq[u.b], layer, 1, u.kh) + (size_t)k0 * D;
         const int nch = (cnt + CH - 1) / CH;
         const int total_chunks = 2 * nch;                // K chunks then V chunks
         const size_t qrow = ((size_t)u.l * a.n + u.b) * a.hq + (size_t)u.kh * GROUP;
@@ -356,26 +355,36 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
 
 }  // namespace
 
-int decode_max_records(int max_len) { return max_len / 64 + 3; }
+size_t DecodePlan::partial_floats() const { return (size_t)units * max_records * PARTIAL_FLOATS; }
 
-// Even split: C ranges of T/C keys, C a multiple of the SM count with 2 CTAs per SM, each
-// range between 64 and MAX_RANGE keys (one wave at 4K context: 889K keys over 296 CTAs).
-void launch_attn_decode_sm100(const KVLayout& kv, const float* q, float* out, int seq, int layer0, int n_layers,
-                              int pos0, int n, int hq, int hkv, float* partial, int max_records, int* counters,
-                              int* error, cudaStream_t s) {
-    DecodeArgs a{};
-    a.q = q; a.out = out; a.kv = kv; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0;
-    a.n = n; a.hq = hq; a.hkv = hkv;
-    a.total_keys = (long long)n_layers * hkv * ((long long)n * pos0 + (long long)n * (n + 1) / 2);
+// Even split: C ranges of T/C keys, C = 2 CTAs per SM (one wave) unless that makes a range
+// longer than MAX_RANGE keys or shorter than 64.
+DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos) {
+    DecodePlan p{};
+    long long row_keys = 0;
+    int max_len = 0;
+    for (int b = 0; b < n; ++b) { row_keys += pos[b] + 1; max_len = std::max(max_len, pos[b] + 1); }
+    p.total_keys = (long long)n_layers * hkv * row_keys;
     long long ctas = (long long)NUM_SMS_B200 * 2;
-    ctas = std::min<long long>(ctas, std::max<long long>(1, a.total_keys / 64));
-    ctas = std::max<long long>(ctas, (a.total_keys + MAX_RANGE - 1) / MAX_RANGE);
-    // records per unit are bounded: a unit of len keys meets at most len/(T/C)+2 CTAs
-    const long long max_len = pos0 + n;
-    while (ctas > 1 && (max_len * ctas) / a.total_keys + 2 > max_records) --ctas;
-    a.ctas = (int)ctas;
-    a.max_keys = (int)((a.total_keys + ctas - 1) / ctas) + 1;
-    a.max_records = max_records;
+    ctas = std::min<long long>(ctas, std::max<long long>(1, p.total_keys / 64));
+    ctas = std::max<long long>(ctas, (p.total_keys + MAX_RANGE - 1) / MAX_RANGE);
+    p.ctas = (int)ctas;
+    p.max_keys = (int)((p.total_keys + ctas - 1) / ctas) + 1;
+    // a unit of len keys meets at most floor(len*C/T) + 2 of the C ranges
+    p.max_records = (int)(((long long)max_len * ctas) / p.total_keys) + 2;
+    p.units = n_layers * n * hkv;
+    return p;
+}
+
+void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const float* q, float* out, int layer0,
+                              int n_layers, int n, const int* seq, const int* pos, int hq, int hkv, float* partial,
+                              int* counters, int* error, cudaStream_t s) {
+    DecodeArgs a{};
+    a.q = q; a.out = out; a.kv = kv; a.layer0 = layer0; a.n_layers = n_layers; a.n = n; a.hq = hq; a.hkv = hkv;
+    a.start[0] = 0;
+    for (int b = 0; b < n; ++b) { a.seq[b] = seq[b]; a.pos[b] = pos[b]; a.start[b + 1] = a.start[b] + pos[b] + 1; }
+    a.total_keys = plan.total_keys; a.ctas = plan.ctas; a.max_keys = plan.max_keys;
+    a.max_records = plan.max_records;
     a.partial = partial; a.counters = counters; a.error = error;
     const size_t smem = (size_t)NST * CHUNK_BYTES + (size_t)GROUP * a.max_keys * sizeof(float);
     static bool attr = false;

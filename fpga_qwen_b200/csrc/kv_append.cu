@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(TPB * 4 * HKV) kv_append_kernel(const AppendAr
     // ---- stage per-token tables: cos, sin of the position; q_norm, k_norm of the layer ----
     for (int i = threadIdx.x; i < ntok * (SLOT / 4); i += ROWS) {
         const int tb = i / (SLOT / 4), c = i - tb * (SLOT / 4);   // 96 chunks of 16 bytes per token
-        const int pos = a.pos0 + b0 + tb;
+        const int pos = a.rows.pos_of(b0 + tb, a.pos0);
         const float* src = c < 16 ? a.cosines + (size_t)pos * 64 + c * 4
                          : c < 32 ? a.sines + (size_t)pos * 64 + (c - 16) * 4
                                   : a.norms + (size_t)(a.layer0 + l) * 2 * D + (c - 32) * 4;
@@ -134,7 +134,8 @@ __global__ void __launch_bounds__(TPB * 4 * HKV) kv_append_kernel(const AppendAr
             uint4 packed;
             packed.x = *reinterpret_cast<uint32_t*>(&h0); packed.y = *reinterpret_cast<uint32_t*>(&h1);
             packed.z = *reinterpret_cast<uint32_t*>(&h2); packed.w = *reinterpret_cast<uint32_t*>(&h3);
-            __half* dst = a.kv.plane(a.seq, a.layer0 + l, kind - 1, head) + (size_t)(a.pos0 + b0 + tb) * D;
+            __half* dst = a.kv.plane(a.rows.seq_of(b0 + tb, a.seq), a.layer0 + l, kind - 1, head) +
+                          (size_t)a.rows.pos_of(b0 + tb, a.pos0) * D;
             reinterpret_cast<uint4*>(dst)[lane] = packed;
         }
     }

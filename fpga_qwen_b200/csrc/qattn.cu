@@ -45,8 +45,7 @@ struct qa_ctx {
     float* partial = nullptr;              // split-context records
     size_t partial_floats = 0;
     int* counters = nullptr;
-    int max_units = 0;
-    int max_records = 0;                   // split records per unit
+    int max_units = 0;                     // counters held
     float* staging = nullptr;              // device staging for io_host calls
     size_t staging_floats = 0;
     CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
@@ -252,11 +251,15 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     if (cudaMalloc(&ctx->norms, ones.size() * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMemcpy(ctx->norms, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) return cleanup(QA_ERR_CUDA);
 
-    // Split-context records: every (layer, decode row, head) unit, as many records as the
-    // decode partition can give one unit at this context length.
-    ctx->max_units = c.n_layers * QA_MAX_DECODE_ROWS * ctx->hkv;
-    ctx->max_records = decode_max_records(c.context);
-    ctx->partial_floats = (size_t)ctx->max_units * ctx->max_records * PARTIAL_FLOATS;
+    // Split-context records sized for a full-length decode step of every layer (the decode
+    // plan of a larger batched call grows them on demand).
+    {
+        int pos[QA_MAX_DECODE_ROWS];
+        for (int b = 0; b < QA_MAX_DECODE_ROWS; ++b) pos[b] = c.context - QA_MAX_DECODE_ROWS + b;
+        const DecodePlan plan = plan_attn_decode(c.n_layers, ctx->hkv, QA_MAX_DECODE_ROWS, pos);
+        ctx->max_units = std::max(plan.units, c.n_layers * QA_MAX_DECODE_ROWS * ctx->hkv);
+        ctx->partial_floats = std::max(plan.partial_floats(), (size_t)ctx->max_units * 32 * PARTIAL_FLOATS);
+    }
     if (cudaMalloc(&ctx->partial, ctx->partial_floats * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMalloc(&ctx->counters, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMemset(ctx->counters, 0, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
@@ -385,6 +388,26 @@ int qa_append(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n,
     return QA_OK;
 }
 
+// Grows the split-decode scratch for a plan (records and zeroed counters).
+static int ensure_decode_scratch(qa_ctx* ctx, const DecodePlan& plan) {
+    if (plan.partial_floats() > ctx->partial_floats) {
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+        cudaFree(ctx->partial);
+        ctx->partial = nullptr; ctx->partial_floats = 0;
+        QA_CUDA(cudaMalloc(&ctx->partial, plan.partial_floats() * sizeof(float)));
+        ctx->partial_floats = plan.partial_floats();
+    }
+    if (plan.units > ctx->max_units) {
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+        cudaFree(ctx->counters);
+        ctx->counters = nullptr; ctx->max_units = 0;
+        QA_CUDA(cudaMalloc(&ctx->counters, (size_t)plan.units * sizeof(int)));
+        QA_CUDA(cudaMemsetAsync(ctx->counters, 0, (size_t)plan.units * sizeof(int), ctx->stream));
+        ctx->max_units = plan.units;
+    }
+    return QA_OK;
+}
+
 static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q, float* out,
                   bool decode) {
     int st;
@@ -406,8 +429,12 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
     r.pos0 = pos0; r.n = n; r.hq = ctx->hq; r.hkv = ctx->hkv; r.row_begin = 0; r.row_end = n;
     r.partial = ctx->partial; r.counters = ctx->counters;
     if (decode) {
-        launch_attn_decode_sm100(ctx->kv, qd, od, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv, ctx->partial,
-                                 ctx->max_records, ctx->counters, ctx->error, ctx->stream);
+        int seqs[QA_MAX_DECODE_ROWS], pos[QA_MAX_DECODE_ROWS];
+        for (int b = 0; b < n; ++b) { seqs[b] = seq; pos[b] = pos0 + b; }
+        const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
+        if ((st = ensure_decode_scratch(ctx, plan))) return st;
+        launch_attn_decode_sm100(plan, ctx->kv, qd, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
+                                 ctx->partial, ctx->counters, ctx->error, ctx->stream);
     } else {
         // rows below position TC_MIN_POSITION: FP32 CUDA cores; the rest: tcgen05 tensor cores
         const int tc_begin = std::min(n, std::max(0, TC_MIN_POSITION - pos0));
@@ -436,6 +463,96 @@ int qa_attn_prefill(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int
 int qa_attn_decode(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q, float* out) {
     if (!ctx) return QA_ERR_INVALID;
     return attend(ctx, seq, layer, n_layers, pos0, n, q, out, true);
+}
+
+// ---- batched decode: one row for each of n sequences, each at its own position ----------------
+static int check_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_layers) {
+    int st;
+    if (!seqs) return fail(ctx, QA_ERR_INVALID, "null sequence list");
+    if (n < 1 || n > QA_MAX_BATCH) return fail(ctx, QA_ERR_INVALID, "batch of %d sequences (1..%d)", n, QA_MAX_BATCH);
+    if ((st = check_layers(ctx, layer, n_layers))) return st;
+    for (int b = 0; b < n; ++b) {
+        if ((st = check_seq(ctx, seqs[b]))) return st;
+        for (int c = 0; c < b; ++c)
+            if (seqs[c] == seqs[b]) return fail(ctx, QA_ERR_INVALID, "sequence %d listed twice", seqs[b]);
+        if (ctx->pos[seqs[b]] >= ctx->cfg.context)
+            return fail(ctx, QA_ERR_CAPACITY, "sequence %d is at context capacity", seqs[b]);
+    }
+    return QA_OK;
+}
+
+int qa_append_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_layers, const float* q_pre,
+                    const float* k_pre, const float* v, float* q_out) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_batch(ctx, seqs, n, layer, n_layers))) return st;
+    if (!q_pre || !k_pre || !v || !q_out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const size_t qn = (size_t)n_layers * n * ctx->hq * D, kn = (size_t)n_layers * n * ctx->hkv * D;
+    AppendArgs a{};
+    a.q_pre = q_pre; a.k_pre = k_pre; a.v_pre = v; a.q_out = q_out;
+    if (ctx->cfg.io_host) {
+        if ((st = ensure_staging(ctx, 2 * qn + 2 * kn))) return st;
+        float* s = ctx->staging;
+        QA_CUDA(cudaMemcpyAsync(s, q_pre, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        QA_CUDA(cudaMemcpyAsync(s + qn, k_pre, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        QA_CUDA(cudaMemcpyAsync(s + qn + kn, v, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        a.q_pre = s; a.k_pre = s + qn; a.v_pre = s + qn + kn; a.q_out = s + qn + 2 * kn;
+    }
+    a.kv = ctx->kv; a.seq = seqs[0]; a.layer0 = layer; a.n_layers = n_layers; a.pos0 = 0; a.n = n;
+    a.hq = ctx->hq; a.hkv = ctx->hkv; a.norms = ctx->norms; a.cosines = ctx->cosines; a.sines = ctx->sines;
+    a.eps = ctx->cfg.norm_eps;
+    a.rows.batched = 1;
+    for (int b = 0; b < n; ++b) { a.rows.seq[b] = seqs[b]; a.rows.pos[b] = ctx->pos[seqs[b]]; }
+    launch_kv_append(a, ctx->stream);
+    if ((st = after_launch(ctx, -1, "kv_append_batch"))) return st;
+    for (int b = 0; b < n; ++b)
+        for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seqs[b]][l] = ctx->pos[seqs[b]] + 1;
+    if (ctx->cfg.io_host) {
+        QA_CUDA(cudaMemcpyAsync(q_out, a.q_out, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
+    return QA_OK;
+}
+
+int qa_attn_decode_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_layers, const float* q, float* out) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_batch(ctx, seqs, n, layer, n_layers))) return st;
+    if (!q || !out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
+    int pos[QA_MAX_BATCH];
+    for (int b = 0; b < n; ++b) {
+        pos[b] = ctx->pos[seqs[b]];
+        if ((st = check_appended(ctx, seqs[b], layer, n_layers, pos[b] + 1))) return st;
+    }
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const size_t qn = (size_t)n_layers * n * ctx->hq * D;
+    const float* qd = q; float* od = out;
+    if (ctx->cfg.io_host) {
+        if ((st = ensure_staging(ctx, 2 * qn))) return st;
+        QA_CUDA(cudaMemcpyAsync(ctx->staging, q, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        qd = ctx->staging; od = ctx->staging + qn;
+    }
+    const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
+    if ((st = ensure_decode_scratch(ctx, plan))) return st;
+    launch_attn_decode_sm100(plan, ctx->kv, qd, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv, ctx->partial,
+                             ctx->counters, ctx->error, ctx->stream);
+    if ((st = after_launch(ctx, -1, "attn_decode_batch"))) return st;
+    if (ctx->cfg.io_host) {
+        QA_CUDA(cudaMemcpyAsync(out, od, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
+    return QA_OK;
+}
+
+int qa_commit_batch(qa_ctx* ctx, const int* seqs, int n) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_batch(ctx, seqs, n, 0, ctx->cfg.n_layers))) return st;
+    for (int b = 0; b < n; ++b)
+        if ((st = check_appended(ctx, seqs[b], 0, ctx->cfg.n_layers, ctx->pos[seqs[b]] + 1))) return st;
+    for (int b = 0; b < n; ++b) ctx->pos[seqs[b]] += 1;
+    return QA_OK;
 }
 
 int qa_copy_prefix(qa_ctx* ctx, int src, int dst, int ntok) {

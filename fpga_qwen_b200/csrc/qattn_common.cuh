@@ -26,9 +26,21 @@ struct KVLayout {
     }
 };
 
+// Sequence slot and absolute position of each row of a call. Plain calls use (seq, pos0 + b);
+// batched decode calls give every row its own sequence (one row per sequence).
+constexpr int MAX_BATCH = 64;
+struct RowMap {
+    int batched;
+    int seq[MAX_BATCH];
+    int pos[MAX_BATCH];
+    __host__ __device__ int seq_of(int b, int seq0) const { return batched ? seq[b] : seq0; }
+    __host__ __device__ int pos_of(int b, int pos0) const { return batched ? pos[b] : pos0 + b; }
+};
+
 struct AppendArgs {
     const float* q_pre; const float* k_pre; const float* v_pre; float* q_out;
     KVLayout kv; int seq; int layer0; int n_layers; int pos0; int n; int hq; int hkv;
+    RowMap rows;
     const float* norms;      // [layers][2][128]: q_norm, k_norm
     const float* cosines;    // [ctx][64]
     const float* sines;      // [ctx][64]
@@ -56,12 +68,17 @@ void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cuda
 int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
                                int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
                                cudaStream_t s);
-// TMA-streamed split-context decode (rows pos0..pos0+n-1, n <= QA_MAX_DECODE_ROWS).
-void launch_attn_decode_sm100(const KVLayout& kv, const float* q, float* out, int seq, int layer0, int n_layers,
-                              int pos0, int n, int hq, int hkv, float* partial, int max_records, int* counters,
-                              int* error, cudaStream_t s);
-// Partial records reserved per (layer, row, head) unit for contexts up to max_len keys.
-int decode_max_records(int max_len);
+// TMA-streamed split-context decode. Row b of the call is sequence rows.seq[b] at position
+// rows.pos[b] (context rows.pos[b] + 1), b < n <= MAX_BATCH.
+struct DecodePlan {
+    int ctas, max_keys, max_records, units;
+    long long total_keys;
+    size_t partial_floats() const;
+};
+DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos);
+void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const float* q, float* out, int layer0,
+                              int n_layers, int n, const int* seq, const int* pos, int hq, int hkv, float* partial,
+                              int* counters, int* error, cudaStream_t s);
 // Rows at absolute positions below this go to the FP32 CUDA-core kernel.
 constexpr int TC_MIN_POSITION = 128;
 void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n,

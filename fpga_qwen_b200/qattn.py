@@ -22,6 +22,7 @@ QA_ERR_INVALID, QA_ERR_CAPACITY, QA_ERR_STATE, QA_ERR_CUDA = 1, 2, 3, 4
 QA_ERR_NCCL, QA_ERR_TIMEOUT, QA_ERR_OOM, QA_ERR_UNSUPPORTED = 5, 6, 7, 8
 PREFIX_CHUNK = 512
 MAX_DECODE_ROWS = 4
+MAX_BATCH = 64
 HEAD_DIM = 128
 
 
@@ -70,6 +71,11 @@ _SIGNATURES = {
     "qa_kv_pointer": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.POINTER(ctypes.c_void_p)]),
     "qa_kv_slot_bytes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "qa_append_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    "qa_attn_decode_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "qa_commit_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]),
     "qa_comm_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
     "qa_comm_init": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_char_p]),
     "qa_comm_destroy": (ctypes.c_int, [ctypes.c_void_p]),
@@ -201,6 +207,24 @@ class Context:
         out = ctypes.c_void_p()
         self._check(lib().qa_kv_pointer(self._h, seq, layer, kv, head, ctypes.byref(out)))
         return out.value
+
+    # -- batched decode over sequences ------------------------------------------------------
+    @staticmethod
+    def _seq_array(seqs):
+        arr = (ctypes.c_int * len(seqs))(*[int(x) for x in seqs])
+        return arr, len(seqs)
+
+    def append_batch(self, seqs, layer, n_layers, q_pre, k_pre, v, q_out):
+        arr, n = self._seq_array(seqs)
+        self._check(lib().qa_append_batch(self._h, arr, n, layer, n_layers, q_pre, k_pre, v, q_out))
+
+    def attn_decode_batch(self, seqs, layer, n_layers, q, out):
+        arr, n = self._seq_array(seqs)
+        self._check(lib().qa_attn_decode_batch(self._h, arr, n, layer, n_layers, q, out))
+
+    def commit_batch(self, seqs):
+        arr, n = self._seq_array(seqs)
+        self._check(lib().qa_commit_batch(self._h, arr, n))
 
     # -- multi-GPU ------------------------------------------------------------------------
     def comm_init(self, nranks: int, rank: int, unique_id: bytes):

@@ -124,6 +124,20 @@ int qa_attn_prefill(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int
 int qa_attn_decode(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n,
                    const float* q, float* out);
 
+/* Batched decode over independent sequences (multi-request serving). Row b of the tensors
+ * belongs to sequence seqs[b] (host array of 1..QA_MAX_BATCH distinct slots) at that
+ * sequence's committed position; q_pre/k_pre/v/q_out/out use the layouts above with
+ * n = n_seqs. Each row is exactly one reference decode step (core.cpp:395-406 then
+ * :606-624) for its sequence; the batch runs as one append launch and one attention launch
+ * whose key work is split evenly over the GPU. qa_commit_batch advances every listed
+ * sequence by one position (core.cpp:643 for batch 1). */
+#define QA_MAX_BATCH 64
+int qa_append_batch(qa_ctx* ctx, const int* seqs, int n_seqs, int layer, int n_layers,
+                    const float* q_pre, const float* k_pre, const float* v, float* q_out);
+int qa_attn_decode_batch(qa_ctx* ctx, const int* seqs, int n_seqs, int layer, int n_layers,
+                         const float* q, float* out);
+int qa_commit_batch(qa_ctx* ctx, const int* seqs, int n_seqs);
+
 /* Canonical prefix reuse by device block copy: copies KV rows [0, ntok) of every layer,
  * K/V and head from slot src_seq to slot dst_seq and sets dst's position to ntok.
  * ntok must be a positive multiple of QA_PREFIX_CHUNK and <= src's position.

@@ -380,3 +380,57 @@ def test_head_sharded_context_single_gpu(begin, count):
         mx, rms = H.err_stats(got[layer], ref)
         assert mx < H.MAX_ABS and rms < H.RMS, (layer, mx, rms)
     ctx.close()
+
+
+def test_batched_decode_over_sequences():
+    """Config-5 style serving: six sequences of different lengths decode together through
+    qa_append_batch / qa_attn_decode_batch / qa_commit_batch; every sequence's KV rows are
+    bit-exact and its outputs within tolerance of the oracle, and a batch equals the same
+    rows decoded one sequence at a time."""
+    L, steps = 2, 3
+    lengths = [5, 130, 700, 1500, 3000, 4000]
+    S = len(lengths)
+    ctx = make_ctx(L, max_seqs=S, context=4096)
+    qw, kw = H.norms(90, L)
+    H.set_norms(ctx, qw, kw)
+    data = []
+    for s_, n in enumerate(lengths):
+        q, k, v = H.inputs(900 + s_, L, 0, n + steps)
+        data.append((q, k, v))
+        gpu_append(ctx, s_, 0, q[:, :n].contiguous(), k[:, :n].contiguous(), v[:, :n].contiguous())
+        ctx.commit(s_, n)
+    seqs = list(range(S))
+    outs = []
+    for st in range(steps):
+        qb = torch.stack([data[s_][0][:, lengths[s_] + st] for s_ in seqs], dim=1).contiguous()   # [L][S][16][128]
+        kb = torch.stack([data[s_][1][:, lengths[s_] + st] for s_ in seqs], dim=1).contiguous()
+        vb = torch.stack([data[s_][2][:, lengths[s_] + st] for s_ in seqs], dim=1).contiguous()
+        qn = torch.empty_like(qb)
+        ctx.append_batch(seqs, 0, L, qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), qn.data_ptr())
+        out = torch.empty_like(qn)
+        ctx.attn_decode_batch(seqs, 0, L, qn.data_ptr(), out.data_ptr())
+        # the same rows one sequence at a time (positions not yet committed)
+        single = torch.empty_like(qn)
+        for s_ in seqs:
+            q1 = qn[:, s_:s_ + 1].contiguous()
+            o1 = torch.empty_like(q1)
+            ctx.attn_decode(s_, 0, L, lengths[s_] + st, 1, q1.data_ptr(), o1.data_ptr())
+            single[:, s_:s_ + 1] = o1
+        ctx.commit_batch(seqs)
+        torch.cuda.synchronize()
+        mx, _ = H.err_stats(out.cpu().numpy(), single.cpu().numpy())
+        assert mx < 1e-5, mx
+        outs.append(out.cpu().numpy())
+    for s_ in seqs:
+        n = lengths[s_]
+        assert ctx.position(s_) == n + steps
+        q, k, v = (t.cpu().numpy() for t in data[s_])
+        for layer in range(L):
+            kv, qref = oracle_layer(q[layer], k[layer], v[layer], qw[layer], kw[layer], 0, ctx_len=4096)
+            gk = np.stack([H.read_plane(ctx, s_, layer, 0, h, 0, n + steps) for h in range(8)])
+            assert np.array_equal(gk, kv.k[:, :n + steps])
+            for st in range(steps):
+                ref = O.attention(kv, n + st, qref[n + st:n + st + 1], threads=8)[0]
+                mx, rms = H.err_stats(outs[st][layer, s_], ref)
+                assert mx < H.MAX_ABS and rms < H.RMS, (s_, layer, st, mx, rms)
+    ctx.close()
