@@ -426,6 +426,164 @@ def e2e_decode(args, seed):
             "note": "128 decode steps per step, host wall clock around C-ABI calls with host buffers"}
 
 
+def run_config5(args):
+    """64 independent requests, prompt lengths ~ U[85, 3968] (seeded), each a
+    batched prefill followed by 128 decode steps. Requests are sharded over the ranks by
+    estimated cost (no collective on the data path); each rank decodes all of its sequences
+    in one batched launch per step. With --disagg, ranks [0, W/2) prefill and hand every
+    request's FP16 KV blocks (114,688 B per position) over NVLink to rank r + W/2, which decodes.
+    value = whole-job decode-attention GB/s (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from fpga_qwen_b200 import dist as qd
+    from fpga_qwen_b200 import qattn
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    disagg = bool(args.disagg) and world >= 2
+    if disagg and world % 2:
+        raise SystemExit("--disagg needs an even number of GPUs")
+    lengths = qd.config5_lengths()
+    groups = world // 2 if disagg else world
+    parts = qd.balance_requests(lengths, groups, DECODE)
+    group = rank % groups
+    mine = parts[group]
+    is_prefill = (not disagg) or rank < groups
+    is_decode = (not disagg) or rank >= groups
+    stream = torch.cuda.current_stream(dev)
+    ctx = qattn.Context(n_layers=L, context=4096, max_seqs=len(mine), device=local)
+    ctx.set_stream(stream.cuda_stream)
+    if disagg:
+        qd.init_comm(ctx)
+    seed = 5
+
+    def synth(kind, pos0, n, heads):
+        t = torch.empty((L, n, heads, D), dtype=torch.float32, device=dev)
+        qattn.synth_fill(t.data_ptr(), seed, kind, 0, L, pos0, n, 0, heads, 0.0, 1.0, stream.cuda_stream)
+        return t
+
+    qn_w = synth(3, 0, 1, 1).reshape(L, D)
+    kn_w = synth(4, 0, 1, 1).reshape(L, D)
+    qn_w.mul_(0.05).add_(1.0); kn_w.mul_(0.05).add_(1.0)
+    qwh, kwh = qn_w.cpu().numpy(), kn_w.cpu().numpy()
+    for layer in range(L):
+        a, b = np.ascontiguousarray(qwh[layer]), np.ascontiguousarray(kwh[layer])
+        ctx.set_norms(layer, a.ctypes.data, b.ctypes.data)
+    R = len(mine)
+    slots = list(range(R))
+    # decode inputs for every step: [L][R][heads][128] per step (request i's row at its position)
+    if is_decode:
+        dq, dk, dv = [], [], []
+        for st in range(DECODE):
+            dq.append(torch.stack([synth(0, lengths[i] + st, 1, HQ)[:, 0] for i in mine], dim=1).contiguous())
+            dk.append(torch.stack([synth(1, lengths[i] + st, 1, HKV)[:, 0] for i in mine], dim=1).contiguous())
+            dv.append(torch.stack([synth(2, lengths[i] + st, 1, HKV)[:, 0] for i in mine], dim=1).contiguous())
+        dqn, dout = torch.empty_like(dq[0]), torch.empty_like(dq[0])
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def one_pass(timed):
+        for s_ in slots:
+            ctx.reset(s_)
+        pre_ms, pre_flops, hand_ms, hand_bytes = 0.0, 0.0, 0.0, 0.0
+        if is_prefill:
+            for s_, i in enumerate(mine):
+                n = lengths[i]
+                q, k, v = synth(0, 0, n, HQ), synth(1, 0, n, HKV), synth(2, 0, n, HKV)
+                qn, out = torch.empty_like(q), torch.empty_like(q)
+                e0, e1 = ev(), ev()
+                e0.record(stream)
+                ctx.append(s_, 0, L, 0, n, q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr())
+                ctx.attn_prefill(s_, 0, L, 0, n, qn.data_ptr(), out.data_ptr())
+                e1.record(stream)
+                ctx.commit(s_, n)
+                torch.cuda.synchronize()
+                pre_ms += e0.elapsed_time(e1)
+                pre_flops += prefill_flops(0, n)
+                del q, k, v, qn, out
+        if disagg:
+            h0, h1 = ev(), ev()
+            h0.record(stream)
+            for s_, i in enumerate(mine):
+                if is_prefill:
+                    ctx.kv_send(s_, lengths[i], rank + groups)
+                else:
+                    ctx.kv_recv(s_, lengths[i], rank - groups)
+                hand_bytes += KV_BYTES_PER_POS * lengths[i]
+            h1.record(stream)
+            torch.cuda.synchronize()
+            hand_ms = h0.elapsed_time(h1)
+        dec_ms, dec_bytes = 0.0, 0.0
+        if is_decode:
+            d0, d1 = ev(), ev()
+            torch.cuda.synchronize()
+            d0.record(stream)
+            for st in range(DECODE):
+                ctx.append_batch(slots, 0, L, dq[st].data_ptr(), dk[st].data_ptr(), dv[st].data_ptr(), dqn.data_ptr())
+                ctx.attn_decode_batch(slots, 0, L, dqn.data_ptr(), dout.data_ptr())
+                ctx.commit_batch(slots)
+            d1.record(stream)
+            torch.cuda.synchronize()
+            dec_ms = d0.elapsed_time(d1)
+            dec_bytes = sum(decode_bytes(lengths[i] + st + 1) for i in mine for st in range(DECODE))
+        return pre_ms, pre_flops, hand_ms, hand_bytes, dec_ms, dec_bytes
+
+    for _ in range(args.warmup):
+        one_pass(False)
+    res = [one_pass(True) for _ in range(args.steps)]
+    pre_ms = statistics.median(r[0] for r in res)
+    hand_ms = statistics.median(r[2] for r in res)
+    dec_ms = statistics.median(r[4] for r in res)
+    t = torch.tensor([pre_ms, hand_ms, dec_ms], device=dev, dtype=torch.float64)
+    tot = torch.tensor([res[0][1], res[0][3], res[0][5]], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    pre_ms, hand_ms, dec_ms = t.tolist()
+    pre_flops, hand_bytes, dec_bytes = tot.tolist()
+    if disagg:
+        hand_bytes /= 2                               # counted on both ends of each transfer
+    if rank == 0:
+        hbm_peak, tf_peak, peak_kind = load_peaks()
+        value = dec_bytes / (dec_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(pre_ms + hand_ms + dec_ms, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (fp16 KV)", "data": "synthetic",
+            "config": {"workload": "config5: 64 requests, prompt lengths U[85,3968] (seed 5), 128 batched decode "
+                                   "steps each, 28 layers, 16 q / 8 kv heads",
+                       "requests": len(lengths), "decode_steps": DECODE,
+                       "parallelism": (f"disaggregated: {groups} prefill + {groups} decode GPUs" if disagg
+                                       else f"request shard x{world}"),
+                       "l2": "inputs larger than L2 (14.7 GB KV read per batched decode step at N=1)"},
+            "decode_phase_ms": round(dec_ms, 3),
+            "prefill": {"metric": "prefill-attn TFLOP/s", "value": round(pre_flops / (pre_ms * 1e-3) / 1e12, 3),
+                        "unit": "TFLOP/s", "phase_ms": round(pre_ms, 3)},
+            "roofline": {"bound": "hbm", "achieved": round(value / (groups if not disagg else groups), 1),
+                         "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(value / groups / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
+                         "note": "per decode GPU, decode phase including batched appends"},
+        }
+        if disagg:
+            line["handoff"] = {"bytes": round(hand_bytes), "ms": round(hand_ms, 3),
+                               "gbs": round(hand_bytes / (hand_ms * 1e-3) / 1e9, 2),
+                               "note": "per prefill->decode pair, max over ranks; NCCL send/recv over NVLink"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        if disagg:
+            ctx.comm_destroy()
+        dist.destroy_process_group()
+    ctx.close()
+    return 0
+
+
 def run_profile_case(args):
     """Small, self-contained launches of one kernel for ncu captures (few GB on the device,
     few launches before the captured ones):
@@ -486,6 +644,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", choices=["config4", "config5"], default="config4",
+                    help="config4: head-sharded 3968+128 (the metric's config); config5: 64 requests, request-sharded")
+    ap.add_argument("--disagg", action="store_true", help="config5: prefill on the first half of the GPUs, decode on the rest")
     ap.add_argument("--profile-case", choices=["decode", "prefill", "append"], default=None,
                     help="run a small single-kernel case for ncu instead of the benchmark")
     args = ap.parse_args()
@@ -493,6 +654,8 @@ def main():
         return run_profile_case(args)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "config5":
+        return run_config5(args)
     return run_ours(args)
 
 
