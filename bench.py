@@ -462,9 +462,10 @@ def run_config5(args):
         qd.init_comm(ctx)
     seed = 5
 
-    def synth(kind, pos0, n, heads):
+    def synth(kind, pos0, n, heads, req=0):      # request i draws from its own seed
         t = torch.empty((L, n, heads, D), dtype=torch.float32, device=dev)
-        qattn.synth_fill(t.data_ptr(), seed, kind, 0, L, pos0, n, 0, heads, 0.0, 1.0, stream.cuda_stream)
+        qattn.synth_fill(t.data_ptr(), seed + 1000 * req, kind, 0, L, pos0, n, 0, heads, 0.0, 1.0,
+                         stream.cuda_stream)
         return t
 
     qn_w = synth(3, 0, 1, 1).reshape(L, D)
@@ -478,11 +479,11 @@ def run_config5(args):
     slots = list(range(R))
     # decode inputs for every step: [L][R][heads][128] per step (request i's row at its position)
     if is_decode:
-        dq, dk, dv = [], [], []
-        for st in range(DECODE):
-            dq.append(torch.stack([synth(0, lengths[i] + st, 1, HQ)[:, 0] for i in mine], dim=1).contiguous())
-            dk.append(torch.stack([synth(1, lengths[i] + st, 1, HKV)[:, 0] for i in mine], dim=1).contiguous())
-            dv.append(torch.stack([synth(2, lengths[i] + st, 1, HKV)[:, 0] for i in mine], dim=1).contiguous())
+        # per request [L][DECODE][h][128] at its own positions, regrouped per step to [L][R][h][128]
+        def per_step(kind, heads):
+            allr = torch.stack([synth(kind, lengths[i], DECODE, heads, i) for i in mine], dim=2)  # [L][DECODE][R][h][D]
+            return [allr[:, st].contiguous() for st in range(DECODE)]
+        dq, dk, dv = per_step(0, HQ), per_step(1, HKV), per_step(2, HKV)
         dqn, dout = torch.empty_like(dq[0]), torch.empty_like(dq[0])
 
     def ev():
@@ -495,7 +496,7 @@ def run_config5(args):
         if is_prefill:
             for s_, i in enumerate(mine):
                 n = lengths[i]
-                q, k, v = synth(0, 0, n, HQ), synth(1, 0, n, HKV), synth(2, 0, n, HKV)
+                q, k, v = synth(0, 0, n, HQ, i), synth(1, 0, n, HKV, i), synth(2, 0, n, HKV, i)
                 qn, out = torch.empty_like(q), torch.empty_like(q)
                 e0, e1 = ev(), ev()
                 e0.record(stream)
@@ -565,7 +566,7 @@ def run_config5(args):
             "decode_phase_ms": round(dec_ms, 3),
             "prefill": {"metric": "prefill-attn TFLOP/s", "value": round(pre_flops / (pre_ms * 1e-3) / 1e12, 3),
                         "unit": "TFLOP/s", "phase_ms": round(pre_ms, 3)},
-            "roofline": {"bound": "hbm", "achieved": round(value / (groups if not disagg else groups), 1),
+            "roofline": {"bound": "hbm", "achieved": round(value / groups, 1),
                          "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(value / groups / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
                          "note": "per decode GPU, decode phase including batched appends"},
