@@ -13,7 +13,10 @@
 //     same number of keys and there is no tail wave.
 //   * TMA bulk copies. K and V rows of one (layer, head) are contiguous, so a 64-key chunk
 //     is one 16 KB cp.async.bulk. One thread keeps a 4-stage ring of chunks in flight
-//     (64 KB per CTA, 2 CTAs per SM), so the CTA never waits on individual loads.
+//     (64 KB per CTA, 2 CTAs per SM), so the CTA never waits on individual loads. The ring
+//     runs over the CTA's whole chunk stream (segment after segment, K chunks then V chunks
+//     of each), so it stays full across segment boundaries: a batched step over many short
+//     sequences crosses dozens of them per CTA.
 //   * Both GQA query heads share every K and V chunk (the reference pairs heads the same
 //     way, core.cpp:150-159). Scores of the range stay in shared memory; the max and sum
 //     over the range are exact; V is streamed after K.
@@ -37,7 +40,7 @@ constexpr int HALF_WARPS = THREADS / 16;
 constexpr int CH = 64;                        // keys per chunk
 constexpr int NST = 4;                        // ring stages
 constexpr uint32_t CHUNK_BYTES = CH * D * 2;  // 16 KB
-constexpr int MAX_RANGE = 6144;               // keys per CTA range (scores: 2 x 24 KB of shared memory)
+constexpr int MAX_UNIT_KEYS = 4096;           // longest unit (QA_MAX_CONTEXT): a segment's scores fit in 2 x 16 KB
 
 struct DecodeArgs {
     const float* q; float* out;               // [n_layers][n][hq][128]
@@ -71,6 +74,21 @@ __device__ __forceinline__ Unit unit_of(const DecodeArgs& a, long long g) {
     u.kh = (int)(rr / u.len);
     u.off = (long long)u.l * layer_keys + (long long)a.hkv * a.start[b] + (long long)u.kh * u.len;
     return u;
+}
+
+// The part of one unit that a CTA range covers: keys [k0, k0+cnt) of unit u.
+struct Seg { Unit u; int k0, cnt, nch; const __half* K; const __half* V; };
+
+__device__ __forceinline__ Seg segment_at(const DecodeArgs& a, long long g, long long g_end) {
+    Seg s;
+    s.u = unit_of(a, g);
+    s.k0 = (int)(g - s.u.off);
+    s.cnt = (int)min((long long)s.u.len, g_end - s.u.off) - s.k0;
+    s.nch = (s.cnt + CH - 1) / CH;
+    const int layer = a.layer0 + s.u.l;
+    s.K = a.kv.plane(a.seq[s.u.b], layer, 0, s.u.kh) + (size_t)s.k0 * D;
+    s.V = a.kv.plane(a.seq[s.u.b], layer, 1, s.u.kh) + (size_t)s.k0 * D;
+    return s;
 }
 
 // CTA whose range holds global key g: the largest c with floor(c*T/C) <= g.
@@ -120,32 +138,40 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
     uint32_t issued = 0, consumed = 0;                 // ring sequence numbers (thread 0 issues)
     const float qscale = 1.4426950408889634f * 0.08838834764831845f;   // log2(e)/sqrt(128)
 
+    // Producer cursor (thread 0): the CTA's chunk stream is, segment after segment, the K
+    // chunks then the V chunks of each; the consumers walk the same stream in the same order.
+    long long pg = g_begin;
+    Seg ps{};
+    int pj = 0;
+    bool pseg = false;
+    auto produce = [&]() {
+        if (!pseg || pj == 2 * ps.nch) {
+            if (pg >= g_end) return;
+            ps = segment_at(a, pg, g_end);
+            pg = ps.u.off + ps.k0 + ps.cnt;
+            pj = 0;
+            pseg = true;
+        }
+        const int stage = issued % NST;
+        const bool is_v = pj >= ps.nch;
+        const int jj = is_v ? pj - ps.nch : pj;
+        const int keys = min(CH, ps.cnt - jj * CH);
+        const __half* src = (is_v ? ps.V : ps.K) + (size_t)jj * CH * D;
+        mbar_arrive_expect_tx(&full[stage], keys * D * 2);
+        bulk_copy(ring + stage * CHUNK_BYTES, src, keys * D * 2, &full[stage]);
+        ++issued;
+        ++pj;
+    };
+    if (tid == 0)
+        for (int i = 0; i < NST; ++i) produce();
+
     for (long long g = g_begin; g < g_end;) {
-        const Unit u = unit_of(a, g);
-        const int k0 = (int)(g - u.off);
-        const int k1 = (int)min((long long)u.len, g_end - u.off);
-        const int cnt = k1 - k0;
-        g = u.off + k1;
-        const int layer = a.layer0 + u.l;
-        const __half* Kp = a.kv.plane(a.seq[u.b], layer, 0, u.kh) + (size_t)k0 * D;
-        const __half* Vp = a.kv.plane(a.seq[u.b], layer, 1, u.kh) + (size_t)k0 * D;
-        const int nch = (cnt + CH - 1) / CH;
+        const Seg sg = segment_at(a, g, g_end);
+        const Unit u = sg.u;
+        const int cnt = sg.cnt, nch = sg.nch;
+        g = u.off + sg.k0 + cnt;
         const int total_chunks = 2 * nch;                // K chunks then V chunks
         const size_t qrow = ((size_t)u.l * a.n + u.b) * a.hq + (size_t)u.kh * GROUP;
-
-        auto issue = [&](int j) {                        // chunk j of this segment -> ring
-            const int stage = issued % NST;
-            const bool is_v = j >= nch;
-            const int jj = is_v ? j - nch : j;
-            const int keys = min(CH, cnt - jj * CH);
-            const __half* src = (is_v ? Vp : Kp) + (size_t)jj * CH * D;
-            mbar_arrive_expect_tx(&full[stage], keys * D * 2);
-            bulk_copy(ring + stage * CHUNK_BYTES, src, keys * D * 2, &full[stage]);
-            ++issued;
-        };
-        if (tid == 0)
-            for (int j = 0; j < min(NST, total_chunks); ++j) issue(j);
-        int next_issue = min(NST, total_chunks);
 
         float q[GROUP][8];
         #pragma unroll
@@ -234,8 +260,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             ++consumed;
             __syncthreads();                       // everyone is done with this stage
             if (abort_flag) { aborted = true; break; }
-            if (tid == 0 && next_issue < total_chunks) { issue(next_issue); }
-            ++next_issue;
+            if (tid == 0) produce();               // refill the freed stage (next segment's chunks too)
             if (j == nch - 1) {
                 // ---- end of the K pass: exact max and exp-sum over this range ----
                 float m0 = mloc0, m1 = mloc1;
@@ -358,7 +383,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
 size_t DecodePlan::partial_floats() const { return (size_t)units * max_records * PARTIAL_FLOATS; }
 
 // Even split: C ranges of T/C keys, C = 2 CTAs per SM (one wave) unless that makes a range
-// longer than MAX_RANGE keys or shorter than 64.
+// shorter than 64 keys. A segment (one range within one unit) holds at most
+// min(ceil(T/C), longest unit) keys, which sizes the score buffer.
 DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos) {
     DecodePlan p{};
     long long row_keys = 0;
@@ -367,9 +393,8 @@ DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos) {
     p.total_keys = (long long)n_layers * hkv * row_keys;
     long long ctas = (long long)NUM_SMS_B200 * 2;
     ctas = std::min<long long>(ctas, std::max<long long>(1, p.total_keys / 64));
-    ctas = std::max<long long>(ctas, (p.total_keys + MAX_RANGE - 1) / MAX_RANGE);
     p.ctas = (int)ctas;
-    p.max_keys = (int)((p.total_keys + ctas - 1) / ctas) + 1;
+    p.max_keys = (int)std::min<long long>((p.total_keys + ctas - 1) / ctas + 1, max_len);
     // a unit of len keys meets at most floor(len*C/T) + 2 of the C ranges
     p.max_records = (int)(((long long)max_len * ctas) / p.total_keys) + 2;
     p.units = n_layers * n * hkv;
@@ -390,7 +415,7 @@ void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const 
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(attn_decode_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             NST * CHUNK_BYTES + GROUP * (MAX_RANGE + 2) * (int)sizeof(float));
+                             NST * CHUNK_BYTES + GROUP * MAX_UNIT_KEYS * (int)sizeof(float));
         attr = true;
     }
     attn_decode_sm100_kernel<<<a.ctas, THREADS, smem, s>>>(a);

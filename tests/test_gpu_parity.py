@@ -434,3 +434,56 @@ def test_batched_decode_over_sequences():
                 mx, rms = H.err_stats(outs[st][layer, s_], ref)
                 assert mx < H.MAX_ABS and rms < H.RMS, (s_, layer, st, mx, rms)
     ctx.close()
+
+
+def test_batched_decode_64_requests_many_segments_per_cta():
+    """BASELINE config-5 shape: 64 sequences with the seeded U[85, 3968] prompt lengths decode
+    in one batched launch. Each CTA's key range then spans several (layer, sequence, head)
+    units, so the copy ring runs across segment boundaries and the score buffer is sized by
+    the longest unit rather than by the range. The batch equals the same rows decoded one
+    sequence at a time, and sampled sequences (shortest, longest, two others) agree with the
+    oracle on the GPU's own KV planes."""
+    from fpga_qwen_b200 import dist as qd
+    L, steps = 2, 2
+    lengths = qd.config5_lengths()
+    S = len(lengths)
+    ctx = make_ctx(L, max_seqs=S, context=4096)
+    qw, kw = H.norms(91, L)
+    H.set_norms(ctx, qw, kw)
+    for s_, n in enumerate(lengths):
+        q, k, v = H.inputs(2000 + s_, L, 0, n)
+        gpu_append(ctx, s_, 0, q, k, v)
+        ctx.commit(s_, n)
+        torch.cuda.synchronize()
+        del q, k, v
+    seqs = list(range(S))
+    check = sorted({int(np.argmin(lengths)), int(np.argmax(lengths)), 7, 40})
+    for st in range(steps):
+        rows = [H.inputs(2000 + s_, L, lengths[s_] + st, 1) for s_ in seqs]
+        qb, kb, vb = (torch.cat([r[i] for r in rows], dim=1).contiguous() for i in range(3))   # [L][S][h][128]
+        qn = torch.empty_like(qb)
+        ctx.append_batch(seqs, 0, L, qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), qn.data_ptr())
+        out = torch.full_like(qn, float("nan"))
+        ctx.attn_decode_batch(seqs, 0, L, qn.data_ptr(), out.data_ptr())
+        single = torch.empty_like(qn)
+        for s_ in seqs:
+            q1 = qn[:, s_:s_ + 1].contiguous()
+            o1 = torch.empty_like(q1)
+            ctx.attn_decode(s_, 0, L, lengths[s_] + st, 1, q1.data_ptr(), o1.data_ptr())
+            single[:, s_:s_ + 1] = o1
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        assert np.isfinite(got).all()
+        mx, _ = H.err_stats(got, single.cpu().numpy())
+        assert mx < 1e-5, mx
+        qh = qn.cpu().numpy()
+        for s_ in check:
+            pos = lengths[s_] + st
+            for layer in range(L):
+                kv = H.read_layer_kv(ctx, s_, layer, pos + 1, 4096)
+                ref = O.attention(kv, pos, qh[layer, s_:s_ + 1], threads=8)[0]
+                mx, rms = H.err_stats(got[layer, s_], ref)
+                assert mx < H.MAX_ABS and rms < H.RMS, (s_, layer, st, mx, rms)
+        ctx.commit_batch(seqs)
+    assert all(ctx.position(s_) == lengths[s_] + steps for s_ in seqs)
+    ctx.close()
