@@ -76,19 +76,14 @@ __device__ __forceinline__ Unit unit_of(const DecodeArgs& a, long long g) {
     return u;
 }
 
-// The part of one unit that a CTA range covers: keys [k0, k0+cnt) of unit u.
-struct Seg { Unit u; int k0, cnt, nch; const __half* K; const __half* V; };
-
-__device__ __forceinline__ Seg segment_at(const DecodeArgs& a, long long g, long long g_end) {
-    Seg s;
-    s.u = unit_of(a, g);
-    s.k0 = (int)(g - s.u.off);
-    s.cnt = (int)min((long long)s.u.len, g_end - s.u.off) - s.k0;
-    s.nch = (s.cnt + CH - 1) / CH;
-    const int layer = a.layer0 + s.u.l;
-    s.K = a.kv.plane(a.seq[s.u.b], layer, 0, s.u.kh) + (size_t)s.k0 * D;
-    s.V = a.kv.plane(a.seq[s.u.b], layer, 1, s.u.kh) + (size_t)s.k0 * D;
-    return s;
+// The unit after u in (layer, row, KV head) order, without divisions.
+__device__ __forceinline__ void next_unit(const DecodeArgs& a, Unit& u) {
+    u.off += u.len;
+    if (++u.kh == a.hkv) {
+        u.kh = 0;
+        if (++u.b == a.n) { u.b = 0; ++u.l; }
+        u.len = a.pos[u.b] + 1;
+    }
 }
 
 // CTA whose range holds global key g: the largest c with floor(c*T/C) <= g.
@@ -138,38 +133,52 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
     uint32_t issued = 0, consumed = 0;                 // ring sequence numbers (thread 0 issues)
     const float qscale = 1.4426950408889634f * 0.08838834764831845f;   // log2(e)/sqrt(128)
 
-    // Producer cursor (thread 0): the CTA's chunk stream is, segment after segment, the K
-    // chunks then the V chunks of each; the consumers walk the same stream in the same order.
-    long long pg = g_begin;
-    Seg ps{};
-    int pj = 0;
-    bool pseg = false;
+    // Producer cursor (thread 0, in shared memory so that it holds no registers in the
+    // consumer loop). The CTA's chunk stream is, segment after segment, the K chunks then the
+    // V chunks of each segment (the part of one unit inside the range); the consumers walk
+    // the same stream in the same order.
+    __shared__ struct { Unit u; const __half* K; const __half* V; int j, nch, cnt; } pc;
     auto produce = [&]() {
-        if (!pseg || pj == 2 * ps.nch) {
-            if (pg >= g_end) return;
-            ps = segment_at(a, pg, g_end);
-            pg = ps.u.off + ps.k0 + ps.cnt;
-            pj = 0;
-            pseg = true;
+        if (pc.j == 2 * pc.nch) {                      // next segment: the next unit from key 0
+            next_unit(a, pc.u);
+            if (pc.u.off >= g_end) return;
+            pc.cnt = (int)min((long long)pc.u.len, g_end - pc.u.off);
+            pc.nch = (pc.cnt + CH - 1) / CH;
+            pc.j = 0;
+            const int layer = a.layer0 + pc.u.l;
+            pc.K = a.kv.plane(a.seq[pc.u.b], layer, 0, pc.u.kh);
+            pc.V = a.kv.plane(a.seq[pc.u.b], layer, 1, pc.u.kh);
         }
         const int stage = issued % NST;
-        const bool is_v = pj >= ps.nch;
-        const int jj = is_v ? pj - ps.nch : pj;
-        const int keys = min(CH, ps.cnt - jj * CH);
-        const __half* src = (is_v ? ps.V : ps.K) + (size_t)jj * CH * D;
+        const bool is_v = pc.j >= pc.nch;
+        const int jj = is_v ? pc.j - pc.nch : pc.j;
+        const int keys = min(CH, pc.cnt - jj * CH);
+        const __half* src = (is_v ? pc.V : pc.K) + (size_t)jj * CH * D;
         mbar_arrive_expect_tx(&full[stage], keys * D * 2);
         bulk_copy(ring + stage * CHUNK_BYTES, src, keys * D * 2, &full[stage]);
         ++issued;
-        ++pj;
+        ++pc.j;
     };
-    if (tid == 0)
-        for (int i = 0; i < NST; ++i) produce();
+    Unit u = unit_of(a, g_begin);                      // consumers' unit cursor
+    if (tid == 0) {
+        // first segment: keys [g_begin - off, ...) of the unit holding g_begin
+        const int k0 = (int)(g_begin - u.off);
+        pc.u = u;
+        pc.cnt = (int)min((long long)u.len, g_end - u.off) - k0;
+        pc.nch = (pc.cnt + CH - 1) / CH;
+        pc.j = 0;
+        const int layer = a.layer0 + u.l;
+        pc.K = a.kv.plane(a.seq[u.b], layer, 0, u.kh) + (size_t)k0 * D;
+        pc.V = a.kv.plane(a.seq[u.b], layer, 1, u.kh) + (size_t)k0 * D;
+        for (int i = 0; i < NST && g_begin < g_end; ++i) produce();
+    }
 
     for (long long g = g_begin; g < g_end;) {
-        const Seg sg = segment_at(a, g, g_end);
-        const Unit u = sg.u;
-        const int cnt = sg.cnt, nch = sg.nch;
-        g = u.off + sg.k0 + cnt;
+        if (g != g_begin) next_unit(a, u);
+        const int k0 = (int)(g - u.off);
+        const int cnt = (int)min((long long)u.len, g_end - u.off) - k0;
+        const int nch = (cnt + CH - 1) / CH;
+        g = u.off + k0 + cnt;
         const int total_chunks = 2 * nch;                // K chunks then V chunks
         const size_t qrow = ((size_t)u.l * a.n + u.b) * a.hq + (size_t)u.kh * GROUP;
 
