@@ -8,7 +8,7 @@
 // the CTA and share every K/V tile (the reference pairs heads for the same reason,
 // core.cpp:150-159). Rows whose absolute position is below 128 are not handled here: they
 // attend to few keys, where FP16 probabilities are not accurate enough, and go to the
-// FP32 CUDA-core kernel (attn_rows.cu).
+// FP32 CUDA-core kernel (attn_head_rows.cu).
 //
 // Warp roles (384 threads, three warpgroups):
 //   warps 0-3  softmax group for query head 0 (thread t owns query row t of the tile)
@@ -20,16 +20,23 @@
 // Per 128-key tile j:
 //   S_h = Q_h K_j^T         tcgen05.mma kind::f16, M=128 N=128 K=128, FP32 accumulate in TMEM
 //   softmax group h: tcgen05.ld S_h row, causal mask, running max (log2 domain, lazy
-//   rescale when the max grows by more than 8), P = 2^(s - m) -> FP16 into shared memory
-//   O_h += P_h V_j          tcgen05.mma, A = P (K-major), B = V (MN-major), accumulate in TMEM
+//   rescale when the max grows by more than 8), P = 2^(s - m) -> FP16 written back into the
+//   first 64 TMEM columns of S_h with tcgen05.st (two FP16 keys per 32-bit column)
+//   O_h += P_h V_j          tcgen05.mma with A = P from TMEM, B = V (MN-major, shared memory)
 // The MMA thread issues PV_h(j) then S_h(j+1) for h = 0, 1, so the tensor pipe works on one
-// head while the other head's softmax runs. Key tiles above the diagonal of the
-// query tile are skipped; tiles crossing it are masked per element.
+// head while the other head's softmax runs. S_h(j+1) overwrites P_h(j) only after PV_h(j)
+// has read it: MMAs issued by one thread execute in order. The commit that announces S_h(j)
+// also covers PV_h(j-1), so the softmax group may rescale O_h without another barrier.
+// Key tiles above the diagonal of the query tile are skipped; tiles crossing it are masked
+// per element.
 //
-// Memory: Q_0, Q_1 (FP16, 32 KB each), a 3-stage K/V ring (32 KB stages), P_0, P_1 (32 KB each)
-// = 224 KB shared; TMEM 512 columns = S_0, S_1, O_0, O_1 (128 FP32 columns each).
+// Memory: Q_0, Q_1 (FP16, 32 KB each) and a 5-stage K/V ring (32 KB stages) = 224 KB of
+// shared memory; TMEM 512 columns = S_0/P_0, S_1/P_1, O_0, O_1 (128 FP32 columns each).
 // K/V tiles come from the HBM KV store through one 3-D tensor map
-// {128 channels, ctx positions, planes} with 64x128 boxes and 128-byte swizzle.
+// {128 channels, ctx positions, planes} with 64x128 boxes and 128-byte swizzle; loads run
+// up to 2.5 tiles ahead of the tensor pipe.
+// Q rows are read with coalesced 512-byte row loads; the output rows leave through the
+// head's Q buffer (free once the last MMA of the head has completed) as coalesced stores.
 //
 // Every wait is bounded (globaltimer, 2 s): on expiry the CTA raises an abort flag, writes
 // an error code to the host-visible flag, drains what it issued and frees its TMEM.
@@ -51,18 +58,19 @@ constexpr int THREADS = 384;                              // 12 warps = 3 warpgr
 constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 224, REGS_CONTROL = 56;
 static_assert(2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL == THREADS * REGS_LAUNCH, "register split must match launch");
 constexpr uint32_t TILE_BYTES = BN * D * 2;               // 32 KB FP16 K or V tile
-// K and V tiles share one 3-stage ring in load order K0, V0, K1, V1, ...: item i = 2j (K_j)
-// or 2j+1 (V_j) lives in stage i % 3, so every load is issued about 1.5 tiles before use.
-constexpr int RING = 3;
-constexpr int OFF_Q = 0, OFF_RING = 65536, OFF_P = OFF_RING + RING * 32768, OFF_BAR = OFF_P + 65536;
+// K and V tiles share one 5-stage ring in load order K0, V0, K1, V1, ...: item i = 2j (K_j)
+// or 2j+1 (V_j) lives in stage i % 5, so every load is issued about 2.5 tiles before use.
+constexpr int RING = 5;
+constexpr int OFF_Q = 0, OFF_RING = 65536, OFF_BAR = OFF_RING + RING * 32768;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;          // + barriers + alignment slack
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr float RESCALE_THRESHOLD = 8.0f;                 // log2 units
 
 enum {
-    B_Q0, B_Q1, B_FULL0, B_FULL1, B_FULL2, B_EMPTY0, B_EMPTY1, B_EMPTY2, B_SF0, B_SF1, B_SE0, B_SE1, B_PF0, B_PF1,
-    B_OD0, B_OD1,
+    B_Q0, B_Q1, B_FULL0, B_EMPTY0 = B_FULL0 + RING, B_SF0 = B_EMPTY0 + RING, B_SF1, B_PF0, B_PF1, B_OD0, B_OD1,
     B_DRAIN, B_COUNT
 };
+static_assert(B_COUNT * 8 + 4 <= 256, "barrier area");
 
 struct PrefillArgs {
     const float* q; float* out;       // [n_layers][n][hq][128]
@@ -132,7 +140,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         never_abort = 0;
         mbar_init(&bar[B_Q0], 128); mbar_init(&bar[B_Q1], 128);
         for (int i = 0; i < RING; ++i) { mbar_init(&bar[B_FULL0 + i], 1); mbar_init(&bar[B_EMPTY0 + i], 1); }
-        mbar_init(&bar[B_SF0], 1); mbar_init(&bar[B_SF1], 1); mbar_init(&bar[B_SE0], 128); mbar_init(&bar[B_SE1], 128);
+        mbar_init(&bar[B_SF0], 1); mbar_init(&bar[B_SF1], 1);
         mbar_init(&bar[B_PF0], 128); mbar_init(&bar[B_PF1], 128); mbar_init(&bar[B_OD0], 1); mbar_init(&bar[B_OD1], 1);
         mbar_init(&bar[B_DRAIN], 1);
         fence_mbar_init();
@@ -151,32 +159,32 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
     if (warp < 8) {
         // ================================ softmax groups ================================
         const int h = warp >> 2;                             // query head within the pair
+        const int wq = warp & 3;                             // this warp's 32-row quarter
         const int t = tid & 127;                             // row within the tile
-        const int r = r0 + t;
-        const bool row_ok = r < a.n;
-        const int row_pos = a.pos0 + r;
-        const size_t qoff = (((size_t)l * a.n + r) * a.hq + (size_t)kh * 2 + h) * D;
+        const int row_pos = a.pos0 + r0 + t;
+        auto row_off = [&](int r) { return (((size_t)l * a.n + r) * a.hq + (size_t)kh * 2 + h) * D; };
         uint8_t* Qs = smem + OFF_Q + h * 32768;
-        uint8_t* Ps = smem + OFF_P + h * 32768;
-        // Q row -> FP16 in the swizzled K-major layout: all 32 loads of the row in flight at once
+        // Q rows of this warp's quarter -> FP16 in the swizzled K-major layout. Lane i reads
+        // channels 4i..4i+3 of each row (coalesced 512-byte rows), all 32 rows in flight.
         {
             float4 xr[32];
             #pragma unroll
-            for (int c = 0; c < 32; ++c)
-                xr[c] = row_ok ? __ldg(reinterpret_cast<const float4*>(a.q + qoff) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                const float4 x = xr[2 * c], y = xr[2 * c + 1];
-                *reinterpret_cast<uint4*>(Qs + swz(t, c)) =
-                    make_uint4(pack_half2(x.x, x.y), pack_half2(x.z, x.w), pack_half2(y.x, y.y), pack_half2(y.z, y.w));
+            for (int rr = 0; rr < 32; ++rr) {
+                const int r = r0 + wq * 32 + rr;
+                xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(a.q + row_off(r)) + lane)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             }
+            #pragma unroll
+            for (int rr = 0; rr < 32; ++rr)
+                *reinterpret_cast<uint2*>(Qs + swz(wq * 32 + rr, lane >> 1) + (lane & 1) * 8) =
+                    make_uint2(pack_half2(xr[rr].x, xr[rr].y), pack_half2(xr[rr].z, xr[rr].w));
         }
         fence_proxy_async_smem();
         mbar_arrive(&bar[B_Q0 + h]);
 
         const float scale = 1.4426950408889634f * 0.08838834764831845f;   // log2(e)/sqrt(128)
-        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t s_col = tmem + lane_base + h * 128;
+        const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+        const uint32_t s_col = tmem + lane_base + h * 128;   // S_h; P_h in its first 64 columns
         const uint32_t o_col = tmem + lane_base + 256 + h * 128;
         float m = -INFINITY, lsum = 0.f;
         bool ok = true;
@@ -193,8 +201,6 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             for (int c = 0; c < 4; ++c)
                 #pragma unroll
                 for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
-            tc_fence_before();
-            mbar_arrive(&bar[B_SE0 + h]);                       // S_h may now be overwritten
             float* v = reinterpret_cast<float*>(&sr[0][0]);
             const int k0 = j * BN;
             const int lim = row_pos - k0;                       // keys c > lim are in the future
@@ -202,19 +208,42 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 #pragma unroll
                 for (int c = 0; c < BN; ++c) v[c] = (c > lim) ? -INFINITY : v[c];
             }
-            float mt = fmax3(v[0], v[1], v[2]);
+            // row max: four independent 3-input max chains, then combined
+            float mq[4];
             #pragma unroll
-            for (int c = 3; c < BN - 1; c += 2) mt = fmax3(mt, v[c], v[c + 1]);
-            mt = fmaxf(mt, v[BN - 1]);
-            mt *= scale;
+            for (int q4 = 0; q4 < 4; ++q4) {
+                const float* w = v + q4 * 32;
+                float x = fmax3(w[0], w[1], w[2]);
+                #pragma unroll
+                for (int c = 3; c < 31; c += 2) x = fmax3(x, w[c], w[c + 1]);
+                mq[q4] = fmaxf(x, w[31]);
+            }
+            float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
             float alpha = 1.f;
             bool rescale = false;
             if (j == 0) m = mt;
             else if (mt > m + RESCALE_THRESHOLD) { alpha = ex2_approx(m - mt); m = mt; rescale = true; }
-            // P buffer and O_h are free once PV_h(j-1) has completed
-            if (j > 0 && !mbar_wait(&bar[B_OD0 + h], (j - 1) & 1, abortp)) { fail(12); ok = false; break; }
+            // p = 2^(s*scale - m): packed FMA pairs, MUFU ex2, FP16 pairs into TMEM over S_h
+            // (the first half is stored while the second half is computed)
+            const float2 sc2 = make_float2(scale, scale), mn2 = make_float2(-m, -m);
+            float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            #pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t pk[32];
+                #pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const int k = half * 64 + 2 * c;
+                    const float2 x = ffma2(make_float2(v[k], v[k + 1]), sc2, mn2);
+                    const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                    ps[c & 3] = fadd2(ps[c & 3], e);
+                    pk[c] = pack_half2(e.x, e.y);
+                }
+                tmem_st32(s_col + half * 32, pk);
+            }
+            const float psum = (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) + (ps[3].x + ps[3].y);
             if (rescale) {
-                tc_fence_after();
+                // O_h holds PV_h(0..j-1) (the commit that announced S_h(j) covered them); it is
+                // rescaled before PV_h(j) is allowed to accumulate into it
                 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     uint32_t rr[32];
@@ -224,47 +253,43 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
                     tmem_st32(o_col + c * 32, rr);
                 }
-                tmem_wait_st();
                 lsum *= alpha;
             }
-            // p = 2^(s*scale - m): packed FMA pairs, MUFU ex2, FP16 P into the swizzled
-            // shared-memory operand, 4 independent packed partial sums
-            const float2 sc2 = make_float2(scale, scale), mn2 = make_float2(-m, -m);
-            float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                uint32_t packed[4];
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 x = ffma2(make_float2(v[c * 8 + 2 * i], v[c * 8 + 2 * i + 1]), sc2, mn2);
-                    const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                    ps[i] = fadd2(ps[i], e);
-                    packed[i] = pack_half2(e.x, e.y);
-                }
-                *reinterpret_cast<uint4*>(Ps + swz(t, c)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            }
-            const float psum = (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) + (ps[3].x + ps[3].y);
             lsum += psum;
-            fence_proxy_async_smem();
+            tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bar[B_PF0 + h]);
         }
-        if (ok && mbar_wait(&bar[B_OD0 + h], (nk - 1) & 1, abortp)) {
+        if (ok && mbar_wait(&bar[B_OD0 + h], 0, abortp)) {
+            // Output rows leave through this head's Q buffer (its last reader, QK_h of the last
+            // tile, has completed): each thread writes its normalised row half (64 columns) into
+            // a 32-row x 256-byte block of the warp, then the warp stores two rows per
+            // instruction as coalesced 256-byte segments.
             tc_fence_after();
             const float inv = 1.f / lsum;
-            float* dst = a.out + qoff;
+            uint8_t* stage = Qs + wq * 8192;
             #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t rr[32];
-                tmem_ld32(o_col + c * 32, rr);
+            for (int part = 0; part < 2; ++part) {
+                uint32_t ra[32], rb[32];
+                tmem_ld32(o_col + part * 64, ra);
+                tmem_ld32(o_col + part * 64 + 32, rb);
                 tmem_wait_ld();
-                if (row_ok) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<float4*>(dst + c * 32 + i) =
-                            make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
-                                        __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
+                #pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const uint32_t* src = c < 8 ? ra + 4 * c : rb + 4 * (c - 8);
+                    *reinterpret_cast<float4*>(stage + lane * 256 + ((c ^ (lane & 15)) << 4)) =
+                        make_float4(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv,
+                                    __uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
                 }
+                __syncwarp();
+                #pragma unroll 4
+                for (int k = 0; k < 16; ++k) {
+                    const int rr = 2 * k + (lane >> 4), c = lane & 15;
+                    const float4 val = *reinterpret_cast<const float4*>(stage + rr * 256 + ((c ^ (rr & 15)) << 4));
+                    const int r = r0 + wq * 32 + rr;
+                    if (r < a.n) *reinterpret_cast<float4*>(a.out + row_off(r) + part * 64 + c * 4) = val;
+                }
+                __syncwarp();
             }
         } else if (ok) {
             fail(13);
@@ -274,7 +299,6 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         const uint32_t idesc_qk = idesc_f16_f32(BM, BN, false);
         const uint32_t idesc_pv = idesc_f16_f32(BM, D, true);
         const uint32_t q_addr = smem_u32(smem + OFF_Q), ring_addr = smem_u32(smem + OFF_RING);
-        const uint32_t p_addr = smem_u32(smem + OFF_P);
         bool ok = true;
         auto wait_item = [&](int i) {                    // ring item i has landed
             return mbar_wait(&bar[B_FULL0 + i % RING], (i / RING) & 1, abortp);
@@ -295,16 +319,14 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             }
             __syncwarp();
         };
-        auto issue_pv = [&](int j, int h) {
-            const uint32_t pb = p_addr + h * 32768, vb = ring_addr + ((2 * j + 1) % RING) * TILE_BYTES;
+        auto issue_pv = [&](int j, int h) {              // A = P_h in TMEM: 8 columns per 16 keys
+            const uint32_t vb = ring_addr + ((2 * j + 1) % RING) * TILE_BYTES;
             if (lane == 0) {
                 #pragma unroll
-                for (int s = 0; s < 8; ++s) {
-                    const uint32_t offa = (s >> 2) * 16384 + (s & 3) * 32;
-                    mma_f16_ss(tmem + 256 + h * 128, sw128_desc(pb + offa, 16, 1024),
-                               sw128_desc(vb + s * 2048, 16384, 1024), idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
-                }
-                mma_commit(&bar[B_OD0 + h]);
+                for (int s = 0; s < 8; ++s)
+                    mma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + s * 8, sw128_desc(vb + s * 2048, 16384, 1024),
+                               idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
+                if (j == nk - 1) mma_commit(&bar[B_OD0 + h]);   // O_h final
             }
             __syncwarp();
         };
@@ -344,9 +366,9 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 issue_pv(j, h);
                 if (h == 1) release_item(2 * j + 1);         // V_j free when PV_1(j) completes
                 if (j + 1 < nk) {
+                    // S_h(j+1) over P_h(j): ordered after PV_h(j), issued just above
                     const int jn = j + 1;
                     if (h == 0 && !wait_item(2 * jn)) { fail(24); ok = false; break; }
-                    if (!mbar_wait(&bar[B_SE0 + h], j & 1, abortp)) { fail(25); ok = false; break; }
                     tc_fence_after();
                     issue_qk(jn, h);
                     if (h == 1) release_item(2 * jn);        // K_{j+1} free when QK_1(j+1) completes

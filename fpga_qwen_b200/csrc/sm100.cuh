@@ -1,6 +1,7 @@
 // sm100.cuh — thin inline-PTX wrappers for the Blackwell (sm_100a) features the prefill
 // kernel uses: mbarriers with bounded waits, TMA tiled loads, TMEM allocation, tcgen05.mma
-// (kind::f16, FP32 accumulate), tcgen05.commit / ld and the shared-memory matrix and
+// (kind::f16, FP32 accumulate, A from shared memory or TMEM), tcgen05.commit / ld / st and
+// the shared-memory matrix and
 // instruction descriptors. Field layouts follow the PTX ISA description of tcgen05
 // descriptors (the same fields CUTLASS's cute::UMMA::SmemDescriptor / InstrDescriptor name).
 #pragma once
@@ -120,6 +121,15 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16: A is M rows in TMEM lanes, two 16-bit K
+// elements per 32-bit column (element 2c in the low half of column c).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
 // Arrives once on `bar` when all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
