@@ -509,6 +509,9 @@ def run_config5(args):
                 pre_flops += prefill_flops(0, n)
                 del q, k, v, qn, out
         if disagg:
+            # every prefill is finished before the handoff clock starts on both ends
+            torch.cuda.synchronize()
+            dist.barrier()
             h0, h1 = ev(), ev()
             h0.record(stream)
             for s_, i in enumerate(mine):
@@ -517,6 +520,7 @@ def run_config5(args):
                 else:
                     ctx.kv_recv(s_, lengths[i], rank - groups)
                 hand_bytes += KV_BYTES_PER_POS * lengths[i]
+            ctx.comm_join()                      # the sender's stream waits for its last transfer
             h1.record(stream)
             torch.cuda.synchronize()
             hand_ms = h0.elapsed_time(h1)

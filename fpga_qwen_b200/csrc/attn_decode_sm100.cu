@@ -25,8 +25,18 @@
 // finish (one atomic counter, no waiting) merges them.
 // Every wait is bounded (globaltimer): on expiry the CTA records an error code for the
 // host, stops consuming, drains its outstanding copies and exits.
+//
+// Fused decode step (FUSED = true): the kernel also performs the append of the one new row
+// per sequence (core.cpp:395-406 for a single token), so a decode step is one launch. At the
+// start of each segment the CTA normalises and rotates the unit's two query rows from the
+// pre-norm input (norm_rope.cuh, the same arithmetic as kv_append, so q_out and the
+// attention input are bit-identical to an append followed by a decode); the copy ring keeps
+// filling meanwhile. The new row is the last key of its unit, so exactly one CTA reads it:
+// that CTA builds the FP16 K and V rows, stores them in the KV store (and q_out), and patches
+// them into the ring chunk that holds the stale row before scoring it.
 #include <algorithm>
 
+#include "norm_rope.cuh"
 #include "qattn_common.cuh"
 #include "sm100.cuh"
 
@@ -44,6 +54,7 @@ constexpr int MAX_UNIT_KEYS = 4096;           // longest unit (QA_MAX_CONTEXT): 
 
 struct DecodeArgs {
     const float* q; float* out;               // [n_layers][n][hq][128]
+    StepInputs step;                          // fused decode step only
     KVLayout kv; int layer0, n_layers, n, hq, hkv;
     int seq[MAX_BATCH];                       // sequence slot of row b
     int pos[MAX_BATCH];                       // absolute position of row b (context pos+1)
@@ -107,6 +118,7 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+template <bool FUSED>
 __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem;                                              // NST x 16 KB
@@ -116,6 +128,9 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
     __shared__ float stat[2 * GROUP];
     __shared__ float accbuf[HALF_WARPS][GROUP][D];
     __shared__ int is_last, abort_flag, never_abort;
+    __shared__ __align__(16) float s_q[GROUP][D];          // fused: the unit's normalised query rows
+    __shared__ __align__(16) __half s_new[2][D];           // fused: the new K and V rows (FP16)
+    __shared__ float s_inv[3];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hw = tid >> 4, sl = tid & 15;
@@ -182,13 +197,63 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         const int total_chunks = 2 * nch;                // K chunks then V chunks
         const size_t qrow = ((size_t)u.l * a.n + u.b) * a.hq + (size_t)u.kh * GROUP;
 
+        // the segment ends at the unit's last key: in a fused step that is the new row
+        const bool owns_new = FUSED && k0 + cnt == u.len;
         float q[GROUP][8];
-        #pragma unroll
-        for (int gq = 0; gq < GROUP; ++gq) {
-            const float4* src = reinterpret_cast<const float4*>(a.q + (qrow + gq) * D + sl * 8);
-            const float4 x = __ldg(src), y = __ldg(src + 1);
-            q[gq][0] = x.x * qscale; q[gq][1] = x.y * qscale; q[gq][2] = x.z * qscale; q[gq][3] = x.w * qscale;
-            q[gq][4] = y.x * qscale; q[gq][5] = y.y * qscale; q[gq][6] = y.z * qscale; q[gq][7] = y.w * qscale;
+        if constexpr (FUSED) {
+            const int layer = a.layer0 + u.l;
+            const int pos = u.len - 1;                          // position of the new row
+            const size_t krow = ((size_t)u.l * a.n + u.b) * a.hkv + u.kh;
+            const float* qp = a.step.q_pre + qrow * D;
+            const float* kp = a.step.k_pre + krow * D;
+            // the three sequential FP64 chains run on three warps at once
+            if (tid == 0) s_inv[0] = rms_inv(qp, a.step.eps);
+            else if (tid == 32) s_inv[1] = rms_inv(qp + D, a.step.eps);
+            else if (tid == 64 && owns_new) s_inv[2] = rms_inv(kp, a.step.eps);
+            __syncthreads();
+            {
+                const int r = tid >> 6, j = tid & 63;           // query head r, channel pair (j, j+64)
+                const float* w = a.step.norms + (size_t)layer * 2 * D;
+                const float c = a.step.cosines[(size_t)pos * 64 + j], sn = a.step.sines[(size_t)pos * 64 + j];
+                float ra, rb;
+                norm_rope_pair(qp[r * D + j], qp[r * D + j + 64], w[j], w[j + 64], c, sn, s_inv[r], ra, rb);
+                s_q[r][j] = ra;
+                s_q[r][j + 64] = rb;
+                if (owns_new) {
+                    if (a.step.q_out) {
+                        a.step.q_out[(qrow + r) * D + j] = ra;
+                        a.step.q_out[(qrow + r) * D + j + 64] = rb;
+                    }
+                    if (tid < 64) {                             // K row pair j
+                        float ka, kb;
+                        norm_rope_pair(kp[j], kp[j + 64], w[D + j], w[D + j + 64], c, sn, s_inv[2], ka, kb);
+                        s_new[0][j] = __float2half_rn(ka);
+                        s_new[0][j + 64] = __float2half_rn(kb);
+                    } else {                                    // V row channels 2i, 2i+1
+                        const int c2 = 2 * (tid - 64);
+                        const float* vp = a.step.v_pre + krow * D;
+                        *reinterpret_cast<__half2*>(&s_new[1][c2]) = __floats2half2_rn(vp[c2], vp[c2 + 1]);
+                    }
+                }
+            }
+            __syncthreads();
+            if (owns_new && tid < 32) {                         // store the new rows (16 B per lane)
+                const int kv = tid >> 4, c16 = tid & 15;
+                __half* dst = a.kv.plane(a.seq[u.b], layer, kv, u.kh) + (size_t)pos * D;
+                reinterpret_cast<uint4*>(dst)[c16] = reinterpret_cast<const uint4*>(s_new[kv])[c16];
+            }
+            #pragma unroll
+            for (int gq = 0; gq < GROUP; ++gq)
+                #pragma unroll
+                for (int e = 0; e < 8; ++e) q[gq][e] = s_q[gq][sl * 8 + e] * qscale;
+        } else {
+            #pragma unroll
+            for (int gq = 0; gq < GROUP; ++gq) {
+                const float4* src = reinterpret_cast<const float4*>(a.q + (qrow + gq) * D + sl * 8);
+                const float4 x = __ldg(src), y = __ldg(src + 1);
+                q[gq][0] = x.x * qscale; q[gq][1] = x.y * qscale; q[gq][2] = x.z * qscale; q[gq][3] = x.w * qscale;
+                q[gq][4] = y.x * qscale; q[gq][5] = y.y * qscale; q[gq][6] = y.z * qscale; q[gq][7] = y.w * qscale;
+            }
         }
         float mloc0 = -INFINITY, mloc1 = -INFINITY;
         float acc[GROUP][8];
@@ -204,10 +269,17 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             bool got = mbar_wait(&full[stage], parity, &abort_flag);
             if (!got) { abort_flag = 1; atomicCAS(a.error, 0, 41); }
             got = __all_sync(0xffffffffu, got);           // warp-uniform: the shuffles below need all lanes
-            const uint8_t* buf = ring + stage * CHUNK_BYTES;
+            uint8_t* buf = ring + stage * CHUNK_BYTES;
             const bool is_v = j >= nch;
             const int jj = is_v ? j - nch : j;
             const int keys = min(CH, cnt - jj * CH);
+            if (owns_new && jj == nch - 1) {
+                // the last chunk of each pass holds the new row, copied before it was written:
+                // replace it with the row built above (CTA-uniform branch)
+                if (tid < 16)
+                    reinterpret_cast<uint4*>(buf + (keys - 1) * 256)[tid] = reinterpret_cast<const uint4*>(s_new[is_v])[tid];
+                __syncthreads();
+            }
             if (got) {
                 if (!is_v) {
                     // ---- scores: half-warp hw takes keys hw, hw+8, hw+16, hw+24 (+32) ----
@@ -412,9 +484,10 @@ DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos) {
 
 void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const float* q, float* out, int layer0,
                               int n_layers, int n, const int* seq, const int* pos, int hq, int hkv, float* partial,
-                              int* counters, int* error, cudaStream_t s) {
+                              int* counters, int* error, cudaStream_t s, const StepInputs* step) {
     DecodeArgs a{};
     a.q = q; a.out = out; a.kv = kv; a.layer0 = layer0; a.n_layers = n_layers; a.n = n; a.hq = hq; a.hkv = hkv;
+    if (step) a.step = *step;
     a.start[0] = 0;
     for (int b = 0; b < n; ++b) { a.seq[b] = seq[b]; a.pos[b] = pos[b]; a.start[b + 1] = a.start[b] + pos[b] + 1; }
     a.total_keys = plan.total_keys; a.ctas = plan.ctas; a.max_keys = plan.max_keys;
@@ -423,11 +496,13 @@ void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const 
     const size_t smem = (size_t)NST * CHUNK_BYTES + (size_t)GROUP * a.max_keys * sizeof(float);
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(attn_decode_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             NST * CHUNK_BYTES + GROUP * MAX_UNIT_KEYS * (int)sizeof(float));
+        const int max_smem = NST * CHUNK_BYTES + GROUP * MAX_UNIT_KEYS * (int)sizeof(float);
+        cudaFuncSetAttribute(attn_decode_sm100_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+        cudaFuncSetAttribute(attn_decode_sm100_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
         attr = true;
     }
-    attn_decode_sm100_kernel<<<a.ctas, THREADS, smem, s>>>(a);
+    if (step) attn_decode_sm100_kernel<true><<<a.ctas, THREADS, smem, s>>>(a);
+    else attn_decode_sm100_kernel<false><<<a.ctas, THREADS, smem, s>>>(a);
 }
 
 }  // namespace qattn

@@ -1,12 +1,9 @@
 // kv_append.cu — fused QK-RMSNorm + RoPE + FP16 KV write.
 //
 // Reference arithmetic (tampajohn/fpga-qwen engine/core.cpp), reproduced bit for bit:
-//   norm  :207-215  square = x*x (FP32); sum = Σ double(square) in ascending j (FP64);
-//                   inv = 1 / sqrt(float(sum)/128 + 1e-6); out = (x*inv)*w
-//   rope  :216-218  x[j] = a*c - b*s; x[j+64] = b*c + a*s  (unfused products)
+//   norm  :207-215 and rope :216-218 through norm_rope.cuh (shared with the fused decode
+//                  step, so both paths write the same bits)
 //   store :399-405  K, V -> FP16 round-to-nearest-even at (layer, pos+b, head)
-// Every rounding step is written with an explicit _rn intrinsic so that no compiler
-// contraction can change a result.
 //
 // Layout: one "row" is one head vector of 128 FP32 values. Per token there are hq query
 // rows, hkv key rows and hkv value rows. A block owns TPB consecutive tokens of one layer,
@@ -18,7 +15,7 @@
 // chain), normalises and rotates in place. The block writes back with coalesced stores:
 // FP32 query rows to q_out, FP16 K/V rows into the HBM KV store.
 // HBM-bound: 28,672 algorithmic bytes per (token, layer) at hq=16, hkv=8.
-#include "qattn_common.cuh"
+#include "norm_rope.cuh"
 
 namespace qattn {
 namespace {
@@ -79,18 +76,7 @@ __global__ void __launch_bounds__(TPB * 4 * HKV) kv_append_kernel(const AppendAr
             const float* cs = slot;
             const float* sn = slot + 64;
             const float* w = slot + 128 + kind * D;
-            // FP32 squares and their FP64 values are independent; only the adds chain
-            double precise_sum = 0.0;
-            #pragma unroll 8
-            for (int j = 0; j < D; j += 4) {
-                const float4 v = *reinterpret_cast<const float4*>(x + j);
-                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.x, v.x));
-                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.y, v.y));
-                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.z, v.z));
-                precise_sum = __dadd_rn(precise_sum, (double)__fmul_rn(v.w, v.w));
-            }
-            const float sum = __double2float_rn(precise_sum);
-            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)D), a.eps)));
+            const float inv = rms_inv(x, a.eps);
             #pragma unroll 4
             for (int j = 0; j < 64; j += 4) {
                 const float4 xa = *reinterpret_cast<const float4*>(x + j);
@@ -99,17 +85,11 @@ __global__ void __launch_bounds__(TPB * 4 * HKV) kv_append_kernel(const AppendAr
                 const float4 wb = *reinterpret_cast<const float4*>(w + j + 64);
                 const float4 c = *reinterpret_cast<const float4*>(cs + j);
                 const float4 s = *reinterpret_cast<const float4*>(sn + j);
-                const float na[4] = {__fmul_rn(__fmul_rn(xa.x, inv), wa.x), __fmul_rn(__fmul_rn(xa.y, inv), wa.y),
-                                     __fmul_rn(__fmul_rn(xa.z, inv), wa.z), __fmul_rn(__fmul_rn(xa.w, inv), wa.w)};
-                const float nb[4] = {__fmul_rn(__fmul_rn(xb.x, inv), wb.x), __fmul_rn(__fmul_rn(xb.y, inv), wb.y),
-                                     __fmul_rn(__fmul_rn(xb.z, inv), wb.z), __fmul_rn(__fmul_rn(xb.w, inv), wb.w)};
-                const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {s.x, s.y, s.z, s.w};
                 float ra[4], rb[4];
-                #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    ra[e] = __fsub_rn(__fmul_rn(na[e], cc[e]), __fmul_rn(nb[e], ss[e]));
-                    rb[e] = __fadd_rn(__fmul_rn(nb[e], cc[e]), __fmul_rn(na[e], ss[e]));
-                }
+                norm_rope_pair(xa.x, xb.x, wa.x, wb.x, c.x, s.x, inv, ra[0], rb[0]);
+                norm_rope_pair(xa.y, xb.y, wa.y, wb.y, c.y, s.y, inv, ra[1], rb[1]);
+                norm_rope_pair(xa.z, xb.z, wa.z, wb.z, c.z, s.z, inv, ra[2], rb[2]);
+                norm_rope_pair(xa.w, xb.w, wa.w, wb.w, c.w, s.w, inv, ra[3], rb[3]);
                 *reinterpret_cast<float4*>(x + j) = make_float4(ra[0], ra[1], ra[2], ra[3]);
                 *reinterpret_cast<float4*>(x + j + 64) = make_float4(rb[0], rb[1], rb[2], rb[3]);
             }

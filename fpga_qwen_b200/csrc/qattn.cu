@@ -56,8 +56,16 @@ struct qa_ctx {
     int nranks = 1, rank = 0;
     float* gather_buf = nullptr;           // all-gather landing buffer
     size_t gather_floats = 0;
-    void* kv_buf = nullptr;                // packed KV rows for the handoff
-    size_t kv_buf_bytes = 0;
+    // KV handoff staging: two buffers used alternately, so the pack (or unpack) of one request
+    // overlaps the NVLink transfer of the previous one. kv_comm_done[b]: the NCCL op that used
+    // buffer b has finished (comm stream); kv_unpacked[b]: the unpack from buffer b has finished
+    // (context stream).
+    void* kv_buf[2] = {nullptr, nullptr};
+    size_t kv_buf_bytes[2] = {0, 0};
+    cudaEvent_t kv_comm_done[2] = {nullptr, nullptr};
+    cudaEvent_t kv_unpacked[2] = {nullptr, nullptr};
+    cudaEvent_t kv_packed = nullptr;
+    int kv_next = 0;
     std::string err;
 };
 
@@ -282,7 +290,10 @@ void qa_destroy(qa_ctx* ctx) {
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
     cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->staging); cudaFree(ctx->error);
-    cudaFree(ctx->gather_buf); cudaFree(ctx->kv_buf);
+    cudaFree(ctx->gather_buf); cudaFree(ctx->kv_buf[0]); cudaFree(ctx->kv_buf[1]);
+    for (cudaEvent_t e : ctx->kv_comm_done) if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->kv_unpacked) if (e) cudaEventDestroy(e);
+    if (ctx->kv_packed) cudaEventDestroy(ctx->kv_packed);
     nccl_comm_destroy(ctx->comm);
     if (ctx->comm_stream) cudaStreamDestroy(ctx->comm_stream);
     for (cudaEvent_t e : ctx->comm_ev) if (e) cudaEventDestroy(e);
@@ -300,6 +311,7 @@ int qa_sync(qa_ctx* ctx) {
     if (!ctx) return QA_ERR_INVALID;
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
     QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (ctx->comm_stream) QA_CUDA(cudaStreamSynchronize(ctx->comm_stream));
     return check_device_error(ctx);
 }
 
@@ -545,6 +557,60 @@ int qa_attn_decode_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_l
     return QA_OK;
 }
 
+// ---- fused decode step: append of one new row per sequence + decode attention, one launch ----
+static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int layer, int n_layers,
+                       const float* q_pre, const float* k_pre, const float* v, float* q_out, float* out) {
+    int st;
+    if (!q_pre || !k_pre || !v || !out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const size_t qn = (size_t)n_layers * n * ctx->hq * D, kn = (size_t)n_layers * n * ctx->hkv * D;
+    StepInputs in{};
+    in.q_pre = q_pre; in.k_pre = k_pre; in.v_pre = v; in.q_out = q_out;
+    float* od = out;
+    if (ctx->cfg.io_host) {
+        if ((st = ensure_staging(ctx, 3 * qn + 2 * kn))) return st;
+        float* sg = ctx->staging;
+        QA_CUDA(cudaMemcpyAsync(sg, q_pre, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        QA_CUDA(cudaMemcpyAsync(sg + qn, k_pre, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        QA_CUDA(cudaMemcpyAsync(sg + qn + kn, v, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        in.q_pre = sg; in.k_pre = sg + qn; in.v_pre = sg + qn + kn;
+        in.q_out = q_out ? sg + qn + 2 * kn : nullptr;
+        od = sg + 2 * qn + 2 * kn;
+    }
+    in.norms = ctx->norms; in.cosines = ctx->cosines; in.sines = ctx->sines; in.eps = ctx->cfg.norm_eps;
+    const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
+    if ((st = ensure_decode_scratch(ctx, plan))) return st;
+    launch_attn_decode_sm100(plan, ctx->kv, nullptr, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
+                             ctx->partial, ctx->counters, ctx->error, ctx->stream, &in);
+    if ((st = after_launch(ctx, n == 1 ? seqs[0] : -1, "attn_decode_step"))) return st;
+    for (int b = 0; b < n; ++b)
+        for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seqs[b]][l] = pos[b] + 1;
+    if (ctx->cfg.io_host) {
+        if (q_out) QA_CUDA(cudaMemcpyAsync(q_out, in.q_out, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        QA_CUDA(cudaMemcpyAsync(out, od, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
+    return QA_OK;
+}
+
+int qa_decode_step(qa_ctx* ctx, int seq, int layer, int n_layers, int pos, const float* q_pre, const float* k_pre,
+                   const float* v, float* q_out, float* out) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_rows(ctx, seq, layer, n_layers, pos, 1))) return st;
+    return decode_step(ctx, &seq, &pos, 1, layer, n_layers, q_pre, k_pre, v, q_out, out);
+}
+
+int qa_decode_step_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_layers, const float* q_pre,
+                         const float* k_pre, const float* v, float* q_out, float* out) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_batch(ctx, seqs, n, layer, n_layers))) return st;
+    int pos[QA_MAX_BATCH];
+    for (int b = 0; b < n; ++b) pos[b] = ctx->pos[seqs[b]];
+    return decode_step(ctx, seqs, pos, n, layer, n_layers, q_pre, k_pre, v, q_out, out);
+}
+
 int qa_commit_batch(qa_ctx* ctx, const int* seqs, int n) {
     if (!ctx) return QA_ERR_INVALID;
     int st;
@@ -617,6 +683,7 @@ namespace {
 int grow(qa_ctx* ctx, void** buf, size_t& have, size_t need) {
     if (need <= have) return QA_OK;
     QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (ctx->comm_stream) QA_CUDA(cudaStreamSynchronize(ctx->comm_stream));
     cudaFree(*buf);
     *buf = nullptr; have = 0;
     QA_CUDA(cudaMalloc(buf, need));
@@ -655,6 +722,11 @@ int qa_comm_init(qa_ctx* ctx, int nranks, int rank, const char id[128]) {
         QA_CUDA(cudaStreamCreateWithFlags(&ctx->comm_stream, cudaStreamNonBlocking));
         QA_CUDA(cudaEventCreateWithFlags(&ctx->comm_ev[0], cudaEventDisableTiming));
         QA_CUDA(cudaEventCreateWithFlags(&ctx->comm_ev[1], cudaEventDisableTiming));
+        for (int b = 0; b < 2; ++b) {
+            QA_CUDA(cudaEventCreateWithFlags(&ctx->kv_comm_done[b], cudaEventDisableTiming));
+            QA_CUDA(cudaEventCreateWithFlags(&ctx->kv_unpacked[b], cudaEventDisableTiming));
+        }
+        QA_CUDA(cudaEventCreateWithFlags(&ctx->kv_packed, cudaEventDisableTiming));
     }
     std::string err;
     const int st = nccl_comm_init(&ctx->comm, nranks, rank, id, err);
@@ -715,29 +787,47 @@ static int kv_transfer(qa_ctx* ctx, int seq, int ntok, int peer, bool send) {
         return fail(ctx, QA_ERR_STATE, "sequence holds %d committed rows, send wants %d", ctx->pos[seq], ntok);
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
     const size_t bytes = (size_t)ctx->cfg.n_layers * 2 * ctx->hkv * ntok * D * sizeof(__half);
-    if ((st = grow(ctx, &ctx->kv_buf, ctx->kv_buf_bytes, bytes))) return st;
+    const int b = ctx->kv_next;
+    if ((st = grow(ctx, &ctx->kv_buf[b], ctx->kv_buf_bytes[b], bytes))) return st;
+    void* buf = ctx->kv_buf[b];
     std::string err;
     if (send) {
-        launch_pack_kv(ctx->kv, seq, ntok, ctx->kv_buf, false, ctx->stream);
+        // pack on the context stream once the previous NCCL op on this buffer is done; the
+        // send then runs on the communication stream while the context stream moves on
+        QA_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->kv_comm_done[b], 0));
+        launch_pack_kv(ctx->kv, seq, ntok, buf, false, ctx->stream);
         if ((st = after_launch(ctx, -1, "pack_kv"))) return st;
-        if ((st = comm_enter(ctx))) return st;
-        if ((st = nccl_send_recv_bytes(ctx->comm, ctx->kv_buf, bytes, peer, true, ctx->comm_stream, err)))
+        QA_CUDA(cudaEventRecord(ctx->kv_packed, ctx->stream));
+        QA_CUDA(cudaStreamWaitEvent(ctx->comm_stream, ctx->kv_packed, 0));
+        if ((st = nccl_send_recv_bytes(ctx->comm, buf, bytes, peer, true, ctx->comm_stream, err)))
             return fail(ctx, st, "ncclSend: %s", err.c_str());
-        if ((st = comm_leave(ctx))) return st;
+        QA_CUDA(cudaEventRecord(ctx->kv_comm_done[b], ctx->comm_stream));
     } else {
-        if ((st = comm_enter(ctx))) return st;
-        if ((st = nccl_send_recv_bytes(ctx->comm, ctx->kv_buf, bytes, peer, false, ctx->comm_stream, err)))
+        // receive on the communication stream once the previous unpack from this buffer is
+        // done; the unpack follows on the context stream
+        QA_CUDA(cudaStreamWaitEvent(ctx->comm_stream, ctx->kv_unpacked[b], 0));
+        if ((st = nccl_send_recv_bytes(ctx->comm, buf, bytes, peer, false, ctx->comm_stream, err)))
             return fail(ctx, st, "ncclRecv: %s", err.c_str());
-        if ((st = comm_leave(ctx))) return st;
-        launch_pack_kv(ctx->kv, seq, ntok, ctx->kv_buf, true, ctx->stream);
+        QA_CUDA(cudaEventRecord(ctx->kv_comm_done[b], ctx->comm_stream));
+        QA_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->kv_comm_done[b], 0));
+        launch_pack_kv(ctx->kv, seq, ntok, buf, true, ctx->stream);
         if ((st = after_launch(ctx, seq, "unpack_kv"))) return st;
+        QA_CUDA(cudaEventRecord(ctx->kv_unpacked[b], ctx->stream));
         ctx->pos[seq] = ntok;
         std::fill(ctx->appended[seq].begin(), ctx->appended[seq].end(), ntok);
     }
+    ctx->kv_next = b ^ 1;
     return QA_OK;
 }
 
 int qa_kv_send(qa_ctx* ctx, int seq, int ntok, int peer) { return kv_transfer(ctx, seq, ntok, peer, true); }
 int qa_kv_recv(qa_ctx* ctx, int seq, int ntok, int peer) { return kv_transfer(ctx, seq, ntok, peer, false); }
+
+int qa_comm_join(qa_ctx* ctx) {
+    if (!ctx) return QA_ERR_INVALID;
+    if (!ctx->comm_stream) return QA_OK;
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    return comm_leave(ctx);
+}
 
 }  // extern "C"

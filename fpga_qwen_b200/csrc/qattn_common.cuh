@@ -76,9 +76,17 @@ struct DecodePlan {
     size_t partial_floats() const;
 };
 DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos);
+// Inputs of a fused decode step (append of the one new row per sequence + decode attention).
+struct StepInputs {
+    const float* q_pre = nullptr; const float* k_pre = nullptr; const float* v_pre = nullptr;   // [L][n][h][128]
+    float* q_out = nullptr;                                    // optional
+    const float* norms = nullptr; const float* cosines = nullptr; const float* sines = nullptr;
+    float eps = 0.f;
+};
 void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const float* q, float* out, int layer0,
                               int n_layers, int n, const int* seq, const int* pos, int hq, int hkv, float* partial,
-                              int* counters, int* error, cudaStream_t s);
+                              int* counters, int* error, cudaStream_t s,
+                              const StepInputs* step = nullptr);
 // Rows at absolute positions below this go to the FP32 CUDA-core kernel.
 constexpr int TC_MIN_POSITION = 128;
 void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n,

@@ -82,6 +82,13 @@ _SIGNATURES = {
     "qa_gather_heads": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "qa_kv_send": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_kv_recv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "qa_comm_join": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_decode_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_void_p]),
+    "qa_decode_step_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_void_p]),
     "qa_attn_decode_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                               ctypes.c_void_p, ctypes.c_void_p]),
@@ -222,6 +229,14 @@ class Context:
         arr, n = self._seq_array(seqs)
         self._check(lib().qa_attn_decode_batch(self._h, arr, n, layer, n_layers, q, out))
 
+    def decode_step(self, seq, layer, n_layers, pos, q_pre, k_pre, v, q_out, out):
+        """Append of one new row + its decode attention in one launch (q_out may be 0)."""
+        self._check(lib().qa_decode_step(self._h, seq, layer, n_layers, pos, q_pre, k_pre, v, q_out or None, out))
+
+    def decode_step_batch(self, seqs, layer, n_layers, q_pre, k_pre, v, q_out, out):
+        arr, n = self._seq_array(seqs)
+        self._check(lib().qa_decode_step_batch(self._h, arr, n, layer, n_layers, q_pre, k_pre, v, q_out or None, out))
+
     def commit_batch(self, seqs):
         arr, n = self._seq_array(seqs)
         self._check(lib().qa_commit_batch(self._h, arr, n))
@@ -243,6 +258,10 @@ class Context:
 
     def kv_recv(self, seq: int, ntok: int, peer: int):
         self._check(lib().qa_kv_recv(self._h, seq, ntok, peer))
+
+    def comm_join(self):
+        """Makes the context stream wait for the communication queued so far."""
+        self._check(lib().qa_comm_join(self._h))
 
     def kv_slot_bytes(self) -> int:
         out = ctypes.c_size_t()

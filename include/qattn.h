@@ -138,6 +138,20 @@ int qa_attn_decode_batch(qa_ctx* ctx, const int* seqs, int n_seqs, int layer, in
                          const float* q, float* out);
 int qa_commit_batch(qa_ctx* ctx, const int* seqs, int n_seqs);
 
+/* Fused decode step: qa_append of one new row followed by qa_attn_decode of that row, in a
+ * single launch (the per-token work of core.cpp:395-406 then :606-624 for every requested
+ * layer). Same tensors and layouts as those two calls with n = 1; q_out (the normalised,
+ * rotated query rows) may be NULL when the caller does not need it. K/V rows and q_out are
+ * bit-identical to qa_append; out matches qa_attn_decode. pos must be the sequence's
+ * committed position; qa_commit advances it afterwards, as after qa_append.
+ * The batch form takes one row per listed sequence at its committed position (layouts of
+ * qa_append_batch / qa_attn_decode_batch). */
+int qa_decode_step(qa_ctx* ctx, int seq, int layer, int n_layers, int pos, const float* q_pre,
+                   const float* k_pre, const float* v, float* q_out, float* out);
+int qa_decode_step_batch(qa_ctx* ctx, const int* seqs, int n_seqs, int layer, int n_layers,
+                         const float* q_pre, const float* k_pre, const float* v, float* q_out,
+                         float* out);
+
 /* Canonical prefix reuse by device block copy: copies KV rows [0, ntok) of every layer,
  * K/V and head from slot src_seq to slot dst_seq and sets dst's position to ntok.
  * ntok must be a positive multiple of QA_PREFIX_CHUNK and <= src's position.
@@ -174,9 +188,17 @@ int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float*
 /* Prefill -> decode KV handoff. qa_kv_send ships KV rows [0, ntok) of every layer, K|V and
  * local head of sequence `seq` to rank `peer`; the peer's matching qa_kv_recv stores them in
  * its slot `seq` and sets that sequence's position to ntok. Both contexts must hold the
- * same heads. 114,688*ntok bytes at 28 layers and 8 KV heads. Asynchronous on the stream. */
+ * same heads. 114,688*ntok bytes at 28 layers and 8 KV heads.
+ * Asynchronous and pipelined: the rows are packed on the context stream into one of two
+ * staging buffers and cross NVLink on the context's communication stream, so consecutive
+ * handoffs overlap (pack of request i+1 / unpack of request i-1 with the transfer of
+ * request i). Work queued later on the context stream is ordered after the pack (sender)
+ * or the unpack (receiver); the sender's context stream does not wait for the transfer
+ * itself: qa_comm_join or qa_sync does. */
 int qa_kv_send(qa_ctx* ctx, int seq, int ntok, int peer);
 int qa_kv_recv(qa_ctx* ctx, int seq, int ntok, int peer);
+/* Makes the context stream wait for all communication queued so far (no host wait). */
+int qa_comm_join(qa_ctx* ctx);
 
 /* Size of the fixed device array behind qa_attn_decode_noalloc: 4 MiB per GPU, held by
  * every GPU that loads the library until the process exits. */

@@ -3,9 +3,10 @@
 * KV-head sharding: each rank holds 4 of the 8 KV heads; prefill + decode outputs gathered
   with qa_gather_heads equal a single-GPU context holding all heads (within the attention
   tolerance), and each rank's KV bytes equal the matching heads of the single-GPU store.
-* Prefill -> decode handoff: rank 0 prefills, ships the KV rows to rank 1 with
-  qa_kv_send/qa_kv_recv; rank 1's KV bytes equal rank 0's bit for bit and its decode
-  output equals rank 0's.
+* Prefill -> decode handoff: rank 0 appends three sequences and ships their KV rows to
+  rank 1 back to back with qa_kv_send/qa_kv_recv (double-buffered staging, so the third
+  transfer reuses the first buffer); rank 1's KV bytes equal the same sequences appended
+  locally, bit for bit, and its positions are the sent row counts.
 NVLS is switched off (NCCL_NVLS_ENABLE=0) and ranks leave only between steps.
 """
 import os
@@ -103,31 +104,43 @@ def _worker(rank, world, port, out_dir):
                 kv_equal &= bool(np.array_equal(a, b))
     report["kv_equal"] = kv_equal
 
-    # prefill -> decode handoff of the full-head sequence: rank 0 sends slot 0, rank 1 receives into slot 1
+    # prefill -> decode handoff of three sequences back to back (the third reuses the first
+    # staging buffer): rank 0 sends its slots 0, 1, 2, rank 1 receives them into slots 1, 2, 3
+    # and compares every plane with the same sequences appended locally
     dist.barrier()
-    full_comm = qattn.Context(n_layers=L, context=1024, max_seqs=2, device=rank)
+    lens = (n, 150, 257)
+    full_comm = qattn.Context(n_layers=L, context=1024, max_seqs=4, device=rank)
     full_comm.set_stream(stream)
     H.set_norms(full_comm, qw, kw)
     qd.init_comm(full_comm)
-    if rank == 0:
-        qn = torch.empty_like(q[:, :n])
-        qp, kp, vp = q[:, :n].contiguous(), k[:, :n].contiguous(), v[:, :n].contiguous()
-        keep.extend((qp, kp, vp))
-        full_comm.append(0, 0, L, 0, n, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), qn.data_ptr())
-        full_comm.commit(0, n)
-        full_comm.kv_send(0, n, 1)
-    else:
-        full_comm.kv_recv(1, n, 0)
+    local_ref = qattn.Context(n_layers=L, context=1024, max_seqs=3, device=rank)
+    local_ref.set_stream(stream)
+    H.set_norms(local_ref, qw, kw)
+    for i, ln in enumerate(lens):
+        qi, ki, vi = H.inputs(300 + i, L, 0, ln)
+        keep.extend((qi, ki, vi))
+        dst = full_comm if rank == 0 else local_ref
+        qn_i = torch.empty_like(qi)
+        keep.append(qn_i)
+        dst.append(i, 0, L, 0, ln, qi.data_ptr(), ki.data_ptr(), vi.data_ptr(), qn_i.data_ptr())
+        dst.commit(i, ln)
+    for i, ln in enumerate(lens):
+        if rank == 0:
+            full_comm.kv_send(i, ln, 1)
+        else:
+            full_comm.kv_recv(i + 1, ln, 0)
     full_comm.sync()
+    local_ref.sync()
     if rank == 1:
         same = True
-        for layer in range(L):
-            for h in range(8):
-                for kvsel in (0, 1):
-                    same &= bool(np.array_equal(H.read_plane(full_comm, 1, layer, kvsel, h, 0, n),
-                                                H.read_plane(full, 0, layer, kvsel, h, 0, n)))
+        for i, ln in enumerate(lens):
+            for layer in range(L):
+                for h in range(8):
+                    for kvsel in (0, 1):
+                        same &= bool(np.array_equal(H.read_plane(full_comm, i + 1, layer, kvsel, h, 0, ln),
+                                                    H.read_plane(local_ref, i, layer, kvsel, h, 0, ln)))
         report["handoff_equal"] = same
-        report["handoff_pos"] = full_comm.position(1)
+        report["handoff_pos"] = [full_comm.position(i + 1) for i in range(3)]
     dist.barrier()
     full_comm.comm_destroy()
     shard.comm_destroy()
@@ -143,4 +156,4 @@ def test_head_sharded_gather_and_kv_handoff(tmp_path):
         assert rep["kv_equal"], rep
         assert rep["gather_max"] < H.MAX_ABS and rep["gather_rms"] < H.RMS, rep
         if rank == 1:
-            assert rep["handoff_equal"] and rep["handoff_pos"] == 300, rep
+            assert rep["handoff_equal"] and rep["handoff_pos"] == [300, 150, 257], rep

@@ -231,6 +231,10 @@ def test_validation_leaves_state_unchanged():
         lambda: ctx.truncate(0, 9),
         lambda: ctx.commit(0, 1),                                                                      # not appended
         lambda: ctx.copy_prefix(0, 1, 512),                                                            # too short
+        lambda: ctx.decode_step(0, 0, 2, 7, q.data_ptr(), k.data_ptr(), v.data_ptr(), 0, qn.data_ptr()),  # wrong pos
+        lambda: ctx.decode_step(0, 0, 2, 8, 0, k.data_ptr(), v.data_ptr(), 0, qn.data_ptr()),            # null input
+        lambda: ctx.decode_step_batch([0, 0], 0, 2, q.data_ptr(), k.data_ptr(), v.data_ptr(), 0,
+                                      qn.data_ptr()),                                                  # duplicate seq
     ]
     for case in cases:
         with pytest.raises(qattn.QAttnError):
@@ -487,3 +491,141 @@ def test_batched_decode_64_requests_many_segments_per_cta():
         ctx.commit_batch(seqs)
     assert all(ctx.position(s_) == lengths[s_] + steps for s_ in seqs)
     ctx.close()
+
+
+def _decode_ref_and_fused(L, P, steps, seed, q_out_too=True):
+    """Two contexts with the same P-row history: one decodes with qa_append + qa_attn_decode,
+    the other with the fused qa_decode_step. Returns per-step (ref, fused) outputs and the
+    contexts."""
+    ref, fus = make_ctx(L, context=4096), make_ctx(L, context=4096)
+    qw, kw = H.norms(seed, L)
+    for c in (ref, fus):
+        H.set_norms(c, qw, kw)
+    q, k, v = H.inputs(seed, L, 0, P + steps)
+    if P:
+        hist = [t[:, :P].contiguous() for t in (q, k, v)]
+        for c in (ref, fus):
+            gpu_append(c, 0, 0, *hist)
+            c.commit(0, P)
+    res = []
+    for st in range(steps):
+        p = P + st
+        q1, k1, v1 = (t[:, p:p + 1].contiguous() for t in (q, k, v))
+        qn_r, out_r = torch.empty_like(q1), torch.empty_like(q1)
+        ref.append(0, 0, L, p, 1, q1.data_ptr(), k1.data_ptr(), v1.data_ptr(), qn_r.data_ptr())
+        ref.attn_decode(0, 0, L, p, 1, qn_r.data_ptr(), out_r.data_ptr())
+        ref.commit(0, 1)
+        qn_f = torch.full_like(q1, float("nan"))
+        out_f = torch.full_like(q1, float("nan"))
+        fus.decode_step(0, 0, L, p, q1.data_ptr(), k1.data_ptr(), v1.data_ptr(),
+                        qn_f.data_ptr() if q_out_too else 0, out_f.data_ptr())
+        fus.commit(0, 1)
+        torch.cuda.synchronize()
+        res.append((qn_r, out_r, qn_f, out_f, (q1, k1, v1)))
+    return ref, fus, res, (qw, kw)
+
+
+@pytest.mark.parametrize("P", [0, 5, 3000])
+def test_fused_decode_step_is_bit_identical_to_append_then_decode(P):
+    """qa_decode_step (one launch) writes the same K/V bits and q_out as qa_append and returns
+    the same attention output bits as qa_attn_decode, including the first token (P = 0, the
+    new row is the only key) and a 3000-row history."""
+    L, steps = 28, 3
+    ref, fus, res, _ = _decode_ref_and_fused(L, P, steps, 70 + P)
+    for qn_r, out_r, qn_f, out_f, _ in res:
+        assert torch.equal(qn_r, qn_f)
+        assert torch.equal(out_r, out_f)
+    for layer in (0, 13, 27):
+        for h in range(8):
+            for kvsel in (0, 1):
+                assert np.array_equal(H.read_plane(ref, 0, layer, kvsel, h, 0, P + steps),
+                                      H.read_plane(fus, 0, layer, kvsel, h, 0, P + steps))
+    assert fus.position(0) == P + steps
+    ref.close(); fus.close()
+
+
+def test_fused_decode_step_without_q_out_and_against_the_oracle():
+    L, P, steps = 2, 140, 2
+    ref, fus, res, (qw, kw) = _decode_ref_and_fused(L, P, steps, 81, q_out_too=False)
+    for qn_r, out_r, qn_f, out_f, _ in res:
+        assert torch.equal(out_r, out_f)
+        assert torch.isnan(qn_f).all()            # q_out = NULL: nothing written
+    q, k, v = H.inputs(81, L, 0, P + steps)
+    qh, kh, vh = (t.cpu().numpy() for t in (q, k, v))
+    for layer in range(L):
+        kv, qref = oracle_layer(qh[layer], kh[layer], vh[layer], qw[layer], kw[layer], 0, ctx_len=4096)
+        for st in range(steps):
+            o = O.attention(kv, P + st, qref[P + st:P + st + 1], threads=8)[0]
+            mx, rms = H.err_stats(res[st][3][layer, 0].cpu().numpy(), o)
+            assert mx < H.MAX_ABS and rms < H.RMS, (layer, st, mx, rms)
+    ref.close(); fus.close()
+
+
+def test_fused_decode_step_batch_64_requests():
+    """qa_decode_step_batch over the 64 config-5 sequences equals qa_append_batch +
+    qa_attn_decode_batch bit for bit (outputs, q_out and the new K/V rows)."""
+    from fpga_qwen_b200 import dist as qd
+    L = 2
+    lengths = qd.config5_lengths()
+    S = len(lengths)
+    ctxs = [make_ctx(L, max_seqs=S, context=4096) for _ in range(2)]
+    qw, kw = H.norms(92, L)
+    for c in ctxs:
+        H.set_norms(c, qw, kw)
+    for s_, n in enumerate(lengths):
+        q, k, v = H.inputs(3000 + s_, L, 0, n)
+        for c in ctxs:
+            gpu_append(c, s_, 0, q, k, v)
+            c.commit(s_, n)
+        torch.cuda.synchronize()
+        del q, k, v
+    seqs = list(range(S))
+    for st in range(2):
+        rows = [H.inputs(3000 + s_, L, lengths[s_] + st, 1) for s_ in seqs]
+        qb, kb, vb = (torch.cat([r[i] for r in rows], dim=1).contiguous() for i in range(3))
+        qn_r, out_r = torch.empty_like(qb), torch.empty_like(qb)
+        ctxs[0].append_batch(seqs, 0, L, qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), qn_r.data_ptr())
+        ctxs[0].attn_decode_batch(seqs, 0, L, qn_r.data_ptr(), out_r.data_ptr())
+        qn_f, out_f = torch.full_like(qb, float("nan")), torch.full_like(qb, float("nan"))
+        ctxs[1].decode_step_batch(seqs, 0, L, qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), qn_f.data_ptr(),
+                                  out_f.data_ptr())
+        for c in ctxs:
+            c.commit_batch(seqs)
+        torch.cuda.synchronize()
+        assert torch.equal(qn_r, qn_f)
+        assert torch.equal(out_r, out_f)
+    for s_ in (0, 7, 40, 63):
+        n = lengths[s_] + 2
+        for kvsel in (0, 1):
+            assert np.array_equal(H.read_plane(ctxs[0], s_, 1, kvsel, 3, n - 3, 3),
+                                  H.read_plane(ctxs[1], s_, 1, kvsel, 3, n - 3, 3))
+    for c in ctxs:
+        c.close()
+
+
+def test_fused_decode_step_host_buffers():
+    """The io_host form of qa_decode_step (host input/output arrays, copies inside the call)
+    gives the device form's results."""
+    L, P = 4, 200
+    dev = make_ctx(L, context=1024)
+    host = qattn.Context(n_layers=L, context=1024, io_host=1)
+    qw, kw = H.norms(93, L)
+    q, k, v = H.inputs(93, L, 0, P + 1)
+    for c in (dev, host):
+        H.set_norms(c, qw, kw)
+    gpu_append(dev, 0, 0, *(t[:, :P].contiguous() for t in (q, k, v)))
+    dev.commit(0, P)
+    qh, kh, vh = (np.ascontiguousarray(t[:, :P].cpu().numpy()) for t in (q, k, v))
+    qo = np.empty_like(qh)
+    host.append(0, 0, L, 0, P, qh.ctypes.data, kh.ctypes.data, vh.ctypes.data, qo.ctypes.data)
+    host.commit(0, P)
+    q1, k1, v1 = (t[:, P:P + 1].contiguous() for t in (q, k, v))
+    qn_d, out_d = torch.empty_like(q1), torch.empty_like(q1)
+    dev.decode_step(0, 0, L, P, q1.data_ptr(), k1.data_ptr(), v1.data_ptr(), qn_d.data_ptr(), out_d.data_ptr())
+    torch.cuda.synchronize()
+    qh1, kh1, vh1 = (np.ascontiguousarray(t.cpu().numpy()) for t in (q1, k1, v1))
+    qn_h, out_h = np.empty_like(qh1), np.empty_like(qh1)
+    host.decode_step(0, 0, L, P, qh1.ctypes.data, kh1.ctypes.data, vh1.ctypes.data, qn_h.ctypes.data, out_h.ctypes.data)
+    assert np.array_equal(qn_h, qn_d.cpu().numpy())
+    assert np.array_equal(out_h, out_d.cpu().numpy())
+    dev.close(); host.close()
