@@ -45,6 +45,11 @@ def prefill_flops(pos0: int, n: int, layers: int = L, heads: int = HQ) -> float:
     return 4.0 * D * heads * layers * keys
 
 
+# The fused decode step also reads the new row's pre-norm k and v (FP32) and writes its FP16
+# K and V rows: 344,064 B per step over all layers and heads, on top of decode_bytes.
+STEP_APPEND_BYTES = L * HKV * D * (4 + 4 + 2 + 2)
+
+
 def decode_bytes(ctx_len: int, layers: int = L, hkv: int = HKV) -> float:
     hq = 2 * hkv
     return layers * hkv * ctx_len * D * 2 * 2 + 2 * layers * hq * D * 4
@@ -274,17 +279,24 @@ def run_ours(args):
         ctx.commit(0, PREFILL)
         for s in range(DECODE):
             pos = PREFILL + s
-            ctx.append(0, 0, L, pos, 1, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), dqn.data_ptr())
-            if evs:
-                evs["d0"][s].record(stream)
-            ctx.attn_decode(0, 0, L, pos, 1, dqn.data_ptr(), dout.data_ptr())
+            if args.split_decode:       # qa_append then qa_attn_decode (two launches)
+                ctx.append(0, 0, L, pos, 1, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), dqn.data_ptr())
+                if evs:
+                    evs["d0"][s].record(stream)
+                ctx.attn_decode(0, 0, L, pos, 1, dqn.data_ptr(), dout.data_ptr())
+                launches += 2
+            else:                       # fused decode step: append of the new row + attention, one launch
+                if evs:
+                    evs["d0"][s].record(stream)
+                ctx.decode_step(0, 0, L, pos, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), 0,
+                                dout.data_ptr())
+                launches += 1
             if world > 1:
                 ctx.gather_heads(L, 1, dout.data_ptr(), dfull.data_ptr())
                 launches += 1
             if evs:
                 evs["d1"][s].record(stream)
             ctx.commit(0, 1)
-            launches += 2
         if evs:
             evs["e"].record(stream)
         launches_per_step = launches
@@ -329,12 +341,13 @@ def run_ours(args):
     total_ms, prefill_phase, decode_phase, pattn, dattn = t.tolist()
 
     dec_bytes = sum(decode_bytes(PREFILL + s + 1) for s in range(DECODE))      # whole job (all heads)
+    kern_bytes = dec_bytes + (0 if args.split_decode else STEP_APPEND_BYTES * DECODE)
     pre_flops = prefill_flops(0, PREFILL)
     hbm_peak, tf_peak, peak_kind = load_peaks()
     value = dec_bytes / (decode_phase * 1e-3) / 1e9
     line = None
     if rank == 0:
-        dec_kernel_gbs = dec_bytes / world / (dattn * 1e-3) / 1e9     # this GPU's kernel bytes / kernel time
+        dec_kernel_gbs = kern_bytes / world / (dattn * 1e-3) / 1e9    # this GPU's kernel bytes / kernel time
         pre_kernel_tfs = pre_flops / world / (pattn * 1e-3) / 1e12
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -356,9 +369,11 @@ def run_ours(args):
                                      "kernel_ms": round(pattn, 3)}},
             "roofline": {"bound": "hbm", "achieved": round(dec_kernel_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(dec_kernel_gbs / hbm_peak, 4),
-                         "traffic": round(DECODE_TRAFFIC_RATIO * dec_bytes / DECODE / world),
-                         "algorithmic_bytes": round(dec_bytes / DECODE / world), "peak_kind": peak_kind,
-                         "kernel": "attn_decode (28 layers per launch)",
+                         "traffic": round(DECODE_TRAFFIC_RATIO * kern_bytes / DECODE / world),
+                         "algorithmic_bytes": round(kern_bytes / DECODE / world), "peak_kind": peak_kind,
+                         "kernel": ("attn_decode (28 layers per launch)" if args.split_decode else
+                                    "fused decode step: append of the new row + attn_decode, 28 layers per launch")
+                                   + (" + head gather" if world > 1 else ""),
                          "kernel_us": round(dattn / DECODE * 1e3, 2)},
             "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
@@ -400,7 +415,7 @@ def e2e_decode(args, seed):
     dk = [host(1, PREFILL + s, 1, HKV) for s in range(DECODE)]
     dv = [host(2, PREFILL + s, 1, HKV) for s in range(DECODE)]
     pqn, pout = torch.empty_like(pq).pin_memory(), torch.empty_like(pq).pin_memory()
-    dqn, dout = torch.empty_like(dq[0]).pin_memory(), torch.empty_like(dq[0]).pin_memory()
+    dout = torch.empty_like(dq[0]).pin_memory()
     times = []
     for it in range(args.warmup + args.steps):
         ctx.reset(0)
@@ -410,8 +425,7 @@ def e2e_decode(args, seed):
         t0 = time.perf_counter()
         for s in range(DECODE):
             pos = PREFILL + s
-            ctx.append(0, 0, L, pos, 1, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), dqn.data_ptr())
-            ctx.attn_decode(0, 0, L, pos, 1, dqn.data_ptr(), dout.data_ptr())
+            ctx.decode_step(0, 0, L, pos, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), 0, dout.data_ptr())
             ctx.commit(0, 1)
         t1 = time.perf_counter()
         if it >= args.warmup:
@@ -419,11 +433,12 @@ def e2e_decode(args, seed):
     ctx.close()
     dec_bytes = sum(decode_bytes(PREFILL + s + 1) for s in range(DECODE))
     t = statistics.median(times)
-    per_step_in = (HQ + 2 * HKV) * D * 4 * L + HQ * D * 4 * L     # q/k/v in + q_out back in
-    per_step_out = 2 * HQ * D * 4 * L                               # q_out and attention out
+    per_step_in = (HQ + 2 * HKV) * D * 4 * L                        # pre-norm q, k, v of the new row
+    per_step_out = HQ * D * 4 * L                                   # attention output
     return {"value": round(dec_bytes / t / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": per_step_in * DECODE,
             "d2h_bytes_per_step": per_step_out * DECODE,
-            "note": "128 decode steps per step, host wall clock around C-ABI calls with host buffers"}
+            "note": "128 fused decode steps (qa_decode_step, io_host) per step, host wall clock around the "
+                    "C-ABI calls with host buffers"}
 
 
 def run_config5(args):
@@ -531,9 +546,15 @@ def run_config5(args):
             torch.cuda.synchronize()
             d0.record(stream)
             for st in range(DECODE):
-                ctx.append_batch(slots, 0, L, dq[st].data_ptr(), dk[st].data_ptr(), dv[st].data_ptr(), dqn.data_ptr())
-                k0[st].record(stream)
-                ctx.attn_decode_batch(slots, 0, L, dqn.data_ptr(), dout.data_ptr())
+                if args.split_decode:
+                    ctx.append_batch(slots, 0, L, dq[st].data_ptr(), dk[st].data_ptr(), dv[st].data_ptr(),
+                                     dqn.data_ptr())
+                    k0[st].record(stream)
+                    ctx.attn_decode_batch(slots, 0, L, dqn.data_ptr(), dout.data_ptr())
+                else:
+                    k0[st].record(stream)
+                    ctx.decode_step_batch(slots, 0, L, dq[st].data_ptr(), dk[st].data_ptr(), dv[st].data_ptr(), 0,
+                                          dout.data_ptr())
                 k1[st].record(stream)
                 ctx.commit_batch(slots)
             d1.record(stream)
@@ -562,7 +583,8 @@ def run_config5(args):
     if rank == 0:
         hbm_peak, tf_peak, peak_kind = load_peaks()
         value = dec_bytes / (dec_ms * 1e-3) / 1e9
-        kern_gbs = dec_bytes / groups / (kern_ms * 1e-3) / 1e9
+        kern_gbs = (dec_bytes + (0 if args.split_decode else STEP_APPEND_BYTES * DECODE * len(lengths))) \
+            / groups / (kern_ms * 1e-3) / 1e9
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(pre_ms + hand_ms + dec_ms, 3), "higher_is_better": True,
@@ -578,7 +600,7 @@ def run_config5(args):
                         "unit": "TFLOP/s", "phase_ms": round(pre_ms, 3)},
             "roofline": {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(kern_gbs / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind,
-                         "kernel": "attn_decode batched over the GPU's requests (28 layers per launch)",
+                         "kernel": "fused decode step batched over the GPU's requests (28 layers per launch)",
                          "kernel_us": round(kern_ms * 1e3 / DECODE, 2),
                          "note": "per decode GPU; slowest GPU's kernel time"},
         }
@@ -599,12 +621,12 @@ def run_config5(args):
 def run_profile_case(args):
     """Small, self-contained launches of one kernel for ncu captures (few GB on the device,
     few launches before the captured ones):
-      decode   28 layers with a 3968-row KV history built chunk by chunk, then 3 decode steps
-               (each attn_decode launch reads 470 MB of KV, more than L2)
+      decode   28 layers with a 3968-row KV history built chunk by chunk, then 3 fused decode
+               steps (each launch reads 470 MB of KV, more than L2)
       prefill  4 layers, 3968-row prefill (append + attention) repeated 3 times
       append   28 layers x 1024-row append repeated 3 times
-      decode_batch  8 sequences with the first 8 config-5 prompt lengths, then 3 batched decode
-               steps (each launch reads ~1.8 GB of KV)"""
+      decode_batch  8 sequences with the first 8 config-5 prompt lengths, then 3 batched fused
+               decode steps (each launch reads ~1.8 GB of KV)"""
     import torch
     from fpga_qwen_b200 import qattn
     dev = torch.device("cuda", 0)
@@ -635,9 +657,8 @@ def run_profile_case(args):
         for s in range(3):
             q = torch.randn((layers, nseq, HQ, D), device=dev)
             k, v = torch.randn((layers, nseq, HKV, D), device=dev), torch.randn((layers, nseq, HKV, D), device=dev)
-            qn, out = torch.empty_like(q), torch.empty_like(q)
-            ctx.append_batch(slots, 0, layers, q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr())
-            ctx.attn_decode_batch(slots, 0, layers, qn.data_ptr(), out.data_ptr())
+            out = torch.empty_like(q)
+            ctx.decode_step_batch(slots, 0, layers, q.data_ptr(), k.data_ptr(), v.data_ptr(), 0, out.data_ptr())
             ctx.commit_batch(slots)
             torch.cuda.synchronize()
     elif args.profile_case == "decode":
@@ -652,9 +673,8 @@ def run_profile_case(args):
         for s in range(3):
             pos = PREFILL + s
             q, k, v = synth(0, pos, 1, HQ), synth(1, pos, 1, HKV), synth(2, pos, 1, HKV)
-            qn, out = torch.empty_like(q), torch.empty_like(q)
-            ctx.append(0, 0, layers, pos, 1, q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr())
-            ctx.attn_decode(0, 0, layers, pos, 1, qn.data_ptr(), out.data_ptr())
+            out = torch.empty_like(q)
+            ctx.decode_step(0, 0, layers, pos, q.data_ptr(), k.data_ptr(), v.data_ptr(), 0, out.data_ptr())
             ctx.commit(0, 1)
     else:
         n = PREFILL if args.profile_case == "prefill" else 1024
@@ -683,6 +703,8 @@ def main():
     ap.add_argument("--workload", choices=["config4", "config5"], default="config4",
                     help="config4: head-sharded 3968+128 (the metric's config); config5: 64 requests, request-sharded")
     ap.add_argument("--disagg", action="store_true", help="config5: prefill on the first half of the GPUs, decode on the rest")
+    ap.add_argument("--split-decode", action="store_true",
+                    help="decode with qa_append + qa_attn_decode (two launches) instead of the fused qa_decode_step")
     ap.add_argument("--profile-case", choices=["decode", "prefill", "append", "decode_batch"], default=None,
                     help="run a small single-kernel case for ncu instead of the benchmark")
     args = ap.parse_args()
