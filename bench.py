@@ -74,7 +74,7 @@ def load_peaks():
 
 # ------------------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms around the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -85,17 +85,32 @@ class ClockSampler:
         self.proc = None
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
 
+    def _lines(self):
+        self.file.flush()
+        try:
+            return len(Path(self.file.name).read_text().splitlines())
+        except OSError:
+            return 0
+
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        # the timed region starts only once the sampler is producing samples
+        t0 = time.time()
+        while self.proc and self._lines() == 0 and time.time() - t0 < 5.0:
+            time.sleep(0.01)
+        self.first = self._lines()
         return self
 
     def __exit__(self, *exc):
         if self.proc:
+            t0 = time.time()                 # at least one sample taken after the region started
+            while self._lines() <= self.first and time.time() - t0 < 1.0:
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)

@@ -27,13 +27,15 @@
 // host, stops consuming, drains its outstanding copies and exits.
 //
 // Fused decode step (FUSED = true): the kernel also performs the append of the one new row
-// per sequence (core.cpp:395-406 for a single token), so a decode step is one launch. At the
-// start of each segment the CTA normalises and rotates the unit's two query rows from the
-// pre-norm input (norm_rope.cuh, the same arithmetic as kv_append, so q_out and the
-// attention input are bit-identical to an append followed by a decode); the copy ring keeps
-// filling meanwhile. The new row is the last key of its unit, so exactly one CTA reads it:
-// that CTA builds the FP16 K and V rows, stores them in the KV store (and q_out), and patches
-// them into the ring chunk that holds the stale row before scoring it.
+// per sequence (core.cpp:395-406 for a single token), so a decode step is one launch. Before
+// its first segment the CTA normalises and rotates the query rows of every unit its range
+// touches (at most FUSED_MAX_UNITS; the host falls back to append + decode otherwise) from the
+// pre-norm input (norm_rope.cuh, the same arithmetic as kv_append, so q_out and the attention
+// input are bit-identical to an append followed by a decode). Each row's sequential FP64 sum
+// runs on its own lane, all rows at once, while the copy ring fills. The new row is the last
+// key of its unit, so exactly one CTA reads it: that CTA builds the FP16 K and V rows, stores
+// them in the KV store (and q_out), and patches them into the ring chunk that holds the stale
+// row before scoring it.
 #include <algorithm>
 
 #include "norm_rope.cuh"
@@ -128,9 +130,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
     __shared__ float stat[2 * GROUP];
     __shared__ float accbuf[HALF_WARPS][GROUP][D];
     __shared__ int is_last, abort_flag, never_abort;
-    __shared__ __align__(16) float s_q[GROUP][D];          // fused: the unit's normalised query rows
-    __shared__ __align__(16) __half s_new[2][D];           // fused: the new K and V rows (FP16)
-    __shared__ float s_inv[3];
+    constexpr int QB = FUSED ? FUSED_MAX_UNITS : 1;
+    __shared__ __align__(16) float s_q[QB][GROUP][D];      // fused: normalised query rows of unit i
+    __shared__ __align__(16) __half s_new[QB][2][D];       // fused: the new K and V rows (FP16)
+    __shared__ float s_inv[QB][3];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hw = tid >> 4, sl = tid & 15;
@@ -188,8 +191,73 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         for (int i = 0; i < NST && g_begin < g_end; ++i) produce();
     }
 
+    if constexpr (FUSED) {
+        // ---- append of the new rows of the units this range touches (i-th unit: unit_at(i)) ----
+        auto unit_at = [&](int i) {
+            Unit w = u;
+            for (int k = 0; k < i; ++k) next_unit(a, w);
+            return w;
+        };
+        if (tid < 3 * QB) {                            // one lane per sequential FP64 chain
+            const int i = tid / 3, r = tid - 3 * i;    // rows: query head 0, query head 1, key
+            const Unit w = unit_at(i);
+            if (w.off < g_end && (r < 2 || w.off + w.len <= g_end)) {
+                const float* x = r < 2 ? a.step.q_pre + ((((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP) + r) * D
+                                       : a.step.k_pre + (((size_t)w.l * a.n + w.b) * a.hkv + w.kh) * D;
+                s_inv[i][r] = rms_inv(x, a.step.eps);
+            }
+        }
+        __syncthreads();
+        for (int idx = tid; idx < QB * 4 * 64; idx += THREADS) {
+            const int i = idx >> 8, r = (idx >> 6) & 3, j = idx & 63;   // unit, row (q0 q1 k v), pair j
+            const Unit w = unit_at(i);
+            const bool owns = w.off + w.len <= g_end;                   // the new row is in this range
+            if (w.off >= g_end || (r >= 2 && !owns)) continue;
+            const int layer = a.layer0 + w.l, pos = w.len - 1;
+            const size_t qrow_w = ((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP;
+            const size_t krow_w = ((size_t)w.l * a.n + w.b) * a.hkv + w.kh;
+            if (r == 3) {                                               // V: plain FP16 rounding
+                const float* vp = a.step.v_pre + krow_w * D;
+                s_new[i][1][j] = __float2half_rn(vp[j]);
+                s_new[i][1][j + 64] = __float2half_rn(vp[j + 64]);
+                continue;
+            }
+            const float* w8 = a.step.norms + (size_t)layer * 2 * D + (r == 2 ? D : 0);
+            const float* x = r < 2 ? a.step.q_pre + (qrow_w + r) * D : a.step.k_pre + krow_w * D;
+            const float c = a.step.cosines[(size_t)pos * 64 + j], sn = a.step.sines[(size_t)pos * 64 + j];
+            float ra, rb;
+            norm_rope_pair(x[j], x[j + 64], w8[j], w8[j + 64], c, sn, s_inv[i][r], ra, rb);
+            if (r == 2) {
+                s_new[i][0][j] = __float2half_rn(ra);
+                s_new[i][0][j + 64] = __float2half_rn(rb);
+            } else {
+                s_q[i][r][j] = ra;
+                s_q[i][r][j + 64] = rb;
+                if (owns && a.step.q_out) {
+                    a.step.q_out[(qrow_w + r) * D + j] = ra;
+                    a.step.q_out[(qrow_w + r) * D + j + 64] = rb;
+                }
+            }
+        }
+        __syncthreads();
+        if (tid < QB * 32) {                          // store the new K and V rows, 16 B per lane
+            const int i = tid >> 5, kv = (tid >> 4) & 1, c16 = tid & 15;
+            const Unit w = unit_at(i);
+            if (w.off < g_end && w.off + w.len <= g_end) {
+                __half* dst = a.kv.plane(a.seq[w.b], a.layer0 + w.l, kv, w.kh) + (size_t)(w.len - 1) * D;
+                reinterpret_cast<uint4*>(dst)[c16] = reinterpret_cast<const uint4*>(s_new[i][kv])[c16];
+            }
+        }
+    }
+
+    int si = -1;                                       // segment index within this range
     for (long long g = g_begin; g < g_end;) {
         if (g != g_begin) next_unit(a, u);
+        ++si;
+        if (FUSED && si >= QB) {                       // the host bounds units per range; never expected
+            if (tid == 0) atomicCAS(a.error, 0, 42);
+            break;
+        }
         const int k0 = (int)(g - u.off);
         const int cnt = (int)min((long long)u.len, g_end - u.off) - k0;
         const int nch = (cnt + CH - 1) / CH;
@@ -201,51 +269,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         const bool owns_new = FUSED && k0 + cnt == u.len;
         float q[GROUP][8];
         if constexpr (FUSED) {
-            const int layer = a.layer0 + u.l;
-            const int pos = u.len - 1;                          // position of the new row
-            const size_t krow = ((size_t)u.l * a.n + u.b) * a.hkv + u.kh;
-            const float* qp = a.step.q_pre + qrow * D;
-            const float* kp = a.step.k_pre + krow * D;
-            // the three sequential FP64 chains run on three warps at once
-            if (tid == 0) s_inv[0] = rms_inv(qp, a.step.eps);
-            else if (tid == 32) s_inv[1] = rms_inv(qp + D, a.step.eps);
-            else if (tid == 64 && owns_new) s_inv[2] = rms_inv(kp, a.step.eps);
-            __syncthreads();
-            {
-                const int r = tid >> 6, j = tid & 63;           // query head r, channel pair (j, j+64)
-                const float* w = a.step.norms + (size_t)layer * 2 * D;
-                const float c = a.step.cosines[(size_t)pos * 64 + j], sn = a.step.sines[(size_t)pos * 64 + j];
-                float ra, rb;
-                norm_rope_pair(qp[r * D + j], qp[r * D + j + 64], w[j], w[j + 64], c, sn, s_inv[r], ra, rb);
-                s_q[r][j] = ra;
-                s_q[r][j + 64] = rb;
-                if (owns_new) {
-                    if (a.step.q_out) {
-                        a.step.q_out[(qrow + r) * D + j] = ra;
-                        a.step.q_out[(qrow + r) * D + j + 64] = rb;
-                    }
-                    if (tid < 64) {                             // K row pair j
-                        float ka, kb;
-                        norm_rope_pair(kp[j], kp[j + 64], w[D + j], w[D + j + 64], c, sn, s_inv[2], ka, kb);
-                        s_new[0][j] = __float2half_rn(ka);
-                        s_new[0][j + 64] = __float2half_rn(kb);
-                    } else {                                    // V row channels 2i, 2i+1
-                        const int c2 = 2 * (tid - 64);
-                        const float* vp = a.step.v_pre + krow * D;
-                        *reinterpret_cast<__half2*>(&s_new[1][c2]) = __floats2half2_rn(vp[c2], vp[c2 + 1]);
-                    }
-                }
-            }
-            __syncthreads();
-            if (owns_new && tid < 32) {                         // store the new rows (16 B per lane)
-                const int kv = tid >> 4, c16 = tid & 15;
-                __half* dst = a.kv.plane(a.seq[u.b], layer, kv, u.kh) + (size_t)pos * D;
-                reinterpret_cast<uint4*>(dst)[c16] = reinterpret_cast<const uint4*>(s_new[kv])[c16];
-            }
             #pragma unroll
             for (int gq = 0; gq < GROUP; ++gq)
                 #pragma unroll
-                for (int e = 0; e < 8; ++e) q[gq][e] = s_q[gq][sl * 8 + e] * qscale;
+                for (int e = 0; e < 8; ++e) q[gq][e] = s_q[si][gq][sl * 8 + e] * qscale;
         } else {
             #pragma unroll
             for (int gq = 0; gq < GROUP; ++gq) {
@@ -277,7 +304,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
                 // the last chunk of each pass holds the new row, copied before it was written:
                 // replace it with the row built above (CTA-uniform branch)
                 if (tid < 16)
-                    reinterpret_cast<uint4*>(buf + (keys - 1) * 256)[tid] = reinterpret_cast<const uint4*>(s_new[is_v])[tid];
+                    reinterpret_cast<uint4*>(buf + (keys - 1) * 256)[tid] = reinterpret_cast<const uint4*>(s_new[si][is_v])[tid];
                 __syncthreads();
             }
             if (got) {
@@ -479,6 +506,11 @@ DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos) {
     // a unit of len keys meets at most floor(len*C/T) + 2 of the C ranges
     p.max_records = (int)(((long long)max_len * ctas) / p.total_keys) + 2;
     p.units = n_layers * n * hkv;
+    // a range of R keys meets at most ceil(R / shortest unit) + 1 units
+    int min_len = max_len;
+    for (int b = 0; b < n; ++b) min_len = std::min(min_len, pos[b] + 1);
+    const long long range = (p.total_keys + ctas - 1) / ctas;
+    p.max_units_per_cta = (int)std::min<long long>((range + min_len - 1) / min_len + 1, 1 << 30);
     return p;
 }
 

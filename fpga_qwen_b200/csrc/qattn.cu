@@ -558,6 +558,10 @@ int qa_attn_decode_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_l
 }
 
 // ---- fused decode step: append of one new row per sequence + decode attention, one launch ----
+static size_t qn_floats(const qa_ctx* ctx, int n, int n_layers) { return (size_t)n_layers * n * ctx->hq * D; }
+static size_t kn_floats(const qa_ctx* ctx, int n, int n_layers) { return (size_t)n_layers * n * ctx->hkv * D; }
+// io_host staging of a decode step: [q_pre][k_pre][v][q_out][out]
+static size_t qn_off_io(size_t qn, size_t kn) { return qn + 2 * kn; }
 static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int layer, int n_layers,
                        const float* q_pre, const float* k_pre, const float* v, float* q_out, float* out) {
     int st;
@@ -574,14 +578,38 @@ static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int 
         QA_CUDA(cudaMemcpyAsync(sg + qn, k_pre, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
         QA_CUDA(cudaMemcpyAsync(sg + qn + kn, v, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
         in.q_pre = sg; in.k_pre = sg + qn; in.v_pre = sg + qn + kn;
-        in.q_out = q_out ? sg + qn + 2 * kn : nullptr;
+        in.q_out = q_out ? sg + qn_off_io(qn, kn) : nullptr;
         od = sg + 2 * qn + 2 * kn;
     }
     in.norms = ctx->norms; in.cosines = ctx->cosines; in.sines = ctx->sines; in.eps = ctx->cfg.norm_eps;
     const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
     if ((st = ensure_decode_scratch(ctx, plan))) return st;
-    launch_attn_decode_sm100(plan, ctx->kv, nullptr, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
-                             ctx->partial, ctx->counters, ctx->error, ctx->stream, &in);
+    if (plan.max_units_per_cta <= FUSED_MAX_UNITS) {
+        launch_attn_decode_sm100(plan, ctx->kv, nullptr, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
+                                 ctx->partial, ctx->counters, ctx->error, ctx->stream, &in);
+    } else {
+        // Short contexts or many sequences per CTA range: the same results as append + decode,
+        // run as those two launches (the normalised query rows go to q_out or to staging).
+        float* qn = in.q_out;
+        if (!qn) {
+            if (ctx->cfg.io_host) {
+                qn = ctx->staging + qn_off_io(qn_floats(ctx, n, n_layers), kn_floats(ctx, n, n_layers));
+            } else {
+                if ((st = ensure_staging(ctx, qn_floats(ctx, n, n_layers)))) return st;
+                qn = ctx->staging;
+            }
+        }
+        AppendArgs ap{};
+        ap.q_pre = in.q_pre; ap.k_pre = in.k_pre; ap.v_pre = in.v_pre; ap.q_out = qn;
+        ap.kv = ctx->kv; ap.seq = seqs[0]; ap.layer0 = layer; ap.n_layers = n_layers; ap.pos0 = 0; ap.n = n;
+        ap.hq = ctx->hq; ap.hkv = ctx->hkv; ap.norms = ctx->norms; ap.cosines = ctx->cosines; ap.sines = ctx->sines;
+        ap.eps = ctx->cfg.norm_eps;
+        ap.rows.batched = 1;
+        for (int b = 0; b < n; ++b) { ap.rows.seq[b] = seqs[b]; ap.rows.pos[b] = pos[b]; }
+        launch_kv_append(ap, ctx->stream);
+        launch_attn_decode_sm100(plan, ctx->kv, qn, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
+                                 ctx->partial, ctx->counters, ctx->error, ctx->stream);
+    }
     if ((st = after_launch(ctx, n == 1 ? seqs[0] : -1, "attn_decode_step"))) return st;
     for (int b = 0; b < n; ++b)
         for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seqs[b]][l] = pos[b] + 1;

@@ -72,11 +72,15 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out
 // rows.pos[b] (context rows.pos[b] + 1), b < n <= MAX_BATCH.
 struct DecodePlan {
     int ctas, max_keys, max_records, units;
+    int max_units_per_cta;            // bound on the units one CTA range touches
     long long total_keys;
     size_t partial_floats() const;
 };
 DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos);
 // Inputs of a fused decode step (append of the one new row per sequence + decode attention).
+// The fused kernel prepares the rows of at most FUSED_MAX_UNITS units per CTA before it
+// streams; plans with more units per CTA run as append + decode.
+constexpr int FUSED_MAX_UNITS = 4;
 struct StepInputs {
     const float* q_pre = nullptr; const float* k_pre = nullptr; const float* v_pre = nullptr;   // [L][n][h][128]
     float* q_out = nullptr;                                    // optional

@@ -525,11 +525,13 @@ def _decode_ref_and_fused(L, P, steps, seed, q_out_too=True):
     return ref, fus, res, (qw, kw)
 
 
-@pytest.mark.parametrize("P", [0, 5, 3000])
+@pytest.mark.parametrize("P", [0, 5, 40, 3000])
 def test_fused_decode_step_is_bit_identical_to_append_then_decode(P):
-    """qa_decode_step (one launch) writes the same K/V bits and q_out as qa_append and returns
-    the same attention output bits as qa_attn_decode, including the first token (P = 0, the
-    new row is the only key) and a 3000-row history."""
+    """qa_decode_step writes the same K/V bits and q_out as qa_append and returns the same
+    attention output bits as qa_attn_decode: the first token (P = 0, the new row is the only
+    key), P = 5, P = 40 (one CTA range spans three units) and a 3000-row history. The short
+    contexts (P = 0, 5) take the entry point's append + decode fallback; the others run the
+    single fused kernel."""
     L, steps = 28, 3
     ref, fus, res, _ = _decode_ref_and_fused(L, P, steps, 70 + P)
     for qn_r, out_r, qn_f, out_f, _ in res:
@@ -629,3 +631,40 @@ def test_fused_decode_step_host_buffers():
     assert np.array_equal(qn_h, qn_d.cpu().numpy())
     assert np.array_equal(out_h, out_d.cpu().numpy())
     dev.close(); host.close()
+
+
+def test_fused_decode_step_batch_long_sequences():
+    """A batch whose CTA ranges stay within four units (three sequences of 3000-4000 rows,
+    28 layers) runs the fused kernel; it equals qa_append_batch + qa_attn_decode_batch."""
+    L, lengths = 28, [3000, 3500, 4000]
+    S = len(lengths)
+    ctxs = [make_ctx(L, max_seqs=S, context=4096) for _ in range(2)]
+    qw, kw = H.norms(94, L)
+    for c in ctxs:
+        H.set_norms(c, qw, kw)
+    for s_, n in enumerate(lengths):
+        q, k, v = H.inputs(4000 + s_, L, 0, n - 1)
+        for c in ctxs:
+            gpu_append(c, s_, 0, q, k, v)
+            c.commit(s_, n - 1)
+        torch.cuda.synchronize()
+        del q, k, v
+    seqs = list(range(S))
+    rows = [H.inputs(4000 + s_, L, lengths[s_] - 1, 1) for s_ in seqs]
+    qb, kb, vb = (torch.cat([r[i] for r in rows], dim=1).contiguous() for i in range(3))
+    qn_r, out_r = torch.empty_like(qb), torch.empty_like(qb)
+    ctxs[0].append_batch(seqs, 0, L, qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), qn_r.data_ptr())
+    ctxs[0].attn_decode_batch(seqs, 0, L, qn_r.data_ptr(), out_r.data_ptr())
+    qn_f, out_f = torch.full_like(qb, float("nan")), torch.full_like(qb, float("nan"))
+    ctxs[1].decode_step_batch(seqs, 0, L, qb.data_ptr(), kb.data_ptr(), vb.data_ptr(), qn_f.data_ptr(),
+                              out_f.data_ptr())
+    torch.cuda.synchronize()
+    ctxs[1].sync()
+    assert torch.equal(qn_r, qn_f)
+    assert torch.equal(out_r, out_f)
+    for s_, n in enumerate(lengths):
+        for kvsel in (0, 1):
+            assert np.array_equal(H.read_plane(ctxs[0], s_, 27, kvsel, 5, n - 1, 1),
+                                  H.read_plane(ctxs[1], s_, 27, kvsel, 5, n - 1, 1))
+    for c in ctxs:
+        c.close()
