@@ -198,6 +198,33 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             for (int k = 0; k < i; ++k) next_unit(a, w);
             return w;
         };
+        // Thread t owns channel pair j = t % 64 of rows {h, 2 + h} (h = t / 64) of every unit:
+        // rows 0, 1 are the query heads, 2 the key, 3 the value. All its inputs are loaded first,
+        // so those loads overlap the sequential FP64 sums below.
+        constexpr int TASKS = 2 * QB;
+        const int j = tid & 63, h = tid >> 6;
+        float xa[TASKS], xb[TASKS], wa[TASKS], wb[TASKS], cc[QB], ss[QB];
+        #pragma unroll
+        for (int i = 0; i < QB; ++i) {
+            const Unit w = unit_at(i);
+            const bool touched = w.off < g_end, owns = w.off + w.len <= g_end;
+            const int layer = a.layer0 + w.l, pos = w.len - 1;
+            const size_t qrow_w = ((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP;
+            const size_t krow_w = ((size_t)w.l * a.n + w.b) * a.hkv + w.kh;
+            const float* nw = a.step.norms + (size_t)layer * 2 * D;
+            cc[i] = touched ? __ldg(a.step.cosines + (size_t)pos * 64 + j) : 0.f;
+            ss[i] = touched ? __ldg(a.step.sines + (size_t)pos * 64 + j) : 0.f;
+            const float* xq = a.step.q_pre + (qrow_w + h) * D;                       // row h
+            const float* xk = (h == 0 ? a.step.k_pre : a.step.v_pre) + krow_w * D;   // row 2 + h
+            xa[2 * i] = touched ? __ldg(xq + j) : 0.f;
+            xb[2 * i] = touched ? __ldg(xq + j + 64) : 0.f;
+            wa[2 * i] = touched ? __ldg(nw + j) : 0.f;
+            wb[2 * i] = touched ? __ldg(nw + j + 64) : 0.f;
+            xa[2 * i + 1] = owns ? __ldg(xk + j) : 0.f;
+            xb[2 * i + 1] = owns ? __ldg(xk + j + 64) : 0.f;
+            wa[2 * i + 1] = owns && h == 0 ? __ldg(nw + D + j) : 0.f;
+            wb[2 * i + 1] = owns && h == 0 ? __ldg(nw + D + j + 64) : 0.f;
+        }
         if (tid < 3 * QB) {                            // one lane per sequential FP64 chain
             const int i = tid / 3, r = tid - 3 * i;    // rows: query head 0, query head 1, key
             const Unit w = unit_at(i);
@@ -208,34 +235,29 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             }
         }
         __syncthreads();
-        for (int idx = tid; idx < QB * 4 * 64; idx += THREADS) {
-            const int i = idx >> 8, r = (idx >> 6) & 3, j = idx & 63;   // unit, row (q0 q1 k v), pair j
+        #pragma unroll
+        for (int i = 0; i < QB; ++i) {
             const Unit w = unit_at(i);
-            const bool owns = w.off + w.len <= g_end;                   // the new row is in this range
-            if (w.off >= g_end || (r >= 2 && !owns)) continue;
-            const int layer = a.layer0 + w.l, pos = w.len - 1;
+            if (w.off >= g_end) continue;
+            const bool owns = w.off + w.len <= g_end;
             const size_t qrow_w = ((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP;
-            const size_t krow_w = ((size_t)w.l * a.n + w.b) * a.hkv + w.kh;
-            if (r == 3) {                                               // V: plain FP16 rounding
-                const float* vp = a.step.v_pre + krow_w * D;
-                s_new[i][1][j] = __float2half_rn(vp[j]);
-                s_new[i][1][j + 64] = __float2half_rn(vp[j + 64]);
-                continue;
-            }
-            const float* w8 = a.step.norms + (size_t)layer * 2 * D + (r == 2 ? D : 0);
-            const float* x = r < 2 ? a.step.q_pre + (qrow_w + r) * D : a.step.k_pre + krow_w * D;
-            const float c = a.step.cosines[(size_t)pos * 64 + j], sn = a.step.sines[(size_t)pos * 64 + j];
             float ra, rb;
-            norm_rope_pair(x[j], x[j + 64], w8[j], w8[j + 64], c, sn, s_inv[i][r], ra, rb);
-            if (r == 2) {
-                s_new[i][0][j] = __float2half_rn(ra);
-                s_new[i][0][j + 64] = __float2half_rn(rb);
-            } else {
-                s_q[i][r][j] = ra;
-                s_q[i][r][j + 64] = rb;
-                if (owns && a.step.q_out) {
-                    a.step.q_out[(qrow_w + r) * D + j] = ra;
-                    a.step.q_out[(qrow_w + r) * D + j + 64] = rb;
+            norm_rope_pair(xa[2 * i], xb[2 * i], wa[2 * i], wb[2 * i], cc[i], ss[i], s_inv[i][h], ra, rb);
+            s_q[i][h][j] = ra;
+            s_q[i][h][j + 64] = rb;
+            if (owns) {
+                if (a.step.q_out) {
+                    a.step.q_out[(qrow_w + h) * D + j] = ra;
+                    a.step.q_out[(qrow_w + h) * D + j + 64] = rb;
+                }
+                if (h == 0) {                          // key row: norm + rope, FP16
+                    norm_rope_pair(xa[2 * i + 1], xb[2 * i + 1], wa[2 * i + 1], wb[2 * i + 1], cc[i], ss[i],
+                                   s_inv[i][2], ra, rb);
+                    s_new[i][0][j] = __float2half_rn(ra);
+                    s_new[i][0][j + 64] = __float2half_rn(rb);
+                } else {                               // value row: FP16 rounding only
+                    s_new[i][1][j] = __float2half_rn(xa[2 * i + 1]);
+                    s_new[i][1][j + 64] = __float2half_rn(xb[2 * i + 1]);
                 }
             }
         }
