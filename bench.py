@@ -57,11 +57,11 @@ def decode_bytes(ctx_len: int, layers: int = L, hkv: int = HKV) -> float:
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture per kernel
 # (commands: `bench.py --profile-case decode|prefill` under ncu --set full):
-#   decode: 461.3 MB for a 28-layer launch at context 3971 whose algorithmic bytes are 455.9 MB,
-#           applied as a ratio to the average launch of the timed region;
-#   prefill: 279.3 MB for a 4-layer, 3968-row launch; traffic grows with the layer count.
-DECODE_TRAFFIC_RATIO = 461.27e6 / 455.90e6
-PREFILL_TRAFFIC_PER_LAYER = 279.28e6 / 4
+#   fused decode step: 463.06 MB for a 28-layer launch at context 3970 whose algorithmic bytes
+#           are 456.11 MB, applied as a ratio to the average launch of the timed region;
+#   prefill: 280.58 MB for a 4-layer, 3968-row launch; traffic grows with the layer count.
+DECODE_TRAFFIC_RATIO = 463.06e6 / 456.11e6
+PREFILL_TRAFFIC_PER_LAYER = 280.58e6 / 4
 
 
 def load_peaks():
