@@ -248,9 +248,11 @@ def run_ours(args):
 
     ctx = qattn.Context(n_layers=L, context=4096, max_seqs=1, kv_head_begin=head0, kv_head_count=hkv, device=local)
     ctx.set_stream(stream.cuda_stream)
+    peer_mapped = False
     if world > 1:
         from fpga_qwen_b200 import dist as qd
         qd.init_comm(ctx)           # NCCL communicator of the library (outputs gathered over NVLink)
+        peer_mapped = ctx.comm_info()[2]
 
     def synth(kind, pos0, n, heads, h0, mean=0.0, std=1.0):
         t = torch.empty((L, n, heads, D), dtype=torch.float32, device=dev)
@@ -294,6 +296,17 @@ def run_ours(args):
         ctx.commit(0, PREFILL)
         for s in range(DECODE):
             pos = PREFILL + s
+            if world > 1 and not (args.split_decode or args.nccl_gather):
+                # fused decode step whose kernel stores every output row into all ranks' buffers
+                if evs:
+                    evs["d0"][s].record(stream)
+                ctx.decode_step_gather(0, 0, L, pos, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), 0,
+                                       dfull.data_ptr())
+                launches += 2           # decode step + wait/copy
+                if evs:
+                    evs["d1"][s].record(stream)
+                ctx.commit(0, 1)
+                continue
             if args.split_decode:       # qa_append then qa_attn_decode (two launches)
                 ctx.append(0, 0, L, pos, 1, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), dqn.data_ptr())
                 if evs:
@@ -373,6 +386,9 @@ def run_ours(args):
                                    "head_dim 128, FP16 KV",
                        "prefill_tokens": PREFILL, "decode_steps": DECODE, "layers": L,
                        "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                       "head_gather": None if world == 1 else (
+                           "NCCL all-gather + permute" if (args.split_decode or args.nccl_gather or not peer_mapped)
+                           else "peer stores over NVLink inside the decode step"),
                        "l2": "inputs larger than L2 (470 MB KV read per decode step, 1.8 GB prefill inputs)"},
             "decode_phase_ms": round(decode_phase, 3),
             "prefill": {"metric": "prefill-attn TFLOP/s", "value": round(pre_flops / (prefill_phase * 1e-3) / 1e12, 3),
@@ -718,6 +734,8 @@ def main():
     ap.add_argument("--workload", choices=["config4", "config5"], default="config4",
                     help="config4: head-sharded 3968+128 (the metric's config); config5: 64 requests, request-sharded")
     ap.add_argument("--disagg", action="store_true", help="config5: prefill on the first half of the GPUs, decode on the rest")
+    ap.add_argument("--nccl-gather", action="store_true",
+                    help="N>1: gather decode outputs with NCCL after the step instead of peer stores inside it")
     ap.add_argument("--split-decode", action="store_true",
                     help="decode with qa_append + qa_attn_decode (two launches) instead of the fused qa_decode_step")
     ap.add_argument("--profile-case", choices=["decode", "prefill", "append", "decode_batch"], default=None,

@@ -57,6 +57,7 @@ constexpr int MAX_UNIT_KEYS = 4096;           // longest unit (QA_MAX_CONTEXT): 
 struct DecodeArgs {
     const float* q; float* out;               // [n_layers][n][hq][128]
     StepInputs step;                          // fused decode step only
+    GatherArgs g;                             // head gather through peer memory (out_hq == 0: off)
     KVLayout kv; int layer0, n_layers, n, hq, hkv;
     int seq[MAX_BATCH];                       // sequence slot of row b
     int pos[MAX_BATCH];                       // absolute position of row b (context pos+1)
@@ -272,6 +273,18 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         }
     }
 
+    // final output of (unit u, head gq of its pair, channel jc): this GPU's output buffer, or
+    // every rank's landing buffer when gathering heads through peer memory
+    auto store_out = [&](const Unit& uu, int gq, int jc, float val) {
+        if (a.g.out_hq == 0) {
+            a.out[((((size_t)uu.l * a.n + uu.b) * a.hq + (size_t)uu.kh * GROUP) + gq) * D + jc] = val;
+        } else {
+            const size_t o = ((((size_t)uu.l * a.n + uu.b) * a.g.out_hq + a.g.out_h0 + (size_t)uu.kh * GROUP) + gq) * D + jc;
+            a.out[o] = val;
+            for (int p = 0; p < a.g.n_peers; ++p) a.g.peer_out[p][o] = val;
+        }
+    };
+
     int si = -1;                                       // segment index within this range
     for (long long g = g_begin; g < g_end;) {
         if (g != g_begin) next_unit(a, u);
@@ -456,7 +469,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             #pragma unroll
             for (int i = 0; i < GROUP * D / THREADS; ++i) {
                 const int idx = tid + i * THREADS, gq = idx / D, jc = idx % D;
-                a.out[(qrow + gq) * D + jc] = o[i] / stat[GROUP + gq];
+                store_out(u, gq, jc, o[i] / stat[GROUP + gq]);
             }
         } else {
             const int unit = (u.l * a.n + u.b) * a.hkv + u.kh;
@@ -491,7 +504,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
                     for (int s = 0; s < nrec; ++s)
                         v += exp2f(__ldcg(recs + (size_t)s * PARTIAL_FLOATS + gq) - mall[gq]) *
                              __ldcg(recs + (size_t)s * PARTIAL_FLOATS + 4 + idx);
-                    a.out[(qrow + gq) * D + jc] = v / lall[gq];
+                    store_out(u, gq, jc, v / lall[gq]);
                 }
                 if (tid == 0) a.counters[unit] = 0;    // ready for the next call on this stream
             }
@@ -504,6 +517,21 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         while (consumed < issued) {
             mbar_wait(&full[consumed % NST], (consumed / NST) & 1, &never_abort, 500000000ull);
             ++consumed;
+        }
+    }
+    if (a.g.n_flags > 0) {
+        // every thread orders its own output stores (peers' memory included) at system scope;
+        // then the last CTA of the grid marks the step done in every rank's flags with a
+        // release store
+        __threadfence_system();
+        __syncthreads();
+        if (tid == 0) {
+            if (atomicAdd(a.g.done, 1u) == gridDim.x - 1) {
+                __threadfence_system();
+                for (int r = 0; r < a.g.n_flags; ++r)
+                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.g.flags[r]), "r"(a.g.step) : "memory");
+                *a.g.done = 0;                         // ready for the next launch on this stream
+            }
         }
     }
 }
@@ -538,10 +566,12 @@ DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos) {
 
 void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const float* q, float* out, int layer0,
                               int n_layers, int n, const int* seq, const int* pos, int hq, int hkv, float* partial,
-                              int* counters, int* error, cudaStream_t s, const StepInputs* step) {
+                              int* counters, int* error, cudaStream_t s, const StepInputs* step,
+                              const GatherArgs* gather) {
     DecodeArgs a{};
     a.q = q; a.out = out; a.kv = kv; a.layer0 = layer0; a.n_layers = n_layers; a.n = n; a.hq = hq; a.hkv = hkv;
     if (step) a.step = *step;
+    if (gather) a.g = *gather;
     a.start[0] = 0;
     for (int b = 0; b < n; ++b) { a.seq[b] = seq[b]; a.pos[b] = pos[b]; a.start[b + 1] = a.start[b] + pos[b] + 1; }
     a.total_keys = plan.total_keys; a.ctas = plan.ctas; a.max_keys = plan.max_keys;

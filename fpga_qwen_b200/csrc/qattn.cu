@@ -29,6 +29,7 @@ int nccl_comm_init(void** comm, int nranks, int rank, const char id_bytes[128], 
 void nccl_comm_destroy(void* comm);
 int nccl_all_gather_f32(void* comm, const float* send, float* recv, size_t count, cudaStream_t s, std::string& err);
 int nccl_send_recv_bytes(void* comm, void* buf, size_t bytes, int peer, bool send, cudaStream_t s, std::string& err);
+int nccl_all_gather_bytes(void* comm, const void* send, void* recv, size_t bytes, cudaStream_t s, std::string& err);
 }  // namespace qattn
 
 struct qa_ctx {
@@ -66,10 +67,30 @@ struct qa_ctx {
     cudaEvent_t kv_unpacked[2] = {nullptr, nullptr};
     cudaEvent_t kv_packed = nullptr;
     int kv_next = 0;
+    // Head gather through peer memory: one allocation per rank, [landing 0][landing 1][flags],
+    // mapped into every other rank with CUDA IPC. Landing buffers alternate by step.
+    char* peer_block = nullptr;
+    size_t landing_bytes = 0, flags_off = 0;
+    char* peer_base[MAX_RANKS] = {};       // every rank's allocation (this rank's at [rank])
+    bool peer_ok = false;
+    unsigned* gather_done = nullptr;       // CTAs of the gathering launch that finished
+    unsigned gather_step = 0;
+    float* step_out = nullptr;             // local output of the NCCL fallback
+    size_t step_out_bytes = 0;
     std::string err;
 };
 
 namespace {
+
+void peer_release(qa_ctx* ctx) {
+    for (int r = 0; r < MAX_RANKS; ++r) {
+        if (ctx->peer_base[r] && ctx->peer_base[r] != ctx->peer_block) cudaIpcCloseMemHandle(ctx->peer_base[r]);
+        ctx->peer_base[r] = nullptr;
+    }
+    cudaFree(ctx->peer_block);
+    cudaFree(ctx->gather_done);
+    ctx->peer_block = nullptr; ctx->gather_done = nullptr; ctx->peer_ok = false;
+}
 
 int fail(qa_ctx* c, int status, const char* fmt, ...) {
     if (c) {
@@ -294,6 +315,8 @@ void qa_destroy(qa_ctx* ctx) {
     for (cudaEvent_t e : ctx->kv_comm_done) if (e) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->kv_unpacked) if (e) cudaEventDestroy(e);
     if (ctx->kv_packed) cudaEventDestroy(ctx->kv_packed);
+    peer_release(ctx);
+    cudaFree(ctx->step_out);
     nccl_comm_destroy(ctx->comm);
     if (ctx->comm_stream) cudaStreamDestroy(ctx->comm_stream);
     for (cudaEvent_t e : ctx->comm_ev) if (e) cudaEventDestroy(e);
@@ -563,7 +586,8 @@ static size_t kn_floats(const qa_ctx* ctx, int n, int n_layers) { return (size_t
 // io_host staging of a decode step: [q_pre][k_pre][v][q_out][out]
 static size_t qn_off_io(size_t qn, size_t kn) { return qn + 2 * kn; }
 static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int layer, int n_layers,
-                       const float* q_pre, const float* k_pre, const float* v, float* q_out, float* out) {
+                       const float* q_pre, const float* k_pre, const float* v, float* q_out, float* out,
+                       const GatherArgs* gather = nullptr) {
     int st;
     if (!q_pre || !k_pre || !v || !out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
@@ -586,7 +610,7 @@ static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int 
     if ((st = ensure_decode_scratch(ctx, plan))) return st;
     if (plan.max_units_per_cta <= FUSED_MAX_UNITS) {
         launch_attn_decode_sm100(plan, ctx->kv, nullptr, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
-                                 ctx->partial, ctx->counters, ctx->error, ctx->stream, &in);
+                                 ctx->partial, ctx->counters, ctx->error, ctx->stream, &in, gather);
     } else {
         // Short contexts or many sequences per CTA range: the same results as append + decode,
         // run as those two launches (the normalised query rows go to q_out or to staging).
@@ -608,7 +632,7 @@ static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int 
         for (int b = 0; b < n; ++b) { ap.rows.seq[b] = seqs[b]; ap.rows.pos[b] = pos[b]; }
         launch_kv_append(ap, ctx->stream);
         launch_attn_decode_sm100(plan, ctx->kv, qn, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
-                                 ctx->partial, ctx->counters, ctx->error, ctx->stream);
+                                 ctx->partial, ctx->counters, ctx->error, ctx->stream, nullptr, gather);
     }
     if ((st = after_launch(ctx, n == 1 ? seqs[0] : -1, "attn_decode_step"))) return st;
     for (int b = 0; b < n; ++b)
@@ -720,6 +744,61 @@ int grow(qa_ctx* ctx, void** buf, size_t& have, size_t need) {
 }
 }  // namespace
 
+// Maps every rank's gather allocation into every other rank (collective over the context's
+// communicator). The peer path is used only if every rank succeeded; otherwise the gathering
+// decode step falls back to the NCCL all-gather. CUDA IPC failures are not errors.
+int peer_setup(qa_ctx* ctx) {
+    const int R = ctx->nranks;
+    if (R < 2 || R > MAX_RANKS) return QA_OK;
+    ctx->landing_bytes = ((size_t)ctx->cfg.n_layers * ctx->hq * R * D * sizeof(float) + 255) & ~size_t(255);
+    ctx->flags_off = 2 * ctx->landing_bytes;
+    const size_t total = ctx->flags_off + 256;
+    struct Slot { cudaIpcMemHandle_t h; int ok; int pad[3]; };
+    int local_ok = 0;
+    Slot mine{};
+    if (cudaMalloc(&ctx->peer_block, total) == cudaSuccess && cudaMalloc(&ctx->gather_done, sizeof(unsigned)) == cudaSuccess &&
+        cudaMemset(ctx->peer_block, 0, total) == cudaSuccess && cudaMemset(ctx->gather_done, 0, sizeof(unsigned)) == cudaSuccess &&
+        cudaIpcGetMemHandle(&mine.h, ctx->peer_block) == cudaSuccess)
+        local_ok = 1;
+    cudaGetLastError();
+    mine.ok = local_ok;
+    // exchange handles (one all-gather), open the peers', then agree (a second all-gather)
+    Slot* dslots = nullptr;
+    QA_CUDA(cudaMalloc(&dslots, sizeof(Slot) * R));
+    std::vector<Slot> slots(R);
+    std::string err;
+    int st = QA_OK;
+    do {
+        if (cudaMemcpy(dslots + ctx->rank, &mine, sizeof(Slot), cudaMemcpyHostToDevice) != cudaSuccess) { st = QA_ERR_CUDA; break; }
+        if ((st = nccl_all_gather_bytes(ctx->comm, dslots + ctx->rank, dslots, sizeof(Slot), ctx->comm_stream, err))) break;
+        if (cudaStreamSynchronize(ctx->comm_stream) != cudaSuccess) { st = QA_ERR_CUDA; break; }
+        if (cudaMemcpy(slots.data(), dslots, sizeof(Slot) * R, cudaMemcpyDeviceToHost) != cudaSuccess) { st = QA_ERR_CUDA; break; }
+        int ok = 1;
+        for (int r = 0; r < R; ++r) ok &= slots[r].ok;
+        if (ok) {
+            ctx->peer_base[ctx->rank] = ctx->peer_block;
+            for (int r = 0; r < R && ok; ++r) {
+                if (r == ctx->rank) continue;
+                void* p = nullptr;
+                if (cudaIpcOpenMemHandle(&p, slots[r].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) { ok = 0; cudaGetLastError(); }
+                else ctx->peer_base[r] = static_cast<char*>(p);
+            }
+        }
+        mine.ok = ok;
+        if (cudaMemcpy(dslots + ctx->rank, &mine, sizeof(Slot), cudaMemcpyHostToDevice) != cudaSuccess) { st = QA_ERR_CUDA; break; }
+        if ((st = nccl_all_gather_bytes(ctx->comm, dslots + ctx->rank, dslots, sizeof(Slot), ctx->comm_stream, err))) break;
+        if (cudaStreamSynchronize(ctx->comm_stream) != cudaSuccess) { st = QA_ERR_CUDA; break; }
+        if (cudaMemcpy(slots.data(), dslots, sizeof(Slot) * R, cudaMemcpyDeviceToHost) != cudaSuccess) { st = QA_ERR_CUDA; break; }
+        ok = 1;
+        for (int r = 0; r < R; ++r) ok &= slots[r].ok;
+        ctx->peer_ok = ok != 0;
+    } while (false);
+    cudaFree(dslots);
+    if (!ctx->peer_ok) peer_release(ctx);
+    if (st) return fail(ctx, st, "peer memory set-up: %s", err.empty() ? "CUDA error" : err.c_str());
+    return QA_OK;
+}
+
 // NCCL runs on the context's own communication stream: it waits for the work already on the
 // context stream, and the context stream waits for it (any stream handle works, including
 // the legacy default stream).
@@ -760,6 +839,12 @@ int qa_comm_init(qa_ctx* ctx, int nranks, int rank, const char id[128]) {
     const int st = nccl_comm_init(&ctx->comm, nranks, rank, id, err);
     if (st) return fail(ctx, st, "ncclCommInitRank: %s", err.c_str());
     ctx->nranks = nranks; ctx->rank = rank;
+    return peer_setup(ctx);
+}
+
+int qa_comm_info(const qa_ctx* ctx, int* nranks, int* rank, int* peer_mapped) {
+    if (!ctx || !nranks || !rank || !peer_mapped) return QA_ERR_INVALID;
+    *nranks = ctx->nranks; *rank = ctx->rank; *peer_mapped = ctx->peer_ok ? 1 : 0;
     return QA_OK;
 }
 
@@ -768,6 +853,8 @@ int qa_comm_destroy(qa_ctx* ctx) {
     if (ctx->comm) {
         cudaSetDevice(ctx->cfg.device);
         cudaStreamSynchronize(ctx->stream);
+        if (ctx->comm_stream) cudaStreamSynchronize(ctx->comm_stream);
+        peer_release(ctx);
         nccl_comm_destroy(ctx->comm);
         ctx->comm = nullptr;
     }
@@ -802,6 +889,45 @@ int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float*
     if ((st = comm_leave(ctx))) return st;
     launch_permute_heads(ctx->gather_buf, full, ctx->nranks, n_layers, n, ctx->hq, ctx->stream);
     return after_launch(ctx, -1, "permute_heads");
+}
+
+int qa_decode_step_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos, const float* q_pre,
+                          const float* k_pre, const float* v, float* q_out, float* full) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_rows(ctx, seq, layer, n_layers, pos, 1))) return st;
+    if (!ctx->comm) return fail(ctx, QA_ERR_STATE, "no communicator (qa_comm_init)");
+    if (ctx->cfg.io_host) return fail(ctx, QA_ERR_UNSUPPORTED, "qa_decode_step_gather takes device pointers");
+    if (!q_pre || !k_pre || !v || !full) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
+    if (ctx->cfg.kv_head_begin != ctx->rank * ctx->hkv || ctx->nranks * ctx->hkv != ctx->cfg.n_kv_heads)
+        return fail(ctx, QA_ERR_STATE, "rank %d holds KV heads [%d,%d): not the head shard the gather expects",
+                    ctx->rank, ctx->cfg.kv_head_begin, ctx->cfg.kv_head_begin + ctx->hkv);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    if (!ctx->peer_ok) {
+        // no peer mapping on this machine: local decode step, then the NCCL all-gather
+        const size_t bytes = (size_t)n_layers * ctx->hq * D * sizeof(float);
+        void* buf = ctx->step_out;
+        if ((st = grow(ctx, &buf, ctx->step_out_bytes, bytes))) return st;
+        ctx->step_out = static_cast<float*>(buf);
+        if ((st = decode_step(ctx, &seq, &pos, 1, layer, n_layers, q_pre, k_pre, v, q_out, ctx->step_out))) return st;
+        return qa_gather_heads(ctx, n_layers, 1, ctx->step_out, full);
+    }
+    const unsigned step = ++ctx->gather_step;
+    const size_t par = (size_t)(step & 1) * ctx->landing_bytes;
+    GatherArgs g{};
+    g.out_hq = ctx->hq * ctx->nranks;
+    g.out_h0 = ctx->rank * ctx->hq;
+    for (int r = 0; r < ctx->nranks; ++r) {
+        if (r != ctx->rank) g.peer_out[g.n_peers++] = reinterpret_cast<float*>(ctx->peer_base[r] + par);
+        g.flags[g.n_flags++] = reinterpret_cast<unsigned*>(ctx->peer_base[r] + ctx->flags_off) + ctx->rank;
+    }
+    g.done = ctx->gather_done;
+    g.step = step;
+    float* landing = reinterpret_cast<float*>(ctx->peer_block + par);
+    if ((st = decode_step(ctx, &seq, &pos, 1, layer, n_layers, q_pre, k_pre, v, q_out, landing, &g))) return st;
+    launch_gather_wait_copy(reinterpret_cast<const unsigned*>(ctx->peer_block + ctx->flags_off), ctx->nranks, step,
+                            landing, full, (size_t)n_layers * g.out_hq * D, ctx->error, ctx->stream);
+    return after_launch(ctx, -1, "gather_wait_copy");
 }
 
 static int kv_transfer(qa_ctx* ctx, int seq, int ntok, int peer, bool send) {

@@ -81,6 +81,20 @@ DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos);
 // The fused kernel prepares the rows of at most FUSED_MAX_UNITS units per CTA before it
 // streams; plans with more units per CTA run as append + decode.
 constexpr int FUSED_MAX_UNITS = 4;
+// Head gather through peer memory (decode step on KV-head shards): the kernel stores each
+// output row into the landing buffer of every rank (its own and, over NVLink, its peers'),
+// at this rank's head offset in the full-head layout, then its last CTA marks the step done
+// in every rank's flag array.
+constexpr int MAX_RANKS = 8;
+struct GatherArgs {
+    int out_hq = 0, out_h0 = 0;                  // heads per output row, this rank's first head
+    int n_peers = 0;
+    float* peer_out[MAX_RANKS] = {};             // other ranks' landing buffers (peer pointers)
+    int n_flags = 0;
+    unsigned* flags[MAX_RANKS] = {};             // word "rank me finished step" in each rank's flags
+    unsigned* done = nullptr;                    // CTAs finished (this GPU), zero between launches
+    unsigned step = 0;
+};
 struct StepInputs {
     const float* q_pre = nullptr; const float* k_pre = nullptr; const float* v_pre = nullptr;   // [L][n][h][128]
     float* q_out = nullptr;                                    // optional
@@ -90,7 +104,11 @@ struct StepInputs {
 void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const float* q, float* out, int layer0,
                               int n_layers, int n, const int* seq, const int* pos, int hq, int hkv, float* partial,
                               int* counters, int* error, cudaStream_t s,
-                              const StepInputs* step = nullptr);
+                              const StepInputs* step = nullptr, const GatherArgs* gather = nullptr);
+// Waits (bounded) until every rank marked `step` done in `flags`, then copies the landing
+// buffer to the caller's output. Error code 51 in *error when the wait runs out.
+void launch_gather_wait_copy(const unsigned* flags, int nranks, unsigned step, const float* landing, float* out,
+                             size_t floats, int* error, cudaStream_t s);
 // Rows at absolute positions below this go to the FP32 CUDA-core kernel.
 constexpr int TC_MIN_POSITION = 128;
 void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n,

@@ -13,12 +13,14 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "../../include/qattn.h"
 #include "qattn_common.cuh"
+#include "sm100.cuh"
 
 namespace qattn {
 namespace {
@@ -91,7 +93,39 @@ __global__ void pack_kv_kernel(const KVLayout kv, int seq, int ntok, uint4* buf,
     }
 }
 
+// One CTA per slice of the landing buffer: thread 0 waits until every rank has marked `step`
+// done (acquire at system scope; bounded by 2 s of global time, error code 51 on expiry), then
+// the CTA copies its slice. Peers wrote the landing buffer over NVLink before their release.
+__global__ void gather_wait_copy_kernel(const unsigned* flags, int nranks, unsigned step, const float4* landing,
+                                        float4* out, size_t n4, int* error) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        ok = 1;
+        const uint64_t t0 = sm100::globaltimer();
+        for (int r = 0; r < nranks && ok; ++r) {
+            for (;;) {
+                unsigned v;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+                if ((int)(v - step) >= 0) break;
+                if (sm100::globaltimer() - t0 > 2000000000ull) { ok = 0; atomicCAS(error, 0, 51); break; }
+            }
+        }
+    }
+    __syncthreads();
+    if (!ok) return;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __ldcg(landing + i);
+}
+
 }  // namespace
+
+void launch_gather_wait_copy(const unsigned* flags, int nranks, unsigned step, const float* landing, float* out,
+                             size_t floats, int* error, cudaStream_t s) {
+    const size_t n4 = floats / 4;
+    const int blocks = (int)std::min<size_t>(64, (n4 + 255) / 256);
+    gather_wait_copy_kernel<<<blocks, 256, 0, s>>>(flags, nranks, step, reinterpret_cast<const float4*>(landing),
+                                                   reinterpret_cast<float4*>(out), n4, error);
+}
 
 void launch_permute_heads(const float* gathered, float* full, int nranks, int n_layers, int n, int hq_local,
                           cudaStream_t s) {
@@ -130,6 +164,12 @@ void nccl_comm_destroy(void* comm) {
 
 int nccl_all_gather_f32(void* comm, const float* send, float* recv, size_t count, cudaStream_t s, std::string& err) {
     const ncclResult_t r = nccl().AllGather(send, recv, count, ncclFloat32, static_cast<ncclComm_t>(comm), s);
+    if (r != ncclSuccess) { err = nccl().GetErrorString(r); return QA_ERR_NCCL; }
+    return QA_OK;
+}
+
+int nccl_all_gather_bytes(void* comm, const void* send, void* recv, size_t bytes, cudaStream_t s, std::string& err) {
+    const ncclResult_t r = nccl().AllGather(send, recv, bytes, ncclUint8, static_cast<ncclComm_t>(comm), s);
     if (r != ncclSuccess) { err = nccl().GetErrorString(r); return QA_ERR_NCCL; }
     return QA_OK;
 }

@@ -83,6 +83,11 @@ _SIGNATURES = {
     "qa_kv_send": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_kv_recv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_comm_join": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_comm_info": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                    ctypes.POINTER(ctypes.c_int)]),
+    "qa_decode_step_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_void_p]),
     "qa_decode_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p]),
@@ -258,6 +263,17 @@ class Context:
 
     def kv_recv(self, seq: int, ntok: int, peer: int):
         self._check(lib().qa_kv_recv(self._h, seq, ntok, peer))
+
+    def decode_step_gather(self, seq, layer, n_layers, pos, q_pre, k_pre, v, q_out, full):
+        """Fused decode step on this rank's KV-head shard with the head gather over peer memory."""
+        self._check(lib().qa_decode_step_gather(self._h, seq, layer, n_layers, pos, q_pre, k_pre, v, q_out or None,
+                                                full))
+
+    def comm_info(self):
+        """(nranks, rank, peer_mapped) of the context's communicator."""
+        n, r, pm = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        self._check(lib().qa_comm_info(self._h, ctypes.byref(n), ctypes.byref(r), ctypes.byref(pm)))
+        return n.value, r.value, bool(pm.value)
 
     def comm_join(self):
         """Makes the context stream wait for the communication queued so far."""

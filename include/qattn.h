@@ -197,8 +197,24 @@ int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float*
  * itself: qa_comm_join or qa_sync does. */
 int qa_kv_send(qa_ctx* ctx, int seq, int ntok, int peer);
 int qa_kv_recv(qa_ctx* ctx, int seq, int ntok, int peer);
+/* Communicator shape of a context and whether the other ranks' gather buffers are mapped
+ * into this process (1: qa_decode_step_gather stores over NVLink; 0: it uses NCCL). */
+int qa_comm_info(const qa_ctx* ctx, int* nranks, int* rank, int* peer_mapped);
 /* Makes the context stream wait for all communication queued so far (no host wait). */
 int qa_comm_join(qa_ctx* ctx);
+
+/* Fused decode step with the head gather done by the kernel itself, for KV-head shards
+ * (the layout qa_gather_heads expects): qa_decode_step of one row on this rank's heads, with
+ * every output row stored straight into every rank's landing buffer over NVLink (peer
+ * stores into memory mapped at qa_comm_init), then a wait for all ranks' "step done" marks
+ * and a copy into `full` ([n_layers][1][all query heads][128], device). Collective: every
+ * rank calls it for the same step. A rank whose peers stop answering records
+ * QA_ERR_TIMEOUT (read by qa_sync) after 2 s instead of waiting forever. Where the
+ * machine offers no peer mapping, it runs qa_decode_step + qa_gather_heads (NCCL) instead,
+ * with the same results. Replaces, per token, core.cpp:395-406 + :606-624 and hands o_proj
+ * (core.cpp:625) the full-head rows. */
+int qa_decode_step_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos, const float* q_pre,
+                          const float* k_pre, const float* v, float* q_out, float* full);
 
 /* Size of the fixed device array behind qa_attn_decode_noalloc: 4 MiB per GPU, held by
  * every GPU that loads the library until the process exits. */

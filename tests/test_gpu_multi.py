@@ -7,6 +7,9 @@
   rank 1 back to back with qa_kv_send/qa_kv_recv (double-buffered staging, so the third
   transfer reuses the first buffer); rank 1's KV bytes equal the same sequences appended
   locally, bit for bit, and its positions are the sent row counts.
+* Fused decode step with the head gather done by the kernel (qa_decode_step_gather: peer
+  stores over NVLink, or NCCL where peer mapping is unavailable) equals a full-head
+  context's fused decode step on every rank.
 NVLS is switched off (NCCL_NVLS_ENABLE=0) and ranks leave only between steps.
 """
 import os
@@ -141,7 +144,44 @@ def _worker(rank, world, port, out_dir):
                                                     H.read_plane(local_ref, i, layer, kvsel, h, 0, ln)))
         report["handoff_equal"] = same
         report["handoff_pos"] = [full_comm.position(i + 1) for i in range(3)]
+    # fused decode step with the head gather done over peer memory (qa_decode_step_gather)
+    # against the full-head context's fused decode step
     dist.barrier()
+    P, gsteps = 300, 4
+    g_shard = qattn.Context(n_layers=L, context=1024, max_seqs=1, kv_head_begin=begin, kv_head_count=count,
+                            device=rank)
+    g_full = qattn.Context(n_layers=L, context=1024, max_seqs=1, device=rank)
+    for c in (g_shard, g_full):
+        c.set_stream(stream)
+        H.set_norms(c, qw, kw)
+    qd.init_comm(g_shard)
+    report["peer_mapped"] = g_shard.comm_info()[2]
+    hist_s = [t[:, :P].contiguous() for t in (qs, ks, vs)]
+    hist_f = [t[:, :P].contiguous() for t in (q, k, v)]
+    keep.extend(hist_s + hist_f)
+    for c, hh in ((g_shard, hist_s), (g_full, hist_f)):
+        qn_h = torch.empty_like(hh[0])
+        keep.append(qn_h)
+        c.append(0, 0, L, 0, P, hh[0].data_ptr(), hh[1].data_ptr(), hh[2].data_ptr(), qn_h.data_ptr())
+        c.commit(0, P)
+    gmax = 0.0
+    for st in range(gsteps):
+        p = P + st
+        s1 = [t[:, p:p + 1].contiguous() for t in (qs, ks, vs)]
+        f1 = [t[:, p:p + 1].contiguous() for t in (q, k, v)]
+        keep.extend(s1 + f1)
+        got = torch.full((L, 1, 16, 128), float("nan"), device="cuda")
+        ref = torch.empty((L, 1, 16, 128), device="cuda")
+        g_shard.decode_step_gather(0, 0, L, p, s1[0].data_ptr(), s1[1].data_ptr(), s1[2].data_ptr(), 0, got.data_ptr())
+        g_full.decode_step(0, 0, L, p, f1[0].data_ptr(), f1[1].data_ptr(), f1[2].data_ptr(), 0, ref.data_ptr())
+        g_shard.commit(0, 1)
+        g_full.commit(0, 1)
+        torch.cuda.synchronize()
+        gmax = max(gmax, H.err_stats(got.cpu().numpy(), ref.cpu().numpy())[0])
+    g_shard.sync()
+    report["peer_gather_max"] = gmax
+    dist.barrier()
+    g_shard.comm_destroy()
     full_comm.comm_destroy()
     shard.comm_destroy()
     np.save(os.path.join(out_dir, f"report{rank}.npy"), report, allow_pickle=True)
@@ -155,5 +195,6 @@ def test_head_sharded_gather_and_kv_handoff(tmp_path):
         rep = np.load(tmp_path / f"report{rank}.npy", allow_pickle=True).item()
         assert rep["kv_equal"], rep
         assert rep["gather_max"] < H.MAX_ABS and rep["gather_rms"] < H.RMS, rep
+        assert rep["peer_gather_max"] < 1e-5, rep             # same heads, different key split
         if rank == 1:
             assert rep["handoff_equal"] and rep["handoff_pos"] == [300, 150, 257], rep
