@@ -147,7 +147,7 @@ def _worker(rank, world, port, out_dir):
     # fused decode step with the head gather done over peer memory (qa_decode_step_gather)
     # against the full-head context's fused decode step
     dist.barrier()
-    P, gsteps = 300, 4
+    P, gsteps = 300, 3                        # the inputs hold rows [0, 303)
     g_shard = qattn.Context(n_layers=L, context=1024, max_seqs=1, kv_head_begin=begin, kv_head_count=count,
                             device=rank)
     g_full = qattn.Context(n_layers=L, context=1024, max_seqs=1, device=rank)
