@@ -298,23 +298,23 @@ def run_ours(args):
             pos = PREFILL + s
             if world > 1 and not (args.split_decode or args.nccl_gather):
                 # fused decode step whose kernel stores every output row into all ranks' buffers
-                if evs:
+                if evs and "d0" in evs:
                     evs["d0"][s].record(stream)
                 ctx.decode_step_gather(0, 0, L, pos, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), 0,
                                        dfull.data_ptr())
                 launches += 2           # decode step + wait/copy
-                if evs:
+                if evs and "d1" in evs:
                     evs["d1"][s].record(stream)
                 ctx.commit(0, 1)
                 continue
             if args.split_decode:       # qa_append then qa_attn_decode (two launches)
                 ctx.append(0, 0, L, pos, 1, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), dqn.data_ptr())
-                if evs:
+                if evs and "d0" in evs:
                     evs["d0"][s].record(stream)
                 ctx.attn_decode(0, 0, L, pos, 1, dqn.data_ptr(), dout.data_ptr())
                 launches += 2
             else:                       # fused decode step: append of the new row + attention, one launch
-                if evs:
+                if evs and "d0" in evs:
                     evs["d0"][s].record(stream)
                 ctx.decode_step(0, 0, L, pos, dq[s].data_ptr(), dk[s].data_ptr(), dv[s].data_ptr(), 0,
                                 dout.data_ptr())
@@ -322,7 +322,7 @@ def run_ours(args):
             if world > 1:
                 ctx.gather_heads(L, 1, dout.data_ptr(), dfull.data_ptr())
                 launches += 1
-            if evs:
+            if evs and "d1" in evs:
                 evs["d1"][s].record(stream)
             ctx.commit(0, 1)
         if evs:
@@ -344,9 +344,8 @@ def run_ours(args):
     with sampler:
         start, end = mkev(), mkev()
         start.record(stream)
-        for _ in range(args.steps):
-            evs = {"p0": mkev(), "pa0": mkev(), "pa1": mkev(), "e": mkev(),
-                   "d0": [mkev() for _ in range(DECODE)], "d1": [mkev() for _ in range(DECODE)]}
+        for _ in range(args.steps):       # phase boundaries only: no events between decode launches
+            evs = {"p0": mkev(), "pa0": mkev(), "pa1": mkev(), "e": mkev()}
             step(evs)
             records.append(evs)
         end.record(stream)
@@ -355,12 +354,20 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     clocks = sampler.summary()
+    # per-launch decode times (roofline) from one more step with events around every launch,
+    # outside the timed region (the events themselves add a few microseconds per launch)
+    probe = {"p0": mkev(), "pa0": mkev(), "pa1": mkev(), "e": mkev(),
+             "d0": [mkev() for _ in range(DECODE)], "d1": [mkev() for _ in range(DECODE)]}
+    step(probe)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
 
     total_ms = start.elapsed_time(end)
-    prefill_ms = [r["p0"].elapsed_time(r["d0"][0]) for r in records]   # prefill phase incl. append
+    prefill_ms = [r["p0"].elapsed_time(r["pa1"]) for r in records]    # prefill phase incl. append
     decode_ms = [r["pa1"].elapsed_time(r["e"]) for r in records]       # 128 decode steps incl. appends
     pattn_ms = [r["pa0"].elapsed_time(r["pa1"]) for r in records]
-    dattn_ms = [sum(r["d0"][s].elapsed_time(r["d1"][s]) for s in range(DECODE)) for r in records]
+    dattn_ms = [sum(probe["d0"][s].elapsed_time(probe["d1"][s]) for s in range(DECODE))]
 
     t = torch.tensor([total_ms, statistics.mean(prefill_ms), statistics.mean(decode_ms),
                       statistics.mean(pattn_ms), statistics.mean(dattn_ms)], device=dev, dtype=torch.float64)

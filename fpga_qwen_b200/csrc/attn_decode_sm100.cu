@@ -189,7 +189,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         const int layer = a.layer0 + u.l;
         pc.K = a.kv.plane(a.seq[u.b], layer, 0, u.kh) + (size_t)k0 * D;
         pc.V = a.kv.plane(a.seq[u.b], layer, 1, u.kh) + (size_t)k0 * D;
-        for (int i = 0; i < NST && g_begin < g_end; ++i) produce();
+        if (!FUSED)                                    // the fused kernel primes after its input copies
+            for (int i = 0; i < NST && g_begin < g_end; ++i) produce();
     }
 
     if constexpr (FUSED) {
@@ -199,70 +200,77 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             for (int k = 0; k < i; ++k) next_unit(a, w);
             return w;
         };
-        // Thread t owns channel pair j = t % 64 of rows {h, 2 + h} (h = t / 64) of every unit:
-        // rows 0, 1 are the query heads, 2 the key, 3 the value. All its inputs are loaded first,
-        // so those loads overlap the sequential FP64 sums below.
-        constexpr int TASKS = 2 * QB;
-        const int j = tid & 63, h = tid >> 6;
-        float xa[TASKS], xb[TASKS], wa[TASKS], wb[TASKS], cc[QB], ss[QB];
-        #pragma unroll
+        // Inputs of unit i, staged in the last ring stage (primed only after this prologue):
+        // [q0 | q1 | k | v | cos | sin | q_norm | k_norm] = 896 floats at i * 1024.
+        float* stg = reinterpret_cast<float*>(ring + (NST - 1) * CHUNK_BYTES);
         for (int i = 0; i < QB; ++i) {
             const Unit w = unit_at(i);
-            const bool touched = w.off < g_end, owns = w.off + w.len <= g_end;
+            if (w.off >= g_end) break;
+            const bool owns = w.off + w.len <= g_end;
             const int layer = a.layer0 + w.l, pos = w.len - 1;
             const size_t qrow_w = ((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP;
             const size_t krow_w = ((size_t)w.l * a.n + w.b) * a.hkv + w.kh;
-            const float* nw = a.step.norms + (size_t)layer * 2 * D;
-            cc[i] = touched ? __ldg(a.step.cosines + (size_t)pos * 64 + j) : 0.f;
-            ss[i] = touched ? __ldg(a.step.sines + (size_t)pos * 64 + j) : 0.f;
-            const float* xq = a.step.q_pre + (qrow_w + h) * D;                       // row h
-            const float* xk = (h == 0 ? a.step.k_pre : a.step.v_pre) + krow_w * D;   // row 2 + h
-            xa[2 * i] = touched ? __ldg(xq + j) : 0.f;
-            xb[2 * i] = touched ? __ldg(xq + j + 64) : 0.f;
-            wa[2 * i] = touched ? __ldg(nw + j) : 0.f;
-            wb[2 * i] = touched ? __ldg(nw + j + 64) : 0.f;
-            xa[2 * i + 1] = owns ? __ldg(xk + j) : 0.f;
-            xb[2 * i + 1] = owns ? __ldg(xk + j + 64) : 0.f;
-            wa[2 * i + 1] = owns && h == 0 ? __ldg(nw + D + j) : 0.f;
-            wb[2 * i + 1] = owns && h == 0 ? __ldg(nw + D + j + 64) : 0.f;
+            for (int gidx = tid; gidx < 224; gidx += THREADS) {          // 16-byte granules
+                const float* src;
+                if (gidx < 64) src = a.step.q_pre + qrow_w * D + gidx * 4;
+                else if (gidx < 96) src = owns ? a.step.k_pre + krow_w * D + (gidx - 64) * 4 : nullptr;
+                else if (gidx < 128) src = owns ? a.step.v_pre + krow_w * D + (gidx - 96) * 4 : nullptr;
+                else if (gidx < 144) src = a.step.cosines + (size_t)pos * 64 + (gidx - 128) * 4;
+                else if (gidx < 160) src = a.step.sines + (size_t)pos * 64 + (gidx - 144) * 4;
+                else if (gidx < 192) src = a.step.norms + (size_t)layer * 2 * D + (gidx - 160) * 4;
+                else src = owns ? a.step.norms + (size_t)layer * 2 * D + D + (gidx - 192) * 4 : nullptr;
+                if (src)
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                 ::"r"(smem_u32(stg + i * 1024 + gidx * 4)), "l"(src) : "memory");
+            }
         }
+        if (tid == 0)                                  // K/V stream behind the small input copies
+            for (int i = 0; i < NST - 1 && g_begin < g_end; ++i) produce();
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();
         if (tid < 3 * QB) {                            // one lane per sequential FP64 chain
             const int i = tid / 3, r = tid - 3 * i;    // rows: query head 0, query head 1, key
             const Unit w = unit_at(i);
-            if (w.off < g_end && (r < 2 || w.off + w.len <= g_end)) {
-                const float* x = r < 2 ? a.step.q_pre + ((((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP) + r) * D
-                                       : a.step.k_pre + (((size_t)w.l * a.n + w.b) * a.hkv + w.kh) * D;
-                s_inv[i][r] = rms_inv(x, a.step.eps);
+            if (w.off < g_end && (r < 2 || w.off + w.len <= g_end)) s_inv[i][r] = rms_inv(stg + i * 1024 + r * 128, a.step.eps);
+        }
+        __syncthreads();
+        {
+            // thread t: channel pair j = t % 64 of rows {h, 2 + h} (h = t / 64) of every unit
+            const int j = tid & 63, h = tid >> 6;
+            for (int i = 0; i < QB; ++i) {
+                const Unit w = unit_at(i);
+                if (w.off >= g_end) break;
+                const bool owns = w.off + w.len <= g_end;
+                const float* u8 = stg + i * 1024;
+                const float c = u8[512 + j], sn = u8[576 + j];
+                float ra, rb;
+                norm_rope_pair(u8[h * 128 + j], u8[h * 128 + j + 64], u8[640 + j], u8[640 + j + 64], c, sn, s_inv[i][h],
+                               ra, rb);
+                s_q[i][h][j] = ra;
+                s_q[i][h][j + 64] = rb;
+                if (owns) {
+                    if (a.step.q_out) {
+                        const size_t qrow_w = ((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP;
+                        a.step.q_out[(qrow_w + h) * D + j] = ra;
+                        a.step.q_out[(qrow_w + h) * D + j + 64] = rb;
+                    }
+                    if (h == 0) {                      // key row: norm + rope, FP16
+                        norm_rope_pair(u8[256 + j], u8[256 + j + 64], u8[768 + j], u8[768 + j + 64], c, sn, s_inv[i][2],
+                                       ra, rb);
+                        s_new[i][0][j] = __float2half_rn(ra);
+                        s_new[i][0][j + 64] = __float2half_rn(rb);
+                    } else {                           // value row: FP16 rounding only
+                        s_new[i][1][j] = __float2half_rn(u8[384 + j]);
+                        s_new[i][1][j + 64] = __float2half_rn(u8[384 + j + 64]);
+                    }
+                }
             }
         }
         __syncthreads();
-        #pragma unroll
-        for (int i = 0; i < QB; ++i) {
-            const Unit w = unit_at(i);
-            if (w.off >= g_end) continue;
-            const bool owns = w.off + w.len <= g_end;
-            const size_t qrow_w = ((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP;
-            float ra, rb;
-            norm_rope_pair(xa[2 * i], xb[2 * i], wa[2 * i], wb[2 * i], cc[i], ss[i], s_inv[i][h], ra, rb);
-            s_q[i][h][j] = ra;
-            s_q[i][h][j + 64] = rb;
-            if (owns) {
-                if (a.step.q_out) {
-                    a.step.q_out[(qrow_w + h) * D + j] = ra;
-                    a.step.q_out[(qrow_w + h) * D + j + 64] = rb;
-                }
-                if (h == 0) {                          // key row: norm + rope, FP16
-                    norm_rope_pair(xa[2 * i + 1], xb[2 * i + 1], wa[2 * i + 1], wb[2 * i + 1], cc[i], ss[i],
-                                   s_inv[i][2], ra, rb);
-                    s_new[i][0][j] = __float2half_rn(ra);
-                    s_new[i][0][j + 64] = __float2half_rn(rb);
-                } else {                               // value row: FP16 rounding only
-                    s_new[i][1][j] = __float2half_rn(xa[2 * i + 1]);
-                    s_new[i][1][j + 64] = __float2half_rn(xb[2 * i + 1]);
-                }
-            }
+        if (tid == 0) {                                // the staging stage joins the copy ring
+            fence_proxy_async_smem();
+            produce();
         }
-        __syncthreads();
         if (tid < QB * 32) {                          // store the new K and V rows, 16 B per lane
             const int i = tid >> 5, kv = (tid >> 4) & 1, c16 = tid & 15;
             const Unit w = unit_at(i);
