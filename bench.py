@@ -248,6 +248,7 @@ def run_ours(args):
 
     ctx = qattn.Context(n_layers=L, context=4096, max_seqs=1, kv_head_begin=head0, kv_head_count=hkv, device=local)
     ctx.set_stream(stream.cuda_stream)
+    ctx.set_step_overlap(not args.no_overlap)   # consecutive fused decode steps overlap (PDL)
     peer_mapped = False
     if world > 1:
         from fpga_qwen_b200 import dist as qd
@@ -741,6 +742,8 @@ def main():
     ap.add_argument("--workload", choices=["config4", "config5"], default="config4",
                     help="config4: head-sharded 3968+128 (the metric's config); config5: 64 requests, request-sharded")
     ap.add_argument("--disagg", action="store_true", help="config5: prefill on the first half of the GPUs, decode on the rest")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="do not let consecutive fused decode steps overlap (programmatic dependent launch)")
     ap.add_argument("--nccl-gather", action="store_true",
                     help="N>1: gather decode outputs with NCCL after the step instead of peer stores inside it")
     ap.add_argument("--split-decode", action="store_true",

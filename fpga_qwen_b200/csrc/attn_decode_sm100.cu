@@ -57,6 +57,7 @@ constexpr int MAX_UNIT_KEYS = 4096;           // longest unit (QA_MAX_CONTEXT): 
 struct DecodeArgs {
     const float* q; float* out;               // [n_layers][n][hq][128]
     StepInputs step;                          // fused decode step only
+    int pdl;                                  // launched as a programmatic dependent of the previous step
     GatherArgs g;                             // head gather through peer memory (out_hq == 0: off)
     KVLayout kv; int layer0, n_layers, n, hq, hkv;
     int seq[MAX_BATCH];                       // sequence slot of row b
@@ -156,14 +157,18 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
     // consumer loop). The CTA's chunk stream is, segment after segment, the K chunks then the
     // V chunks of each segment (the part of one unit inside the range); the consumers walk
     // the same stream in the same order.
-    __shared__ struct { Unit u; const __half* K; const __half* V; int j, nch, cnt; } pc;
-    auto produce = [&]() {
+    __shared__ struct { Unit u; const __half* K; const __half* V; int j, nch, cnt, k0; } pc;
+    // limited: before the previous step's grid has finished (programmatic dependent launch),
+    // only chunks that hold neither that step's new row (key len-2 of its unit) nor this step's
+    // (key len-1) may be copied; returns false, issuing nothing, at the first chunk that does.
+    auto produce = [&](bool limited) {
         if (pc.j == 2 * pc.nch) {                      // next segment: the next unit from key 0
             next_unit(a, pc.u);
-            if (pc.u.off >= g_end) return;
+            if (pc.u.off >= g_end) return false;
             pc.cnt = (int)min((long long)pc.u.len, g_end - pc.u.off);
             pc.nch = (pc.cnt + CH - 1) / CH;
             pc.j = 0;
+            pc.k0 = 0;
             const int layer = a.layer0 + pc.u.l;
             pc.K = a.kv.plane(a.seq[pc.u.b], layer, 0, pc.u.kh);
             pc.V = a.kv.plane(a.seq[pc.u.b], layer, 1, pc.u.kh);
@@ -172,17 +177,20 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         const bool is_v = pc.j >= pc.nch;
         const int jj = is_v ? pc.j - pc.nch : pc.j;
         const int keys = min(CH, pc.cnt - jj * CH);
+        if (limited && pc.k0 + jj * CH + keys > pc.u.len - 2) return false;
         const __half* src = (is_v ? pc.V : pc.K) + (size_t)jj * CH * D;
         mbar_arrive_expect_tx(&full[stage], keys * D * 2);
         bulk_copy(ring + stage * CHUNK_BYTES, src, keys * D * 2, &full[stage]);
         ++issued;
         ++pc.j;
+        return true;
     };
     Unit u = unit_of(a, g_begin);                      // consumers' unit cursor
     if (tid == 0) {
         // first segment: keys [g_begin - off, ...) of the unit holding g_begin
         const int k0 = (int)(g_begin - u.off);
         pc.u = u;
+        pc.k0 = k0;
         pc.cnt = (int)min((long long)u.len, g_end - u.off) - k0;
         pc.nch = (pc.cnt + CH - 1) / CH;
         pc.j = 0;
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         pc.K = a.kv.plane(a.seq[u.b], layer, 0, u.kh) + (size_t)k0 * D;
         pc.V = a.kv.plane(a.seq[u.b], layer, 1, u.kh) + (size_t)k0 * D;
         if (!FUSED)                                    // the fused kernel primes after its input copies
-            for (int i = 0; i < NST && g_begin < g_end; ++i) produce();
+            for (int i = 0; i < NST && g_begin < g_end; ++i) produce(false);
     }
 
     if constexpr (FUSED) {
@@ -203,29 +211,46 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         // Inputs of unit i, staged in the last ring stage (primed only after this prologue):
         // [q0 | q1 | k | v | cos | sin | q_norm | k_norm] = 896 floats at i * 1024.
         float* stg = reinterpret_cast<float*>(ring + (NST - 1) * CHUNK_BYTES);
-        for (int i = 0; i < QB; ++i) {
-            const Unit w = unit_at(i);
-            if (w.off >= g_end) break;
-            const bool owns = w.off + w.len <= g_end;
-            const int layer = a.layer0 + w.l, pos = w.len - 1;
-            const size_t qrow_w = ((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP;
-            const size_t krow_w = ((size_t)w.l * a.n + w.b) * a.hkv + w.kh;
-            for (int gidx = tid; gidx < 224; gidx += THREADS) {          // 16-byte granules
-                const float* src;
-                if (gidx < 64) src = a.step.q_pre + qrow_w * D + gidx * 4;
-                else if (gidx < 96) src = owns ? a.step.k_pre + krow_w * D + (gidx - 64) * 4 : nullptr;
-                else if (gidx < 128) src = owns ? a.step.v_pre + krow_w * D + (gidx - 96) * 4 : nullptr;
-                else if (gidx < 144) src = a.step.cosines + (size_t)pos * 64 + (gidx - 128) * 4;
-                else if (gidx < 160) src = a.step.sines + (size_t)pos * 64 + (gidx - 144) * 4;
-                else if (gidx < 192) src = a.step.norms + (size_t)layer * 2 * D + (gidx - 160) * 4;
-                else src = owns ? a.step.norms + (size_t)layer * 2 * D + D + (gidx - 192) * 4 : nullptr;
-                if (src)
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                 ::"r"(smem_u32(stg + i * 1024 + gidx * 4)), "l"(src) : "memory");
+        // tables (RoPE rows, norm weights: constant during a step) or the step's inputs
+        auto stage_inputs = [&](bool tables) {
+            for (int i = 0; i < QB; ++i) {
+                const Unit w = unit_at(i);
+                if (w.off >= g_end) break;
+                const bool owns = w.off + w.len <= g_end;
+                const int layer = a.layer0 + w.l, pos = w.len - 1;
+                const size_t qrow_w = ((size_t)w.l * a.n + w.b) * a.hq + (size_t)w.kh * GROUP;
+                const size_t krow_w = ((size_t)w.l * a.n + w.b) * a.hkv + w.kh;
+                for (int gidx = tid + (tables ? 128 : 0); gidx < (tables ? 224 : 128); gidx += THREADS) {
+                    const float* src;                  // 16-byte granules
+                    if (gidx < 64) src = a.step.q_pre + qrow_w * D + gidx * 4;
+                    else if (gidx < 96) src = owns ? a.step.k_pre + krow_w * D + (gidx - 64) * 4 : nullptr;
+                    else if (gidx < 128) src = owns ? a.step.v_pre + krow_w * D + (gidx - 96) * 4 : nullptr;
+                    else if (gidx < 144) src = a.step.cosines + (size_t)pos * 64 + (gidx - 128) * 4;
+                    else if (gidx < 160) src = a.step.sines + (size_t)pos * 64 + (gidx - 144) * 4;
+                    else if (gidx < 192) src = a.step.norms + (size_t)layer * 2 * D + (gidx - 160) * 4;
+                    else src = owns ? a.step.norms + (size_t)layer * 2 * D + D + (gidx - 192) * 4 : nullptr;
+                    if (src)
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                     ::"r"(smem_u32(stg + i * 1024 + gidx * 4)), "l"(src) : "memory");
+                }
             }
+        };
+        stage_inputs(true);
+        if (a.pdl) {
+            // Launched while the previous step may still run: copy only KV rows it cannot be
+            // writing, then wait for its grid (and its memory) before touching this step's
+            // inputs, records and rows, and let the next step launch.
+            if (tid == 0)
+                for (int i = 0; i < NST - 1 && g_begin < g_end; ++i)
+                    if (!produce(true)) break;
+            asm volatile("griddepcontrol.wait;" ::: "memory");
         }
+        // a following overlapped step may launch now (it waits for this grid before it reads
+        // anything this step writes)
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        stage_inputs(false);
         if (tid == 0)                                  // K/V stream behind the small input copies
-            for (int i = 0; i < NST - 1 && g_begin < g_end; ++i) produce();
+            while ((int)issued < NST - 1 && produce(false)) {}
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
         if (tid < 3 * QB) {                            // one lane per sequential FP64 chain
@@ -269,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         __syncthreads();
         if (tid == 0) {                                // the staging stage joins the copy ring
             fence_proxy_async_smem();
-            produce();
+            produce(false);
         }
         if (tid < QB * 32) {                          // store the new K and V rows, 16 B per lane
             const int i = tid >> 5, kv = (tid >> 4) & 1, c16 = tid & 15;
@@ -411,7 +436,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             ++consumed;
             __syncthreads();                       // everyone is done with this stage
             if (abort_flag) { aborted = true; break; }
-            if (tid == 0) produce();               // refill the freed stage (next segment's chunks too)
+            if (tid == 0) produce(false);          // refill the freed stage (next segment's chunks too)
             if (j == nch - 1) {
                 // ---- end of the K pass: exact max and exp-sum over this range ----
                 float m0 = mloc0, m1 = mloc1;
@@ -593,7 +618,16 @@ void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const 
         cudaFuncSetAttribute(attn_decode_sm100_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
         attr = true;
     }
-    if (step) attn_decode_sm100_kernel<true><<<a.ctas, THREADS, smem, s>>>(a);
+    if (step && step->pdl) {
+        a.pdl = 1;
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(a.ctas); cfg.blockDim = dim3(THREADS); cfg.dynamicSmemBytes = smem; cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr; cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, attn_decode_sm100_kernel<true>, a);
+    } else if (step) attn_decode_sm100_kernel<true><<<a.ctas, THREADS, smem, s>>>(a);
     else attn_decode_sm100_kernel<false><<<a.ctas, THREADS, smem, s>>>(a);
 }
 

@@ -76,6 +76,8 @@ struct qa_ctx {
     unsigned* gather_done = nullptr;       // CTAs of the gathering launch that finished
     unsigned gather_step = 0;
     float* step_out = nullptr;             // local output of the NCCL fallback
+    bool step_overlap = false;             // qa_set_step_overlap
+    bool last_fused_step = false;          // the last launch on the stream was a fused decode step
     size_t step_out_bytes = 0;
     std::string err;
 };
@@ -114,6 +116,7 @@ int cuda_fail(qa_ctx* c, cudaError_t e, const char* what) {
 // After a launch or device error the affected sequence restarts from position 0, like the
 // engine's "Errors ... reset all model ... state" (engine/INTERFACE.md error contract).
 int after_launch(qa_ctx* ctx, int seq, const char* what) {
+    ctx->last_fused_step = false;
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) return QA_OK;
     if (seq >= 0 && seq < (int)ctx->pos.size()) {
@@ -327,6 +330,7 @@ void qa_destroy(qa_ctx* ctx) {
 int qa_set_stream(qa_ctx* ctx, void* s) {
     if (!ctx) return QA_ERR_INVALID;
     ctx->stream = s ? static_cast<cudaStream_t>(s) : ctx->own_stream;
+    ctx->last_fused_step = false;
     return QA_OK;
 }
 
@@ -606,11 +610,15 @@ static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int 
         od = sg + 2 * qn + 2 * kn;
     }
     in.norms = ctx->norms; in.cosines = ctx->cosines; in.sines = ctx->sines; in.eps = ctx->cfg.norm_eps;
+    // overlap with the previous step only right after a fused step of this context on this stream
+    in.pdl = ctx->step_overlap && ctx->last_fused_step && !ctx->cfg.io_host && !gather ? 1 : 0;
+    bool fused = false;
     const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
     if ((st = ensure_decode_scratch(ctx, plan))) return st;
     if (plan.max_units_per_cta <= FUSED_MAX_UNITS) {
         launch_attn_decode_sm100(plan, ctx->kv, nullptr, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
                                  ctx->partial, ctx->counters, ctx->error, ctx->stream, &in, gather);
+        fused = true;
     } else {
         // Short contexts or many sequences per CTA range: the same results as append + decode,
         // run as those two launches (the normalised query rows go to q_out or to staging).
@@ -635,6 +643,7 @@ static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int 
                                  ctx->partial, ctx->counters, ctx->error, ctx->stream, nullptr, gather);
     }
     if ((st = after_launch(ctx, n == 1 ? seqs[0] : -1, "attn_decode_step"))) return st;
+    ctx->last_fused_step = fused && !gather;
     for (int b = 0; b < n; ++b)
         for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seqs[b]][l] = pos[b] + 1;
     if (ctx->cfg.io_host) {
@@ -840,6 +849,13 @@ int qa_comm_init(qa_ctx* ctx, int nranks, int rank, const char id[128]) {
     if (st) return fail(ctx, st, "ncclCommInitRank: %s", err.c_str());
     ctx->nranks = nranks; ctx->rank = rank;
     return peer_setup(ctx);
+}
+
+int qa_set_step_overlap(qa_ctx* ctx, int enable) {
+    if (!ctx) return QA_ERR_INVALID;
+    ctx->step_overlap = enable != 0;
+    ctx->last_fused_step = false;
+    return QA_OK;
 }
 
 int qa_comm_info(const qa_ctx* ctx, int* nranks, int* rank, int* peer_mapped) {

@@ -100,6 +100,7 @@ struct StepInputs {
     float* q_out = nullptr;                                    // optional
     const float* norms = nullptr; const float* cosines = nullptr; const float* sines = nullptr;
     float eps = 0.f;
+    int pdl = 0;                                               // programmatic dependent launch
 };
 void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const float* q, float* out, int layer0,
                               int n_layers, int n, const int* seq, const int* pos, int hq, int hkv, float* partial,

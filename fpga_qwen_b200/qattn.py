@@ -83,6 +83,7 @@ _SIGNATURES = {
     "qa_kv_send": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_kv_recv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_comm_join": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_set_step_overlap": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "qa_comm_info": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                     ctypes.POINTER(ctypes.c_int)]),
     "qa_decode_step_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -237,6 +238,10 @@ class Context:
     def decode_step(self, seq, layer, n_layers, pos, q_pre, k_pre, v, q_out, out):
         """Append of one new row + its decode attention in one launch (q_out may be 0)."""
         self._check(lib().qa_decode_step(self._h, seq, layer, n_layers, pos, q_pre, k_pre, v, q_out or None, out))
+
+    def set_step_overlap(self, enable: bool):
+        """Let consecutive fused decode steps overlap (programmatic dependent launch)."""
+        self._check(lib().qa_set_step_overlap(self._h, 1 if enable else 0))
 
     def decode_step_batch(self, seqs, layer, n_layers, q_pre, k_pre, v, q_out, out):
         arr, n = self._seq_array(seqs)

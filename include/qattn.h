@@ -148,6 +148,14 @@ int qa_commit_batch(qa_ctx* ctx, const int* seqs, int n_seqs);
  * qa_append_batch / qa_attn_decode_batch). */
 int qa_decode_step(qa_ctx* ctx, int seq, int layer, int n_layers, int pos, const float* q_pre,
                    const float* k_pre, const float* v, float* q_out, float* out);
+/* Opt-in overlap of consecutive decode steps (default off). When on, a qa_decode_step launched
+ * right after another fused decode step of this context on the same stream starts while the
+ * previous one finishes (programmatic dependent launch): it sets up and copies KV rows older
+ * than the previous step's new row early, and reads its inputs, and everything the previous
+ * step wrote, only once that step's grid has completed. The caller promises that no kernel
+ * of its own writes this context's KV store between two such steps (the library's own
+ * launches of other kinds end the overlap by themselves). No effect in io_host mode. */
+int qa_set_step_overlap(qa_ctx* ctx, int enable);
 int qa_decode_step_batch(qa_ctx* ctx, const int* seqs, int n_seqs, int layer, int n_layers,
                          const float* q_pre, const float* k_pre, const float* v, float* q_out,
                          float* out);

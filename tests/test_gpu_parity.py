@@ -668,3 +668,39 @@ def test_fused_decode_step_batch_long_sequences():
                                   H.read_plane(ctxs[1], s_, 27, kvsel, 5, n - 1, 1))
     for c in ctxs:
         c.close()
+
+
+def test_overlapped_decode_steps_match_serial_steps():
+    """With qa_set_step_overlap on, 24 fused decode steps issued back to back (each starting
+    while the previous one finishes) write the same K/V rows and outputs as the same steps
+    with the overlap off; a prefix copy issued in between ends the overlap for one step."""
+    L, P, steps = 28, 3000, 24
+    ctxs = [make_ctx(L, max_seqs=2, context=4096) for _ in range(2)]
+    qw, kw = H.norms(95, L)
+    q, k, v = H.inputs(95, L, 0, P + steps)
+    hist = [t[:, :P].contiguous() for t in (q, k, v)]
+    rows = [[t[:, p:p + 1].contiguous() for t in (q, k, v)] for p in range(P, P + steps)]
+    outs = []
+    for idx, c in enumerate(ctxs):
+        H.set_norms(c, qw, kw)
+        gpu_append(c, 0, 0, *hist)
+        c.commit(0, P)
+        c.set_step_overlap(idx == 1)
+        o = torch.empty((steps, L, 1, 16, 128), device="cuda")
+        for st in range(steps):
+            if st == 12:
+                c.copy_prefix(0, 1, 512)           # another kernel between two steps
+            q1, k1, v1 = rows[st]
+            c.decode_step(0, 0, L, P + st, q1.data_ptr(), k1.data_ptr(), v1.data_ptr(), 0, o[st].data_ptr())
+            c.commit(0, 1)
+        outs.append(o)
+    torch.cuda.synchronize()
+    for c in ctxs:
+        c.sync()
+    assert torch.equal(outs[0], outs[1])
+    for layer in (0, 27):
+        for kvsel in (0, 1):
+            assert np.array_equal(H.read_plane(ctxs[0], 0, layer, kvsel, 6, P - 2, steps + 2),
+                                  H.read_plane(ctxs[1], 0, layer, kvsel, 6, P - 2, steps + 2))
+    for c in ctxs:
+        c.close()
