@@ -4,7 +4,10 @@
 // :357-381, :407-605): for each new row b (position pos0+b) and query head h,
 // out = softmax(q.K^T / sqrt(128)) V over keys [0, pos0+b] of KV head h/2.
 //
-// One CTA = (layer, KV head, 128-row query tile). Both query heads of the GQA pair live in
+// Work item = (layer, KV head, 128-row query tile). The kernel is persistent: one CTA per SM
+// takes work items from a global counter (a two-slot tile queue in shared memory hands each
+// item to all warps), keeps its TMEM, barriers and K/V ring across items, and streams the
+// next item's K/V while the current one finishes. Both query heads of the GQA pair live in
 // the CTA and share every K/V tile (the reference pairs heads for the same reason,
 // core.cpp:150-159). Rows whose absolute position is below 128 are not handled here: they
 // attend to few keys, where FP16 probabilities are not accurate enough, and go to the
@@ -53,9 +56,9 @@ using namespace sm100;
 constexpr int BM = 128, BN = 128;
 constexpr int THREADS = 384;                              // 12 warps = 3 warpgroups
 // Register split: launched at 168 per thread (384 x 168 = 64,512); the control warpgroup
-// (MMA + TMA warps) drops to 56 and the two softmax warpgroups rise to 224:
-// 2 x 128 x 224 + 128 x 56 = 64,512, the launch total.
-constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 224, REGS_CONTROL = 56;
+// (MMA + TMA warps) drops to 72 and the two softmax warpgroups rise to 216:
+// 2 x 128 x 216 + 128 x 72 = 64,512, the launch total.
+constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 216, REGS_CONTROL = 72;
 static_assert(2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL == THREADS * REGS_LAUNCH, "register split must match launch");
 constexpr uint32_t TILE_BYTES = BN * D * 2;               // 32 KB FP16 K or V tile
 // K and V tiles share one 5-stage ring in load order K0, V0, K1, V1, ...: item i = 2j (K_j)
@@ -66,18 +69,38 @@ constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;          // + barriers + alignm
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr float RESCALE_THRESHOLD = 8.0f;                 // log2 units
 
+constexpr int TQ = 2;                                     // tile queue slots
 enum {
     B_Q0, B_Q1, B_FULL0, B_EMPTY0 = B_FULL0 + RING, B_SF0 = B_EMPTY0 + RING, B_SF1, B_PF0, B_PF1, B_OD0, B_OD1,
-    B_DRAIN, B_COUNT
+    B_OF0, B_OF1,                                         // O_h read by the epilogue (free for the next tile)
+    B_TF0, B_TE0 = B_TF0 + TQ,                            // tile queue slot filled / read by every consumer
+    B_DRAIN = B_TE0 + TQ, B_COUNT
 };
-static_assert(B_COUNT * 8 + 4 <= 256, "barrier area");
+static_assert(B_COUNT * 8 + 4 + 4 * TQ <= 256, "barrier area");
 
 struct PrefillArgs {
     const float* q; float* out;       // [n_layers][n][hq][128]
     int seq, layer0, n_layers, pos0, n, hq, hkv, layers_total;
-    int row_begin, n_qtiles;
+    int row_begin, n_qtiles, n_tiles;
+    int* tile_counter;                // next tile to hand out; zero before the launch
     int* error;
 };
+
+// Tile t of the launch: the query tiles of one (layer, KV head) are consecutive, heaviest first,
+// so CTAs running at the same time read the same K/V planes and hit in L2.
+struct TileInfo { int l, kh, r0, nk, valid_keys, plane_k; };
+__device__ __forceinline__ TileInfo tile_info(const PrefillArgs& a, int t) {
+    TileInfo ti;
+    const int lh = t / a.n_qtiles;
+    const int tile = a.n_qtiles - 1 - t % a.n_qtiles;
+    ti.kh = lh % a.hkv;
+    ti.l = lh / a.hkv;
+    ti.r0 = a.row_begin + tile * BM;                          // first query row of the tile
+    ti.valid_keys = a.pos0 + min(ti.r0 + BM, a.n);            // keys visible to the tile's last row
+    ti.nk = (ti.valid_keys + BN - 1) / BN;                    // causal key tiles
+    ti.plane_k = ((a.seq * a.layers_total + a.layer0 + ti.l) * 2 + 0) * a.hkv + ti.kh;
+    return ti;
+}
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk16) {   // K-major, 128B swizzle, 2 atom columns
     return (uint32_t)((chunk16 >> 3) * 16384 + (row >> 3) * 1024 + (row & 7) * 128 + (((chunk16 & 7) ^ (row & 7)) << 4));
@@ -117,23 +140,11 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + B_COUNT * 8);
+    volatile int* tq = reinterpret_cast<volatile int*>(smem + OFF_BAR + B_COUNT * 8 + 4);
     __shared__ int abort_flag;
     __shared__ int never_abort;                              // for drains that must not give up early
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-    // ---- work item: the query tiles of one (layer, KV head) are consecutive, heaviest first,
-    // so CTAs running at the same time read the same K/V planes and hit in L2 ----
-    const int lh = (int)(blockIdx.x / a.n_qtiles);
-    const int tile = a.n_qtiles - 1 - (int)(blockIdx.x % a.n_qtiles);
-    const int kh = lh % a.hkv, l = lh / a.hkv;
-    const int layer = a.layer0 + l;
-    const int r0 = a.row_begin + tile * BM;                  // first query row of the tile
-    const int r_last = min(r0 + BM, a.n) - 1;
-    const int nk = (a.pos0 + r_last + 1 + BN - 1) / BN;      // causal key tiles
-    const int valid_keys = a.pos0 + r_last + 1;
-    const int plane_k = ((a.seq * a.layers_total + layer) * 2 + 0) * a.hkv + kh;
-    const int plane_v = plane_k + a.hkv;
 
     if (tid == 0) {
         abort_flag = 0;
@@ -142,6 +153,8 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         for (int i = 0; i < RING; ++i) { mbar_init(&bar[B_FULL0 + i], 1); mbar_init(&bar[B_EMPTY0 + i], 1); }
         mbar_init(&bar[B_SF0], 1); mbar_init(&bar[B_SF1], 1);
         mbar_init(&bar[B_PF0], 128); mbar_init(&bar[B_PF1], 128); mbar_init(&bar[B_OD0], 1); mbar_init(&bar[B_OD1], 1);
+        mbar_init(&bar[B_OF0], 128); mbar_init(&bar[B_OF1], 128);
+        for (int i = 0; i < TQ; ++i) { mbar_init(&bar[B_TF0 + i], 1); mbar_init(&bar[B_TE0 + i], 1 + 256); }
         mbar_init(&bar[B_DRAIN], 1);
         fence_mbar_init();
     }
@@ -160,112 +173,124 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         // ================================ softmax groups ================================
         const int h = warp >> 2;                             // query head within the pair
         const int wq = warp & 3;                             // this warp's 32-row quarter
-        const int t = tid & 127;                             // row within the tile
-        const int row_pos = a.pos0 + r0 + t;
-        auto row_off = [&](int r) { return (((size_t)l * a.n + r) * a.hq + (size_t)kh * 2 + h) * D; };
+        const int trow = tid & 127;                          // row within the tile
         uint8_t* Qs = smem + OFF_Q + h * 32768;
-        // Q rows of this warp's quarter -> FP16 in the swizzled K-major layout. Lane i reads
-        // channels 4i..4i+3 of each row (coalesced 512-byte rows), all 32 rows in flight.
-        {
-            float4 xr[32];
-            #pragma unroll
-            for (int rr = 0; rr < 32; ++rr) {
-                const int r = r0 + wq * 32 + rr;
-                xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(a.q + row_off(r)) + lane)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            #pragma unroll
-            for (int rr = 0; rr < 32; ++rr)
-                *reinterpret_cast<uint2*>(Qs + swz(wq * 32 + rr, lane >> 1) + (lane & 1) * 8) =
-                    make_uint2(pack_half2(xr[rr].x, xr[rr].y), pack_half2(xr[rr].z, xr[rr].w));
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&bar[B_Q0 + h]);
-
         const float scale = 1.4426950408889634f * 0.08838834764831845f;   // log2(e)/sqrt(128)
         const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
         const uint32_t s_col = tmem + lane_base + h * 128;   // S_h; P_h in its first 64 columns
         const uint32_t o_col = tmem + lane_base + 256 + h * 128;
-        float m = -INFINITY, lsum = 0.f;
+        uint32_t kt = 0;                                     // key tiles processed (S, P phases)
         bool ok = true;
-        for (int j = 0; j < nk && ok; ++j) {
-            if (!mbar_wait(&bar[B_SF0 + h], j & 1, abortp)) { fail(11); ok = false; break; }
-            tc_fence_after();
-            // S row -> registers: four 32-column loads in flight, one wait; the empty asm pins
-            // every use of the loaded registers after the wait
-            uint32_t sr[4][32];
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, sr[c]);
-            tmem_wait_ld();
-            #pragma unroll
-            for (int c = 0; c < 4; ++c)
+        for (int i = 0; ok; ++i) {
+            const int slot = i % TQ;
+            if (!mbar_wait(&bar[B_TF0 + slot], (i / TQ) & 1, abortp)) { fail(14); break; }
+            const int tt = tq[slot];
+            mbar_arrive(&bar[B_TE0 + slot]);
+            if (tt < 0) break;
+            const TileInfo ti = tile_info(a, tt);
+            const int row_pos = a.pos0 + ti.r0 + trow;
+            auto row_off = [&](int r) { return (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D; };
+            // Q rows of this warp's quarter -> FP16 in the swizzled K-major layout. Lane i reads
+            // channels 4i..4i+3 of each row (coalesced 512-byte rows), all 32 rows in flight.
+            // The buffer held the previous tile's output staging: the group's four warps are
+            // done with it first.
+            {
+                float4 xr[32];
                 #pragma unroll
-                for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(sr[c][i]));
-            float* v = reinterpret_cast<float*>(&sr[0][0]);
-            const int k0 = j * BN;
-            const int lim = row_pos - k0;                       // keys c > lim are in the future
-            if (lim < BN - 1) {                                 // tile crosses the diagonal
-                #pragma unroll
-                for (int c = 0; c < BN; ++c) v[c] = (c > lim) ? -INFINITY : v[c];
-            }
-            // row max: four independent 3-input max chains, then combined
-            float mq[4];
-            #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-                const float* w = v + q4 * 32;
-                float x = fmax3(w[0], w[1], w[2]);
-                #pragma unroll
-                for (int c = 3; c < 31; c += 2) x = fmax3(x, w[c], w[c + 1]);
-                mq[q4] = fmaxf(x, w[31]);
-            }
-            float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
-            float alpha = 1.f;
-            bool rescale = false;
-            if (j == 0) m = mt;
-            else if (mt > m + RESCALE_THRESHOLD) { alpha = ex2_approx(m - mt); m = mt; rescale = true; }
-            // p = 2^(s*scale - m): packed FMA pairs, MUFU ex2, FP16 pairs into TMEM over S_h
-            // (the first half is stored while the second half is computed)
-            const float2 sc2 = make_float2(scale, scale), mn2 = make_float2(-m, -m);
-            float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t pk[32];
-                #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const int k = half * 64 + 2 * c;
-                    const float2 x = ffma2(make_float2(v[k], v[k + 1]), sc2, mn2);
-                    const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                    ps[c & 3] = fadd2(ps[c & 3], e);
-                    pk[c] = pack_half2(e.x, e.y);
+                for (int rr = 0; rr < 32; ++rr) {
+                    const int r = ti.r0 + wq * 32 + rr;
+                    xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(a.q + row_off(r)) + lane)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                tmem_st32(s_col + half * 32, pk);
-            }
-            const float psum = (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) + (ps[3].x + ps[3].y);
-            if (rescale) {
-                // O_h holds PV_h(0..j-1) (the commit that announced S_h(j) covered them); it is
-                // rescaled before PV_h(j) is allowed to accumulate into it
+                asm volatile("bar.sync %0, 128;" ::"r"(1 + h) : "memory");
                 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t rr[32];
-                    tmem_ld32(o_col + c * 32, rr);
-                    tmem_wait_ld();
+                for (int rr = 0; rr < 32; ++rr)
+                    *reinterpret_cast<uint2*>(Qs + swz(wq * 32 + rr, lane >> 1) + (lane & 1) * 8) =
+                        make_uint2(pack_half2(xr[rr].x, xr[rr].y), pack_half2(xr[rr].z, xr[rr].w));
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&bar[B_Q0 + h]);
+
+            float m = -INFINITY, lsum = 0.f;
+            for (int j = 0; j < ti.nk; ++j, ++kt) {
+                if (!mbar_wait(&bar[B_SF0 + h], kt & 1, abortp)) { fail(11); ok = false; break; }
+                tc_fence_after();
+                // S row -> registers: four 32-column loads in flight, one wait; the empty asm pins
+                // every use of the loaded registers after the wait
+                uint32_t sr[4][32];
+                #pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, sr[c]);
+                tmem_wait_ld();
+                #pragma unroll
+                for (int c = 0; c < 4; ++c)
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * alpha);
-                    tmem_st32(o_col + c * 32, rr);
+                    for (int e = 0; e < 32; ++e) asm volatile("" : "+r"(sr[c][e]));
+                float* v = reinterpret_cast<float*>(&sr[0][0]);
+                const int k0 = j * BN;
+                const int lim = row_pos - k0;                   // keys c > lim are in the future
+                if (lim < BN - 1) {                             // tile crosses the diagonal
+                    #pragma unroll
+                    for (int c = 0; c < BN; ++c) v[c] = (c > lim) ? -INFINITY : v[c];
                 }
-                lsum *= alpha;
+                // row max: four independent 3-input max chains, then combined
+                float mq[4];
+                #pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    const float* w = v + q4 * 32;
+                    float x = fmax3(w[0], w[1], w[2]);
+                    #pragma unroll
+                    for (int c = 3; c < 31; c += 2) x = fmax3(x, w[c], w[c + 1]);
+                    mq[q4] = fmaxf(x, w[31]);
+                }
+                float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * scale;
+                float alpha = 1.f;
+                bool rescale = false;
+                if (j == 0) m = mt;
+                else if (mt > m + RESCALE_THRESHOLD) { alpha = ex2_approx(m - mt); m = mt; rescale = true; }
+                // p = 2^(s*scale - m): packed FMA pairs, MUFU ex2, FP16 pairs into TMEM over S_h
+                // (the first half is stored while the second half is computed)
+                const float2 sc2 = make_float2(scale, scale), mn2 = make_float2(-m, -m);
+                float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                #pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t pk[32];
+                    #pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const int k = half * 64 + 2 * c;
+                        const float2 x = ffma2(make_float2(v[k], v[k + 1]), sc2, mn2);
+                        const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                        ps[c & 3] = fadd2(ps[c & 3], e);
+                        pk[c] = pack_half2(e.x, e.y);
+                    }
+                    tmem_st32(s_col + half * 32, pk);
+                }
+                const float psum = (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) + (ps[3].x + ps[3].y);
+                if (rescale) {
+                    // O_h holds PV_h(0..j-1) (the commit that announced S_h(j) covered them); it is
+                    // rescaled before PV_h(j) is allowed to accumulate into it
+                    #pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t rr[32];
+                        tmem_ld32(o_col + c * 32, rr);
+                        tmem_wait_ld();
+                        #pragma unroll
+                        for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+                        tmem_st32(o_col + c * 32, rr);
+                    }
+                    lsum *= alpha;
+                }
+                lsum += psum;
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&bar[B_PF0 + h]);
             }
-            lsum += psum;
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&bar[B_PF0 + h]);
-        }
-        if (ok && mbar_wait(&bar[B_OD0 + h], 0, abortp)) {
-            // Output rows leave through this head's Q buffer (its last reader, QK_h of the last
-            // tile, has completed): each thread writes its normalised row half (64 columns) into
-            // a 32-row x 256-byte block of the warp, then the warp stores two rows per
-            // instruction as coalesced 256-byte segments.
+            if (!ok) break;
+            // ---- epilogue: O_h of this tile (all its MMAs, QK_h included, have completed) ----
+            if (!mbar_wait(&bar[B_OD0 + h], i & 1, abortp)) { fail(13); break; }
             tc_fence_after();
+            // Output rows leave through this head's Q buffer: each thread writes its normalised
+            // row half (64 columns) into a 32-row x 256-byte block of the warp, then the warp
+            // stores two rows per instruction as coalesced 256-byte segments.
             const float inv = 1.f / lsum;
             uint8_t* stage = Qs + wq * 8192;
             #pragma unroll
@@ -274,6 +299,10 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 tmem_ld32(o_col + part * 64, ra);
                 tmem_ld32(o_col + part * 64 + 32, rb);
                 tmem_wait_ld();
+                if (part == 1) {                              // O_h fully read: the next tile may overwrite it
+                    tc_fence_before();
+                    mbar_arrive(&bar[B_OF0 + h]);
+                }
                 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
                     const uint32_t* src = c < 8 ? ra + 4 * c : rb + 4 * (c - 8);
@@ -286,13 +315,11 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 for (int k = 0; k < 16; ++k) {
                     const int rr = 2 * k + (lane >> 4), c = lane & 15;
                     const float4 val = *reinterpret_cast<const float4*>(stage + rr * 256 + ((c ^ (rr & 15)) << 4));
-                    const int r = r0 + wq * 32 + rr;
+                    const int r = ti.r0 + wq * 32 + rr;
                     if (r < a.n) *reinterpret_cast<float4*>(a.out + row_off(r) + part * 64 + c * 4) = val;
                 }
                 __syncwarp();
             }
-        } else if (ok) {
-            fail(13);
         }
     } else if (warp == 8) {
         // ================================== MMA issuer ==================================
@@ -300,15 +327,15 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         const uint32_t idesc_pv = idesc_f16_f32(BM, D, true);
         const uint32_t q_addr = smem_u32(smem + OFF_Q), ring_addr = smem_u32(smem + OFF_RING);
         bool ok = true;
-        auto wait_item = [&](int i) {                    // ring item i has landed
-            return mbar_wait(&bar[B_FULL0 + i % RING], (i / RING) & 1, abortp);
+        auto wait_item = [&](int it) {                   // ring item it has landed
+            return mbar_wait(&bar[B_FULL0 + it % RING], (it / RING) & 1, abortp);
         };
-        auto release_item = [&](int i) {                 // stage of item i free once prior MMAs finish
-            if (lane == 0) mma_commit(&bar[B_EMPTY0 + i % RING]);
+        auto release_item = [&](int it) {                // stage of item it free once prior MMAs finish
+            if (lane == 0) mma_commit(&bar[B_EMPTY0 + it % RING]);
             __syncwarp();
         };
-        auto issue_qk = [&](int j, int h) {
-            const uint32_t kb = ring_addr + ((2 * j) % RING) * TILE_BYTES, qb = q_addr + h * 32768;
+        auto issue_qk = [&](int it, int h) {
+            const uint32_t kb = ring_addr + (it % RING) * TILE_BYTES, qb = q_addr + h * 32768;
             if (lane == 0) {
                 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
@@ -319,61 +346,73 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             }
             __syncwarp();
         };
-        auto issue_pv = [&](int j, int h) {              // A = P_h in TMEM: 8 columns per 16 keys
-            const uint32_t vb = ring_addr + ((2 * j + 1) % RING) * TILE_BYTES;
+        auto issue_pv = [&](int it, int h, bool first, bool last) {   // A = P_h in TMEM: 8 columns per 16 keys
+            const uint32_t vb = ring_addr + (it % RING) * TILE_BYTES;
             if (lane == 0) {
                 #pragma unroll
                 for (int s = 0; s < 8; ++s)
                     mma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + s * 8, sw128_desc(vb + s * 2048, 16384, 1024),
-                               idesc_pv, (j > 0 || s > 0) ? 1u : 0u);
-                if (j == nk - 1) mma_commit(&bar[B_OD0 + h]);   // O_h final
+                               idesc_pv, (!first || s > 0) ? 1u : 0u);
+                if (last) mma_commit(&bar[B_OD0 + h]);   // O_h final for the tile
             }
             __syncwarp();
         };
-        // prologue: S_0(0), S_1(0)
-        if (!mbar_wait(&bar[B_Q0], 0, abortp) || !mbar_wait(&bar[B_Q1], 0, abortp) || !wait_item(0)) {
-            fail(21); ok = false;
-        }
-        if (ok) {
-            tc_fence_after();
-            issue_qk(0, 0);
-            issue_qk(0, 1);
-            release_item(0);
-        }
-        // Per tile j and head h: O_h += P_h(j) V_j as soon as P_h(j) is written, then
-        // S_h(j+1) = Q_h K_{j+1}^T; the tensor pipe works on one head while the other head's
-        // softmax runs.
-        for (int j = 0; j < nk && ok; ++j) {
-            if (!wait_item(2 * j + 1)) { fail(22); ok = false; break; }
-            if (j == nk - 1 && valid_keys < (j + 1) * BN) {
-                // Rows of the last V tile past the causal end hold stale data: zero them so
-                // that a zero probability never meets a non-finite value.
-                uint8_t* Vs = smem + OFF_RING + ((2 * j + 1) % RING) * TILE_BYTES;
-                const int first = valid_keys - j * BN;
-                for (int idx = first * 16 + lane; idx < BN * 16; idx += 32) {
-                    const int row = idx >> 4, c = idx & 15;        // c: 16-byte chunk of the 256-byte row
-                    const int half_sel = c >> 3, cc = c & 7;
-                    *reinterpret_cast<uint4*>(Vs + half_sel * 16384 + (row >> 3) * 1024 + (row & 7) * 128 +
-                                              ((cc ^ (row & 7)) << 4)) = make_uint4(0, 0, 0, 0);
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
+        int base = 0;                                    // ring item of the tile's K_0
+        uint32_t kt = 0;                                 // key tiles processed (S, P phases)
+        for (int i = 0; ok; ++i) {
+            const int slot = i % TQ;
+            if (!mbar_wait(&bar[B_TF0 + slot], (i / TQ) & 1, abortp)) { fail(20); break; }
+            const int tt = tq[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar[B_TE0 + slot]);
+            if (tt < 0) break;
+            const TileInfo ti = tile_info(a, tt);
+            // tile prologue: S_0(0), S_1(0)
+            if (!mbar_wait(&bar[B_Q0], i & 1, abortp) || !mbar_wait(&bar[B_Q1], i & 1, abortp) || !wait_item(base)) {
+                fail(21); ok = false; break;
             }
             tc_fence_after();
-            for (int h = 0; h < 2 && ok; ++h) {
-                if (!mbar_wait(&bar[B_PF0 + h], j & 1, abortp)) { fail(23); ok = false; break; }
+            issue_qk(base, 0);
+            issue_qk(base, 1);
+            release_item(base);
+            // Per key tile j and head h: O_h += P_h(j) V_j as soon as P_h(j) is written, then
+            // S_h(j+1) = Q_h K_{j+1}^T over P_h(j) (ordered after PV_h(j), issued just before);
+            // the tensor pipe works on one head while the other head's softmax runs.
+            for (int j = 0; j < ti.nk && ok; ++j, ++kt) {
+                const int iv = base + 2 * j + 1;
+                if (!wait_item(iv)) { fail(22); ok = false; break; }
+                if (j == ti.nk - 1 && ti.valid_keys < (j + 1) * BN) {
+                    // Rows of the last V tile past the causal end hold stale data: zero them so
+                    // that a zero probability never meets a non-finite value.
+                    uint8_t* Vs = smem + OFF_RING + (iv % RING) * TILE_BYTES;
+                    const int first = ti.valid_keys - j * BN;
+                    for (int idx = first * 16 + lane; idx < BN * 16; idx += 32) {
+                        const int row = idx >> 4, c = idx & 15;    // c: 16-byte chunk of the 256-byte row
+                        const int half_sel = c >> 3, cc = c & 7;
+                        *reinterpret_cast<uint4*>(Vs + half_sel * 16384 + (row >> 3) * 1024 + (row & 7) * 128 +
+                                                  ((cc ^ (row & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                }
                 tc_fence_after();
-                issue_pv(j, h);
-                if (h == 1) release_item(2 * j + 1);         // V_j free when PV_1(j) completes
-                if (j + 1 < nk) {
-                    // S_h(j+1) over P_h(j): ordered after PV_h(j), issued just above
-                    const int jn = j + 1;
-                    if (h == 0 && !wait_item(2 * jn)) { fail(24); ok = false; break; }
+                for (int h = 0; h < 2 && ok; ++h) {
+                    if (!mbar_wait(&bar[B_PF0 + h], kt & 1, abortp)) { fail(23); ok = false; break; }
+                    // the first PV of a tile overwrites O_h: the previous tile's epilogue has read it
+                    if (j == 0 && i > 0 && !mbar_wait(&bar[B_OF0 + h], (i - 1) & 1, abortp)) { fail(27); ok = false; break; }
                     tc_fence_after();
-                    issue_qk(jn, h);
-                    if (h == 1) release_item(2 * jn);        // K_{j+1} free when QK_1(j+1) completes
+                    issue_pv(iv, h, j == 0, j == ti.nk - 1);
+                    if (h == 1) release_item(iv);                  // V_j free when PV_1(j) completes
+                    if (j + 1 < ti.nk) {
+                        const int ik = base + 2 * j + 2;
+                        if (h == 0 && !wait_item(ik)) { fail(24); ok = false; break; }
+                        tc_fence_after();
+                        issue_qk(ik, h);
+                        if (h == 1) release_item(ik);              // K_{j+1} free when QK_1(j+1) completes
+                    }
                 }
             }
+            base += 2 * ti.nk;
         }
         // drain: every MMA this thread issued has completed before TMEM is released
         if (lane == 0) {
@@ -382,23 +421,35 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         }
         __syncwarp();
     } else if (warp == 9 && lane == 0) {
-        // ================================== TMA producer ==================================
+        // ========================= tile queue + TMA producer =========================
         int issued = 0;
         bool ok = true;
-        for (int i = 0; i < 2 * nk && ok; ++i) {
-            const int st = i % RING;
-            if (i >= RING && !mbar_wait(&bar[B_EMPTY0 + st], ((i / RING) - 1) & 1, abortp)) { fail(31); ok = false; break; }
-            uint8_t* dst = smem + OFF_RING + st * TILE_BYTES;
-            const int plane = (i & 1) ? plane_v : plane_k, key0 = (i >> 1) * BN;
-            mbar_arrive_expect_tx(&bar[B_FULL0 + st], TILE_BYTES);
-            tma_load_3d(dst, &kv_map, 0, key0, plane, &bar[B_FULL0 + st]);
-            tma_load_3d(dst + 16384, &kv_map, 64, key0, plane, &bar[B_FULL0 + st]);
-            ++issued;
+        for (int i = 0; ok; ++i) {
+            const int slot = i % TQ;
+            if (i >= TQ && !mbar_wait(&bar[B_TE0 + slot], ((i / TQ) - 1) & 1, abortp)) { fail(30); break; }
+            int tt = atomicAdd(a.tile_counter, 1);
+            if (tt >= a.n_tiles) tt = -1;
+            tq[slot] = tt;
+            mbar_arrive(&bar[B_TF0 + slot]);                 // the slot's value is visible to the waiters
+            if (tt < 0) break;
+            const TileInfo ti = tile_info(a, tt);
+            for (int j2 = 0; j2 < 2 * ti.nk; ++j2) {
+                const int st = issued % RING;
+                if (issued >= RING && !mbar_wait(&bar[B_EMPTY0 + st], ((issued / RING) - 1) & 1, abortp)) {
+                    fail(31); ok = false; break;
+                }
+                uint8_t* dst = smem + OFF_RING + st * TILE_BYTES;
+                const int plane = (j2 & 1) ? ti.plane_k + a.hkv : ti.plane_k, key0 = (j2 >> 1) * BN;
+                mbar_arrive_expect_tx(&bar[B_FULL0 + st], TILE_BYTES);
+                tma_load_3d(dst, &kv_map, 0, key0, plane, &bar[B_FULL0 + st]);
+                tma_load_3d(dst + 16384, &kv_map, 64, key0, plane, &bar[B_FULL0 + st]);
+                ++issued;
+            }
         }
         if (!ok) {
             // drain the loads this thread issued (bounded, ignoring the abort flag)
-            for (int i = std::max(0, issued - RING); i < issued; ++i)
-                mbar_wait(&bar[B_FULL0 + i % RING], (i / RING) & 1, &never_abort, 500000000ull);
+            for (int it = std::max(0, issued - RING); it < issued; ++it)
+                mbar_wait(&bar[B_FULL0 + it % RING], (it / RING) & 1, &never_abort, 500000000ull);
         }
     }
 
@@ -414,8 +465,8 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
 
 // Host side --------------------------------------------------------------------------------------
 int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
-                              int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
-                              cudaStream_t s) {
+                              int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* tile_counter,
+                              int* error, cudaStream_t s) {
     if (row_begin >= n) return 0;
     static int checked = 0;                      // 1: ready, -1: refused
     if (!checked) {
@@ -434,7 +485,13 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out
     a.q = q; a.out = out; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
     a.hq = hq; a.hkv = hkv; a.layers_total = layers_total; a.row_begin = row_begin;
     a.n_qtiles = (n - row_begin + BM - 1) / BM; a.error = error;
-    const unsigned blocks = (unsigned)(a.n_qtiles * hkv * n_layers);
+    a.n_tiles = a.n_qtiles * hkv * n_layers;
+    a.tile_counter = tile_counter;
+    // persistent: one CTA per SM (225 KB of shared memory each) pulls tiles from the counter
+    int dev = 0, sms = NUM_SMS_B200;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const unsigned blocks = (unsigned)std::min(a.n_tiles, sms);
+    if (cudaMemsetAsync(tile_counter, 0, sizeof(int), s) != cudaSuccess) return -2;
     attn_prefill_sm100_kernel<<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
     return 0;
 }

@@ -51,6 +51,7 @@ struct qa_ctx {
     size_t staging_floats = 0;
     CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
     int* error = nullptr;                  // device-side error code of bounded waits (0 = none)
+    int* prefill_tiles = nullptr;          // work-item counter of the persistent prefill kernel
     void* comm = nullptr;                  // NCCL communicator (multi-GPU)
     cudaStream_t comm_stream = nullptr;    // NCCL work runs here, ordered after/before the context stream
     cudaEvent_t comm_ev[2] = {nullptr, nullptr};
@@ -297,6 +298,7 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     if (cudaMemset(ctx->counters, 0, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
 
     if (cudaMalloc(&ctx->error, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMalloc(&ctx->prefill_tiles, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMemset(ctx->error, 0, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
     if (make_kv_map(ctx) != QA_OK) return cleanup(QA_ERR_CUDA);
 
@@ -314,6 +316,7 @@ void qa_destroy(qa_ctx* ctx) {
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
     cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->staging); cudaFree(ctx->error);
+    cudaFree(ctx->prefill_tiles);
     cudaFree(ctx->gather_buf); cudaFree(ctx->kv_buf[0]); cudaFree(ctx->kv_buf[1]);
     for (cudaEvent_t e : ctx->kv_comm_done) if (e) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->kv_unpacked) if (e) cudaEventDestroy(e);
@@ -482,7 +485,7 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
             launch_attn_head_rows(r, ctx->stream);
         }
         if (launch_attn_prefill_sm100(ctx->kv_map, qd, od, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv,
-                                      ctx->cfg.n_layers, tc_begin, ctx->error, ctx->stream))
+                                      ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->error, ctx->stream))
             return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel has an unexpected register allocation");
     }
     if ((st = after_launch(ctx, seq, decode ? "attn_decode" : "attn_prefill"))) return st;

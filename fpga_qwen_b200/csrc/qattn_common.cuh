@@ -66,8 +66,8 @@ void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cuda
 // Tensor-core prefill for rows [row_begin, n) (all with absolute position >= 128).
 // Returns non-zero (and launches nothing) if the kernel was not built with the expected registers.
 int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
-                               int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* error,
-                               cudaStream_t s);
+                              int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* tile_counter,
+                              int* error, cudaStream_t s);
 // TMA-streamed split-context decode. Row b of the call is sequence rows.seq[b] at position
 // rows.pos[b] (context rows.pos[b] + 1), b < n <= MAX_BATCH.
 struct DecodePlan {
