@@ -192,8 +192,8 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             auto row_off = [&](int r) { return (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D; };
             // Q rows of this warp's quarter -> FP16 in the swizzled K-major layout. Lane i reads
             // channels 4i..4i+3 of each row (coalesced 512-byte rows), all 32 rows in flight.
-            // The buffer held the previous tile's output staging: the group's four warps are
-            // done with it first.
+            // These rows occupy exactly the two 4 KB pieces in which this warp staged its
+            // previous output rows, so a warp-level barrier orders the reuse.
             {
                 float4 xr[32];
                 #pragma unroll
@@ -202,7 +202,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(a.q + row_off(r)) + lane)
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                asm volatile("bar.sync %0, 128;" ::"r"(1 + h) : "memory");
+                __syncwarp();
                 #pragma unroll
                 for (int rr = 0; rr < 32; ++rr)
                     *reinterpret_cast<uint2*>(Qs + swz(wq * 32 + rr, lane >> 1) + (lane & 1) * 8) =
@@ -288,11 +288,12 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             // ---- epilogue: O_h of this tile (all its MMAs, QK_h included, have completed) ----
             if (!mbar_wait(&bar[B_OD0 + h], i & 1, abortp)) { fail(13); break; }
             tc_fence_after();
-            // Output rows leave through this head's Q buffer: each thread writes its normalised
-            // row half (64 columns) into a 32-row x 256-byte block of the warp, then the warp
+            // Output rows leave through this head's Q buffer, in the two 4 KB pieces that hold
+            // this warp's own Q rows (rows 0-15 of the warp in the first, 16-31 in the second):
+            // each thread writes its normalised row half (64 columns, 256 bytes), then the warp
             // stores two rows per instruction as coalesced 256-byte segments.
             const float inv = 1.f / lsum;
-            uint8_t* stage = Qs + wq * 8192;
+            auto stage_row = [&](int rr) { return Qs + (rr >> 4) * 16384 + wq * 4096 + (rr & 15) * 256; };
             #pragma unroll
             for (int part = 0; part < 2; ++part) {
                 uint32_t ra[32], rb[32];
@@ -306,7 +307,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
                     const uint32_t* src = c < 8 ? ra + 4 * c : rb + 4 * (c - 8);
-                    *reinterpret_cast<float4*>(stage + lane * 256 + ((c ^ (lane & 15)) << 4)) =
+                    *reinterpret_cast<float4*>(stage_row(lane) + ((c ^ (lane & 15)) << 4)) =
                         make_float4(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv,
                                     __uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
                 }
@@ -314,7 +315,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 #pragma unroll 4
                 for (int k = 0; k < 16; ++k) {
                     const int rr = 2 * k + (lane >> 4), c = lane & 15;
-                    const float4 val = *reinterpret_cast<const float4*>(stage + rr * 256 + ((c ^ (rr & 15)) << 4));
+                    const float4 val = *reinterpret_cast<const float4*>(stage_row(rr) + ((c ^ (rr & 15)) << 4));
                     const int r = ti.r0 + wq * 32 + rr;
                     if (r < a.n) *reinterpret_cast<float4*>(a.out + row_off(r) + part * 64 + c * 4) = val;
                 }
