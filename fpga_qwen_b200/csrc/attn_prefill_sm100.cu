@@ -134,6 +134,31 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Rows [r_off, r_off + 16) of one warp's 32-row quarter of head h: lane i reads channels
+// 4i..4i+3 of each row (coalesced 512-byte rows), all 16 rows in flight. With prefetch_only,
+// the rows are only pulled into L2 (no registers held).
+__device__ __forceinline__ void q_load_rows(const PrefillArgs& a, const TileInfo& ti, int h, int wq, int lane,
+                                            int r_off, float4 (&xr)[16], bool prefetch_only) {
+    const float* base = a.q + (((size_t)ti.l * a.n) * a.hq + (size_t)ti.kh * 2 + h) * D + lane * 4;
+    #pragma unroll
+    for (int rr = 0; rr < 16; ++rr) {
+        const int r = ti.r0 + wq * 32 + r_off + rr;
+        const float* p = base + (size_t)r * a.hq * D;
+        if (prefetch_only) {
+            if (r < a.n) asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+        } else {
+            xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+}
+// ... as FP16 in the swizzled K-major layout of the head's Q buffer.
+__device__ __forceinline__ void q_store_rows(uint8_t* Qs, int wq, int lane, int r_off, const float4 (&xr)[16]) {
+    #pragma unroll
+    for (int rr = 0; rr < 16; ++rr)
+        *reinterpret_cast<uint2*>(Qs + swz(wq * 32 + r_off + rr, lane >> 1) + (lane & 1) * 8) =
+            make_uint2(pack_half2(xr[rr].x, xr[rr].y), pack_half2(xr[rr].z, xr[rr].w));
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
 attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -180,38 +205,32 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         const uint32_t s_col = tmem + lane_base + h * 128;   // S_h; P_h in its first 64 columns
         const uint32_t o_col = tmem + lane_base + 256 + h * 128;
         uint32_t kt = 0;                                     // key tiles processed (S, P phases)
-        bool ok = true;
-        for (int i = 0; ok; ++i) {
+        // the i-th work item from the tile queue (-1: none left; -2: the wait gave up)
+        auto read_tile = [&](int i) {
             const int slot = i % TQ;
-            if (!mbar_wait(&bar[B_TF0 + slot], (i / TQ) & 1, abortp)) { fail(14); break; }
+            if (!mbar_wait(&bar[B_TF0 + slot], (i / TQ) & 1, abortp)) { fail(14); return -2; }
             const int tt = tq[slot];
             mbar_arrive(&bar[B_TE0 + slot]);
-            if (tt < 0) break;
-            const TileInfo ti = tile_info(a, tt);
-            const int row_pos = a.pos0 + ti.r0 + trow;
-            auto row_off = [&](int r) { return (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D; };
-            // Q rows of this warp's quarter -> FP16 in the swizzled K-major layout. Lane i reads
-            // channels 4i..4i+3 of each row (coalesced 512-byte rows), all 32 rows in flight.
-            // These rows occupy exactly the two 4 KB pieces in which this warp staged its
-            // previous output rows, so a warp-level barrier orders the reuse.
-            {
-                float4 xr[32];
-                #pragma unroll
-                for (int rr = 0; rr < 32; ++rr) {
-                    const int r = ti.r0 + wq * 32 + rr;
-                    xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(a.q + row_off(r)) + lane)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-                __syncwarp();
-                #pragma unroll
-                for (int rr = 0; rr < 32; ++rr)
-                    *reinterpret_cast<uint2*>(Qs + swz(wq * 32 + rr, lane >> 1) + (lane & 1) * 8) =
-                        make_uint2(pack_half2(xr[rr].x, xr[rr].y), pack_half2(xr[rr].z, xr[rr].w));
-            }
+            return tt;
+        };
+        // Q rows of this warp's quarter (q_load_rows / q_store_rows): loaded early, stored as
+        // FP16 into this warp's own rows of the head's Q buffer when that is free.
+        float4 xr[16];
+        auto store_q = [&](const TileInfo& tn) {
+            q_load_rows(a, tn, h, wq, lane, 0, xr, false);
+            q_store_rows(Qs, wq, lane, 0, xr);
+            q_load_rows(a, tn, h, wq, lane, 16, xr, false);
+            q_store_rows(Qs, wq, lane, 16, xr);
             fence_proxy_async_smem();
             mbar_arrive(&bar[B_Q0 + h]);
-
+        };
+        int tt = read_tile(0);
+        if (tt >= 0) store_q(tile_info(a, tt));
+        for (int i = 0; tt >= 0; ++i) {
+            const TileInfo ti = tile_info(a, tt);
+            const int row_pos = a.pos0 + ti.r0 + trow;
             float m = -INFINITY, lsum = 0.f;
+            bool ok = true;
             for (int j = 0; j < ti.nk; ++j, ++kt) {
                 if (!mbar_wait(&bar[B_SF0 + h], kt & 1, abortp)) { fail(11); ok = false; break; }
                 tc_fence_after();
@@ -285,42 +304,50 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 mbar_arrive(&bar[B_PF0 + h]);
             }
             if (!ok) break;
+            // the next work item's Q rows start loading now and land during the epilogue
+            const int next = read_tile(i + 1);
+            if (next >= 0) {                                 // pulled into L2 while the epilogue runs
+                const TileInfo tn = tile_info(a, next);
+                q_load_rows(a, tn, h, wq, lane, 0, xr, true);
+                q_load_rows(a, tn, h, wq, lane, 16, xr, true);
+            }
             // ---- epilogue: O_h of this tile (all its MMAs, QK_h included, have completed) ----
             if (!mbar_wait(&bar[B_OD0 + h], i & 1, abortp)) { fail(13); break; }
             tc_fence_after();
-            // Output rows leave through this head's Q buffer, in the two 4 KB pieces that hold
-            // this warp's own Q rows (rows 0-15 of the warp in the first, 16-31 in the second):
-            // each thread writes its normalised row half (64 columns, 256 bytes), then the warp
-            // stores two rows per instruction as coalesced 256-byte segments.
+            // Output rows leave through the 4 KB piece of this head's Q buffer that holds the
+            // first 64 channels of this warp's own Q rows, 32 columns at a time: each thread
+            // writes its normalised 128-byte row segment (8 chunks, XOR-swizzled by row), then
+            // the warp stores four rows per instruction as coalesced 128-byte segments.
             const float inv = 1.f / lsum;
-            auto stage_row = [&](int rr) { return Qs + (rr >> 4) * 16384 + wq * 4096 + (rr & 15) * 256; };
+            uint8_t* stage = Qs + wq * 4096;
             #pragma unroll
-            for (int part = 0; part < 2; ++part) {
-                uint32_t ra[32], rb[32];
-                tmem_ld32(o_col + part * 64, ra);
-                tmem_ld32(o_col + part * 64 + 32, rb);
+            for (int part = 0; part < 4; ++part) {
+                uint32_t ro[32];
+                tmem_ld32(o_col + part * 32, ro);
                 tmem_wait_ld();
-                if (part == 1) {                              // O_h fully read: the next tile may overwrite it
+                if (part == 3) {                              // O_h fully read: the next tile may overwrite it
                     tc_fence_before();
                     mbar_arrive(&bar[B_OF0 + h]);
                 }
                 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const uint32_t* src = c < 8 ? ra + 4 * c : rb + 4 * (c - 8);
-                    *reinterpret_cast<float4*>(stage_row(lane) + ((c ^ (lane & 15)) << 4)) =
-                        make_float4(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv,
-                                    __uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-                }
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<float4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                        make_float4(__uint_as_float(ro[4 * c]) * inv, __uint_as_float(ro[4 * c + 1]) * inv,
+                                    __uint_as_float(ro[4 * c + 2]) * inv, __uint_as_float(ro[4 * c + 3]) * inv);
                 __syncwarp();
-                #pragma unroll 4
-                for (int k = 0; k < 16; ++k) {
-                    const int rr = 2 * k + (lane >> 4), c = lane & 15;
-                    const float4 val = *reinterpret_cast<const float4*>(stage_row(rr) + ((c ^ (rr & 15)) << 4));
+                #pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int rr = 4 * k + (lane >> 3), c = lane & 7;
+                    const float4 val = *reinterpret_cast<const float4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
                     const int r = ti.r0 + wq * 32 + rr;
-                    if (r < a.n) *reinterpret_cast<float4*>(a.out + row_off(r) + part * 64 + c * 4) = val;
+                    if (r < a.n)
+                        *reinterpret_cast<float4*>(a.out + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D +
+                                                   part * 32 + c * 4) = val;
                 }
                 __syncwarp();
             }
+            tt = next;
+            if (tt >= 0) store_q(tile_info(a, tt));                          // this warp's own Q rows, after its staging
         }
     } else if (warp == 8) {
         // ================================== MMA issuer ==================================
@@ -368,12 +395,12 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             if (lane == 0) mbar_arrive(&bar[B_TE0 + slot]);
             if (tt < 0) break;
             const TileInfo ti = tile_info(a, tt);
-            // tile prologue: S_0(0), S_1(0)
-            if (!mbar_wait(&bar[B_Q0], i & 1, abortp) || !mbar_wait(&bar[B_Q1], i & 1, abortp) || !wait_item(base)) {
-                fail(21); ok = false; break;
-            }
+            // tile prologue: S_0(0) as soon as Q_0 is in place, then S_1(0)
+            if (!wait_item(base) || !mbar_wait(&bar[B_Q0], i & 1, abortp)) { fail(21); ok = false; break; }
             tc_fence_after();
             issue_qk(base, 0);
+            if (!mbar_wait(&bar[B_Q1], i & 1, abortp)) { fail(21); ok = false; break; }
+            tc_fence_after();
             issue_qk(base, 1);
             release_item(base);
             // Per key tile j and head h: O_h += P_h(j) V_j as soon as P_h(j) is written, then
