@@ -560,10 +560,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         __syncthreads();
         if (tid == 0) {
             if (atomicAdd(a.g.done, 1u) == gridDim.x - 1) {
+                *a.g.done = 0;                         // ready for the next launch, before anyone may start it
                 __threadfence_system();
                 for (int r = 0; r < a.g.n_flags; ++r)
                     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.g.flags[r]), "r"(a.g.step) : "memory");
-                *a.g.done = 0;                         // ready for the next launch on this stream
             }
         }
     }

@@ -614,7 +614,8 @@ static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int 
     }
     in.norms = ctx->norms; in.cosines = ctx->cosines; in.sines = ctx->sines; in.eps = ctx->cfg.norm_eps;
     // overlap with the previous step only right after a fused step of this context on this stream
-    in.pdl = ctx->step_overlap && ctx->last_fused_step && !ctx->cfg.io_host && !gather ? 1 : 0;
+    // (or the gather wait that followed one)
+    in.pdl = ctx->step_overlap && ctx->last_fused_step && !ctx->cfg.io_host ? 1 : 0;
     bool fused = false;
     const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
     if ((st = ensure_decode_scratch(ctx, plan))) return st;
@@ -646,7 +647,7 @@ static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int 
                                  ctx->partial, ctx->counters, ctx->error, ctx->stream, nullptr, gather);
     }
     if ((st = after_launch(ctx, n == 1 ? seqs[0] : -1, "attn_decode_step"))) return st;
-    ctx->last_fused_step = fused && !gather;
+    ctx->last_fused_step = fused;
     for (int b = 0; b < n; ++b)
         for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seqs[b]][l] = pos[b] + 1;
     if (ctx->cfg.io_host) {
@@ -944,9 +945,12 @@ int qa_decode_step_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos
     g.step = step;
     float* landing = reinterpret_cast<float*>(ctx->peer_block + par);
     if ((st = decode_step(ctx, &seq, &pos, 1, layer, n_layers, q_pre, k_pre, v, q_out, landing, &g))) return st;
+    const bool chain = ctx->last_fused_step;           // the wait reads no KV rows: the chain goes on
     launch_gather_wait_copy(reinterpret_cast<const unsigned*>(ctx->peer_block + ctx->flags_off), ctx->nranks, step,
                             landing, full, (size_t)n_layers * g.out_hq * D, ctx->error, ctx->stream);
-    return after_launch(ctx, -1, "gather_wait_copy");
+    st = after_launch(ctx, -1, "gather_wait_copy");
+    ctx->last_fused_step = chain && st == QA_OK;
+    return st;
 }
 
 static int kv_transfer(qa_ctx* ctx, int seq, int ntok, int peer, bool send) {

@@ -98,6 +98,9 @@ __global__ void pack_kv_kernel(const KVLayout kv, int seq, int ntok, uint4* buf,
 // the CTA copies its slice. Peers wrote the landing buffer over NVLink before their release.
 __global__ void gather_wait_copy_kernel(const unsigned* flags, int nranks, unsigned step, const float4* landing,
                                         float4* out, size_t n4, int* error) {
+    // Launched as a programmatic dependent of the decode step, this grid starts while that step
+    // runs (it needs nothing from it but the flags it waits for), and lets the next step launch.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ int ok;
     if (threadIdx.x == 0) {
         ok = 1;
@@ -123,8 +126,14 @@ void launch_gather_wait_copy(const unsigned* flags, int nranks, unsigned step, c
                              size_t floats, int* error, cudaStream_t s) {
     const size_t n4 = floats / 4;
     const int blocks = (int)std::min<size_t>(64, (n4 + 255) / 256);
-    gather_wait_copy_kernel<<<blocks, 256, 0, s>>>(flags, nranks, step, reinterpret_cast<const float4*>(landing),
-                                                   reinterpret_cast<float4*>(out), n4, error);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(blocks); cfg.blockDim = dim3(256); cfg.dynamicSmemBytes = 0; cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, gather_wait_copy_kernel, flags, nranks, step, reinterpret_cast<const float4*>(landing),
+                       reinterpret_cast<float4*>(out), n4, error);
 }
 
 void launch_permute_heads(const float* gathered, float* full, int nranks, int n_layers, int n, int hq_local,

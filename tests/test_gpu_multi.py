@@ -155,6 +155,7 @@ def _worker(rank, world, port, out_dir):
         c.set_stream(stream)
         H.set_norms(c, qw, kw)
     qd.init_comm(g_shard)
+    g_shard.set_step_overlap(True)                 # steps and gather waits chained by dependent launch
     report["peer_mapped"] = g_shard.comm_info()[2]
     hist_s = [t[:, :P].contiguous() for t in (qs, ks, vs)]
     hist_f = [t[:, :P].contiguous() for t in (q, k, v)]
