@@ -553,15 +553,16 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         }
     }
     if (a.g.n_flags > 0) {
-        // every thread orders its own output stores (peers' memory included) at system scope;
-        // then the last CTA of the grid marks the step done in every rank's flags with a
-        // release store
-        __threadfence_system();
+        // The CTA's output stores (peers' memory included) are ordered before its count by the
+        // barrier and one system-scope acquire-release add (cumulative over the CTA's stores);
+        // the last CTA, having acquired every count, marks the step done in every rank's flags
+        // with release stores.
         __syncthreads();
         if (tid == 0) {
-            if (atomicAdd(a.g.done, 1u) == gridDim.x - 1) {
+            unsigned prev;
+            asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.g.done) : "memory");
+            if (prev == gridDim.x - 1) {
                 *a.g.done = 0;                         // ready for the next launch, before anyone may start it
-                __threadfence_system();
                 for (int r = 0; r < a.g.n_flags; ++r)
                     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.g.flags[r]), "r"(a.g.step) : "memory");
             }
