@@ -36,6 +36,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode-attn HBM GB/s & prefill-attn TFLOP/s, Qwen3-0.6B GQA, 4K ctx"
 L, HQ, HKV, D = 28, 16, 8, 128
 PREFILL, DECODE = 3968, 128
+PREFILL_GROUP = 7                                # layers per prefill launch when gathering heads (N > 1)
 KV_BYTES_PER_POS = L * HKV * D * 2 * 2          # 114,688 B: K and V rows of one position, all layers
 FLOPS_PER_KEY = 4 * D * HQ * L                  # 229,376 FLOP per (query row, visible key), all layers
 
@@ -287,13 +288,22 @@ def run_ours(args):
         ctx.append(0, 0, L, 0, PREFILL, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), pqn.data_ptr())
         if evs:
             evs["pa0"].record(stream)
-        ctx.attn_prefill(0, 0, L, 0, PREFILL, pqn.data_ptr(), pout.data_ptr())
         if world > 1:
-            ctx.gather_heads(L, PREFILL, pout.data_ptr(), pfull.data_ptr())
-            launches += 1      # permute (the all-gather itself is NCCL's kernel)
+            # layer groups: each group's all-gather (communication stream) overlaps the next
+            # group's attention
+            for c0 in range(0, L, PREFILL_GROUP):
+                nl = min(PREFILL_GROUP, L - c0)
+                off = c0 * PREFILL * hq * D * 4
+                ctx.attn_prefill(0, c0, nl, 0, PREFILL, pqn.data_ptr() + off, pout.data_ptr() + off)
+                ctx.gather_heads_async(nl, PREFILL, pout.data_ptr() + off, pfull.data_ptr() + c0 * PREFILL * HQ * D * 4)
+                launches += 3  # FP32 rows below position 128, tcgen05 prefill, permute (the all-gather is NCCL's)
+            ctx.comm_join()
+        else:
+            ctx.attn_prefill(0, 0, L, 0, PREFILL, pqn.data_ptr(), pout.data_ptr())
+            launches += 2      # FP32 rows below position 128, tcgen05 prefill
         if evs:
             evs["pa1"].record(stream)
-        launches += 3          # append, FP32 rows below position 128, tcgen05 prefill
+        launches += 1          # append
         ctx.commit(0, PREFILL)
         for s in range(DECODE):
             pos = PREFILL + s
@@ -336,13 +346,15 @@ def run_ours(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
 
     records = []
     sampler = ClockSampler(local)
     with sampler:
+        # the ranks leave the barrier together only after every sampler is producing samples
+        # (its start-up time differs by rank; a skew here would land in the first collective)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         start, end = mkev(), mkev()
         start.record(stream)
         for _ in range(args.steps):       # phase boundaries only: no events between decode launches

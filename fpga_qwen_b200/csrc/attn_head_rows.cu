@@ -6,132 +6,187 @@
 // reference's formula (engine/core.cpp:407-605 per output): s_t = q.K_t/sqrt(128), softmax
 // over t <= position, out = Σ p_t V_t.
 //
-// One CTA per (layer, KV head): it stages K (transposed, FP32) and V (FP32) of the first
-// nk <= 128 positions in shared memory once, then each warp takes rows in turn, both GQA
-// query heads at once: lane l scores keys 4l..4l+3 (one 16-byte read of the transposed K
-// feeds 8 FMAs), the warp forms both softmaxes with shuffle reductions, and lane l
-// accumulates output channels 4l..4l+3 of both heads.
+// One CTA per (layer, KV head) stages K (transposed) and V of the first nk <= 128 positions
+// in shared memory as FP32, once. Each warp then takes groups of four consecutive positions
+// with both GQA query heads: eight query rows share every shared-memory read.
+//   scores   lane l owns keys l, l+32, l+64, l+96 (a 32-key chunk is skipped by the whole
+//            warp when it lies above the group's last position); the eight rows' query
+//            values for one channel come as two broadcast float4 reads of the warp's Q
+//            buffer ([channel][row]), so one K read feeds 8 FMAs.
+//   softmax  per row over the warp (shuffle max and sum), probabilities written to the same
+//            warp buffer as [key][row].
+//   output   lane l owns channels 4l..4l+3: per key one float4 of V and two broadcast float4
+//            of probabilities feed 32 FMAs.
 #include "qattn_common.cuh"
 
 namespace qattn {
 namespace {
 
-constexpr int THREADS = 256;
+constexpr int THREADS = 512;
+constexpr int WARPS = THREADS / 32;
 constexpr int MAXK = 128;
-constexpr int KT_STRIDE = MAXK + 4;    // transposed K rows: [channel][key]
+constexpr int POS_PER_GROUP = 4;
+constexpr int QR = POS_PER_GROUP * GROUP;      // query rows per warp pass (row r: position r/2, head r%2)
+static_assert(QR == 8, "the row buffers are read as two float4 per channel or key");
+constexpr size_t SMEM_BYTES = ((size_t)D * MAXK + (size_t)MAXK * D + (size_t)WARPS * QR * MAXK) * sizeof(float);
+
+// Scores of the warp's eight rows against keys lane + 32j, j < NJ.
+template <int NJ>
+__device__ __forceinline__ void score_rows(const float* __restrict__ KT, const float* __restrict__ wq, int lane,
+                                           float (&acc)[4][QR]) {
+    #pragma unroll
+    for (int j = 0; j < NJ; ++j)
+        #pragma unroll
+        for (int r = 0; r < QR; ++r) acc[j][r] = 0.f;
+    #pragma unroll 4
+    for (int c = 0; c < D; ++c) {
+        const float4 qa = *reinterpret_cast<const float4*>(wq + c * QR);
+        const float4 qb = *reinterpret_cast<const float4*>(wq + c * QR + 4);
+        const float q[QR] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        #pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const float k = KT[c * MAXK + lane + 32 * j];
+            #pragma unroll
+            for (int r = 0; r < QR; ++r) acc[j][r] = fmaf(q[r], k, acc[j][r]);
+        }
+    }
+}
 
 __global__ void __launch_bounds__(THREADS, 1) attn_head_rows_kernel(const RowsArgs a) {
     extern __shared__ __align__(16) float smem[];
-    float* KT = smem;                                   // [128 channels][KT_STRIDE]
-    float* Vs = KT + D * KT_STRIDE;                     // [MAXK][128]
-    float* qbuf = Vs + MAXK * D;                        // [warps][GROUP][128]
-    float* pbuf = qbuf + (THREADS / 32) * GROUP * D;    // [warps][GROUP][MAXK]
+    float* KT = smem;                                   // [128 channels][MAXK keys]
+    float* Vs = KT + D * MAXK;                          // [MAXK keys][128 channels]
+    float* wbuf = Vs + MAXK * D;                        // per warp: Q [128][QR], then P [MAXK][QR]
     const int l = blockIdx.x / a.hkv, kh = blockIdx.x % a.hkv;
     const int layer = a.layer0 + l;
     const int rows = a.row_end;                         // rows [0, rows), positions pos0.. < 128
     const int nk = a.pos0 + rows;                       // keys needed (<= 128)
+    const int nk32 = (nk + 31) & ~31;
     const __half* Kp = a.kv.plane(a.seq, layer, 0, kh);
     const __half* Vp = a.kv.plane(a.seq, layer, 1, kh);
     // K transposed: consecutive threads take consecutive keys of one 8-channel group, so
-    // the transposed shared-memory writes are conflict-free
-    for (int i = threadIdx.x; i < nk * (D / 8); i += THREADS) {
-        const int c8 = (i / nk) * 8, t = i % nk;
-        const uint4 ku = *reinterpret_cast<const uint4*>(Kp + (size_t)t * D + c8);
+    // the transposed shared-memory writes are conflict-free; keys [nk, nk32) read as zero
+    for (int i = threadIdx.x; i < nk32 * (D / 8); i += THREADS) {
+        const int c8 = (i / nk32) * 8, t = i % nk32;
+        uint4 ku = make_uint4(0u, 0u, 0u, 0u);
+        if (t < nk) ku = *reinterpret_cast<const uint4*>(Kp + (size_t)t * D + c8);
         const __half* k8 = reinterpret_cast<const __half*>(&ku);
         #pragma unroll
-        for (int e = 0; e < 8; ++e) KT[(c8 + e) * KT_STRIDE + t] = __half2float(k8[e]);
+        for (int e = 0; e < 8; ++e) KT[(c8 + e) * MAXK + t] = __half2float(k8[e]);
     }
     // V row-major: consecutive threads take consecutive 8-channel groups of one key
     for (int i = threadIdx.x; i < nk * (D / 8); i += THREADS) {
         const int t = i / (D / 8), c8 = (i % (D / 8)) * 8;
         const uint4 vu = *reinterpret_cast<const uint4*>(Vp + (size_t)t * D + c8);
         const __half* v8 = reinterpret_cast<const __half*>(&vu);
-        #pragma unroll
-        for (int e = 0; e < 8; ++e) Vs[t * D + c8 + e] = __half2float(v8[e]);
+        float4* dst = reinterpret_cast<float4*>(Vs + t * D + c8);
+        dst[0] = make_float4(__half2float(v8[0]), __half2float(v8[1]), __half2float(v8[2]), __half2float(v8[3]));
+        dst[1] = make_float4(__half2float(v8[4]), __half2float(v8[5]), __half2float(v8[6]), __half2float(v8[7]));
     }
     __syncthreads();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* qw = qbuf + warp * GROUP * D;                // both query heads of the row
-    float* pw = pbuf + warp * GROUP * MAXK;
+    float* wq = wbuf + warp * QR * MAXK;
     const float scale = 1.4426950408889634f * 0.08838834764831845f;   // log2(e)/sqrt(128)
-    // one warp per row, both GQA heads at once; lane l scores keys 4l..4l+3 and accumulates
-    // output channels 4l..4l+3
-    for (int b = warp; b < rows; b += THREADS / 32) {
-        const int pos = a.pos0 + b;
-        const size_t row0 = ((size_t)l * a.n + b) * a.hq + (size_t)kh * GROUP;
+    const int groups = (rows + POS_PER_GROUP - 1) / POS_PER_GROUP;
+    for (int grp = warp; grp < groups; grp += WARPS) {
+        const int b0 = grp * POS_PER_GROUP;
+        const int last = min(b0 + POS_PER_GROUP, rows) - 1;           // last valid row of the group
+        const int pmax = a.pos0 + last;
+        // query rows -> wq[c][r]; rows past the end of the call are zero and never stored
         #pragma unroll
-        for (int g = 0; g < GROUP; ++g)
-            *reinterpret_cast<float4*>(qw + g * D + lane * 4) =
-                __ldg(reinterpret_cast<const float4*>(a.q + (row0 + g) * D) + lane);
-        __syncwarp();
-        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-        #pragma unroll 2
-        for (int c = 0; c < D; c += 4) {
-            const float4 qa = *reinterpret_cast<const float4*>(qw + c);
-            const float4 qb = *reinterpret_cast<const float4*>(qw + D + c);
-            const float q0[4] = {qa.x, qa.y, qa.z, qa.w}, q1[4] = {qb.x, qb.y, qb.z, qb.w};
+        for (int i = 0; i < D / 32; ++i) {
+            const int c = lane + 32 * i;
+            float q[QR];
             #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const float4 k = *reinterpret_cast<const float4*>(KT + (c + cc) * KT_STRIDE + lane * 4);
-                s0[0] = fmaf(q0[cc], k.x, s0[0]); s0[1] = fmaf(q0[cc], k.y, s0[1]);
-                s0[2] = fmaf(q0[cc], k.z, s0[2]); s0[3] = fmaf(q0[cc], k.w, s0[3]);
-                s1[0] = fmaf(q1[cc], k.x, s1[0]); s1[1] = fmaf(q1[cc], k.y, s1[1]);
-                s1[2] = fmaf(q1[cc], k.z, s1[2]); s1[3] = fmaf(q1[cc], k.w, s1[3]);
+            for (int r = 0; r < QR; ++r) {
+                const int b = b0 + (r >> 1);
+                q[r] = b < rows ? __ldg(a.q + (((size_t)l * a.n + b) * a.hq + kh * GROUP + (r & 1)) * D + c) : 0.f;
+            }
+            *reinterpret_cast<float4*>(wq + c * QR) = make_float4(q[0], q[1], q[2], q[3]);
+            *reinterpret_cast<float4*>(wq + c * QR + 4) = make_float4(q[4], q[5], q[6], q[7]);
+        }
+        __syncwarp();
+        float acc[4][QR];
+        const int nj = pmax / 32 + 1;                   // 32-key chunks at or below the last position
+        switch (nj) {
+            case 1: score_rows<1>(KT, wq, lane, acc); break;
+            case 2: score_rows<2>(KT, wq, lane, acc); break;
+            case 3: score_rows<3>(KT, wq, lane, acc); break;
+            default: score_rows<4>(KT, wq, lane, acc); break;
+        }
+        // softmax per row: key t = lane + 32j is visible to row r iff t <= its position
+        float inv[QR];
+        #pragma unroll
+        for (int r = 0; r < QR; ++r) {
+            const int pos = a.pos0 + min(b0 + (r >> 1), last);
+            float m = -INFINITY;
+            #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const bool ok = j < nj && lane + 32 * j <= pos;
+                acc[j][r] = ok ? acc[j][r] * scale : -INFINITY;
+                m = fmaxf(m, acc[j][r]);
+            }
+            #pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            float s = 0.f;
+            #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[j][r] = j < nj ? exp2f(acc[j][r] - m) : 0.f;
+                s += acc[j][r];
+            }
+            #pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+            inv[r] = 1.f / s;
+        }
+        __syncwarp();                                   // every lane is done reading wq
+        float* wp = wq;                                 // probabilities [key][row]
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (j < nj) {
+                const int t = lane + 32 * j;
+                *reinterpret_cast<float4*>(wp + t * QR) = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+                *reinterpret_cast<float4*>(wp + t * QR + 4) = make_float4(acc[j][4], acc[j][5], acc[j][6], acc[j][7]);
             }
         }
-        float m0 = -INFINITY, m1 = -INFINITY;
-        #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const bool ok = lane * 4 + i <= pos;
-            s0[i] = ok ? s0[i] * scale : -INFINITY;
-            s1[i] = ok ? s1[i] * scale : -INFINITY;
-            m0 = fmaxf(m0, s0[i]); m1 = fmaxf(m1, s1[i]);
-        }
-        #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
-            m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
-        }
-        float p0[4], p1[4], l0 = 0.f, l1 = 0.f;
-        #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            p0[i] = exp2f(s0[i] - m0); p1[i] = exp2f(s1[i] - m1);
-            l0 += p0[i]; l1 += p1[i];
-        }
-        *reinterpret_cast<float4*>(pw + lane * 4) = make_float4(p0[0], p0[1], p0[2], p0[3]);
-        *reinterpret_cast<float4*>(pw + MAXK + lane * 4) = make_float4(p1[0], p1[1], p1[2], p1[3]);
-        #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-        }
         __syncwarp();
-        float4 o0 = make_float4(0.f, 0.f, 0.f, 0.f), o1 = o0;
-        for (int t = 0; t <= pos; ++t) {
-            const float pa = pw[t], pb = pw[MAXK + t];
+        float4 o[QR];
+        #pragma unroll
+        for (int r = 0; r < QR; ++r) o[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        #pragma unroll 2
+        for (int t = 0; t <= pmax; ++t) {
+            const float4 pa = *reinterpret_cast<const float4*>(wp + t * QR);
+            const float4 pb = *reinterpret_cast<const float4*>(wp + t * QR + 4);
+            const float p[QR] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
             const float4 v = *reinterpret_cast<const float4*>(Vs + t * D + lane * 4);
-            o0.x = fmaf(pa, v.x, o0.x); o0.y = fmaf(pa, v.y, o0.y); o0.z = fmaf(pa, v.z, o0.z); o0.w = fmaf(pa, v.w, o0.w);
-            o1.x = fmaf(pb, v.x, o1.x); o1.y = fmaf(pb, v.y, o1.y); o1.z = fmaf(pb, v.z, o1.z); o1.w = fmaf(pb, v.w, o1.w);
+            #pragma unroll
+            for (int r = 0; r < QR; ++r) {
+                o[r].x = fmaf(p[r], v.x, o[r].x); o[r].y = fmaf(p[r], v.y, o[r].y);
+                o[r].z = fmaf(p[r], v.z, o[r].z); o[r].w = fmaf(p[r], v.w, o[r].w);
+            }
         }
-        const float i0 = 1.f / l0, i1 = 1.f / l1;
-        reinterpret_cast<float4*>(a.out + row0 * D)[lane] = make_float4(o0.x * i0, o0.y * i0, o0.z * i0, o0.w * i0);
-        reinterpret_cast<float4*>(a.out + (row0 + 1) * D)[lane] = make_float4(o1.x * i1, o1.y * i1, o1.z * i1, o1.w * i1);
-        __syncwarp();                                   // qw / pw reuse by the next row
+        #pragma unroll
+        for (int r = 0; r < QR; ++r) {
+            const int b = b0 + (r >> 1);
+            if (b < rows) {
+                float* dst = a.out + (((size_t)l * a.n + b) * a.hq + kh * GROUP + (r & 1)) * D;
+                reinterpret_cast<float4*>(dst)[lane] =
+                    make_float4(o[r].x * inv[r], o[r].y * inv[r], o[r].z * inv[r], o[r].w * inv[r]);
+            }
+        }
+        __syncwarp();                                   // wq / wp reuse by the next group
     }
 }
 
 }  // namespace
 
 void launch_attn_head_rows(const RowsArgs& a, cudaStream_t s) {
-    const size_t smem = ((size_t)D * KT_STRIDE + (size_t)MAXK * D + (THREADS / 32) * GROUP * (D + MAXK)) *
-                        sizeof(float);
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(attn_head_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(attn_head_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
         attr = true;
     }
-    attn_head_rows_kernel<<<a.n_layers * a.hkv, THREADS, smem, s>>>(a);
+    attn_head_rows_kernel<<<a.n_layers * a.hkv, THREADS, SMEM_BYTES, s>>>(a);
 }
 
 }  // namespace qattn

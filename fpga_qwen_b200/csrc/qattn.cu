@@ -882,7 +882,7 @@ int qa_comm_destroy(qa_ctx* ctx) {
     return QA_OK;
 }
 
-int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float* full) {
+static int gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float* full, bool async) {
     if (!ctx) return QA_ERR_INVALID;
     if (!ctx->comm) return fail(ctx, QA_ERR_STATE, "no communicator (qa_comm_init)");
     if (ctx->cfg.io_host) return fail(ctx, QA_ERR_UNSUPPORTED, "qa_gather_heads takes device pointers");
@@ -906,9 +906,22 @@ int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float*
     if ((st = comm_enter(ctx))) return st;
     if ((st = nccl_all_gather_f32(ctx->comm, local, ctx->gather_buf, count, ctx->comm_stream, err)))
         return fail(ctx, st, "ncclAllGather: %s", err.c_str());
+    if (async) {
+        // the permute stays on the communication stream; the context stream moves on
+        launch_permute_heads(ctx->gather_buf, full, ctx->nranks, n_layers, n, ctx->hq, ctx->comm_stream);
+        return after_launch(ctx, -1, "permute_heads");
+    }
     if ((st = comm_leave(ctx))) return st;
     launch_permute_heads(ctx->gather_buf, full, ctx->nranks, n_layers, n, ctx->hq, ctx->stream);
     return after_launch(ctx, -1, "permute_heads");
+}
+
+int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float* full) {
+    return gather_heads(ctx, n_layers, n, local, full, false);
+}
+
+int qa_gather_heads_async(qa_ctx* ctx, int n_layers, int n, const float* local, float* full) {
+    return gather_heads(ctx, n_layers, n, local, full, true);
 }
 
 int qa_decode_step_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos, const float* q_pre,

@@ -83,6 +83,8 @@ _SIGNATURES = {
     "qa_kv_send": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_kv_recv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_comm_join": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_gather_heads_async": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                             ctypes.c_void_p]),
     "qa_set_step_overlap": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "qa_comm_info": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                     ctypes.POINTER(ctypes.c_int)]),
@@ -279,6 +281,10 @@ class Context:
         n, r, pm = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
         self._check(lib().qa_comm_info(self._h, ctypes.byref(n), ctypes.byref(r), ctypes.byref(pm)))
         return n.value, r.value, bool(pm.value)
+
+    def gather_heads_async(self, n_layers: int, n: int, local_ptr: int, full_ptr: int):
+        """qa_gather_heads on the communication stream; complete after comm_join() or sync()."""
+        self._check(lib().qa_gather_heads_async(self._h, n_layers, n, local_ptr, full_ptr))
 
     def comm_join(self):
         """Makes the context stream wait for the communication queued so far."""

@@ -193,6 +193,11 @@ int qa_comm_destroy(qa_ctx* ctx);
  * device FP32 with heads in global order (the layout the reference's o_proj reads,
  * core.cpp:625). Collective; asynchronous on the context's stream. */
 int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float* full);
+/* The same gather without holding the context stream: the all-gather and the permute run on
+ * the context's communication stream, so work queued next on the context stream (the next
+ * layers' prefill) overlaps them. `local` must stay unchanged and `full` unread until
+ * qa_comm_join or qa_sync. Consecutive gathers run in call order. */
+int qa_gather_heads_async(qa_ctx* ctx, int n_layers, int n, const float* local, float* full);
 /* Prefill -> decode KV handoff. qa_kv_send ships KV rows [0, ntok) of every layer, K|V and
  * local head of sequence `seq` to rank `peer`; the peer's matching qa_kv_recv stores them in
  * its slot `seq` and sets that sequence's position to ntok. Both contexts must hold the

@@ -89,6 +89,20 @@ def _worker(rank, world, port, out_dir):
             return local
         g = torch.empty((L, n + steps, 16, 128), dtype=torch.float32, device="cuda")
         ctx.gather_heads(L, n + steps, local.data_ptr(), g.data_ptr())
+        # the same gather in layer groups on the communication stream (groups of 1 and 3 layers),
+        # with other work queued on the context stream meanwhile: the same bits
+        ga = torch.full_like(g, float("nan"))
+        t = n + steps
+        # filler: the next (uncommitted) row appended again and attended, twice
+        ctx.append(0, 0, L, t, 1, q1.data_ptr(), k1.data_ptr(), v1.data_ptr(), qn1.data_ptr())
+        for l0, nl in ((0, 1), (1, 3)):
+            ctx.gather_heads_async(nl, t, local[l0:].data_ptr(), ga[l0:].data_ptr())
+            scratch = torch.empty_like(qn1)
+            keep.append(scratch)
+            ctx.attn_decode(0, 0, L, t, 1, qn1.data_ptr(), scratch.data_ptr())
+        ctx.comm_join()
+        torch.cuda.synchronize()
+        report["async_gather_equal"] = bool(torch.equal(ga, g))
         return g
 
     gathered = run(shard, qs, ks, vs, gather=True)
@@ -195,6 +209,7 @@ def test_head_sharded_gather_and_kv_handoff(tmp_path):
     for rank in range(world):
         rep = np.load(tmp_path / f"report{rank}.npy", allow_pickle=True).item()
         assert rep["kv_equal"], rep
+        assert rep["async_gather_equal"], rep
         assert rep["gather_max"] < H.MAX_ABS and rep["gather_rms"] < H.RMS, rep
         assert rep["peer_gather_max"] < 1e-5, rep             # same heads, different key split
         if rank == 1:
