@@ -36,7 +36,6 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode-attn HBM GB/s & prefill-attn TFLOP/s, Qwen3-0.6B GQA, 4K ctx"
 L, HQ, HKV, D = 28, 16, 8, 128
 PREFILL, DECODE = 3968, 128
-PREFILL_GROUP = 7                                # layers per prefill launch when gathering heads (N > 1)
 KV_BYTES_PER_POS = L * HKV * D * 2 * 2          # 114,688 B: K and V rows of one position, all layers
 FLOPS_PER_KEY = 4 * D * HQ * L                  # 229,376 FLOP per (query row, visible key), all layers
 
@@ -288,16 +287,14 @@ def run_ours(args):
         ctx.append(0, 0, L, 0, PREFILL, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), pqn.data_ptr())
         if evs:
             evs["pa0"].record(stream)
-        if world > 1:
-            # layer groups: each group's all-gather (communication stream) overlaps the next
-            # group's attention
-            for c0 in range(0, L, PREFILL_GROUP):
-                nl = min(PREFILL_GROUP, L - c0)
-                off = c0 * PREFILL * hq * D * 4
-                ctx.attn_prefill(0, c0, nl, 0, PREFILL, pqn.data_ptr() + off, pout.data_ptr() + off)
-                ctx.gather_heads_async(nl, PREFILL, pout.data_ptr() + off, pfull.data_ptr() + c0 * PREFILL * HQ * D * 4)
-                launches += 3  # FP32 rows below position 128, tcgen05 prefill, permute (the all-gather is NCCL's)
-            ctx.comm_join()
+        if world > 1 and (args.nccl_gather or not peer_mapped):
+            ctx.attn_prefill(0, 0, L, 0, PREFILL, pqn.data_ptr(), pout.data_ptr())
+            ctx.gather_heads(L, PREFILL, pout.data_ptr(), pfull.data_ptr())
+            launches += 3      # FP32 rows below position 128, tcgen05 prefill, permute (the all-gather is NCCL's)
+        elif world > 1:
+            # both prefill kernels store every output row here and into the peers' landing buffers
+            ctx.attn_prefill_gather(0, 0, L, 0, PREFILL, pqn.data_ptr(), pfull.data_ptr())
+            launches += 5      # gate, FP32 rows below position 128, tcgen05 prefill, signal, wait/copy
         else:
             ctx.attn_prefill(0, 0, L, 0, PREFILL, pqn.data_ptr(), pout.data_ptr())
             launches += 2      # FP32 rows below position 128, tcgen05 prefill
@@ -407,8 +404,10 @@ def run_ours(args):
                        "prefill_tokens": PREFILL, "decode_steps": DECODE, "layers": L,
                        "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
                        "head_gather": None if world == 1 else (
-                           "NCCL all-gather + permute" if (args.split_decode or args.nccl_gather or not peer_mapped)
-                           else "peer stores over NVLink inside the decode step"),
+                           "NCCL all-gather + permute" if (args.nccl_gather or not peer_mapped) else
+                           ("peer stores over NVLink inside the prefill kernels; " +
+                            ("NCCL all-gather after the split decode" if args.split_decode else
+                             "peer stores over NVLink inside the decode step"))),
                        "l2": "inputs larger than L2 (470 MB KV read per decode step, 1.8 GB prefill inputs)"},
             "decode_phase_ms": round(decode_phase, 3),
             "prefill": {"metric": "prefill-attn TFLOP/s", "value": round(pre_flops / (prefill_phase * 1e-3) / 1e12, 3),
@@ -757,7 +756,8 @@ def main():
     ap.add_argument("--no-overlap", action="store_true",
                     help="do not let consecutive fused decode steps overlap (programmatic dependent launch)")
     ap.add_argument("--nccl-gather", action="store_true",
-                    help="N>1: gather decode outputs with NCCL after the step instead of peer stores inside it")
+                    help="N>1: gather prefill and decode outputs with NCCL after the kernels instead of peer "
+                         "stores inside them")
     ap.add_argument("--split-decode", action="store_true",
                     help="decode with qa_append + qa_attn_decode (two launches) instead of the fused qa_decode_step")
     ap.add_argument("--profile-case", choices=["decode", "prefill", "append", "decode_batch"], default=None,

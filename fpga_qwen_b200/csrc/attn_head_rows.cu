@@ -16,7 +16,8 @@
 //   softmax  per row over the warp (shuffle max and sum), probabilities written to the same
 //            warp buffer as [key][row].
 //   output   lane l owns channels 4l..4l+3: per key one float4 of V and two broadcast float4
-//            of probabilities feed 32 FMAs.
+//            of probabilities feed 32 FMAs. Rows go where OutRows says (local layout, or the
+//            full-head layout here and on the peers).
 #include "qattn_common.cuh"
 
 namespace qattn {
@@ -52,7 +53,7 @@ __device__ __forceinline__ void score_rows(const float* __restrict__ KT, const f
     }
 }
 
-__global__ void __launch_bounds__(THREADS, 1) attn_head_rows_kernel(const RowsArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) attn_head_rows_kernel(const RowsArgs a, const OutRows o) {
     extern __shared__ __align__(16) float smem[];
     float* KT = smem;                                   // [128 channels][MAXK keys]
     float* Vs = KT + D * MAXK;                          // [MAXK keys][128 channels]
@@ -150,9 +151,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_head_rows_kernel(const RowsAr
             }
         }
         __syncwarp();
-        float4 o[QR];
+        float4 acc_o[QR];
         #pragma unroll
-        for (int r = 0; r < QR; ++r) o[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < QR; ++r) acc_o[r] = make_float4(0.f, 0.f, 0.f, 0.f);
         #pragma unroll 2
         for (int t = 0; t <= pmax; ++t) {
             const float4 pa = *reinterpret_cast<const float4*>(wp + t * QR);
@@ -161,32 +162,40 @@ __global__ void __launch_bounds__(THREADS, 1) attn_head_rows_kernel(const RowsAr
             const float4 v = *reinterpret_cast<const float4*>(Vs + t * D + lane * 4);
             #pragma unroll
             for (int r = 0; r < QR; ++r) {
-                o[r].x = fmaf(p[r], v.x, o[r].x); o[r].y = fmaf(p[r], v.y, o[r].y);
-                o[r].z = fmaf(p[r], v.z, o[r].z); o[r].w = fmaf(p[r], v.w, o[r].w);
+                acc_o[r].x = fmaf(p[r], v.x, acc_o[r].x); acc_o[r].y = fmaf(p[r], v.y, acc_o[r].y);
+                acc_o[r].z = fmaf(p[r], v.z, acc_o[r].z); acc_o[r].w = fmaf(p[r], v.w, acc_o[r].w);
             }
         }
         #pragma unroll
         for (int r = 0; r < QR; ++r) {
             const int b = b0 + (r >> 1);
             if (b < rows) {
-                float* dst = a.out + (((size_t)l * a.n + b) * a.hq + kh * GROUP + (r & 1)) * D;
-                reinterpret_cast<float4*>(dst)[lane] =
-                    make_float4(o[r].x * inv[r], o[r].y * inv[r], o[r].z * inv[r], o[r].w * inv[r]);
+                const size_t off = (((size_t)l * a.n + b) * o.heads + o.head0 + kh * GROUP + (r & 1)) * D;
+                const float4 val = make_float4(acc_o[r].x * inv[r], acc_o[r].y * inv[r], acc_o[r].z * inv[r],
+                                               acc_o[r].w * inv[r]);
+                reinterpret_cast<float4*>(o.out + off)[lane] = val;
+                #pragma unroll
+                for (int p = 0; p < MAX_RANKS - 1; ++p)
+                    if (p < o.n_peers) reinterpret_cast<float4*>(o.peers[p] + off)[lane] = val;
             }
         }
         __syncwarp();                                   // wq / wp reuse by the next group
+    }
+    if (o.n_peers) {                                    // rows stored to peers: visible system-wide at exit
+        __syncthreads();
+        if (threadIdx.x == 0) __threadfence_system();
     }
 }
 
 }  // namespace
 
-void launch_attn_head_rows(const RowsArgs& a, cudaStream_t s) {
+void launch_attn_head_rows(const RowsArgs& a, const OutRows& o, cudaStream_t s) {
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(attn_head_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
         attr = true;
     }
-    attn_head_rows_kernel<<<a.n_layers * a.hkv, THREADS, SMEM_BYTES, s>>>(a);
+    attn_head_rows_kernel<<<a.n_layers * a.hkv, THREADS, SMEM_BYTES, s>>>(a, o);
 }
 
 }  // namespace qattn

@@ -79,7 +79,8 @@ enum {
 static_assert(B_COUNT * 8 + 4 + 4 * TQ <= 256, "barrier area");
 
 struct PrefillArgs {
-    const float* q; float* out;       // [n_layers][n][hq][128]
+    const float* q;                   // [n_layers][n][hq][128]
+    OutRows o;                        // output rows: local layout, or full-head layout here and on peers
     int seq, layer0, n_layers, pos0, n, hq, hkv, layers_total;
     int row_begin, n_qtiles, n_tiles;
     int* tile_counter;                // next tile to hand out; zero before the launch
@@ -340,9 +341,14 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     const int rr = 4 * k + (lane >> 3), c = lane & 7;
                     const float4 val = *reinterpret_cast<const float4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
                     const int r = ti.r0 + wq * 32 + rr;
-                    if (r < a.n)
-                        *reinterpret_cast<float4*>(a.out + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D +
-                                                   part * 32 + c * 4) = val;
+                    if (r < a.n) {
+                        const size_t off = (((size_t)ti.l * a.n + r) * a.o.heads + a.o.head0 + ti.kh * 2 + h) * D +
+                                           part * 32 + c * 4;
+                        *reinterpret_cast<float4*>(a.o.out + off) = val;
+                        #pragma unroll
+                        for (int p = 0; p < MAX_RANKS - 1; ++p)
+                            if (p < a.o.n_peers) *reinterpret_cast<float4*>(a.o.peers[p] + off) = val;
+                    }
                 }
                 __syncwarp();
             }
@@ -487,14 +493,15 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
+    if (a.o.n_peers && tid == 0) __threadfence_system();   // rows stored to peers: visible system-wide at exit
 }
 
 }  // namespace
 
 // Host side --------------------------------------------------------------------------------------
-int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
-                              int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* tile_counter,
-                              int* error, cudaStream_t s) {
+int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutRows& o, int seq, int layer0,
+                              int n_layers, int pos0, int n, int hq, int hkv, int layers_total, int row_begin,
+                              int* tile_counter, int* error, cudaStream_t s) {
     if (row_begin >= n) return 0;
     static int checked = 0;                      // 1: ready, -1: refused
     if (!checked) {
@@ -510,7 +517,7 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out
     }
     if (checked < 0) return -1;
     PrefillArgs a{};
-    a.q = q; a.out = out; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
+    a.q = q; a.o = o; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
     a.hq = hq; a.hkv = hkv; a.layers_total = layers_total; a.row_begin = row_begin;
     a.n_qtiles = (n - row_begin + BM - 1) / BM; a.error = error;
     a.n_tiles = a.n_qtiles * hkv * n_layers;

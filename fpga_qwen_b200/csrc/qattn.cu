@@ -74,9 +74,19 @@ struct qa_ctx {
     size_t landing_bytes = 0, flags_off = 0;
     char* peer_base[MAX_RANKS] = {};       // every rank's allocation (this rank's at [rank])
     bool peer_ok = false;
+    size_t peer_min_bytes = 0;             // every rank's allocation (equal on all ranks)
     unsigned* gather_done = nullptr;       // CTAs of the gathering launch that finished
     unsigned gather_step = 0;
     float* step_out = nullptr;             // local output of the NCCL fallback
+    // Prefill head gather through peer memory: a landing buffer per rank for the other ranks'
+    // heads ([layers][context][all heads][128] FP32), mapped like the decode one on first use.
+    char* pf_block = nullptr;
+    char* pf_base[MAX_RANKS] = {};
+    bool pf_tried = false, pf_ok = false;
+    unsigned pf_call = 0;
+    size_t pf_min_bytes = 0;               // smallest rank's prefill landing buffer
+    float* pf_local = nullptr;             // local output of the NCCL fallback
+    size_t pf_local_bytes = 0;
     bool step_overlap = false;             // qa_set_step_overlap
     bool last_fused_step = false;          // the last launch on the stream was a fused decode step
     size_t step_out_bytes = 0;
@@ -85,11 +95,18 @@ struct qa_ctx {
 
 namespace {
 
-void peer_release(qa_ctx* ctx) {
+void close_mappings(char* (&base)[MAX_RANKS], const char* own) {
     for (int r = 0; r < MAX_RANKS; ++r) {
-        if (ctx->peer_base[r] && ctx->peer_base[r] != ctx->peer_block) cudaIpcCloseMemHandle(ctx->peer_base[r]);
-        ctx->peer_base[r] = nullptr;
+        if (base[r] && base[r] != own) cudaIpcCloseMemHandle(base[r]);
+        base[r] = nullptr;
     }
+}
+
+void peer_release(qa_ctx* ctx) {
+    close_mappings(ctx->pf_base, ctx->pf_block);
+    cudaFree(ctx->pf_block);
+    ctx->pf_block = nullptr; ctx->pf_ok = false; ctx->pf_tried = false;
+    close_mappings(ctx->peer_base, ctx->peer_block);
     cudaFree(ctx->peer_block);
     cudaFree(ctx->gather_done);
     ctx->peer_block = nullptr; ctx->gather_done = nullptr; ctx->peer_ok = false;
@@ -450,8 +467,9 @@ static int ensure_decode_scratch(qa_ctx* ctx, const DecodePlan& plan) {
     return QA_OK;
 }
 
+// Prefill rows go to `gather` when given (full-head layout here and on the peers), else to out.
 static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q, float* out,
-                  bool decode) {
+                  bool decode, const OutRows* gather = nullptr) {
     int st;
     if ((st = check_rows(ctx, seq, layer, n_layers, pos0, n))) return st;
     if (decode && n > QA_MAX_DECODE_ROWS)
@@ -480,11 +498,14 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
     } else {
         // rows below position TC_MIN_POSITION: FP32 CUDA cores; the rest: tcgen05 tensor cores
         const int tc_begin = std::min(n, std::max(0, TC_MIN_POSITION - pos0));
+        OutRows o{};
+        if (gather) o = *gather;
+        else { o.out = od; o.heads = ctx->hq; }
         if (tc_begin > 0) {
             r.row_end = tc_begin;
-            launch_attn_head_rows(r, ctx->stream);
+            launch_attn_head_rows(r, o, ctx->stream);
         }
-        if (launch_attn_prefill_sm100(ctx->kv_map, qd, od, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv,
+        if (launch_attn_prefill_sm100(ctx->kv_map, qd, o, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv,
                                       ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->error, ctx->stream))
             return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel has an unexpected register allocation");
     }
@@ -757,44 +778,46 @@ int grow(qa_ctx* ctx, void** buf, size_t& have, size_t need) {
 }
 }  // namespace
 
-// Maps every rank's gather allocation into every other rank (collective over the context's
-// communicator). The peer path is used only if every rank succeeded; otherwise the gathering
-// decode step falls back to the NCCL all-gather. CUDA IPC failures are not errors.
-int peer_setup(qa_ctx* ctx) {
+// Exchanges CUDA IPC handles of `block` (this rank's allocation of `bytes`, or null when it
+// could not be made) over the context's communicator, opens the peers', then agrees: *ok is
+// set only if every rank mapped every other rank's block; *min_bytes is the smallest block
+// (every store into a peer's block stays below it); with same_size, blocks of different sizes
+// count as a failure. Collective. CUDA IPC failures are not errors; on disagreement the
+// mappings are closed.
+int ipc_exchange(qa_ctx* ctx, char* block, size_t bytes, bool same_size, char* (&base)[MAX_RANKS], bool* ok_out,
+                 size_t* min_bytes) {
     const int R = ctx->nranks;
-    if (R < 2 || R > MAX_RANKS) return QA_OK;
-    ctx->landing_bytes = ((size_t)ctx->cfg.n_layers * ctx->hq * R * D * sizeof(float) + 255) & ~size_t(255);
-    ctx->flags_off = 2 * ctx->landing_bytes;
-    const size_t total = ctx->flags_off + 256;
-    struct Slot { cudaIpcMemHandle_t h; int ok; int pad[3]; };
-    int local_ok = 0;
+    struct Slot { cudaIpcMemHandle_t h; unsigned long long bytes; int ok; int pad[1]; };
     Slot mine{};
-    if (cudaMalloc(&ctx->peer_block, total) == cudaSuccess && cudaMalloc(&ctx->gather_done, sizeof(unsigned)) == cudaSuccess &&
-        cudaMemset(ctx->peer_block, 0, total) == cudaSuccess && cudaMemset(ctx->gather_done, 0, sizeof(unsigned)) == cudaSuccess &&
-        cudaIpcGetMemHandle(&mine.h, ctx->peer_block) == cudaSuccess)
-        local_ok = 1;
+    mine.bytes = bytes;
+    mine.ok = block && cudaIpcGetMemHandle(&mine.h, block) == cudaSuccess;
     cudaGetLastError();
-    mine.ok = local_ok;
     // exchange handles (one all-gather), open the peers', then agree (a second all-gather)
     Slot* dslots = nullptr;
     QA_CUDA(cudaMalloc(&dslots, sizeof(Slot) * R));
     std::vector<Slot> slots(R);
     std::string err;
     int st = QA_OK;
+    bool agreed = false;
     do {
         if (cudaMemcpy(dslots + ctx->rank, &mine, sizeof(Slot), cudaMemcpyHostToDevice) != cudaSuccess) { st = QA_ERR_CUDA; break; }
         if ((st = nccl_all_gather_bytes(ctx->comm, dslots + ctx->rank, dslots, sizeof(Slot), ctx->comm_stream, err))) break;
         if (cudaStreamSynchronize(ctx->comm_stream) != cudaSuccess) { st = QA_ERR_CUDA; break; }
         if (cudaMemcpy(slots.data(), dslots, sizeof(Slot) * R, cudaMemcpyDeviceToHost) != cudaSuccess) { st = QA_ERR_CUDA; break; }
         int ok = 1;
-        for (int r = 0; r < R; ++r) ok &= slots[r].ok;
+        *min_bytes = bytes;
+        for (int r = 0; r < R; ++r) {
+            ok &= slots[r].ok;
+            *min_bytes = std::min<size_t>(*min_bytes, slots[r].bytes);
+            if (same_size && slots[r].bytes != bytes) ok = 0;
+        }
         if (ok) {
-            ctx->peer_base[ctx->rank] = ctx->peer_block;
+            base[ctx->rank] = block;
             for (int r = 0; r < R && ok; ++r) {
                 if (r == ctx->rank) continue;
                 void* p = nullptr;
                 if (cudaIpcOpenMemHandle(&p, slots[r].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) { ok = 0; cudaGetLastError(); }
-                else ctx->peer_base[r] = static_cast<char*>(p);
+                else base[r] = static_cast<char*>(p);
             }
         }
         mine.ok = ok;
@@ -804,12 +827,47 @@ int peer_setup(qa_ctx* ctx) {
         if (cudaMemcpy(slots.data(), dslots, sizeof(Slot) * R, cudaMemcpyDeviceToHost) != cudaSuccess) { st = QA_ERR_CUDA; break; }
         ok = 1;
         for (int r = 0; r < R; ++r) ok &= slots[r].ok;
-        ctx->peer_ok = ok != 0;
+        agreed = ok != 0;
     } while (false);
     cudaFree(dslots);
-    if (!ctx->peer_ok) peer_release(ctx);
+    if (!agreed) close_mappings(base, block);
+    *ok_out = agreed;
     if (st) return fail(ctx, st, "peer memory set-up: %s", err.empty() ? "CUDA error" : err.c_str());
     return QA_OK;
+}
+
+// Maps every rank's decode-gather allocation into every other rank (collective over the
+// context's communicator). The peer path is used only if every rank succeeded; otherwise the
+// gathering decode step falls back to the NCCL all-gather.
+int peer_setup(qa_ctx* ctx) {
+    const int R = ctx->nranks;
+    if (R < 2 || R > MAX_RANKS) return QA_OK;
+    ctx->landing_bytes = ((size_t)ctx->cfg.n_layers * ctx->hq * R * D * sizeof(float) + 255) & ~size_t(255);
+    ctx->flags_off = 2 * ctx->landing_bytes;
+    const size_t total = ctx->flags_off + 256;
+    bool local_ok = cudaMalloc(&ctx->peer_block, total) == cudaSuccess &&
+                    cudaMalloc(&ctx->gather_done, sizeof(unsigned)) == cudaSuccess &&
+                    cudaMemset(ctx->peer_block, 0, total) == cudaSuccess &&
+                    cudaMemset(ctx->gather_done, 0, sizeof(unsigned)) == cudaSuccess;
+    cudaGetLastError();
+    // the flag words sit at an offset derived from the size: every rank's block must match
+    const int st = ipc_exchange(ctx, local_ok ? ctx->peer_block : nullptr, total, true, ctx->peer_base,
+                                &ctx->peer_ok, &ctx->peer_min_bytes);
+    if (!ctx->peer_ok) peer_release(ctx);
+    return st;
+}
+
+// The prefill landing buffer, mapped on the first gathering prefill (collective).
+int prefill_peer_setup(qa_ctx* ctx) {
+    ctx->pf_tried = true;
+    if (!ctx->peer_ok) return QA_OK;
+    const size_t bytes = (size_t)ctx->cfg.n_layers * ctx->cfg.context * ctx->hq * ctx->nranks * D * sizeof(float);
+    bool local_ok = cudaMalloc(&ctx->pf_block, bytes) == cudaSuccess;
+    if (!local_ok) ctx->pf_block = nullptr;
+    cudaGetLastError();
+    const int st = ipc_exchange(ctx, ctx->pf_block, bytes, false, ctx->pf_base, &ctx->pf_ok, &ctx->pf_min_bytes);
+    if (!ctx->pf_ok) { cudaFree(ctx->pf_block); ctx->pf_block = nullptr; }
+    return st;
 }
 
 // NCCL runs on the context's own communication stream: it waits for the work already on the
@@ -922,6 +980,49 @@ int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float*
 
 int qa_gather_heads_async(qa_ctx* ctx, int n_layers, int n, const float* local, float* full) {
     return gather_heads(ctx, n_layers, n, local, full, true);
+}
+
+int qa_attn_prefill_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q,
+                           float* full) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_rows(ctx, seq, layer, n_layers, pos0, n))) return st;
+    if (!ctx->comm) return fail(ctx, QA_ERR_STATE, "no communicator (qa_comm_init)");
+    if (ctx->cfg.io_host) return fail(ctx, QA_ERR_UNSUPPORTED, "qa_attn_prefill_gather takes device pointers");
+    if (!q || !full) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
+    if ((st = check_appended(ctx, seq, layer, n_layers, pos0 + n))) return st;
+    if (ctx->cfg.kv_head_begin != ctx->rank * ctx->hkv || ctx->nranks * ctx->hkv != ctx->cfg.n_kv_heads)
+        return fail(ctx, QA_ERR_STATE, "rank %d holds KV heads [%d,%d): not the head shard the gather expects",
+                    ctx->rank, ctx->cfg.kv_head_begin, ctx->cfg.kv_head_begin + ctx->hkv);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    if (!ctx->pf_tried && (st = prefill_peer_setup(ctx))) return st;     // collective, first call only
+    if (!ctx->pf_ok) {
+        // no peer mapping: local prefill, then the NCCL all-gather
+        const size_t bytes = (size_t)n_layers * n * ctx->hq * D * sizeof(float);
+        void* buf = ctx->pf_local;
+        if ((st = grow(ctx, &buf, ctx->pf_local_bytes, bytes))) return st;
+        ctx->pf_local = static_cast<float*>(buf);
+        if ((st = attend(ctx, seq, layer, n_layers, pos0, n, q, ctx->pf_local, false))) return st;
+        return qa_gather_heads(ctx, n_layers, n, ctx->pf_local, full);
+    }
+    if ((size_t)n_layers * n * ctx->hq * ctx->nranks * D * sizeof(float) > ctx->pf_min_bytes)
+        return fail(ctx, QA_ERR_INVALID, "%d x %d rows exceed the smallest rank's landing buffer", n_layers, n);
+    const unsigned call = ++ctx->pf_call;
+    unsigned* flags[MAX_RANKS] = {};
+    OutRows o{};
+    o.out = full; o.heads = ctx->hq * ctx->nranks; o.head0 = ctx->rank * ctx->hq;
+    for (int r = 0; r < ctx->nranks; ++r) {
+        flags[r] = reinterpret_cast<unsigned*>(ctx->peer_base[r] + ctx->flags_off);
+        if (r != ctx->rank) o.peers[o.n_peers++] = reinterpret_cast<float*>(ctx->pf_base[r]);
+    }
+    launch_prefill_gate(flags, ctx->nranks, ctx->rank, call, ctx->error, ctx->stream);
+    if ((st = after_launch(ctx, -1, "prefill_gate"))) return st;
+    if ((st = attend(ctx, seq, layer, n_layers, pos0, n, q, full, false, &o))) return st;
+    launch_prefill_signal(flags, ctx->nranks, ctx->rank, call, ctx->stream);
+    if ((st = after_launch(ctx, -1, "prefill_signal"))) return st;
+    launch_prefill_wait_copy(flags[ctx->rank], ctx->nranks, ctx->rank, call, reinterpret_cast<const float*>(ctx->pf_block),
+                             full, n_layers, n, ctx->hq, ctx->error, ctx->stream);
+    return after_launch(ctx, -1, "prefill_wait_copy");
 }
 
 int qa_decode_step_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos, const float* q_pre,

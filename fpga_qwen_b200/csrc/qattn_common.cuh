@@ -58,16 +58,30 @@ struct RowsArgs {
     int* counters;                  // [units], zero between calls
 };
 
+constexpr int MAX_RANKS = 8;
+
+// Destination of prefill output rows: row b of layer l, query head h of this context, goes to
+// out[((l * n + b) * heads + head0 + h) * 128 ...] and to the same offset of every peers[i]
+// (other GPUs' buffers, written over NVLink). {out, hq, 0, 0} is the plain local layout.
+// With peers, every CTA ends with a system-scope fence, so a later launch on the stream may
+// publish the rows to the peers with a release store.
+struct OutRows {
+    float* out = nullptr;
+    int heads = 0, head0 = 0;
+    int n_peers = 0;
+    float* peers[MAX_RANKS - 1] = {};
+};
+
 void launch_kv_append(const AppendArgs& a, cudaStream_t s);
 void launch_attn_rows(const RowsArgs& a, cudaStream_t s);
 // FP32 attention of prefill rows [0, row_end) whose positions are all below 128.
-void launch_attn_head_rows(const RowsArgs& a, cudaStream_t s);
+void launch_attn_head_rows(const RowsArgs& a, const OutRows& o, cudaStream_t s);
 void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cudaStream_t s);
 // Tensor-core prefill for rows [row_begin, n) (all with absolute position >= 128).
 // Returns non-zero (and launches nothing) if the kernel was not built with the expected registers.
-int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, float* out, int seq, int layer0, int n_layers,
-                              int pos0, int n, int hq, int hkv, int layers_total, int row_begin, int* tile_counter,
-                              int* error, cudaStream_t s);
+int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutRows& o, int seq, int layer0,
+                              int n_layers, int pos0, int n, int hq, int hkv, int layers_total, int row_begin,
+                              int* tile_counter, int* error, cudaStream_t s);
 // TMA-streamed split-context decode. Row b of the call is sequence rows.seq[b] at position
 // rows.pos[b] (context rows.pos[b] + 1), b < n <= MAX_BATCH.
 struct DecodePlan {
@@ -85,7 +99,6 @@ constexpr int FUSED_MAX_UNITS = 4;
 // output row into the landing buffer of every rank (its own and, over NVLink, its peers'),
 // at this rank's head offset in the full-head layout, then its last CTA marks the step done
 // in every rank's flag array.
-constexpr int MAX_RANKS = 8;
 struct GatherArgs {
     int out_hq = 0, out_h0 = 0;                  // heads per output row, this rank's first head
     int n_peers = 0;
@@ -110,6 +123,21 @@ void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const 
 // buffer to the caller's output. Error code 51 in *error when the wait runs out.
 void launch_gather_wait_copy(const unsigned* flags, int nranks, unsigned step, const float* landing, float* out,
                              size_t floats, int* error, cudaStream_t s);
+// Prefill head gather through peer memory. Each rank's flag array holds, per rank r, the word
+// "r's rows of call k are in your landing buffer" (PF_READY + r) and "r has copied call k out
+// of its landing buffer" (PF_ACK + r).
+constexpr int PF_READY = 16, PF_ACK = 32;
+// One thread: tells every peer that this rank's landing buffer is free of call `call` - 1 (its
+// copy ran earlier on the stream), then waits (bounded, error 52) until every peer said the same.
+// peer_flags[r]: rank r's flag array as mapped here (peer_flags[rank]: this rank's own).
+void launch_prefill_gate(unsigned* const* peer_flags, int nranks, int rank, unsigned call, int* error,
+                         cudaStream_t s);
+// One thread: marks call `call` ready in every peer's flag array (system-scope release).
+void launch_prefill_signal(unsigned* const* peer_flags, int nranks, int rank, unsigned call, cudaStream_t s);
+// Waits (bounded, error 53) for every peer's ready mark of `call`, then copies the other ranks'
+// heads of every row from the landing buffer ([n_layers][n][hq_local * nranks][128]) to full.
+void launch_prefill_wait_copy(const unsigned* my_flags, int nranks, int rank, unsigned call, const float* landing,
+                              float* full, int n_layers, int n, int hq_local, int* error, cudaStream_t s);
 // Rows at absolute positions below this go to the FP32 CUDA-core kernel.
 constexpr int TC_MIN_POSITION = 128;
 void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n,

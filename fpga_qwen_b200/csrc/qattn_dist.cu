@@ -120,7 +120,93 @@ __global__ void gather_wait_copy_kernel(const unsigned* flags, int nranks, unsig
         out[i] = __ldcg(landing + i);
 }
 
+// ---- prefill head gather through peer memory ----
+// Every rank's flag array (its own memory, mapped by the peers) holds PF_READY + r ("rank r's
+// rows of call k are in this rank's landing buffer") and PF_ACK + r ("rank r has copied call k
+// out of its own landing buffer, so this rank may write the next call there"). Marks only
+// grow; comparisons wrap.
+struct PeerFlags { unsigned* p[MAX_RANKS]; };
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded (2 s of global time): every rank other than `rank` has marks[r] at or past target.
+__device__ bool wait_marks(const unsigned* marks, int nranks, int rank, unsigned target) {
+    const uint64_t t0 = sm100::globaltimer();
+    for (int r = 0; r < nranks; ++r) {
+        if (r == rank) continue;
+        for (;;) {
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(marks + r) : "memory");
+            if ((int)(v - target) >= 0) break;
+            if (sm100::globaltimer() - t0 > 2000000000ull) return false;
+        }
+    }
+    return true;
+}
+
+__global__ void prefill_gate_kernel(PeerFlags flags, int nranks, int rank, unsigned call, int* error) {
+    for (int r = 0; r < nranks; ++r)                       // the copy of call - 1 ran before this launch
+        if (r != rank) st_release_sys(flags.p[r] + PF_ACK + rank, call - 1);
+    if (!wait_marks(flags.p[rank] + PF_ACK, nranks, rank, call - 1)) atomicCAS(error, 0, 52);
+}
+
+__global__ void prefill_signal_kernel(PeerFlags flags, int nranks, int rank, unsigned call) {
+    __threadfence_system();                                 // the prefill kernels' stores end with one too
+    for (int r = 0; r < nranks; ++r)
+        if (r != rank) st_release_sys(flags.p[r] + PF_READY + rank, call);
+}
+
+// Copies the rows of the other ranks' heads: lb = layer * n + row, foreign head fh in
+// [0, HQ - hq_local) maps to head fh below this rank's heads and fh + hq_local above them.
+__global__ void prefill_wait_copy_kernel(const unsigned* mine, int nranks, int rank, unsigned call,
+                                         const float4* landing, float4* full, size_t lb_rows, int hq_local,
+                                         int* error) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        ok = wait_marks(mine + PF_READY, nranks, rank, call);
+        if (!ok) atomicCAS(error, 0, 53);
+    }
+    __syncthreads();
+    if (!ok) return;
+    const int hq_all = hq_local * nranks, foreign = hq_all - hq_local, first = rank * hq_local;
+    const size_t total = lb_rows * foreign * (D / 4);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % (D / 4));
+        const size_t rr = i / (D / 4);
+        const int fh = (int)(rr % foreign);
+        const size_t lb = rr / foreign;
+        const int h = fh < first ? fh : fh + hq_local;
+        const size_t idx = (lb * hq_all + h) * (D / 4) + c;
+        full[idx] = __ldcg(landing + idx);
+    }
+}
+
 }  // namespace
+
+void launch_prefill_gate(unsigned* const* peer_flags, int nranks, int rank, unsigned call, int* error,
+                         cudaStream_t s) {
+    PeerFlags f{};
+    for (int r = 0; r < nranks && r < MAX_RANKS; ++r) f.p[r] = peer_flags[r];
+    prefill_gate_kernel<<<1, 1, 0, s>>>(f, nranks, rank, call, error);
+}
+
+void launch_prefill_signal(unsigned* const* peer_flags, int nranks, int rank, unsigned call, cudaStream_t s) {
+    PeerFlags f{};
+    for (int r = 0; r < nranks && r < MAX_RANKS; ++r) f.p[r] = peer_flags[r];
+    prefill_signal_kernel<<<1, 1, 0, s>>>(f, nranks, rank, call);
+}
+
+void launch_prefill_wait_copy(const unsigned* my_flags, int nranks, int rank, unsigned call, const float* landing,
+                              float* full, int n_layers, int n, int hq_local, int* error, cudaStream_t s) {
+    const size_t lb_rows = (size_t)n_layers * n;
+    const size_t n4 = lb_rows * (size_t)hq_local * (nranks - 1) * (D / 4);
+    const int blocks = (int)std::max<size_t>(1, std::min<size_t>((size_t)NUM_SMS_B200 * 4, (n4 + 255) / 256));
+    prefill_wait_copy_kernel<<<blocks, 256, 0, s>>>(my_flags, nranks, rank, call,
+                                                    reinterpret_cast<const float4*>(landing),
+                                                    reinterpret_cast<float4*>(full), lb_rows, hq_local, error);
+}
 
 void launch_gather_wait_copy(const unsigned* flags, int nranks, unsigned step, const float* landing, float* out,
                              size_t floats, int* error, cudaStream_t s) {

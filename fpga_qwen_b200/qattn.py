@@ -85,6 +85,8 @@ _SIGNATURES = {
     "qa_comm_join": (ctypes.c_int, [ctypes.c_void_p]),
     "qa_gather_heads_async": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                              ctypes.c_void_p]),
+    "qa_attn_prefill_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "qa_set_step_overlap": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "qa_comm_info": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                     ctypes.POINTER(ctypes.c_int)]),
@@ -281,6 +283,11 @@ class Context:
         n, r, pm = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
         self._check(lib().qa_comm_info(self._h, ctypes.byref(n), ctypes.byref(r), ctypes.byref(pm)))
         return n.value, r.value, bool(pm.value)
+
+    def attn_prefill_gather(self, seq, layer, n_layers, pos0, n, q, full):
+        """qa_attn_prefill on this rank's heads with the output rows of all ranks in `full`
+        ([n_layers][n][all heads][128]); collective."""
+        self._check(lib().qa_attn_prefill_gather(self._h, seq, layer, n_layers, pos0, n, q, full))
 
     def gather_heads_async(self, n_layers: int, n: int, local_ptr: int, full_ptr: int):
         """qa_gather_heads on the communication stream; complete after comm_join() or sync()."""

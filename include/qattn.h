@@ -198,6 +198,19 @@ int qa_gather_heads(qa_ctx* ctx, int n_layers, int n, const float* local, float*
  * layers' prefill) overlaps them. `local` must stay unchanged and `full` unread until
  * qa_comm_join or qa_sync. Consecutive gathers run in call order. */
 int qa_gather_heads_async(qa_ctx* ctx, int n_layers, int n, const float* local, float* full);
+/* Prefill attention with the head gather done by the kernels themselves, for KV-head shards:
+ * qa_attn_prefill of this rank's heads, with every output row stored straight into `full`
+ * ([n_layers][n][all query heads][128], device) at this rank's head offset and, over NVLink,
+ * into every other rank's landing buffer; then a wait for all ranks' "rows stored" marks and a
+ * copy of the other ranks' heads into `full`. Bit-identical to qa_attn_prefill followed by
+ * qa_gather_heads. Collective: every rank calls it with the same layer range, pos0 and n.
+ * The first call maps the landing buffers ([layers][context][all heads][128] FP32 per rank).
+ * Bounded waits: QA_ERR_TIMEOUT (read by qa_sync) after 2 s. Where the machine offers no peer
+ * mapping, it runs qa_attn_prefill + qa_gather_heads (NCCL), with the same results.
+ * Replaces the batched-prefill attention (core.cpp:357-381, :407-605) on a KV-head shard and
+ * hands o_proj the full-head rows. */
+int qa_attn_prefill_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q,
+                           float* full);
 /* Prefill -> decode KV handoff. qa_kv_send ships KV rows [0, ntok) of every layer, K|V and
  * local head of sequence `seq` to rank `peer`; the peer's matching qa_kv_recv stores them in
  * its slot `seq` and sets that sequence's position to ntok. Both contexts must hold the

@@ -103,6 +103,29 @@ def _worker(rank, world, port, out_dir):
         ctx.comm_join()
         torch.cuda.synchronize()
         report["async_gather_equal"] = bool(torch.equal(ga, g))
+        # prefill with the head gather inside the kernels (peer stores): the same bits as
+        # qa_attn_prefill + qa_gather_heads, for a whole prefill twice in a row (the second
+        # call reuses the landing buffers) and a chunk starting at position 128
+        ctx.reset(1)
+        qn_b = torch.empty_like(qn)
+        keep.append(qn_b)
+        ctx.append(1, 0, L, 0, n, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), qn_b.data_ptr())
+        pf_equal = True
+        for pos0, cnt, reps in ((0, n, 2), (128, n - 128, 1)):
+            if pos0:
+                ctx.commit(1, pos0)
+            qrows = qn_b[:, pos0:pos0 + cnt].contiguous()
+            loc = torch.empty((L, cnt, hq, 128), dtype=torch.float32, device="cuda")
+            ref = torch.empty((L, cnt, 16, 128), dtype=torch.float32, device="cuda")
+            keep.extend((qrows, loc, ref))
+            ctx.attn_prefill(1, 0, L, pos0, cnt, qrows.data_ptr(), loc.data_ptr())
+            ctx.gather_heads(L, cnt, loc.data_ptr(), ref.data_ptr())
+            for _ in range(reps):
+                got = torch.full_like(ref, float("nan"))
+                ctx.attn_prefill_gather(1, 0, L, pos0, cnt, qrows.data_ptr(), got.data_ptr())
+                ctx.sync()
+                pf_equal &= bool(torch.equal(got, ref))
+        report["prefill_gather_equal"] = pf_equal
         return g
 
     gathered = run(shard, qs, ks, vs, gather=True)
@@ -210,6 +233,7 @@ def test_head_sharded_gather_and_kv_handoff(tmp_path):
         rep = np.load(tmp_path / f"report{rank}.npy", allow_pickle=True).item()
         assert rep["kv_equal"], rep
         assert rep["async_gather_equal"], rep
+        assert rep["prefill_gather_equal"], rep
         assert rep["gather_max"] < H.MAX_ABS and rep["gather_rms"] < H.RMS, rep
         assert rep["peer_gather_max"] < 1e-5, rep             # same heads, different key split
         if rank == 1:
