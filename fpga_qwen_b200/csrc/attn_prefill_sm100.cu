@@ -160,6 +160,9 @@ __device__ __forceinline__ void q_store_rows(uint8_t* Qs, int wq, int lane, int 
             make_uint2(pack_half2(xr[rr].x, xr[rr].y), pack_half2(xr[rr].z, xr[rr].w));
 }
 
+// PEERS: rows go where a.o says, peers included; otherwise the local layout {out, hq, 0}
+// (the single-GPU path carries no peer-store code).
+template <bool PEERS>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -342,12 +345,17 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     const float4 val = *reinterpret_cast<const float4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
                     const int r = ti.r0 + wq * 32 + rr;
                     if (r < a.n) {
-                        const size_t off = (((size_t)ti.l * a.n + r) * a.o.heads + a.o.head0 + ti.kh * 2 + h) * D +
-                                           part * 32 + c * 4;
-                        *reinterpret_cast<float4*>(a.o.out + off) = val;
-                        #pragma unroll
-                        for (int p = 0; p < MAX_RANKS - 1; ++p)
-                            if (p < a.o.n_peers) *reinterpret_cast<float4*>(a.o.peers[p] + off) = val;
+                        if constexpr (PEERS) {
+                            const size_t off = (((size_t)ti.l * a.n + r) * a.o.heads + a.o.head0 + ti.kh * 2 + h) * D +
+                                               part * 32 + c * 4;
+                            *reinterpret_cast<float4*>(a.o.out + off) = val;
+                            #pragma unroll
+                            for (int p = 0; p < MAX_RANKS - 1; ++p)
+                                if (p < a.o.n_peers) *reinterpret_cast<float4*>(a.o.peers[p] + off) = val;
+                        } else {
+                            *reinterpret_cast<float4*>(a.o.out + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D +
+                                                       part * 32 + c * 4) = val;
+                        }
                     }
                 }
                 __syncwarp();
@@ -493,7 +501,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
-    if (a.o.n_peers && tid == 0) __threadfence_system();   // rows stored to peers: visible system-wide at exit
+    if (PEERS && a.o.n_peers && tid == 0) __threadfence_system();   // rows stored to peers: visible system-wide at exit
 }
 
 }  // namespace
@@ -503,19 +511,21 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
                               int n_layers, int pos0, int n, int hq, int hkv, int layers_total, int row_begin,
                               int* tile_counter, int* error, cudaStream_t s) {
     if (row_begin >= n) return 0;
-    static int checked = 0;                      // 1: ready, -1: refused
-    if (!checked) {
+    const bool peers = o.n_peers > 0 || o.heads != hq || o.head0 != 0;
+    static int checked[2] = {0, 0};              // per instantiation: 1 ready, -1 refused
+    int& ck = checked[peers ? 1 : 0];
+    if (!ck) {
         // setmaxnreg.inc waits for registers the control warpgroup releases; the split is
         // only consistent with a launch at exactly REGS_LAUNCH registers per thread.
+        const void* fn = peers ? (const void*)attn_prefill_sm100_kernel<true> : (const void*)attn_prefill_sm100_kernel<false>;
         cudaFuncAttributes fa{};
-        if (cudaFuncGetAttributes(&fa, attn_prefill_sm100_kernel) != cudaSuccess || fa.numRegs != REGS_LAUNCH ||
-            cudaFuncSetAttribute(attn_prefill_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-                cudaSuccess)
-            checked = -1;
+        if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess || fa.numRegs != REGS_LAUNCH ||
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+            ck = -1;
         else
-            checked = 1;
+            ck = 1;
     }
-    if (checked < 0) return -1;
+    if (ck < 0) return -1;
     PrefillArgs a{};
     a.q = q; a.o = o; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
     a.hq = hq; a.hkv = hkv; a.layers_total = layers_total; a.row_begin = row_begin;
@@ -527,7 +537,8 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const unsigned blocks = (unsigned)std::min(a.n_tiles, sms);
     if (cudaMemsetAsync(tile_counter, 0, sizeof(int), s) != cudaSuccess) return -2;
-    attn_prefill_sm100_kernel<<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
+    if (peers) attn_prefill_sm100_kernel<true><<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
+    else attn_prefill_sm100_kernel<false><<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
     return 0;
 }
 
