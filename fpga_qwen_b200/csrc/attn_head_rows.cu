@@ -18,6 +18,8 @@
 //   output   lane l owns channels 4l..4l+3: per key one float4 of V and two broadcast float4
 //            of probabilities feed 32 FMAs. Rows go where OutRows says (local layout, or the
 //            full-head layout here and on the peers).
+// Both products run as packed FP32 FMAs over row pairs (fma.rn.f32x2, each lane rounded once,
+// as fmaf), which halves the FMA instructions issued.
 #include "qattn_common.cuh"
 
 namespace qattn {
@@ -31,26 +33,42 @@ constexpr int QR = POS_PER_GROUP * GROUP;      // query rows per warp pass (row 
 static_assert(QR == 8, "the row buffers are read as two float4 per channel or key");
 constexpr size_t SMEM_BYTES = ((size_t)D * MAXK + (size_t)MAXK * D + (size_t)WARPS * QR * MAXK) * sizeof(float);
 
-// Scores of the warp's eight rows against keys lane + 32j, j < NJ.
+// Packed FP32 FMA (one instruction, two lanes, each rounded once like fmaf).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long r, ua = *reinterpret_cast<unsigned long long*>(&a), ub = *reinterpret_cast<unsigned long long*>(&b),
+                          uc = *reinterpret_cast<unsigned long long*>(&c);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(ua), "l"(ub), "l"(uc));
+    return *reinterpret_cast<float2*>(&r);
+}
+
+// Scores of the warp's eight rows against keys lane + 32j, j < NJ; rows 2i and 2i+1 share
+// one packed FMA per key.
 template <int NJ>
 __device__ __forceinline__ void score_rows(const float* __restrict__ KT, const float* __restrict__ wq, int lane,
                                            float (&acc)[4][QR]) {
+    float2 a2[NJ][QR / 2];
     #pragma unroll
     for (int j = 0; j < NJ; ++j)
         #pragma unroll
-        for (int r = 0; r < QR; ++r) acc[j][r] = 0.f;
+        for (int i = 0; i < QR / 2; ++i) a2[j][i] = make_float2(0.f, 0.f);
     #pragma unroll 4
     for (int c = 0; c < D; ++c) {
         const float4 qa = *reinterpret_cast<const float4*>(wq + c * QR);
         const float4 qb = *reinterpret_cast<const float4*>(wq + c * QR + 4);
-        const float q[QR] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        const float2 q2[QR / 2] = {make_float2(qa.x, qa.y), make_float2(qa.z, qa.w), make_float2(qb.x, qb.y),
+                                   make_float2(qb.z, qb.w)};
         #pragma unroll
         for (int j = 0; j < NJ; ++j) {
             const float k = KT[c * MAXK + lane + 32 * j];
+            const float2 kk = make_float2(k, k);
             #pragma unroll
-            for (int r = 0; r < QR; ++r) acc[j][r] = fmaf(q[r], k, acc[j][r]);
+            for (int i = 0; i < QR / 2; ++i) a2[j][i] = ffma2(q2[i], kk, a2[j][i]);
         }
     }
+    #pragma unroll
+    for (int j = 0; j < NJ; ++j)
+        #pragma unroll
+        for (int i = 0; i < QR / 2; ++i) { acc[j][2 * i] = a2[j][i].x; acc[j][2 * i + 1] = a2[j][i].y; }
 }
 
 __global__ void __launch_bounds__(THREADS, 1) attn_head_rows_kernel(const RowsArgs a, const OutRows o) {
@@ -151,28 +169,36 @@ __global__ void __launch_bounds__(THREADS, 1) attn_head_rows_kernel(const RowsAr
             }
         }
         __syncwarp();
-        float4 acc_o[QR];
+        // acc_o[i][ch]: channel 4*lane + ch of rows 2i (.x) and 2i+1 (.y)
+        float2 acc_o[QR / 2][4];
         #pragma unroll
-        for (int r = 0; r < QR; ++r) acc_o[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < QR / 2; ++i)
+            #pragma unroll
+            for (int ch = 0; ch < 4; ++ch) acc_o[i][ch] = make_float2(0.f, 0.f);
         #pragma unroll 2
         for (int t = 0; t <= pmax; ++t) {
             const float4 pa = *reinterpret_cast<const float4*>(wp + t * QR);
             const float4 pb = *reinterpret_cast<const float4*>(wp + t * QR + 4);
-            const float p[QR] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+            const float2 p2[QR / 2] = {make_float2(pa.x, pa.y), make_float2(pa.z, pa.w), make_float2(pb.x, pb.y),
+                                       make_float2(pb.z, pb.w)};
             const float4 v = *reinterpret_cast<const float4*>(Vs + t * D + lane * 4);
+            const float2 vv[4] = {make_float2(v.x, v.x), make_float2(v.y, v.y), make_float2(v.z, v.z),
+                                  make_float2(v.w, v.w)};
             #pragma unroll
-            for (int r = 0; r < QR; ++r) {
-                acc_o[r].x = fmaf(p[r], v.x, acc_o[r].x); acc_o[r].y = fmaf(p[r], v.y, acc_o[r].y);
-                acc_o[r].z = fmaf(p[r], v.z, acc_o[r].z); acc_o[r].w = fmaf(p[r], v.w, acc_o[r].w);
-            }
+            for (int i = 0; i < QR / 2; ++i)
+                #pragma unroll
+                for (int ch = 0; ch < 4; ++ch) acc_o[i][ch] = ffma2(p2[i], vv[ch], acc_o[i][ch]);
         }
         #pragma unroll
         for (int r = 0; r < QR; ++r) {
             const int b = b0 + (r >> 1);
             if (b < rows) {
                 const size_t off = (((size_t)l * a.n + b) * o.heads + o.head0 + kh * GROUP + (r & 1)) * D;
-                const float4 val = make_float4(acc_o[r].x * inv[r], acc_o[r].y * inv[r], acc_o[r].z * inv[r],
-                                               acc_o[r].w * inv[r]);
+                const float2* orow = acc_o[r >> 1];
+                const float4 val = (r & 1) ? make_float4(orow[0].y * inv[r], orow[1].y * inv[r], orow[2].y * inv[r],
+                                                         orow[3].y * inv[r])
+                                           : make_float4(orow[0].x * inv[r], orow[1].x * inv[r], orow[2].x * inv[r],
+                                                         orow[3].x * inv[r]);
                 reinterpret_cast<float4*>(o.out + off)[lane] = val;
                 #pragma unroll
                 for (int p = 0; p < MAX_RANKS - 1; ++p)
