@@ -87,6 +87,10 @@ struct qa_ctx {
     size_t pf_min_bytes = 0;               // smallest rank's prefill landing buffer
     float* pf_local = nullptr;             // local output of the NCCL fallback
     size_t pf_local_bytes = 0;
+    // Prefix block pool (qa_block_pool): block b holds one 512-row chunk of every plane,
+    // [planes][512][128] FP16; pool_chunk[b] is the chunk index it was saved from (-1: empty).
+    __half* pool = nullptr;
+    std::vector<int> pool_chunk;
     bool step_overlap = false;             // qa_set_step_overlap
     bool last_fused_step = false;          // the last launch on the stream was a fused decode step
     size_t step_out_bytes = 0;
@@ -339,7 +343,7 @@ void qa_destroy(qa_ctx* ctx) {
     for (cudaEvent_t e : ctx->kv_unpacked) if (e) cudaEventDestroy(e);
     if (ctx->kv_packed) cudaEventDestroy(ctx->kv_packed);
     peer_release(ctx);
-    cudaFree(ctx->step_out);
+    cudaFree(ctx->step_out); cudaFree(ctx->pf_local); cudaFree(ctx->pool);
     nccl_comm_destroy(ctx->comm);
     if (ctx->comm_stream) cudaStreamDestroy(ctx->comm_stream);
     for (cudaEvent_t e : ctx->comm_ev) if (e) cudaEventDestroy(e);
@@ -723,6 +727,75 @@ int qa_copy_prefix(qa_ctx* ctx, int src, int dst, int ntok) {
     return QA_OK;
 }
 
+static size_t block_bytes(const qa_ctx* ctx) {
+    return (size_t)ctx->cfg.n_layers * 2 * ctx->hkv * QA_PREFIX_CHUNK * D * sizeof(__half);
+}
+
+int qa_block_pool(qa_ctx* ctx, int n_blocks) {
+    if (!ctx) return QA_ERR_INVALID;
+    if (n_blocks < 0) return fail(ctx, QA_ERR_INVALID, "negative block count %d", n_blocks);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));      // no queued copy still uses the old pool
+    cudaFree(ctx->pool);
+    ctx->pool = nullptr;
+    ctx->pool_chunk.clear();
+    if (n_blocks == 0) return QA_OK;
+    void* p = nullptr;
+    if (cudaMalloc(&p, (size_t)n_blocks * block_bytes(ctx)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, QA_ERR_CAPACITY, "no device memory for %d prefix blocks of %zu bytes", n_blocks,
+                    block_bytes(ctx));
+    }
+    ctx->pool = static_cast<__half*>(p);
+    ctx->pool_chunk.assign(n_blocks, -1);
+    return QA_OK;
+}
+
+static int check_block(qa_ctx* ctx, int seq, int chunk, int block) {
+    int st;
+    if ((st = check_seq(ctx, seq))) return st;
+    if (block < 0 || block >= (int)ctx->pool_chunk.size())
+        return fail(ctx, QA_ERR_INVALID, "block %d outside the pool of %zu", block, ctx->pool_chunk.size());
+    if (chunk < 0 || (size_t)(chunk + 1) * QA_PREFIX_CHUNK > (size_t)ctx->cfg.context)
+        return fail(ctx, QA_ERR_INVALID, "chunk %d outside the context", chunk);
+    return QA_OK;
+}
+
+int qa_block_save(qa_ctx* ctx, int seq, int chunk, int block) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_block(ctx, seq, chunk, block))) return st;
+    const int end = (chunk + 1) * QA_PREFIX_CHUNK;
+    if (ctx->pos[seq] < end)
+        return fail(ctx, QA_ERR_STATE, "sequence %d holds %d committed rows, chunk %d needs %d", seq, ctx->pos[seq], chunk, end);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    launch_pack_kv(ctx->kv, seq, chunk * QA_PREFIX_CHUNK, QA_PREFIX_CHUNK,
+                   reinterpret_cast<char*>(ctx->pool) + (size_t)block * block_bytes(ctx), false, ctx->stream);
+    if ((st = after_launch(ctx, -1, "block_save"))) return st;
+    ctx->pool_chunk[block] = chunk;
+    return QA_OK;
+}
+
+int qa_block_load(qa_ctx* ctx, int seq, int chunk, int block) {
+    if (!ctx) return QA_ERR_INVALID;
+    int st;
+    if ((st = check_block(ctx, seq, chunk, block))) return st;
+    if (ctx->pool_chunk[block] != chunk)
+        return fail(ctx, QA_ERR_STATE, "block %d holds chunk %d, not chunk %d (keys carry their positions)", block,
+                    ctx->pool_chunk[block], chunk);
+    if (ctx->pos[seq] != chunk * QA_PREFIX_CHUNK)
+        return fail(ctx, QA_ERR_STATE, "sequence %d is at position %d, chunk %d starts at %d", seq, ctx->pos[seq], chunk,
+                    chunk * QA_PREFIX_CHUNK);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    launch_pack_kv(ctx->kv, seq, chunk * QA_PREFIX_CHUNK, QA_PREFIX_CHUNK,
+                   reinterpret_cast<char*>(ctx->pool) + (size_t)block * block_bytes(ctx), true, ctx->stream);
+    if ((st = after_launch(ctx, seq, "block_load"))) return st;
+    const int end = (chunk + 1) * QA_PREFIX_CHUNK;
+    ctx->pos[seq] = end;
+    std::fill(ctx->appended[seq].begin(), ctx->appended[seq].end(), end);
+    return QA_OK;
+}
+
 int qa_read_kv(qa_ctx* ctx, int seq, int layer, int kv, int head, int pos0, int n, uint16_t* dst) {
     if (!ctx) return QA_ERR_INVALID;
     int st;
@@ -1086,7 +1159,7 @@ static int kv_transfer(qa_ctx* ctx, int seq, int ntok, int peer, bool send) {
         // pack on the context stream once the previous NCCL op on this buffer is done; the
         // send then runs on the communication stream while the context stream moves on
         QA_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->kv_comm_done[b], 0));
-        launch_pack_kv(ctx->kv, seq, ntok, buf, false, ctx->stream);
+        launch_pack_kv(ctx->kv, seq, 0, ntok, buf, false, ctx->stream);
         if ((st = after_launch(ctx, -1, "pack_kv"))) return st;
         QA_CUDA(cudaEventRecord(ctx->kv_packed, ctx->stream));
         QA_CUDA(cudaStreamWaitEvent(ctx->comm_stream, ctx->kv_packed, 0));
@@ -1101,7 +1174,7 @@ static int kv_transfer(qa_ctx* ctx, int seq, int ntok, int peer, bool send) {
             return fail(ctx, st, "ncclRecv: %s", err.c_str());
         QA_CUDA(cudaEventRecord(ctx->kv_comm_done[b], ctx->comm_stream));
         QA_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->kv_comm_done[b], 0));
-        launch_pack_kv(ctx->kv, seq, ntok, buf, true, ctx->stream);
+        launch_pack_kv(ctx->kv, seq, 0, ntok, buf, true, ctx->stream);
         if ((st = after_launch(ctx, seq, "unpack_kv"))) return st;
         QA_CUDA(cudaEventRecord(ctx->kv_unpacked[b], ctx->stream));
         ctx->pos[seq] = ntok;

@@ -146,7 +146,8 @@ void launch_synth(float* dst, uint64_t seed, int kind, int layer0, int n_layers,
 // Multi-GPU helpers (qattn_dist.cu).
 void launch_permute_heads(const float* gathered, float* full, int nranks, int n_layers, int n, int hq_local,
                           cudaStream_t s);
-void launch_pack_kv(const KVLayout& kv, int seq, int ntok, void* buf, bool unpack, cudaStream_t s);
+// Rows [pos0, pos0 + ntok) of every plane of slot seq <-> contiguous [planes][ntok][128] at buf.
+void launch_pack_kv(const KVLayout& kv, int seq, int pos0, int ntok, void* buf, bool unpack, cudaStream_t s);
 
 // Partial record size (floats) of one split in RowsArgs::partial.
 constexpr int PARTIAL_FLOATS = 4 + GROUP * D;

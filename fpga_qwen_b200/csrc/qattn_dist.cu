@@ -79,12 +79,14 @@ __global__ void permute_heads_kernel(const float4* gathered, float4* full, int n
     }
 }
 
-// Slot rows [0, ntok) of every (layer, K|V, head) plane <-> contiguous [planes][ntok][128].
-__global__ void pack_kv_kernel(const KVLayout kv, int seq, int ntok, uint4* buf, int unpack) {
-    const size_t chunks_per_plane = (size_t)ntok * (D * sizeof(__half) / 16);
+// Slot rows [pos0, pos0 + ntok) of every (layer, K|V, head) plane <-> contiguous
+// [planes][ntok][128] (the KV handoff's staging buffer, or a block of the prefix pool).
+__global__ void pack_kv_kernel(const KVLayout kv, int seq, int pos0, int ntok, uint4* buf, int unpack) {
+    const size_t chunks_per_row = D * sizeof(__half) / 16;
+    const size_t chunks_per_plane = (size_t)ntok * chunks_per_row;
     const size_t planes = (size_t)kv.layers * 2 * kv.hkv;
     const size_t total = chunks_per_plane * planes;
-    uint4* slot = reinterpret_cast<uint4*>(kv.base + kv.slot_elems() * seq);
+    uint4* slot = reinterpret_cast<uint4*>(kv.base + kv.slot_elems() * seq) + (size_t)pos0 * chunks_per_row;
     const size_t plane_chunks = kv.plane_elems() * sizeof(__half) / 16;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const size_t plane = i / chunks_per_plane, c = i - plane * chunks_per_plane;
@@ -228,8 +230,8 @@ void launch_permute_heads(const float* gathered, float* full, int nranks, int n_
                                                          reinterpret_cast<float4*>(full), nranks, n_layers, n,
                                                          hq_local);
 }
-void launch_pack_kv(const KVLayout& kv, int seq, int ntok, void* buf, bool unpack, cudaStream_t s) {
-    pack_kv_kernel<<<NUM_SMS_B200 * 4, 512, 0, s>>>(kv, seq, ntok, reinterpret_cast<uint4*>(buf), unpack ? 1 : 0);
+void launch_pack_kv(const KVLayout& kv, int seq, int pos0, int ntok, void* buf, bool unpack, cudaStream_t s) {
+    pack_kv_kernel<<<NUM_SMS_B200 * 4, 512, 0, s>>>(kv, seq, pos0, ntok, reinterpret_cast<uint4*>(buf), unpack ? 1 : 0);
 }
 
 const char* nccl_load_error() { return nccl().ok ? nullptr : nccl().err.c_str(); }

@@ -83,6 +83,9 @@ _SIGNATURES = {
     "qa_kv_send": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_kv_recv": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_comm_join": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_block_pool": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "qa_block_save": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "qa_block_load": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "qa_gather_heads_async": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                              ctypes.c_void_p]),
     "qa_attn_prefill_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -216,6 +219,15 @@ class Context:
 
     def copy_prefix(self, src: int, dst: int, ntok: int):
         self._check(lib().qa_copy_prefix(self._h, src, dst, ntok))
+
+    def block_pool(self, n_blocks: int):
+        self._check(lib().qa_block_pool(self._h, n_blocks))
+
+    def block_save(self, seq: int, chunk: int, block: int):
+        self._check(lib().qa_block_save(self._h, seq, chunk, block))
+
+    def block_load(self, seq: int, chunk: int, block: int):
+        self._check(lib().qa_block_load(self._h, seq, chunk, block))
 
     def read_kv(self, seq, layer, kv, head, pos0, n, dst_ptr):
         self._check(lib().qa_read_kv(self._h, seq, layer, kv, head, pos0, n, dst_ptr))

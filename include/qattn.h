@@ -167,6 +167,21 @@ int qa_decode_step_batch(qa_ctx* ctx, const int* seqs, int n_seqs, int layer, in
  * engine/INTERFACE.md:151-168) for a prefix held by another sequence slot. */
 int qa_copy_prefix(qa_ctx* ctx, int src_seq, int dst_seq, int ntok);
 
+/* Device-resident pool of canonical prefix blocks, for a prefix cache that outlives the
+ * sequence slots (cross-session reuse of engine/INTERFACE.md:151-168's 512-token granule).
+ * A block holds rows [512*chunk, 512*chunk + 512) of every layer, K/V and head of one
+ * sequence: 512 * 114,688 bytes at 28 layers and 8 KV heads. The keys carry RoPE of their
+ * absolute positions, so a block loads back only at the chunk index it was saved from.
+ * qa_block_pool (re)allocates n_blocks (0 frees the pool; existing blocks are dropped;
+ * synchronises the context stream). */
+int qa_block_pool(qa_ctx* ctx, int n_blocks);
+/* Copies chunk `chunk` of sequence seq (committed rows: position >= 512*(chunk+1)) into
+ * pool block `block`. */
+int qa_block_save(qa_ctx* ctx, int seq, int chunk, int block);
+/* Sequence seq, at position 512*chunk, receives the block's rows (saved from the same chunk
+ * index) and advances to 512*(chunk+1): qa_copy_prefix for one chunk, from the pool. */
+int qa_block_load(qa_ctx* ctx, int seq, int chunk, int block);
+
 /* Reads FP16 KV rows [pos0, pos0+n) of (layer, kv = 0 for K / 1 for V, local head) into
  * dst (host memory, n*128 uint16). Synchronous. Diagnostic / parity access to the store. */
 int qa_read_kv(qa_ctx* ctx, int seq, int layer, int kv, int head, int pos0, int n,
