@@ -189,7 +189,11 @@ class BlockPrefixCache:
                 block = self._allocate(chain)
                 if block is None:
                     break
-                self.ctx.block_save(seq, i, block)
+                try:
+                    self.ctx.block_save(seq, i, block)
+                except Exception:
+                    self.free.append(block)      # the block holds nothing cached any more
+                    raise
                 e = _Block(block, i, tuple(prompt_ids[i * CHUNK:(i + 1) * CHUNK]), parent)
                 self.entries[d] = e
                 if parent is not None:

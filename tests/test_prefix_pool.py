@@ -123,3 +123,15 @@ def test_short_requests_reuse_nothing(n):
     cache = BlockPrefixCache(ctx, 2)
     serve(cache, ctx, 0, toks(12, 2 * CHUNK))
     assert cache.load(0, toks(12, n)) == (512 if n == 513 else 0)
+
+
+def test_failed_save_returns_its_block():
+    ctx = PoolCtx(1)
+    cache = BlockPrefixCache(ctx, 2)
+    ids = toks(13, 2 * CHUNK + 1)
+    ctx.prefill(0, ids[:CHUNK + 10])               # only chunk 0 is committed
+    with pytest.raises(AssertionError):
+        cache.save(0, ids)                          # chunk 1 is refused by the (fake) library
+    assert len(cache.entries) == 1 and len(cache.free) == 1
+    ctx.prefill(0, ids[CHUNK + 10:])
+    assert cache.save(0, ids) == 2                  # the returned block serves chunk 1
