@@ -1,7 +1,7 @@
 """Generate golden attention/KV fixtures by running the reference's own NumPy oracle.
 
-Run in the build container, where tampajohn/fpga-qwen is checked out (default
-``/root/reference``, override with ``FPGA_QWEN_REF``)::
+Run where a checkout of tampajohn/fpga-qwen is available (its directory in
+``FPGA_QWEN_REF``, or the default location in the code below)::
 
     python tests/golden/make_golden.py
 
