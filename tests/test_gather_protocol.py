@@ -1,4 +1,4 @@
-"""The prefill head-gather flag protocol, restated on CPU with processes standing in for GPUs.
+"""The head-gather flag protocols, restated on CPU with processes standing in for GPUs.
 
 qa_attn_prefill_gather (csrc/qattn.cu) runs, per call k, on every rank r:
   gate        prefill_gate_kernel: mark "r copied call k-1 out of its landing buffer" in every
@@ -9,10 +9,14 @@ qa_attn_prefill_gather (csrc/qattn.cu) runs, per call k, on every rank r:
               every peer's flag array;
   wait/copy   prefill_wait_copy_kernel: wait for every peer's ready mark of call k, then copy
               the peers' rows from r's landing buffer into r's output.
+qa_decode_step_gather has no acknowledgement: its landing buffers alternate by step, the
+decode kernel's last CTA marks "r finished step s" (word r) in every rank's flag array after all
+of r's stores, and gather_wait_copy_kernel waits for every rank's mark, then copies.
 Here shared arrays stand in for the peer-mapped flag arrays and landing buffers, and random
 pauses interleave the ranks. Every copy must read the rows of its own call: a landing buffer
 may not be rewritten before its owner has copied it. The planted variant without the gate
-(a mistake in this model, not in the library) shows the check catches that overwrite.
+(a mistake in this model, not in the library) shows the check catches that overwrite; so
+does the decode variant with a single landing buffer.
 """
 import multiprocessing as mp
 import random
@@ -105,3 +109,58 @@ def test_slow_copy_holds_back_the_peers():
 def test_planted_missing_gate_is_caught():
     errors = run_protocol(2, calls=4, gate=False, slow_copy_rank=1)
     assert errors[1] > 0          # rank 0 rewrote rank 1's landing buffer during its copy
+
+
+def _rank_decode(rank, nranks, steps, buffers, slow_copy_rank, flags, landing, errors, seed):
+    rnd = random.Random(seed * 103 + rank)
+    deadline = time.monotonic() + 60
+    size = nranks * ROWS
+    out = [0] * size
+    for st in range(1, steps + 1):
+        base = (st % buffers) * nranks * size                  # landing buffer of this step
+        for i in range(ROWS):                                  # the decode kernel's stores, every rank
+            v = value(st, rank, i)
+            for p in range(nranks):
+                landing[base + p * size + rank * ROWS + i] = v
+            if rnd.random() < 0.05:
+                time.sleep(rnd.random() * 0.002)
+        for p in range(nranks):                                # the last CTA's marks
+            flags[p * WORDS + rank] = st
+        if not _wait(flags, rank, 0, nranks, st, deadline) or flags[rank * WORDS + rank] < st:
+            errors[rank] = -51
+            return
+        for i in range(size):                                  # gather_wait_copy_kernel
+            if rank == slow_copy_rank and i == size // 2:
+                time.sleep(0.05)
+            out[i] = landing[base + rank * size + i]
+        for p in range(nranks):
+            for i in range(ROWS):
+                if out[p * ROWS + i] != value(st, p, i):
+                    errors[rank] += 1
+
+
+def run_decode_protocol(nranks, steps, buffers=2, slow_copy_rank=-1, seed=0):
+    ctx = mp.get_context("spawn")
+    flags = ctx.Array("q", nranks * WORDS, lock=False)
+    landing = ctx.Array("q", buffers * nranks * nranks * ROWS, lock=False)
+    errors = ctx.Array("q", nranks, lock=False)
+    procs = [ctx.Process(target=_rank_decode,
+                         args=(r, nranks, steps, buffers, slow_copy_rank, flags, landing, errors, seed))
+             for r in range(nranks)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    return list(errors)
+
+
+@pytest.mark.parametrize("nranks", [2, 4])
+def test_decode_gather_alternating_buffers(nranks):
+    assert run_decode_protocol(nranks, steps=16, seed=nranks) == [0] * nranks
+    assert run_decode_protocol(nranks, steps=4, slow_copy_rank=nranks - 1) == [0] * nranks
+
+
+def test_planted_single_decode_buffer_is_caught():
+    errors = run_decode_protocol(2, steps=4, buffers=1, slow_copy_rank=1)
+    assert errors[1] > 0          # rank 0's next step rewrote the buffer rank 1 was copying
