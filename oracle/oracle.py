@@ -48,8 +48,10 @@ def lib() -> ctypes.CDLL:
         _lib.qo_append.argtypes = [i, i, i, i, i, f32p, f32p, f32p, f32p, f32p, f32p, f32p,
                                    f32p, u16p, u16p]
         _lib.qo_attention.argtypes = [i, i, i, i, i, f32p, u16p, u16p, f32p, i]
+        _lib.qo_project.argtypes = [f32p, u16p, i, i, i, i, f32p, i]
+        _lib.qo_mlp_gate.argtypes = [f32p, f32p, ctypes.c_size_t]
         for name in ("qo_rope_tables", "qo_norm", "qo_rope", "qo_f32_to_f16", "qo_f16_to_f32",
-                     "qo_append", "qo_attention", "qo_release_pool"):
+                     "qo_append", "qo_attention", "qo_release_pool", "qo_project", "qo_mlp_gate"):
             getattr(_lib, name).restype = None
     return _lib
 
@@ -116,3 +118,24 @@ def attention(kv: LayerKV, pos0: int, q, threads: int = 1):
     out = np.empty_like(q)
     lib().qo_attention(hq, kv.hkv, kv.ctx, pos0, n, q, kv.k, kv.v, out, int(threads))
     return out
+
+
+def project(x, w_f16, sgemm: bool = False, threads: int = 1):
+    """core.cpp:292-301: x [batch][cols] FP32 through w [rows][cols] FP16 bits -> [batch][rows].
+    sgemm=False: the eight-lane dot per output (one row, or the FP16-only vocabulary matrix);
+    sgemm=True: ascending-column FP32 sum standing in for cblas_sgemm (parity by tolerance)."""
+    x = _f32(np.atleast_2d(x))
+    w = np.ascontiguousarray(w_f16, dtype=np.uint16)
+    rows, cols = w.shape
+    if cols % 8 or x.shape[1] != cols:
+        raise ValueError("columns must match and be a multiple of 8")
+    y = np.empty((x.shape[0], rows), np.float32)
+    lib().qo_project(x, w, rows, cols, x.shape[0], int(sgemm), y, threads)
+    return y
+
+
+def mlp_gate(gate, up):
+    """core.cpp:636-639: gate * (0.5 + 0.5*tanh(gate*0.5)) * up (glibc tanhf for vvtanhf)."""
+    g = _f32(gate).copy()
+    lib().qo_mlp_gate(g, _f32(up), g.size)
+    return g

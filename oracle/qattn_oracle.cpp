@@ -19,9 +19,17 @@
 //                     sum = sequential ascending FP32 sum; p_t = e_t/sum;
 //                     out_j = fma(p_t, V_tj, out_j) ascending t.
 //   * Pool partitions core.cpp:68 (count*i/n), prefill cost balance core.cpp:357-381.
+//   * projections     core.cpp:292-301  y[b][r] = x[b] . W[r] over an FP16 matrix: one row
+//                                       (or a matrix without an FP32 copy, :267) through the
+//                                       eight-lane dot of :119-127 (dot4 :131-147 keeps the
+//                                       order per row); batches over a layer matrix through
+//                                       cblas_sgemm on the exact FP32 widening (:294)
+//   * MLP gate        core.cpp:636-639  g * (0.5 + 0.5*tanh(g*0.5)) * up
 //
 // Substitutions, stated: the reference calls Apple Accelerate vvexpf (core.cpp:441,617);
-// this file calls glibc expf. NEON intrinsics become x86 FMA/F16C intrinsics with the same
+// this file calls glibc expf. Likewise glibc tanhf for vvtanhf (:638), and for cblas_sgemm
+// (:294), whose summation order Accelerate does not publish, an ascending-column FP32 sum
+// (parity with those by tolerance). NEON intrinsics become x86 FMA/F16C intrinsics with the same
 // lane-wise semantics (vfmaq_f32 == fused multiply-add per lane; vcvt_f32_f16 is exact).
 // The reference's RoPE is built with -ffp-contract=fast (tools/build_native_cpu.py:45-46),
 // which leaves fusion to the compiler; this restatement is compiled with
@@ -107,6 +115,17 @@ inline float dot_f16(const float* q, const uint16_t* key) {
     for (int j = 0; j < D; j += 8) {
         const __m256 k = _mm256_cvtph_ps(_mm_loadu_si128(reinterpret_cast<const __m128i*>(key + j)));
         acc = _mm256_fmadd_ps(_mm256_loadu_ps(q + j), k, acc);
+    }
+    const __m128 c = _mm_add_ps(_mm256_castps256_ps128(acc), _mm256_extractf128_ps(acc, 1));
+    alignas(16) float l[4]; _mm_store_ps(l, c);
+    return (l[0] + l[1]) + (l[2] + l[3]);
+}
+// The same eight-lane order over n columns (n % 8 == 0): one projection output (core.cpp:298-299).
+inline float dot_f16_n(const float* x, const uint16_t* w, int n) {
+    __m256 acc = _mm256_setzero_ps();
+    for (int j = 0; j < n; j += 8) {
+        const __m256 k = _mm256_cvtph_ps(_mm_loadu_si128(reinterpret_cast<const __m128i*>(w + j)));
+        acc = _mm256_fmadd_ps(_mm256_loadu_ps(x + j), k, acc);
     }
     const __m128 c = _mm_add_ps(_mm256_castps256_ps128(acc), _mm256_extractf128_ps(acc, 1));
     alignas(16) float l[4]; _mm_store_ps(l, c);
@@ -273,6 +292,35 @@ void qo_attention(int hq, int hkv, int ctx, int pos0, int n, const float* q,
                 }
         }
     });
+}
+
+// Projection through an FP16 matrix w [rows][cols] (cols % 8 == 0): x [batch][cols] FP32 ->
+// y [batch][rows] FP32 (core.cpp:292-301). sgemm == 0: the eight-lane dot per output, as for
+// one row or the FP16-only embedding/vocabulary matrix; sgemm != 0 (batch > 1 over a layer
+// matrix): FP32 products of the widened weights summed in ascending column order.
+void qo_project(const float* x, const uint16_t* w, int rows, int cols, int batch, int sgemm, float* y,
+                int threads) {
+    Pool& pool = pool_for(threads);
+    pool.run(size_t(batch) * rows, [&](size_t begin, size_t end, int) {
+        for (size_t i = begin; i < end; ++i) {
+            const size_t b = i / rows, r = i % rows;
+            const float* xb = x + b * cols;
+            const uint16_t* wr = w + r * cols;
+            if (!sgemm) { y[i] = dot_f16_n(xb, wr, cols); continue; }
+            float acc = 0.f;
+            for (int j = 0; j < cols; ++j) acc = std::fma(xb[j], f16_to_f32(wr[j]), acc);
+            y[i] = acc;
+        }
+    });
+}
+
+// The MLP gate of core.cpp:636-639 in place over n values: g = g * (0.5 + 0.5*tanh(g*0.5)) * up.
+void qo_mlp_gate(float* gate, const float* up, size_t n) {
+    for (size_t j = 0; j < n; ++j) {
+        const float half = gate[j] * 0.5f;
+        const float t = std::tanh(half);
+        gate[j] = gate[j] * (0.5f + 0.5f * t) * up[j];
+    }
 }
 
 void qo_release_pool() { std::lock_guard<std::mutex> lk(g_pool_mu); delete g_pool; g_pool = nullptr; }

@@ -3,7 +3,8 @@
 Run where a checkout of tampajohn/fpga-qwen is available (its directory in
 ``FPGA_QWEN_REF``, or the default location in the code below)::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py                  # attention fixture
+    python tests/golden/make_golden.py --projections    # projection fixture
 
 It imports ``NumpyQwen`` from the reference's ``tests/test_full_model.py`` (lines 14-80)
 unchanged and runs ``NumpyQwen.token`` on a synthetic checkpoint written in the
@@ -152,5 +153,75 @@ def main() -> None:
     print(f"wrote {out} ({out.stat().st_size} bytes)")
 
 
+PROJ_TOKENS = 3             # projection fixture: tokens, all recorded at layer 0
+PROJ_SEED = 20261202
+
+
+def projections() -> None:
+    """Projection fixture (numpyqwen_proj_t3.npz) for the oracle's projection restatement.
+
+    Runs NumpyQwen with ``weight_precision='f16'`` (matrices rounded to FP16 and widened, as
+    the engine stores them) on a second synthetic checkpoint, and records at layer 0 the
+    input and output of every matrix product (q/k/v/o, gate/up/down) per token, the MLP
+    activation, and for the last token the final normalised hidden state and the logits.
+    """
+    sys.path.insert(0, str(REF))
+    from tests.test_full_model import NumpyQwen  # the reference's oracle, unchanged
+
+    rng = np.random.default_rng(PROJ_SEED)
+    with tempfile.TemporaryDirectory() as tmp:
+        model = Path(tmp)
+        write_checkpoint(model / "model.safetensors", rng)
+        oracle = NumpyQwen(model, weight_precision="f16", kv_precision="f16")
+
+    log = {}
+    current = {"token": -1}
+
+    class Recorded(np.ndarray):
+        def __array_ufunc__(self, ufunc, method, *inputs, **kwargs):
+            args = [np.asarray(a) if isinstance(a, Recorded) else a for a in inputs]
+            out = getattr(ufunc, method)(*args, **kwargs)
+            if ufunc is np.matmul:
+                log[(current["token"], self.kind, "in")] = np.array(args[1], np.float32)
+                log[(current["token"], self.kind, "out")] = np.array(out, np.float32)
+            elif ufunc is np.multiply and self.kind == "final_norm":
+                log[(current["token"], "final_norm", "out")] = np.array(out, np.float32)
+            return out
+
+    kinds = {"self_attn.q_proj": "q", "self_attn.k_proj": "k", "self_attn.v_proj": "v",
+             "self_attn.o_proj": "o", "mlp.gate_proj": "gate", "mlp.up_proj": "up", "mlp.down_proj": "down"}
+    weights = {}
+    for suffix, kind in kinds.items():
+        name = f"model.layers.0.{suffix}.weight"
+        weights[kind] = np.asarray(oracle.weights[name], np.float32)
+        w = oracle.weights[name].view(Recorded)
+        w.kind = kind
+        oracle.weights[name] = w
+    fn = oracle.weights["model.norm.weight"].view(Recorded)
+    fn.kind = "final_norm"
+    oracle.weights["model.norm.weight"] = fn
+
+    ids = rng.integers(0, V, PROJ_TOKENS)
+    logits = None
+    for t, token in enumerate(ids):
+        current["token"] = t
+        logits = oracle.token(int(token), logits=(t == PROJ_TOKENS - 1))
+
+    arrays = {}
+    for kind, w in weights.items():
+        arrays[f"w_{kind}"] = w.astype(np.float16).view(np.uint16)       # exact: already FP16 values
+        arrays[f"{kind}_in"] = np.stack([log[(t, kind, "in")] for t in range(PROJ_TOKENS)])
+        arrays[f"{kind}_out"] = np.stack([log[(t, kind, "out")] for t in range(PROJ_TOKENS)])
+    arrays["embed"] = np.asarray(oracle.weights["model.embed_tokens.weight"], np.float32).astype(np.float16).view(np.uint16)
+    arrays["final_hidden"] = log[(PROJ_TOKENS - 1, "final_norm", "out")]
+    arrays["logits"] = np.asarray(logits, np.float32)
+    out = HERE / f"numpyqwen_proj_t{PROJ_TOKENS}.npz"
+    np.savez_compressed(out, **arrays)
+    print(f"wrote {out} ({out.stat().st_size} bytes)")
+
+
 if __name__ == "__main__":
-    main()
+    if "--projections" in sys.argv:
+        projections()
+    else:
+        main()
