@@ -10,10 +10,14 @@
 // array below instead of memory from qa_create. The caller passes the KV slot, the
 // queries and the output buffer; the call allocates nothing.
 //
-// The array is QA_NOALLOC_SCRATCH_BYTES (4 MiB) and every GPU that loads the library holds
-// it until the process exits. Every call shares it and it keeps the last call's contents:
-// each call clears the counters it uses before its launch, and calls that overlap on the
-// GPU (for example on two streams at once) race on it.
+// The array is QA_NOALLOC_SCRATCH_BYTES (4 MiB). With lazy module loading (the CUDA default)
+// the module holding it is loaded onto a GPU when its address is first looked up, and the
+// kernel's module at its first launch; qa_create does both for its device, so a host that
+// creates its context before it reserves the rest of HBM meets no load (and no allocation) at
+// its first call. The GPU then holds the array until the process exits.
+// Every call shares it and it keeps the last call's contents: each call clears the counters
+// it uses before its launch, and calls that overlap on the GPU (for example on two streams at
+// once) race on it.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -30,24 +34,54 @@ static __device__ __align__(256) unsigned char g_scratch[SCRATCH_BYTES];
 
 constexpr int MAX_DEVICES = 64;
 std::mutex g_mu;
-void* g_scratch_addr[MAX_DEVICES] = {};   // device address of g_scratch, per device ordinal
+// Device address of g_scratch per device ordinal, and the CUDA context it was looked up in: a
+// device reset or a new primary context invalidates the address, so it is looked up again then.
+void* g_scratch_addr[MAX_DEVICES] = {};
+CUcontext g_scratch_ctx[MAX_DEVICES] = {};
 
-// Looks up the device address of g_scratch on the current device (once per device). In host
-// code `g_scratch` names a host-side stand-in, not device memory, so it is never passed to a
-// kernel directly.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CUcontext current_context() {
+    static CtxGetCurrentFn fn = [] {
+        CtxGetCurrentFn f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", reinterpret_cast<void**>(&f), cudaEnableDefault, &q) !=
+            cudaSuccess)
+            f = nullptr;
+        return f;
+    }();
+    CUcontext c = nullptr;
+    if (fn) fn(&c);
+    return c;
+}
+
+// Looks up the device address of g_scratch on the current device. In host code `g_scratch`
+// names a host-side stand-in, not device memory, so it is never passed to a kernel directly.
 cudaError_t scratch_address(int device, void** out) {
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_scratch_addr[device]) {
+    const CUcontext cur = current_context();
+    if (!cur || !g_scratch_addr[device] || g_scratch_ctx[device] != cur) {
         void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);   // initialises the context if needed
         if (e != cudaSuccess) return e;
         g_scratch_addr[device] = p;
+        g_scratch_ctx[device] = current_context();
     }
     *out = g_scratch_addr[device];
     return cudaSuccess;
 }
 
 }  // namespace
+
+cudaError_t noalloc_prepare(int device) {
+    if (device < 0 || device >= MAX_DEVICES) return cudaErrorInvalidDevice;
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return e;
+    void* p = nullptr;
+    if ((e = scratch_address(device, &p)) != cudaSuccess) return e;
+    return prepare_attn_rows();                 // the kernel the entry point launches, loaded too
+}
+
 }  // namespace qattn
 
 using namespace qattn;

@@ -574,6 +574,11 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
 
 size_t DecodePlan::partial_floats() const { return (size_t)units * max_records * PARTIAL_FLOATS; }
 
+size_t decode_partial_floats_bound(int n_layers, int hkv, int n_max) {
+    const size_t ctas = (size_t)NUM_SMS_B200 * 2, units = (size_t)n_layers * n_max * hkv;
+    return ((size_t)n_max * ctas + 2 * units) * PARTIAL_FLOATS;
+}
+
 // Even split: C ranges of T/C keys, C = 2 CTAs per SM (one wave) unless that makes a range
 // shorter than 64 keys. A segment (one range within one unit) holds at most
 // min(ceil(T/C), longest unit) keys, which sizes the score buffer.

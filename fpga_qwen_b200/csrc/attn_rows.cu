@@ -283,4 +283,9 @@ void launch_attn_rows(const RowsArgs& a, cudaStream_t s) {
     attn_rows_kernel<<<blocks, THREADS, smem, s>>>(a);
 }
 
+cudaError_t prepare_attn_rows() {
+    cudaFuncAttributes attr{};
+    return cudaFuncGetAttributes(&attr, attn_rows_kernel);     // loads the kernel's module now
+}
+
 }  // namespace qattn

@@ -43,14 +43,19 @@ struct qa_ctx {
     float* sines = nullptr;
     std::vector<int> pos;                  // committed position per sequence
     std::vector<std::vector<int>> appended;  // per sequence, per layer: rows written through
-    float* partial = nullptr;              // split-context records
+    float* partial = nullptr;              // split-context records, sized at creation for any call
     size_t partial_floats = 0;
     int* counters = nullptr;
     int max_units = 0;                     // counters held
-    float* staging = nullptr;              // device staging for io_host calls
-    size_t staging_floats = 0;
+    // One device allocation made at creation: [error block (ERR_BLOCK_BYTES)][staging]. io_host
+    // contexts stage [outputs: io_out_floats][inputs: io_in_floats]; device-pointer contexts keep
+    // the query rows of the fused decode step's two-launch form there.
+    char* io_dev = nullptr;
+    float* staging = nullptr;
+    size_t staging_floats = 0, io_out_floats = 0, io_in_floats = 0;
+    char* io_pin = nullptr;                // io_host: pinned [error block][outputs][inputs] of packed copies
     CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
-    int* error = nullptr;                  // device-side error code of bounded waits (0 = none)
+    int* error = nullptr;                  // device error block (qattn_common.cuh: ERR_*), at io_dev
     int* prefill_tiles = nullptr;          // work-item counter of the persistent prefill kernel
     void* comm = nullptr;                  // NCCL communicator (multi-GPU)
     cudaStream_t comm_stream = nullptr;    // NCCL work runs here, ordered after/before the context stream
@@ -179,14 +184,95 @@ int check_appended(qa_ctx* ctx, int seq, int layer, int n_layers, int end) {
     return QA_OK;
 }
 
-// Device staging for io_host calls: grows on demand (the only allocation after create).
-int ensure_staging(qa_ctx* ctx, size_t floats) {
-    if (floats <= ctx->staging_floats) return QA_OK;
-    QA_CUDA(cudaStreamSynchronize(ctx->stream));
-    if (ctx->staging) cudaFree(ctx->staging);
-    ctx->staging = nullptr; ctx->staging_floats = 0;
-    QA_CUDA(cudaMalloc(&ctx->staging, floats * sizeof(float)));
-    ctx->staging_floats = floats;
+// ---- host-buffer (io_host) calls -----------------------------------------------------------------
+// A host-buffer call copies its inputs into the device staging, launches, then copies its outputs
+// back together with the device error block, and waits for the stream: one host->device and one
+// device->host copy when the inputs and the outputs each fit IO_PACK_BYTES (packed through the
+// pinned mirror io_pin), one copy per tensor otherwise. Calls whose rows x layers exceed the
+// staging made at creation run in chunks of whole layers (every layer is independent). A bounded
+// wait that ran out during the call fails it with QA_ERR_TIMEOUT and resets the sequence.
+constexpr size_t IO_PACK_BYTES = size_t(4) << 20;
+
+struct IoCall {
+    const float* in[3] = {};       // host inputs, [n_layers][...] layer-major
+    size_t in_floats[3] = {};      // floats per layer of each input (0: unused)
+    float* out[2] = {};            // host outputs: out[0] always, out[1] optional (may be null)
+    size_t out_floats[2] = {};     // floats per layer (device room for out[1] is kept even when null)
+};
+
+// launch(l0, nl, din, dout) enqueues the work of layers [l0, l0 + nl) on device pointers and
+// returns a status (after_launch).
+template <class Launch>
+int io_host_call(qa_ctx* ctx, int seq, int layer, int n_layers, const IoCall& c, Launch&& launch) {
+    const size_t in_pl = c.in_floats[0] + c.in_floats[1] + c.in_floats[2];
+    const size_t out_pl = c.out_floats[0] + c.out_floats[1];
+    size_t fit = (size_t)n_layers;
+    if (in_pl) fit = std::min(fit, ctx->io_in_floats / in_pl);
+    if (out_pl) fit = std::min(fit, ctx->io_out_floats / out_pl);
+    if (fit < 1) return fail(ctx, QA_ERR_CAPACITY, "one layer of this call exceeds the host-buffer staging");
+    const int chunk = (int)fit;
+    float* const d_out = ctx->staging;
+    float* const d_in = ctx->staging + ctx->io_out_floats;
+    int* const h_err = reinterpret_cast<int*>(ctx->io_pin);
+    float* const h_out = reinterpret_cast<float*>(ctx->io_pin + ERR_BLOCK_BYTES);
+    float* const h_in = h_out + IO_PACK_BYTES / sizeof(float);
+    for (int l0 = layer; l0 < layer + n_layers; l0 += chunk) {
+        const int nl = std::min(chunk, layer + n_layers - l0);
+        const size_t lo = (size_t)(l0 - layer);
+        const float* din[3] = {};
+        float* dout[2] = {};
+        size_t in_total = 0, back = 0;
+        for (int i = 0; i < 3; ++i)
+            if (c.in_floats[i]) { din[i] = d_in + in_total; in_total += c.in_floats[i] * nl; }
+        dout[0] = d_out;
+        if (c.out_floats[1]) dout[1] = d_out + c.out_floats[0] * nl;
+        back = c.out_floats[0] * nl + (c.out[1] ? c.out_floats[1] * nl : 0);
+        const bool pack = in_total * sizeof(float) <= IO_PACK_BYTES && back * sizeof(float) <= IO_PACK_BYTES;
+        if (pack) {
+            size_t o = 0;
+            for (int i = 0; i < 3; ++i)
+                if (c.in_floats[i]) {
+                    std::memcpy(h_in + o, c.in[i] + lo * c.in_floats[i], c.in_floats[i] * nl * sizeof(float));
+                    o += c.in_floats[i] * nl;
+                }
+            if (in_total) QA_CUDA(cudaMemcpyAsync(d_in, h_in, in_total * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        } else {
+            for (int i = 0; i < 3; ++i)
+                if (c.in_floats[i])
+                    QA_CUDA(cudaMemcpyAsync(const_cast<float*>(din[i]), c.in[i] + lo * c.in_floats[i],
+                                            c.in_floats[i] * nl * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+        }
+        int st = launch(l0, nl, din, dout);
+        if (st) return st;
+        if (pack) {
+            QA_CUDA(cudaMemcpyAsync(h_err, ctx->io_dev, ERR_BLOCK_BYTES + back * sizeof(float), cudaMemcpyDeviceToHost,
+                                    ctx->stream));
+        } else {
+            QA_CUDA(cudaMemcpyAsync(h_err, ctx->io_dev, ERR_BLOCK_BYTES, cudaMemcpyDeviceToHost, ctx->stream));
+            for (int j = 0; j < 2; ++j)
+                if (c.out[j])
+                    QA_CUDA(cudaMemcpyAsync(c.out[j] + lo * c.out_floats[j], dout[j], c.out_floats[j] * nl * sizeof(float),
+                                            cudaMemcpyDeviceToHost, ctx->stream));
+        }
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+        if (pack) {
+            size_t o = 0;
+            for (int j = 0; j < 2; ++j)
+                if (c.out_floats[j]) {
+                    if (c.out[j]) std::memcpy(c.out[j] + lo * c.out_floats[j], h_out + o, c.out_floats[j] * nl * sizeof(float));
+                    o += c.out_floats[j] * nl;
+                }
+        }
+        if (const int code = h_err[ERR_CODE]) {
+            QA_CUDA(cudaMemsetAsync(ctx->error + ERR_CODE, 0, sizeof(int), ctx->stream));
+            QA_CUDA(cudaStreamSynchronize(ctx->stream));
+            if (seq >= 0 && seq < (int)ctx->pos.size()) {
+                ctx->pos[seq] = 0;
+                std::fill(ctx->appended[seq].begin(), ctx->appended[seq].end(), 0);
+            }
+            return fail(ctx, QA_ERR_TIMEOUT, "a device-side wait expired (code %d); the call's results are invalid", code);
+        }
+    }
     return QA_OK;
 }
 
@@ -222,6 +308,15 @@ int check_device_error(qa_ctx* ctx) {
         return fail(ctx, QA_ERR_TIMEOUT, "a device-side wait expired (code %d); results of the last calls are invalid", code);
     }
     return QA_OK;
+}
+
+// Runs `launch` on the caller's device pointers, or through the host-buffer staging (io_host).
+template <class Launch>
+int run_call(qa_ctx* ctx, int seq, int layer, int n_layers, const IoCall& c, Launch&& launch) {
+    if (ctx->cfg.io_host) return io_host_call(ctx, seq, layer, n_layers, c, launch);
+    const float* din[3] = {c.in[0], c.in[1], c.in[2]};
+    float* dout[2] = {c.out[0], c.out[1]};
+    return launch(layer, n_layers, din, dout);
 }
 
 }  // namespace
@@ -305,22 +400,37 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     if (cudaMalloc(&ctx->norms, ones.size() * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMemcpy(ctx->norms, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) return cleanup(QA_ERR_CUDA);
 
-    // Split-context records sized for a full-length decode step of every layer (the decode
-    // plan of a larger batched call grows them on demand).
-    {
-        int pos[QA_MAX_DECODE_ROWS];
-        for (int b = 0; b < QA_MAX_DECODE_ROWS; ++b) pos[b] = c.context - QA_MAX_DECODE_ROWS + b;
-        const DecodePlan plan = plan_attn_decode(c.n_layers, ctx->hkv, QA_MAX_DECODE_ROWS, pos);
-        ctx->max_units = std::max(plan.units, c.n_layers * QA_MAX_DECODE_ROWS * ctx->hkv);
-        ctx->partial_floats = std::max(plan.partial_floats(), (size_t)ctx->max_units * 32 * PARTIAL_FLOATS);
-    }
+    // Split-context records and counters sized for the largest decode plan any call can make
+    // (QA_MAX_DECODE_ROWS rows, or a batch of up to min(max_seqs, QA_MAX_BATCH) sequences, over
+    // all layers), so that no hot call allocates.
+    const int n_max = std::min(QA_MAX_BATCH, std::max(c.max_seqs, QA_MAX_DECODE_ROWS));
+    ctx->max_units = c.n_layers * n_max * ctx->hkv;
+    ctx->partial_floats = decode_partial_floats_bound(c.n_layers, ctx->hkv, n_max);
     if (cudaMalloc(&ctx->partial, ctx->partial_floats * sizeof(float)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMalloc(&ctx->counters, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMemset(ctx->counters, 0, (size_t)ctx->max_units * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
 
-    if (cudaMalloc(&ctx->error, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    // Error block + staging. io_host: room for io_rows rows of every tensor of one layer
+    // (io_rows = max(context, QA_MAX_BATCH)); larger calls run in layer chunks. Device pointers:
+    // the normalised query rows of the fused decode step's two-launch form (all layers, n_max rows).
+    if (c.io_host) {
+        const size_t io_rows = (size_t)std::max(c.context, QA_MAX_BATCH);
+        ctx->io_out_floats = io_rows * 2 * ctx->hq * D;
+        ctx->io_in_floats = io_rows * (ctx->hq + 2 * ctx->hkv) * D;
+        ctx->staging_floats = ctx->io_out_floats + ctx->io_in_floats;
+        if (cudaMallocHost(&ctx->io_pin, ERR_BLOCK_BYTES + 2 * IO_PACK_BYTES) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    } else {
+        ctx->staging_floats = (size_t)c.n_layers * n_max * ctx->hq * D;
+    }
+    if (cudaMalloc(&ctx->io_dev, ERR_BLOCK_BYTES + ctx->staging_floats * sizeof(float)) != cudaSuccess)
+        return cleanup(QA_ERR_OOM);
+    if (cudaMemset(ctx->io_dev, 0, ERR_BLOCK_BYTES) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+    ctx->error = reinterpret_cast<int*>(ctx->io_dev);
+    ctx->staging = reinterpret_cast<float*>(ctx->io_dev + ERR_BLOCK_BYTES);
     if (cudaMalloc(&ctx->prefill_tiles, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
-    if (cudaMemset(ctx->error, 0, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
+    // the device address of qa_attn_decode_noalloc's fixed scratch, looked up now (it loads that
+    // module onto the GPU) rather than at its first call, when the host may own all free memory
+    if (noalloc_prepare(c.device) != cudaSuccess) return cleanup(QA_ERR_CUDA);
     if (make_kv_map(ctx) != QA_OK) return cleanup(QA_ERR_CUDA);
 
     ctx->pos.assign(c.max_seqs, 0);
@@ -336,7 +446,7 @@ void qa_destroy(qa_ctx* ctx) {
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
-    cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->staging); cudaFree(ctx->error);
+    cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->io_dev); cudaFreeHost(ctx->io_pin);
     cudaFree(ctx->prefill_tiles);
     cudaFree(ctx->gather_buf); cudaFree(ctx->kv_buf[0]); cudaFree(ctx->kv_buf[1]);
     for (cudaEvent_t e : ctx->kv_comm_done) if (e) cudaEventDestroy(e);
@@ -364,6 +474,25 @@ int qa_sync(qa_ctx* ctx) {
     QA_CUDA(cudaStreamSynchronize(ctx->stream));
     if (ctx->comm_stream) QA_CUDA(cudaStreamSynchronize(ctx->comm_stream));
     return check_device_error(ctx);
+}
+
+int qa_set_wait_limit(qa_ctx* ctx, int microseconds) {
+    if (!ctx) return QA_ERR_INVALID;
+    if (microseconds < 0) return fail(ctx, QA_ERR_INVALID, "negative wait limit %d", microseconds);
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const unsigned us = (unsigned)microseconds;
+    QA_CUDA(cudaMemcpyAsync(ctx->error + ERR_WAIT_US, &us, sizeof us, cudaMemcpyHostToDevice, ctx->stream));
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    return QA_OK;
+}
+
+int qa_selftest_timeout(qa_ctx* ctx) {
+    if (!ctx) return QA_ERR_INVALID;
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    // the head gather's wait kernel, waiting for one rank's mark of step 1 in a word that stays 0
+    launch_gather_wait_copy(reinterpret_cast<const unsigned*>(ctx->error + ERR_NEVER), 1, 1u, nullptr, nullptr, 0,
+                            ctx->error, ctx->stream);
+    return after_launch(ctx, -1, "selftest_timeout");
 }
 
 int qa_set_norms(qa_ctx* ctx, int layer, const float* q_norm, const float* k_norm) {
@@ -420,6 +549,7 @@ int qa_commit(qa_ctx* ctx, int seq, int n) {
     return QA_OK;
 }
 
+
 int qa_append(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n,
               const float* q_pre, const float* k_pre, const float* v, float* q_out) {
     if (!ctx) return QA_ERR_INVALID;
@@ -427,47 +557,30 @@ int qa_append(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n,
     if ((st = check_rows(ctx, seq, layer, n_layers, pos0, n))) return st;
     if (!q_pre || !k_pre || !v || !q_out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
-    const size_t qn = (size_t)n_layers * n * ctx->hq * D, kn = (size_t)n_layers * n * ctx->hkv * D;
-    AppendArgs a{};
-    a.q_pre = q_pre; a.k_pre = k_pre; a.v_pre = v; a.q_out = q_out;
-    if (ctx->cfg.io_host) {
-        if ((st = ensure_staging(ctx, 2 * qn + 2 * kn))) return st;
-        float* s = ctx->staging;
-        QA_CUDA(cudaMemcpyAsync(s, q_pre, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        QA_CUDA(cudaMemcpyAsync(s + qn, k_pre, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        QA_CUDA(cudaMemcpyAsync(s + qn + kn, v, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        a.q_pre = s; a.k_pre = s + qn; a.v_pre = s + qn + kn; a.q_out = s + qn + 2 * kn;
-    }
-    a.kv = ctx->kv; a.seq = seq; a.layer0 = layer; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
-    a.hq = ctx->hq; a.hkv = ctx->hkv; a.norms = ctx->norms; a.cosines = ctx->cosines; a.sines = ctx->sines;
-    a.eps = ctx->cfg.norm_eps;
-    launch_kv_append(a, ctx->stream);
-    if ((st = after_launch(ctx, seq, "kv_append"))) return st;
+    const size_t qn = (size_t)n * ctx->hq * D, kn = (size_t)n * ctx->hkv * D;     // floats per layer
+    IoCall c;
+    c.in[0] = q_pre; c.in[1] = k_pre; c.in[2] = v; c.in_floats[0] = qn; c.in_floats[1] = kn; c.in_floats[2] = kn;
+    c.out[0] = q_out; c.out_floats[0] = qn;
+    st = run_call(ctx, seq, layer, n_layers, c, [&](int l0, int nl, const float* const* din, float* const* dout) {
+        AppendArgs a{};
+        a.q_pre = din[0]; a.k_pre = din[1]; a.v_pre = din[2]; a.q_out = dout[0];
+        a.kv = ctx->kv; a.seq = seq; a.layer0 = l0; a.n_layers = nl; a.pos0 = pos0; a.n = n;
+        a.hq = ctx->hq; a.hkv = ctx->hkv; a.norms = ctx->norms; a.cosines = ctx->cosines; a.sines = ctx->sines;
+        a.eps = ctx->cfg.norm_eps;
+        launch_kv_append(a, ctx->stream);
+        return after_launch(ctx, seq, "kv_append");
+    });
+    if (st) return st;
     for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seq][l] = pos0 + n;
-    if (ctx->cfg.io_host) {
-        QA_CUDA(cudaMemcpyAsync(q_out, a.q_out, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        QA_CUDA(cudaStreamSynchronize(ctx->stream));
-    }
     return QA_OK;
 }
 
-// Grows the split-decode scratch for a plan (records and zeroed counters).
-static int ensure_decode_scratch(qa_ctx* ctx, const DecodePlan& plan) {
-    if (plan.partial_floats() > ctx->partial_floats) {
-        QA_CUDA(cudaStreamSynchronize(ctx->stream));
-        cudaFree(ctx->partial);
-        ctx->partial = nullptr; ctx->partial_floats = 0;
-        QA_CUDA(cudaMalloc(&ctx->partial, plan.partial_floats() * sizeof(float)));
-        ctx->partial_floats = plan.partial_floats();
-    }
-    if (plan.units > ctx->max_units) {
-        QA_CUDA(cudaStreamSynchronize(ctx->stream));
-        cudaFree(ctx->counters);
-        ctx->counters = nullptr; ctx->max_units = 0;
-        QA_CUDA(cudaMalloc(&ctx->counters, (size_t)plan.units * sizeof(int)));
-        QA_CUDA(cudaMemsetAsync(ctx->counters, 0, (size_t)plan.units * sizeof(int), ctx->stream));
-        ctx->max_units = plan.units;
-    }
+// The split-decode scratch is sized at creation for every plan a call can make (see
+// decode_partial_floats_bound); a plan beyond it would be an internal error, refused here.
+static int check_decode_scratch(qa_ctx* ctx, const DecodePlan& plan) {
+    if (plan.partial_floats() > ctx->partial_floats || plan.units > ctx->max_units)
+        return fail(ctx, QA_ERR_CAPACITY, "decode plan (%d units, %zu record floats) beyond the scratch made at creation",
+                    plan.units, plan.partial_floats());
     return QA_OK;
 }
 
@@ -481,45 +594,38 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
     if (!q || !out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
     if ((st = check_appended(ctx, seq, layer, n_layers, pos0 + n))) return st;
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
-    const size_t qn = (size_t)n_layers * n * ctx->hq * D;
-    const float* qd = q; float* od = out;
-    if (ctx->cfg.io_host) {
-        if ((st = ensure_staging(ctx, 2 * qn))) return st;
-        QA_CUDA(cudaMemcpyAsync(ctx->staging, q, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        qd = ctx->staging; od = ctx->staging + qn;
-    }
-    RowsArgs r{};
-    r.q = qd; r.out = od; r.kv = ctx->kv; r.seq = seq; r.layer0 = layer; r.n_layers = n_layers;
-    r.pos0 = pos0; r.n = n; r.hq = ctx->hq; r.hkv = ctx->hkv; r.row_begin = 0; r.row_end = n;
-    r.partial = ctx->partial; r.counters = ctx->counters;
-    if (decode) {
-        int seqs[QA_MAX_DECODE_ROWS], pos[QA_MAX_DECODE_ROWS];
-        for (int b = 0; b < n; ++b) { seqs[b] = seq; pos[b] = pos0 + b; }
-        const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
-        if ((st = ensure_decode_scratch(ctx, plan))) return st;
-        launch_attn_decode_sm100(plan, ctx->kv, qd, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
-                                 ctx->partial, ctx->counters, ctx->error, ctx->stream);
-    } else {
-        // rows below position TC_MIN_POSITION: FP32 CUDA cores; the rest: tcgen05 tensor cores
-        const int tc_begin = std::min(n, std::max(0, TC_MIN_POSITION - pos0));
-        OutRows o{};
-        if (gather) o = *gather;
-        else { o.out = od; o.heads = ctx->hq; }
-        if (tc_begin > 0) {
-            r.row_end = tc_begin;
-            launch_attn_head_rows(r, o, ctx->stream);
+    const size_t qn = (size_t)n * ctx->hq * D;
+    IoCall c;
+    c.in[0] = q; c.in_floats[0] = qn;
+    c.out[0] = out; c.out_floats[0] = qn;
+    return run_call(ctx, seq, layer, n_layers, c, [&](int l0, int nl, const float* const* din, float* const* dout) {
+        int s2;
+        if (decode) {
+            int seqs[QA_MAX_DECODE_ROWS], pos[QA_MAX_DECODE_ROWS];
+            for (int b = 0; b < n; ++b) { seqs[b] = seq; pos[b] = pos0 + b; }
+            const DecodePlan plan = plan_attn_decode(nl, ctx->hkv, n, pos);
+            if ((s2 = check_decode_scratch(ctx, plan))) return s2;
+            launch_attn_decode_sm100(plan, ctx->kv, din[0], dout[0], l0, nl, n, seqs, pos, ctx->hq, ctx->hkv,
+                                     ctx->partial, ctx->counters, ctx->error, ctx->stream);
+        } else {
+            RowsArgs r{};
+            r.q = din[0]; r.out = dout[0]; r.kv = ctx->kv; r.seq = seq; r.layer0 = l0; r.n_layers = nl;
+            r.pos0 = pos0; r.n = n; r.hq = ctx->hq; r.hkv = ctx->hkv; r.row_begin = 0; r.row_end = n;
+            // rows below position TC_MIN_POSITION: FP32 CUDA cores; the rest: tcgen05 tensor cores
+            const int tc_begin = std::min(n, std::max(0, TC_MIN_POSITION - pos0));
+            OutRows o{};
+            if (gather) o = *gather;
+            else { o.out = dout[0]; o.heads = ctx->hq; }
+            if (tc_begin > 0) {
+                r.row_end = tc_begin;
+                launch_attn_head_rows(r, o, ctx->stream);
+            }
+            if (launch_attn_prefill_sm100(ctx->kv_map, din[0], o, seq, l0, nl, pos0, n, ctx->hq, ctx->hkv,
+                                          ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->error, ctx->stream))
+                return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel has an unexpected register allocation");
         }
-        if (launch_attn_prefill_sm100(ctx->kv_map, qd, o, seq, layer, n_layers, pos0, n, ctx->hq, ctx->hkv,
-                                      ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->error, ctx->stream))
-            return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel has an unexpected register allocation");
-    }
-    if ((st = after_launch(ctx, seq, decode ? "attn_decode" : "attn_prefill"))) return st;
-    if (ctx->cfg.io_host) {
-        QA_CUDA(cudaMemcpyAsync(out, od, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        QA_CUDA(cudaStreamSynchronize(ctx->stream));
-        if (!decode) return check_device_error(ctx);
-    }
-    return QA_OK;
+        return after_launch(ctx, seq, decode ? "attn_decode" : "attn_prefill");
+    });
 }
 
 int qa_attn_prefill(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n, const float* q, float* out) {
@@ -555,30 +661,24 @@ int qa_append_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_layers
     if ((st = check_batch(ctx, seqs, n, layer, n_layers))) return st;
     if (!q_pre || !k_pre || !v || !q_out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
-    const size_t qn = (size_t)n_layers * n * ctx->hq * D, kn = (size_t)n_layers * n * ctx->hkv * D;
-    AppendArgs a{};
-    a.q_pre = q_pre; a.k_pre = k_pre; a.v_pre = v; a.q_out = q_out;
-    if (ctx->cfg.io_host) {
-        if ((st = ensure_staging(ctx, 2 * qn + 2 * kn))) return st;
-        float* s = ctx->staging;
-        QA_CUDA(cudaMemcpyAsync(s, q_pre, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        QA_CUDA(cudaMemcpyAsync(s + qn, k_pre, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        QA_CUDA(cudaMemcpyAsync(s + qn + kn, v, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        a.q_pre = s; a.k_pre = s + qn; a.v_pre = s + qn + kn; a.q_out = s + qn + 2 * kn;
-    }
-    a.kv = ctx->kv; a.seq = seqs[0]; a.layer0 = layer; a.n_layers = n_layers; a.pos0 = 0; a.n = n;
-    a.hq = ctx->hq; a.hkv = ctx->hkv; a.norms = ctx->norms; a.cosines = ctx->cosines; a.sines = ctx->sines;
-    a.eps = ctx->cfg.norm_eps;
-    a.rows.batched = 1;
-    for (int b = 0; b < n; ++b) { a.rows.seq[b] = seqs[b]; a.rows.pos[b] = ctx->pos[seqs[b]]; }
-    launch_kv_append(a, ctx->stream);
-    if ((st = after_launch(ctx, -1, "kv_append_batch"))) return st;
+    const size_t qn = (size_t)n * ctx->hq * D, kn = (size_t)n * ctx->hkv * D;
+    IoCall c;
+    c.in[0] = q_pre; c.in[1] = k_pre; c.in[2] = v; c.in_floats[0] = qn; c.in_floats[1] = kn; c.in_floats[2] = kn;
+    c.out[0] = q_out; c.out_floats[0] = qn;
+    st = run_call(ctx, -1, layer, n_layers, c, [&](int l0, int nl, const float* const* din, float* const* dout) {
+        AppendArgs a{};
+        a.q_pre = din[0]; a.k_pre = din[1]; a.v_pre = din[2]; a.q_out = dout[0];
+        a.kv = ctx->kv; a.seq = seqs[0]; a.layer0 = l0; a.n_layers = nl; a.pos0 = 0; a.n = n;
+        a.hq = ctx->hq; a.hkv = ctx->hkv; a.norms = ctx->norms; a.cosines = ctx->cosines; a.sines = ctx->sines;
+        a.eps = ctx->cfg.norm_eps;
+        a.rows.batched = 1;
+        for (int b = 0; b < n; ++b) { a.rows.seq[b] = seqs[b]; a.rows.pos[b] = ctx->pos[seqs[b]]; }
+        launch_kv_append(a, ctx->stream);
+        return after_launch(ctx, -1, "kv_append_batch");
+    });
+    if (st) return st;
     for (int b = 0; b < n; ++b)
         for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seqs[b]][l] = ctx->pos[seqs[b]] + 1;
-    if (ctx->cfg.io_host) {
-        QA_CUDA(cudaMemcpyAsync(q_out, a.q_out, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        QA_CUDA(cudaStreamSynchronize(ctx->stream));
-    }
     return QA_OK;
 }
 
@@ -593,93 +693,70 @@ int qa_attn_decode_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_l
         if ((st = check_appended(ctx, seqs[b], layer, n_layers, pos[b] + 1))) return st;
     }
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
-    const size_t qn = (size_t)n_layers * n * ctx->hq * D;
-    const float* qd = q; float* od = out;
-    if (ctx->cfg.io_host) {
-        if ((st = ensure_staging(ctx, 2 * qn))) return st;
-        QA_CUDA(cudaMemcpyAsync(ctx->staging, q, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        qd = ctx->staging; od = ctx->staging + qn;
-    }
-    const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
-    if ((st = ensure_decode_scratch(ctx, plan))) return st;
-    launch_attn_decode_sm100(plan, ctx->kv, qd, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv, ctx->partial,
-                             ctx->counters, ctx->error, ctx->stream);
-    if ((st = after_launch(ctx, -1, "attn_decode_batch"))) return st;
-    if (ctx->cfg.io_host) {
-        QA_CUDA(cudaMemcpyAsync(out, od, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        QA_CUDA(cudaStreamSynchronize(ctx->stream));
-    }
-    return QA_OK;
+    const size_t qn = (size_t)n * ctx->hq * D;
+    IoCall c;
+    c.in[0] = q; c.in_floats[0] = qn;
+    c.out[0] = out; c.out_floats[0] = qn;
+    return run_call(ctx, -1, layer, n_layers, c, [&](int l0, int nl, const float* const* din, float* const* dout) {
+        const DecodePlan plan = plan_attn_decode(nl, ctx->hkv, n, pos);
+        int s2;
+        if ((s2 = check_decode_scratch(ctx, plan))) return s2;
+        launch_attn_decode_sm100(plan, ctx->kv, din[0], dout[0], l0, nl, n, seqs, pos, ctx->hq, ctx->hkv, ctx->partial,
+                                 ctx->counters, ctx->error, ctx->stream);
+        return after_launch(ctx, -1, "attn_decode_batch");
+    });
 }
 
 // ---- fused decode step: append of one new row per sequence + decode attention, one launch ----
-static size_t qn_floats(const qa_ctx* ctx, int n, int n_layers) { return (size_t)n_layers * n * ctx->hq * D; }
-static size_t kn_floats(const qa_ctx* ctx, int n, int n_layers) { return (size_t)n_layers * n * ctx->hkv * D; }
-// io_host staging of a decode step: [q_pre][k_pre][v][q_out][out]
-static size_t qn_off_io(size_t qn, size_t kn) { return qn + 2 * kn; }
 static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int layer, int n_layers,
                        const float* q_pre, const float* k_pre, const float* v, float* q_out, float* out,
                        const GatherArgs* gather = nullptr) {
     int st;
     if (!q_pre || !k_pre || !v || !out) return fail(ctx, QA_ERR_INVALID, "null tensor pointer");
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
-    const size_t qn = (size_t)n_layers * n * ctx->hq * D, kn = (size_t)n_layers * n * ctx->hkv * D;
-    StepInputs in{};
-    in.q_pre = q_pre; in.k_pre = k_pre; in.v_pre = v; in.q_out = q_out;
-    float* od = out;
-    if (ctx->cfg.io_host) {
-        if ((st = ensure_staging(ctx, 3 * qn + 2 * kn))) return st;
-        float* sg = ctx->staging;
-        QA_CUDA(cudaMemcpyAsync(sg, q_pre, qn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        QA_CUDA(cudaMemcpyAsync(sg + qn, k_pre, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        QA_CUDA(cudaMemcpyAsync(sg + qn + kn, v, kn * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-        in.q_pre = sg; in.k_pre = sg + qn; in.v_pre = sg + qn + kn;
-        in.q_out = q_out ? sg + qn_off_io(qn, kn) : nullptr;
-        od = sg + 2 * qn + 2 * kn;
-    }
-    in.norms = ctx->norms; in.cosines = ctx->cosines; in.sines = ctx->sines; in.eps = ctx->cfg.norm_eps;
-    // overlap with the previous step only right after a fused step of this context on this stream
-    // (or the gather wait that followed one)
-    in.pdl = ctx->step_overlap && ctx->last_fused_step && !ctx->cfg.io_host ? 1 : 0;
+    const size_t qn = (size_t)n * ctx->hq * D, kn = (size_t)n * ctx->hkv * D;
+    IoCall c;
+    c.in[0] = q_pre; c.in[1] = k_pre; c.in[2] = v; c.in_floats[0] = qn; c.in_floats[1] = kn; c.in_floats[2] = kn;
+    c.out[0] = out; c.out_floats[0] = qn;
+    c.out[1] = q_out; c.out_floats[1] = qn;
     bool fused = false;
-    const DecodePlan plan = plan_attn_decode(n_layers, ctx->hkv, n, pos);
-    if ((st = ensure_decode_scratch(ctx, plan))) return st;
-    if (plan.max_units_per_cta <= FUSED_MAX_UNITS) {
-        launch_attn_decode_sm100(plan, ctx->kv, nullptr, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
-                                 ctx->partial, ctx->counters, ctx->error, ctx->stream, &in, gather);
-        fused = true;
-    } else {
-        // Short contexts or many sequences per CTA range: the same results as append + decode,
-        // run as those two launches (the normalised query rows go to q_out or to staging).
-        float* qn = in.q_out;
-        if (!qn) {
-            if (ctx->cfg.io_host) {
-                qn = ctx->staging + qn_off_io(qn_floats(ctx, n, n_layers), kn_floats(ctx, n, n_layers));
-            } else {
-                if ((st = ensure_staging(ctx, qn_floats(ctx, n, n_layers)))) return st;
-                qn = ctx->staging;
-            }
+    const int seq1 = n == 1 ? seqs[0] : -1;
+    st = run_call(ctx, seq1, layer, n_layers, c, [&](int l0, int nl, const float* const* din, float* const* dout) {
+        StepInputs in{};
+        in.q_pre = din[0]; in.k_pre = din[1]; in.v_pre = din[2]; in.q_out = dout[1];
+        in.norms = ctx->norms; in.cosines = ctx->cosines; in.sines = ctx->sines; in.eps = ctx->cfg.norm_eps;
+        // overlap with the previous step only right after a fused step of this context on this stream
+        // (or the gather wait that followed one)
+        in.pdl = ctx->step_overlap && ctx->last_fused_step && !ctx->cfg.io_host ? 1 : 0;
+        const DecodePlan plan = plan_attn_decode(nl, ctx->hkv, n, pos);
+        int s2;
+        if ((s2 = check_decode_scratch(ctx, plan))) return s2;
+        if (plan.max_units_per_cta <= FUSED_MAX_UNITS) {
+            launch_attn_decode_sm100(plan, ctx->kv, nullptr, dout[0], l0, nl, n, seqs, pos, ctx->hq, ctx->hkv,
+                                     ctx->partial, ctx->counters, ctx->error, ctx->stream, &in, gather);
+            fused = true;
+        } else {
+            // Short contexts or many sequences per CTA range: the same results as append + decode,
+            // run as those two launches (the normalised query rows go to q_out or to staging).
+            float* qrows = in.q_out ? in.q_out : ctx->staging;
+            AppendArgs ap{};
+            ap.q_pre = in.q_pre; ap.k_pre = in.k_pre; ap.v_pre = in.v_pre; ap.q_out = qrows;
+            ap.kv = ctx->kv; ap.seq = seqs[0]; ap.layer0 = l0; ap.n_layers = nl; ap.pos0 = 0; ap.n = n;
+            ap.hq = ctx->hq; ap.hkv = ctx->hkv; ap.norms = ctx->norms; ap.cosines = ctx->cosines;
+            ap.sines = ctx->sines; ap.eps = ctx->cfg.norm_eps;
+            ap.rows.batched = 1;
+            for (int b = 0; b < n; ++b) { ap.rows.seq[b] = seqs[b]; ap.rows.pos[b] = pos[b]; }
+            launch_kv_append(ap, ctx->stream);
+            launch_attn_decode_sm100(plan, ctx->kv, qrows, dout[0], l0, nl, n, seqs, pos, ctx->hq, ctx->hkv,
+                                     ctx->partial, ctx->counters, ctx->error, ctx->stream, nullptr, gather);
+            fused = false;
         }
-        AppendArgs ap{};
-        ap.q_pre = in.q_pre; ap.k_pre = in.k_pre; ap.v_pre = in.v_pre; ap.q_out = qn;
-        ap.kv = ctx->kv; ap.seq = seqs[0]; ap.layer0 = layer; ap.n_layers = n_layers; ap.pos0 = 0; ap.n = n;
-        ap.hq = ctx->hq; ap.hkv = ctx->hkv; ap.norms = ctx->norms; ap.cosines = ctx->cosines; ap.sines = ctx->sines;
-        ap.eps = ctx->cfg.norm_eps;
-        ap.rows.batched = 1;
-        for (int b = 0; b < n; ++b) { ap.rows.seq[b] = seqs[b]; ap.rows.pos[b] = pos[b]; }
-        launch_kv_append(ap, ctx->stream);
-        launch_attn_decode_sm100(plan, ctx->kv, qn, od, layer, n_layers, n, seqs, pos, ctx->hq, ctx->hkv,
-                                 ctx->partial, ctx->counters, ctx->error, ctx->stream, nullptr, gather);
-    }
-    if ((st = after_launch(ctx, n == 1 ? seqs[0] : -1, "attn_decode_step"))) return st;
+        return after_launch(ctx, seq1, "attn_decode_step");
+    });
+    if (st) return st;
     ctx->last_fused_step = fused;
     for (int b = 0; b < n; ++b)
         for (int l = layer; l < layer + n_layers; ++l) ctx->appended[seqs[b]][l] = pos[b] + 1;
-    if (ctx->cfg.io_host) {
-        if (q_out) QA_CUDA(cudaMemcpyAsync(q_out, in.q_out, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        QA_CUDA(cudaMemcpyAsync(out, od, qn * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream));
-        QA_CUDA(cudaStreamSynchronize(ctx->stream));
-    }
     return QA_OK;
 }
 

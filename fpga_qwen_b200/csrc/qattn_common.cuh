@@ -60,6 +60,18 @@ struct RowsArgs {
 
 constexpr int MAX_RANKS = 8;
 
+// Device error block of a context (256 bytes, zeroed at creation):
+//   word ERR_CODE     first error code recorded by a bounded wait (0 = none); read and cleared
+//                     by qa_sync and by every host-buffer call
+//   word ERR_WAIT_US  limit of the waits on other GPUs' flags, in microseconds (0 = 2 s)
+//   word ERR_NEVER    a flag word that nothing ever sets (qa_selftest_timeout waits on it)
+constexpr int ERR_CODE = 0, ERR_WAIT_US = 1, ERR_NEVER = 2;
+constexpr size_t ERR_BLOCK_BYTES = 256;
+__device__ __forceinline__ unsigned long long peer_wait_limit_ns(const int* error) {
+    const unsigned us = *reinterpret_cast<const volatile unsigned*>(error + ERR_WAIT_US);
+    return us ? us * 1000ull : 2000000000ull;
+}
+
 // Destination of prefill output rows: row b of layer l, query head h of this context, goes to
 // out[((l * n + b) * heads + head0 + h) * 128 ...] and to the same offset of every peers[i]
 // (other GPUs' buffers, written over NVLink). {out, hq, 0, 0} is the plain local layout.
@@ -74,6 +86,9 @@ struct OutRows {
 
 void launch_kv_append(const AppendArgs& a, cudaStream_t s);
 void launch_attn_rows(const RowsArgs& a, cudaStream_t s);
+// Loads attn_rows_kernel's module onto the current device (lazy module loading defers that to
+// the first launch, which may then need device memory).
+cudaError_t prepare_attn_rows();
 // FP32 attention of prefill rows [0, row_end) whose positions are all below 128.
 void launch_attn_head_rows(const RowsArgs& a, const OutRows& o, cudaStream_t s);
 void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cudaStream_t s);
@@ -91,6 +106,10 @@ struct DecodePlan {
     size_t partial_floats() const;
 };
 DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos);
+// Upper bound of DecodePlan::partial_floats() over every plan of at most n_layers layers and
+// n_max rows (any positions): the record count units * max_records is at most
+// n_max * ctas + 2 * units, because total_keys >= n_layers_call * hkv * max_len.
+size_t decode_partial_floats_bound(int n_layers, int hkv, int n_max);
 // Inputs of a fused decode step (append of the one new row per sequence + decode attention).
 // The fused kernel prepares the rows of at most FUSED_MAX_UNITS units per CTA before it
 // streams; plans with more units per CTA run as append + decode.
@@ -151,5 +170,9 @@ void launch_pack_kv(const KVLayout& kv, int seq, int pos0, int ntok, void* buf, 
 
 // Partial record size (floats) of one split in RowsArgs::partial.
 constexpr int PARTIAL_FLOATS = 4 + GROUP * D;
+
+// Looks up, for `device` and its current context, the device address of the fixed scratch array
+// behind qa_attn_decode_noalloc (attn_decode_noalloc.cu). Makes `device` current.
+cudaError_t noalloc_prepare(int device);
 
 }  // namespace qattn

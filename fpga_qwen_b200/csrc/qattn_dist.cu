@@ -1,10 +1,10 @@
 // qattn_dist.cu — multi-GPU entry points: KV-head sharding with an all-gather of the
 // attention outputs, and the prefill -> decode KV-block handoff, over NCCL on NVLink.
 //
-// The reference runs on one host (no distributed backend); BASELINE's multi-GPU plan splits
-// the 8 KV heads over 1/2/4/8 GPUs (each GPU keeps the 2 query heads of its KV heads and
-// the outputs [pos, 16, 128] are gathered over NVLink), shards independent requests over
-// GPUs (no collective), and hands prefilled KV blocks from prefill GPUs to decode GPUs.
+// The reference runs on one host (no distributed backend). Here the 8 KV heads split over
+// 1/2/4/8 GPUs (each GPU keeps the 2 query heads of its KV heads and the outputs
+// [pos, 16, 128] are gathered over NVLink), independent requests spread over GPUs (no
+// collective), and prefilled KV blocks move from prefill GPUs to decode GPUs.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2 — the copy a PyTorch process has
 // already loaded, or the system one), so the library links neither NCCL nor PyTorch.
@@ -96,8 +96,9 @@ __global__ void pack_kv_kernel(const KVLayout kv, int seq, int pos0, int ntok, u
 }
 
 // One CTA per slice of the landing buffer: thread 0 waits until every rank has marked `step`
-// done (acquire at system scope; bounded by 2 s of global time, error code 51 on expiry), then
-// the CTA copies its slice. Peers wrote the landing buffer over NVLink before their release.
+// done (acquire at system scope; bounded by the context's peer-wait limit, 2 s by default, error
+// code 51 on expiry), then the CTA copies its slice. Peers wrote the landing buffer over
+// NVLink before their release.
 __global__ void gather_wait_copy_kernel(const unsigned* flags, int nranks, unsigned step, const float4* landing,
                                         float4* out, size_t n4, int* error) {
     // Launched as a programmatic dependent of the decode step, this grid starts while that step
@@ -106,13 +107,13 @@ __global__ void gather_wait_copy_kernel(const unsigned* flags, int nranks, unsig
     __shared__ int ok;
     if (threadIdx.x == 0) {
         ok = 1;
-        const uint64_t t0 = sm100::globaltimer();
+        const uint64_t t0 = sm100::globaltimer(), limit = peer_wait_limit_ns(error);
         for (int r = 0; r < nranks && ok; ++r) {
             for (;;) {
                 unsigned v;
                 asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
                 if ((int)(v - step) >= 0) break;
-                if (sm100::globaltimer() - t0 > 2000000000ull) { ok = 0; atomicCAS(error, 0, 51); break; }
+                if (sm100::globaltimer() - t0 > limit) { ok = 0; atomicCAS(error, 0, 51); break; }
             }
         }
     }
@@ -133,16 +134,17 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Bounded (2 s of global time): every rank other than `rank` has marks[r] at or past target.
-__device__ bool wait_marks(const unsigned* marks, int nranks, int rank, unsigned target) {
-    const uint64_t t0 = sm100::globaltimer();
+// Bounded by the context's peer-wait limit (2 s by default): every rank other than `rank` has
+// marks[r] at or past target.
+__device__ bool wait_marks(const unsigned* marks, int nranks, int rank, unsigned target, const int* error) {
+    const uint64_t t0 = sm100::globaltimer(), limit = peer_wait_limit_ns(error);
     for (int r = 0; r < nranks; ++r) {
         if (r == rank) continue;
         for (;;) {
             unsigned v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(marks + r) : "memory");
             if ((int)(v - target) >= 0) break;
-            if (sm100::globaltimer() - t0 > 2000000000ull) return false;
+            if (sm100::globaltimer() - t0 > limit) return false;
         }
     }
     return true;
@@ -151,7 +153,7 @@ __device__ bool wait_marks(const unsigned* marks, int nranks, int rank, unsigned
 __global__ void prefill_gate_kernel(PeerFlags flags, int nranks, int rank, unsigned call, int* error) {
     for (int r = 0; r < nranks; ++r)                       // the copy of call - 1 ran before this launch
         if (r != rank) st_release_sys(flags.p[r] + PF_ACK + rank, call - 1);
-    if (!wait_marks(flags.p[rank] + PF_ACK, nranks, rank, call - 1)) atomicCAS(error, 0, 52);
+    if (!wait_marks(flags.p[rank] + PF_ACK, nranks, rank, call - 1, error)) atomicCAS(error, 0, 52);
 }
 
 __global__ void prefill_signal_kernel(PeerFlags flags, int nranks, int rank, unsigned call) {
@@ -167,7 +169,7 @@ __global__ void prefill_wait_copy_kernel(const unsigned* mine, int nranks, int r
                                          int* error) {
     __shared__ int ok;
     if (threadIdx.x == 0) {
-        ok = wait_marks(mine + PF_READY, nranks, rank, call);
+        ok = wait_marks(mine + PF_READY, nranks, rank, call, error);
         if (!ok) atomicCAS(error, 0, 53);
     }
     __syncthreads();
@@ -213,7 +215,7 @@ void launch_prefill_wait_copy(const unsigned* my_flags, int nranks, int rank, un
 void launch_gather_wait_copy(const unsigned* flags, int nranks, unsigned step, const float* landing, float* out,
                              size_t floats, int* error, cudaStream_t s) {
     const size_t n4 = floats / 4;
-    const int blocks = (int)std::min<size_t>(64, (n4 + 255) / 256);
+    const int blocks = (int)std::max<size_t>(1, std::min<size_t>(64, (n4 + 255) / 256));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(blocks); cfg.blockDim = dim3(256); cfg.dynamicSmemBytes = 0; cfg.stream = s;
     cudaLaunchAttribute attr[1];

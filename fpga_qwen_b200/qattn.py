@@ -53,6 +53,8 @@ _SIGNATURES = {
     "qa_version": (ctypes.c_char_p, []),
     "qa_set_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "qa_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "qa_set_wait_limit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "qa_selftest_timeout": (ctypes.c_int, [ctypes.c_void_p]),
     "qa_set_norms": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "qa_position": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "qa_reset": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
@@ -188,6 +190,14 @@ class Context:
 
     def sync(self):
         self._check(lib().qa_sync(self._h))
+
+    def set_wait_limit(self, microseconds: int):
+        """Limit of the bounded waits on other GPUs' flags (0: the default 2 s)."""
+        self._check(lib().qa_set_wait_limit(self._h, microseconds))
+
+    def selftest_timeout(self):
+        """Launches a bounded wait on a flag nothing sets; the next sync() raises the timeout."""
+        self._check(lib().qa_selftest_timeout(self._h))
 
     def set_norms(self, layer: int, q_norm_ptr: int, k_norm_ptr: int):
         self._check(lib().qa_set_norms(self._h, layer, q_norm_ptr, k_norm_ptr))

@@ -19,7 +19,13 @@
  *     where hkv_local = kv_head_count and hq_local = kv_head_count * (n_q_heads/n_kv_heads).
  *     Device pointers when the context was created with io_host = 0 (calls are
  *     asynchronous on the context's stream); host pointers when io_host = 1 (the call
- *     stages through device buffers and returns after the results are in host memory).
+ *     stages through device buffers made at qa_create, returns after the results are in
+ *     host memory, and reports a device-side wait that ran out as QA_ERR_TIMEOUT with the
+ *     sequence reset). Small calls move their inputs in one host->device copy and their
+ *     outputs in one device->host copy through pinned memory of the context.
+ *   - No hot call allocates device memory or synchronises beyond its own stream: the KV
+ *     store, split-context scratch and staging are sized at qa_create for every call the
+ *     context accepts (up to min(max_seqs, QA_MAX_BATCH) rows of a batched decode).
  *   - KV history lives in HBM, one slot per sequence, laid out
  *        [seq][layer][K|V][kv_head][pos][128] FP16, 256-byte rows
  *     (reference: two arrays [layer][head][pos][128], core.cpp:223, :277, :350-352).
@@ -80,6 +86,18 @@ const char* qa_last_error(const qa_ctx* ctx);
 const char* qa_status_string(int status);
 /* Library build identification, e.g. "qattn sm_100a". */
 const char* qa_version(void);
+
+/* Limit of the bounded device-side waits on other GPUs (the flag waits of the head gathers,
+ * qa_attn_prefill_gather and qa_decode_step_gather), in microseconds; 0 restores the default
+ * of 2 s. A wait that runs out records QA_ERR_TIMEOUT, which qa_sync and the next host-buffer
+ * call report, instead of holding the GPU. No counterpart in the reference (one CPU host). */
+int qa_set_wait_limit(qa_ctx* ctx, int microseconds);
+/* Self-test of that failure path on a single GPU: launches the head gather's wait kernel on a
+ * flag word of this context that nothing ever sets. After the wait limit the kernel gives up
+ * and records the timeout exactly as when a peer GPU stops answering; the next qa_sync (or
+ * host-buffer call, which then resets its sequence) returns QA_ERR_TIMEOUT and clears it.
+ * Asynchronous on the context stream. No counterpart in the reference. */
+int qa_selftest_timeout(qa_ctx* ctx);
 
 /* Runs subsequent work on an external cudaStream_t (NULL restores the context's own). */
 int qa_set_stream(qa_ctx* ctx, void* cuda_stream);
@@ -257,8 +275,9 @@ int qa_comm_join(qa_ctx* ctx);
 int qa_decode_step_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos, const float* q_pre,
                           const float* k_pre, const float* v, float* q_out, float* full);
 
-/* Size of the fixed device array behind qa_attn_decode_noalloc: 4 MiB per GPU, held by
- * every GPU that loads the library until the process exits. */
+/* Size of the fixed device array behind qa_attn_decode_noalloc: 4 MiB per GPU. It is loaded
+ * onto a GPU when qa_create runs on that device (or, without a context, at the first
+ * qa_attn_decode_noalloc call there) and held until the process exits. */
 #define QA_NOALLOC_SCRATCH_BYTES (4u << 20)
 
 /* Split-context decode attention that allocates nothing. It has no counterpart in the
@@ -272,8 +291,11 @@ int qa_decode_step_gather(qa_ctx* ctx, int seq, int layer, int n_layers, int pos
  *            pos0..pos0+n-1 of layers [layer, layer+n_layers), 1 <= n <= QA_MAX_DECODE_ROWS
  *   stream   cudaStream_t (NULL: the legacy default stream)
  * Scratch lives in one static device array of QA_NOALLOC_SCRATCH_BYTES; requests whose
- * (layer, row, head) records do not fit return QA_ERR_CAPACITY before anything runs. The
- * first call on a device looks up that array's address (make it before any stream capture).
+ * (layer, row, head) records do not fit return QA_ERR_CAPACITY before anything runs.
+ * qa_create looks up that array's address for its device, which loads it onto the GPU; a
+ * host that reserves the rest of HBM for its own arena should create its context first.
+ * Without a context on the device, the first call there does the look-up (make it before
+ * any stream capture). After a device reset the address is looked up again.
  * Every call shares the array: calls that overlap on the GPU race, so issue them on one
  * stream or order them. Asynchronous on `stream`. */
 int qa_attn_decode_noalloc(const void* kv_slot, int n_layers_total, int n_kv_heads, int context,
