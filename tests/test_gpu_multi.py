@@ -238,3 +238,97 @@ def test_head_sharded_gather_and_kv_handoff(tmp_path):
         assert rep["peer_gather_max"] < 1e-5, rep             # same heads, different key split
         if rank == 1:
             assert rep["handoff_equal"] and rep["handoff_pos"] == [300, 150, 257], rep
+
+
+def _skip_worker(rank, world, port, out_dir):
+    """Rank 1 leaves one gathering call out (between steps, nothing of its own in flight); rank
+    0's bounded wait for rank 1's mark runs out after the lowered limit and its qa_sync reports
+    QA_ERR_TIMEOUT, after which rank 0's context keeps working. Done once for the decode step's
+    gather (error code 51: the wait for the peers' "step done" marks) and once for the
+    prefill's (code 52: the gate's wait for the peers' "landing buffer free" marks)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from fpga_qwen_b200 import dist as qd
+    from fpga_qwen_b200 import qattn
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=qd.short_timeout(120))
+    L, P = 2, 200
+    begin, count = qd.head_shard(rank, world)
+    stream = torch.cuda.current_stream().cuda_stream
+    q, k, v = H.inputs(81, L, 0, P + 2)
+    qs, ks, vs = (q[:, :, 2 * begin:2 * begin + 2 * count].contiguous(), k[:, :, begin:begin + count].contiguous(),
+                  v[:, :, begin:begin + count].contiguous())
+    report = {}
+    for kind in ("decode", "prefill"):
+        ctx = qattn.Context(n_layers=L, context=512, max_seqs=1, kv_head_begin=begin, kv_head_count=count,
+                            device=rank)
+        ctx.set_stream(stream)
+        qd.init_comm(ctx)
+        mapped = ctx.comm_info()[2]
+        flags = [None, None]
+        dist.all_gather_object(flags, mapped)
+        report[kind + "_mapped"] = all(flags)
+        if not all(flags):          # the NCCL fallback has no bounded wait to exercise: skip
+            ctx.comm_destroy()
+            ctx.close()
+            continue
+        ctx.set_wait_limit(200000)                      # 200 ms
+        hist = [t[:, :P].contiguous() for t in (qs, ks, vs)]
+        qn = torch.empty_like(hist[0])
+        ctx.append(0, 0, L, 0, P, hist[0].data_ptr(), hist[1].data_ptr(), hist[2].data_ptr(), qn.data_ptr())
+        full = torch.empty((L, P, 16, 128), device="cuda")
+        if kind == "prefill":
+            # both ranks once, then rank 1 leaves the second call out
+            ctx.attn_prefill_gather(0, 0, L, 0, P, qn.data_ptr(), full.data_ptr())
+            ctx.sync()
+            dist.barrier()
+            if rank == 0:
+                ctx.attn_prefill_gather(0, 0, L, 0, P, qn.data_ptr(), full.data_ptr())
+        else:
+            ctx.commit(0, P)
+            row = [t[:, P:P + 1].contiguous() for t in (qs, ks, vs)]
+            out = torch.empty((L, 1, 16, 128), device="cuda")
+            ctx.decode_step_gather(0, 0, L, P, row[0].data_ptr(), row[1].data_ptr(), row[2].data_ptr(), 0,
+                                   out.data_ptr())
+            ctx.commit(0, 1)
+            ctx.sync()
+            dist.barrier()
+            row2 = [t[:, P + 1:P + 2].contiguous() for t in (qs, ks, vs)]
+            if rank == 0:
+                ctx.decode_step_gather(0, 0, L, P + 1, row2[0].data_ptr(), row2[1].data_ptr(), row2[2].data_ptr(),
+                                       0, out.data_ptr())
+        status = 0
+        try:
+            ctx.sync()
+        except qattn.QAttnError as e:
+            status = e.status
+            report[kind + "_message"] = str(e)
+        report[kind + "_status"] = status
+        if rank == 0:
+            ctx.sync()                                   # reported once, then cleared
+            # the context keeps working: a local decode of its heads on a fresh sequence
+            ctx.reset(0)
+            ctx.append(0, 0, L, 0, P, hist[0].data_ptr(), hist[1].data_ptr(), hist[2].data_ptr(), qn.data_ptr())
+            ctx.commit(0, P - 1)
+            o = torch.empty_like(qn[:, P - 1:P])
+            q1 = qn[:, P - 1:P].contiguous()
+            ctx.attn_decode(0, 0, L, P - 1, 1, q1.data_ptr(), o.data_ptr())
+            ctx.sync()
+            report[kind + "_after_finite"] = bool(torch.isfinite(o).all())
+        dist.barrier()                                   # nobody's kernels are in flight now
+        ctx.comm_destroy()
+        ctx.close()
+    np.save(os.path.join(out_dir, f"skip{rank}.npy"), report, allow_pickle=True)
+    dist.destroy_process_group()
+
+
+def test_peer_that_skips_a_gather_makes_the_wait_expire(tmp_path):
+    world = 2
+    mp.start_processes(_skip_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    r0 = np.load(tmp_path / "skip0.npy", allow_pickle=True).item()
+    r1 = np.load(tmp_path / "skip1.npy", allow_pickle=True).item()
+    for kind, code in (("decode", 51), ("prefill", 52)):
+        if not r0[kind + "_mapped"]:
+            pytest.skip("no peer mapping between the GPUs: the gathers run on NCCL")
+        assert r0[kind + "_status"] == 6 and f"code {code}" in r0[kind + "_message"], r0
+        assert r0[kind + "_after_finite"], r0
+        assert r1[kind + "_status"] == 0, r1

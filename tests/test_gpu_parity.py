@@ -127,7 +127,7 @@ def test_prefill_attention_parity(pos0, n):
 
 
 def test_config1_prefill_then_32_decode_steps():
-    """85-row prefill + 32 decode steps, 28 layers, vs the oracle."""
+    """85-row prefill + 32 decode steps (the odd final row), 28 layers, vs the oracle."""
     L, n, steps = 28, 85, 32
     ctx = make_ctx(L, context=256)
     qw, kw = H.norms(1, L)
@@ -181,7 +181,7 @@ def test_decode_rows_and_verify_two():
 
 
 def test_prefix_copy_bit_exact_config3():
-    """A prefills 1024 rows; B copies A's 512-row canonical prefix, then
+    """Canonical prefix reuse: A prefills 1024 rows; B copies A's 512-row canonical prefix, then
     prefills its own 512-row tail and decodes. B's KV equals a fresh prefill of B, bit for bit."""
     L = 28
     ctx = make_ctx(L, max_seqs=3, context=1280)
@@ -272,7 +272,7 @@ def test_engine_mirror_state_machine():
 
 
 def test_config4_full_size_sampled_rows():
-    """BASELINE config 4 at full size on one GPU: 3968-row prefill over 28 layers, then 4
+    """The 3968 + 128 workload at full size on one GPU: 3968-row prefill over 28 layers, then 4
     decode steps. KV bytes of sampled layers are bit-exact with the oracle's append; sampled
     rows (tile edges, the position-128 boundary between the FP32 and tensor-core paths,
     random rows) and the decode outputs are within tolerance of the oracle."""
@@ -441,7 +441,7 @@ def test_batched_decode_over_sequences():
 
 
 def test_batched_decode_64_requests_many_segments_per_cta():
-    """BASELINE config-5 shape: 64 sequences with the seeded U[85, 3968] prompt lengths decode
+    """The multi-request shape: 64 sequences with the seeded U[85, 3968] prompt lengths decode
     in one batched launch. Each CTA's key range then spans several (layer, sequence, head)
     units, so the copy ring runs across segment boundaries and the score buffer is sized by
     the longest unit rather than by the range. The batch equals the same rows decoded one
@@ -630,6 +630,54 @@ def test_fused_decode_step_host_buffers():
     host.decode_step(0, 0, L, P, qh1.ctypes.data, kh1.ctypes.data, vh1.ctypes.data, qn_h.ctypes.data, out_h.ctypes.data)
     assert np.array_equal(qn_h, qn_d.cpu().numpy())
     assert np.array_equal(out_h, out_d.cpu().numpy())
+    dev.close(); host.close()
+
+
+def test_host_buffer_calls_in_layer_chunks_and_per_layer():
+    """io_host calls whose rows x layers exceed the staging made at creation (one layer of the
+    context's rows) run in layer chunks; per-layer decode steps, the shape an engine that
+    interleaves its projections makes, go through the packed one-copy-each-way path. Both give
+    the device-pointer context's results bit for bit."""
+    L, P, steps = 6, 1000, 3
+    dev = make_ctx(L, context=1024)
+    host = qattn.Context(n_layers=L, context=1024, io_host=1)
+    qw, kw = H.norms(96, L)
+    for c in (dev, host):
+        H.set_norms(c, qw, kw)
+    q, k, v = H.inputs(96, L, 0, P + steps)
+    qd, kd, vd = (t[:, :P].contiguous() for t in (q, k, v))
+    qn_d = gpu_append(dev, 0, 0, qd, kd, vd)
+    out_d = gpu_attend(dev, 0, 0, qn_d)
+    dev.commit(0, P)
+    qh, kh, vh = (np.ascontiguousarray(t[:, :P].cpu().numpy()) for t in (q, k, v))
+    qn_h, out_h = np.empty_like(qh), np.empty_like(qh)
+    host.append(0, 0, L, 0, P, qh.ctypes.data, kh.ctypes.data, vh.ctypes.data, qn_h.ctypes.data)
+    host.attn_prefill(0, 0, L, 0, P, qn_h.ctypes.data, out_h.ctypes.data)
+    host.commit(0, P)
+    torch.cuda.synchronize()
+    assert np.array_equal(qn_h, qn_d.cpu().numpy())
+    assert np.array_equal(out_h, out_d.cpu().numpy())
+    keep = []
+    for st in range(steps):
+        p = P + st
+        for layer in range(L):
+            r = [t[layer:layer + 1, p:p + 1].contiguous() for t in (q, k, v)]
+            keep.extend(r)
+            qo_d, o_d = torch.empty_like(r[0]), torch.empty_like(r[0])
+            dev.decode_step(0, layer, 1, p, r[0].data_ptr(), r[1].data_ptr(), r[2].data_ptr(), qo_d.data_ptr(),
+                            o_d.data_ptr())
+            rh = [np.ascontiguousarray(t.cpu().numpy()) for t in r]
+            qo_h, o_h = np.empty_like(rh[0]), np.empty_like(rh[0])
+            host.decode_step(0, layer, 1, p, rh[0].ctypes.data, rh[1].ctypes.data, rh[2].ctypes.data,
+                             qo_h.ctypes.data, o_h.ctypes.data)
+            torch.cuda.synchronize()
+            assert np.array_equal(qo_h, qo_d.cpu().numpy()) and np.array_equal(o_h, o_d.cpu().numpy())
+        dev.commit(0, 1)
+        host.commit(0, 1)
+    for layer in (0, L - 1):
+        for kvsel in (0, 1):
+            assert np.array_equal(H.read_plane(dev, 0, layer, kvsel, 2, 0, P + steps),
+                                  H.read_plane(host, 0, layer, kvsel, 2, 0, P + steps))
     dev.close(); host.close()
 
 

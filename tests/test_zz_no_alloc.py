@@ -8,8 +8,18 @@ counts and positions, so the second call meets the first call's leftovers in the
 array) and checks each result against qa_attn_decode on the same inputs, within the
 attention tolerance used by every parity test (max-abs 1e-3, RMS 1e-4).
 
+It also checks the property the entry point exists for: device free memory does not change
+across a call, and, in a fresh process with lazy module loading (the CUDA default, which
+defers loading a kernel's module and its device arrays to first use), not even across the
+first call after qa_create, which loads the fixed array and the kernel up front.
+
 The file sorts last so that a run stopping at the first failure has run everything else.
 """
+import os
+import subprocess
+import sys
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -51,8 +61,12 @@ def test_noalloc_decode_matches_the_regular_entry_point_on_two_calls():
     # call 2: one row over a layer sub-range, reusing the array the first call left behind
     q1 = qn[3:20, :1].contiguous()
     out2 = torch.full_like(q1, float("nan"))
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
     st = qattn.attn_decode_noalloc(kv_slot, L, 8, 4096, 3, 17, P, 1, q1.data_ptr(), out2.data_ptr(), stream)
     assert st == qattn.QA_OK
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before          # the call took no device memory
 
     ref1 = _regular_decode(ctx, P, qn)
     ref2 = torch.empty_like(q1)
@@ -77,3 +91,44 @@ def test_noalloc_decode_rejects_requests_beyond_its_fixed_array():
     assert qattn.attn_decode_noalloc(p, 28, 8, 4096, 0, 28, 4095, 2, p, p, 0) == qattn.QA_ERR_CAPACITY
     assert qattn.attn_decode_noalloc(p, 28, 8, 4096, 0, 28, 10, 5, p, p, 0) == qattn.QA_ERR_INVALID
     assert qattn.attn_decode_noalloc(0, 28, 8, 4096, 0, 28, 10, 1, p, p, 0) == qattn.QA_ERR_INVALID
+
+
+_LAZY_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+from fpga_qwen_b200 import qattn
+from tests import helpers as H
+L, P = 4, 500
+ctx = qattn.Context(n_layers=L, context=1024)
+stream = torch.cuda.current_stream().cuda_stream
+ctx.set_stream(stream)
+q, k, v = H.inputs(33, L, 0, P + 1)
+qn = torch.empty_like(q)
+ctx.append(0, 0, L, 0, P + 1, q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr())
+ctx.commit(0, P)
+q1 = qn[:, P:].contiguous()
+out = torch.empty_like(q1)
+ref = torch.empty_like(q1)
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info()[0]
+for _ in range(2):
+    st = qattn.attn_decode_noalloc(ctx.kv_pointer(0, 0, 0, 0), L, 8, 1024, 0, L, P, 1, q1.data_ptr(),
+                                   out.data_ptr(), stream)
+    assert st == 0, st
+torch.cuda.synchronize()
+free1 = torch.cuda.mem_get_info()[0]
+ctx.attn_decode(0, 0, L, P, 1, q1.data_ptr(), ref.data_ptr())
+ctx.sync()
+mx, rms = H.err_stats(out.cpu().numpy(), ref.cpu().numpy())
+print(free0, free1, mx, rms)
+assert free1 == free0, (free0, free1)
+assert mx < H.MAX_ABS and rms < H.RMS, (mx, rms)
+"""
+
+
+def test_first_call_after_create_allocates_nothing_under_lazy_loading():
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, CUDA_MODULE_LOADING="LAZY")
+    res = subprocess.run([sys.executable, "-c", _LAZY_SCRIPT, str(root)], env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
