@@ -68,7 +68,7 @@ def balance_requests(lengths, world: int, decode_steps: int = 128):
 
 
 def config5_lengths(n: int = 64, lo: int = 85, hi: int = 3968, seed: int = 5):
-    """BASELINE config 5 prompt lengths: n draws from U[lo, hi] with a fixed seed."""
+    """Prompt lengths of the 64-request workload: n draws from U[lo, hi] with a fixed seed."""
     rng = np.random.default_rng(seed)
     return [int(x) for x in rng.integers(lo, hi + 1, n)]
 

@@ -1,10 +1,11 @@
 """Generate golden attention/KV fixtures by running the reference's own NumPy oracle.
 
-Run where a checkout of tampajohn/fpga-qwen is available (its directory in
-``FPGA_QWEN_REF``, or the default location in the code below)::
+Run where a checkout of tampajohn/fpga-qwen is available, with its directory in
+``FPGA_QWEN_REF``::
 
-    python tests/golden/make_golden.py                  # attention fixture
-    python tests/golden/make_golden.py --projections    # projection fixture
+    FPGA_QWEN_REF=<checkout> python tests/golden/make_golden.py                 # 40 tokens
+    FPGA_QWEN_REF=<checkout> python tests/golden/make_golden.py --tokens 200    # 200 tokens
+    FPGA_QWEN_REF=<checkout> python tests/golden/make_golden.py --projections   # projections
 
 It imports ``NumpyQwen`` from the reference's ``tests/test_full_model.py`` (lines 14-80)
 unchanged and runs ``NumpyQwen.token`` on a synthetic checkpoint written in the
@@ -24,6 +25,11 @@ While it runs, two probes record what the reference computes:
 The FP16 K/V rows come from the oracle's own cache payload. The recorded arrays for a few
 layers are written to ``tests/golden/numpyqwen_t{T}.npz``; the tests feed the pre-norm
 inputs to the C++ restatement and to the CUDA library and compare.
+
+``--tokens 200`` writes ``numpyqwen_t200.npz``: layer 27 only, with the rotated query and the
+attention output kept for rows 96..199 (key ``rows``), so that the rows at positions >= 128,
+which the library computes on the tensor cores, and the 127/128/129 boundary are pinned to the
+reference; the FP16 K/V rows are stored as float16. The pre-norm inputs cover every row.
 """
 from __future__ import annotations
 
@@ -37,9 +43,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("FPGA_QWEN_REF", "/root/reference"))
 TOKENS = 40                 # covers causal lengths 1..40, incl. the 31/32/33 edges
 KEEP_LAYERS = (0, 27)       # layers written to the fixture
+LONG_TOKENS, LONG_LAYERS, LONG_FIRST_ROW = 200, (27,), 96    # the --tokens 200 fixture
 H, F, V = 64, 8, 16
 SEED = 20261201
 
@@ -85,9 +91,20 @@ def write_checkpoint(path: Path, rng: np.random.Generator) -> None:
             f.write(raw)
 
 
-def main() -> None:
-    sys.path.insert(0, str(REF))
+def reference_dir() -> Path:
+    ref = os.environ.get("FPGA_QWEN_REF")
+    if not ref:
+        raise SystemExit("set FPGA_QWEN_REF to a checkout of tampajohn/fpga-qwen")
+    return Path(ref)
+
+
+def main(tokens: int = TOKENS) -> None:
+    sys.path.insert(0, str(reference_dir()))
     from tests.test_full_model import NumpyQwen  # the reference's oracle, unchanged
+
+    long_form = tokens != TOKENS
+    keep_layers = LONG_LAYERS if long_form else KEEP_LAYERS
+    rows = np.arange(LONG_FIRST_ROW if long_form else 0, tokens)
 
     rng = np.random.default_rng(SEED)
     with tempfile.TemporaryDirectory() as tmp:
@@ -128,7 +145,7 @@ def main() -> None:
 
     np.einsum = einsum
     try:
-        ids = rng.integers(0, V, TOKENS)
+        ids = rng.integers(0, V, tokens)
         for t, token in enumerate(ids):
             current["token"] = t
             einsum_layer["qk"] = einsum_layer["pv"] = 0
@@ -136,19 +153,22 @@ def main() -> None:
     finally:
         np.einsum = real_einsum
 
-    arrays = {"layers": np.array(KEEP_LAYERS, np.int32)}
-    for layer in KEEP_LAYERS:
+    kv_type = np.float16 if long_form else np.float32
+    arrays = {"layers": np.array(keep_layers, np.int32)}
+    if long_form:
+        arrays["rows"] = rows.astype(np.int32)
+    for layer in keep_layers:
         p = f"model.layers.{layer}.self_attn."
-        arrays[f"L{layer}_q_pre"] = np.stack([log[(t, layer, "q")].reshape(16, 128) for t in range(TOKENS)])
-        arrays[f"L{layer}_k_pre"] = np.stack([log[(t, layer, "k")].reshape(8, 128) for t in range(TOKENS)])
-        arrays[f"L{layer}_v_pre"] = np.stack([log[(t, layer, "v")].reshape(8, 128) for t in range(TOKENS)])
-        arrays[f"L{layer}_q_rot"] = np.stack([log[(t, layer, "q_rot")] for t in range(TOKENS)])
-        arrays[f"L{layer}_k16"] = np.stack([oracle.cache[t][layer][0] for t in range(TOKENS)]).astype(np.float32)
-        arrays[f"L{layer}_v16"] = np.stack([oracle.cache[t][layer][1] for t in range(TOKENS)]).astype(np.float32)
-        arrays[f"L{layer}_out"] = np.stack([log[(t, layer, "out")] for t in range(TOKENS)])
+        arrays[f"L{layer}_q_pre"] = np.stack([log[(t, layer, "q")].reshape(16, 128) for t in range(tokens)])
+        arrays[f"L{layer}_k_pre"] = np.stack([log[(t, layer, "k")].reshape(8, 128) for t in range(tokens)])
+        arrays[f"L{layer}_v_pre"] = np.stack([log[(t, layer, "v")].reshape(8, 128) for t in range(tokens)])
+        arrays[f"L{layer}_q_rot"] = np.stack([log[(t, layer, "q_rot")] for t in rows])
+        arrays[f"L{layer}_k16"] = np.stack([oracle.cache[t][layer][0] for t in range(tokens)]).astype(kv_type)
+        arrays[f"L{layer}_v16"] = np.stack([oracle.cache[t][layer][1] for t in range(tokens)]).astype(kv_type)
+        arrays[f"L{layer}_out"] = np.stack([log[(t, layer, "out")] for t in rows])
         arrays[f"L{layer}_q_norm"] = np.asarray(oracle.weights[p + "q_norm.weight"], np.float32)
         arrays[f"L{layer}_k_norm"] = np.asarray(oracle.weights[p + "k_norm.weight"], np.float32)
-    out = HERE / f"numpyqwen_t{TOKENS}.npz"
+    out = HERE / f"numpyqwen_t{tokens}.npz"
     np.savez_compressed(out, **arrays)
     print(f"wrote {out} ({out.stat().st_size} bytes)")
 
@@ -165,7 +185,7 @@ def projections() -> None:
     input and output of every matrix product (q/k/v/o, gate/up/down) per token, the MLP
     activation, and for the last token the final normalised hidden state and the logits.
     """
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(reference_dir()))
     from tests.test_full_model import NumpyQwen  # the reference's oracle, unchanged
 
     rng = np.random.default_rng(PROJ_SEED)
@@ -223,5 +243,7 @@ def projections() -> None:
 if __name__ == "__main__":
     if "--projections" in sys.argv:
         projections()
+    elif "--tokens" in sys.argv:
+        main(int(sys.argv[sys.argv.index("--tokens") + 1]))
     else:
         main()

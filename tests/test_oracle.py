@@ -129,3 +129,45 @@ def test_known_answers(tables):
     mean = kv.v[:, :8].view(np.float16).astype(np.float64).mean(axis=1)
     for h in range(16):
         assert np.allclose(out[0, h], mean[h // 2], atol=2e-6)
+
+
+# ---- the 200-token fixture: rows at positions >= 128 (the library's tensor-core rows) ----------
+def _oracle_layer200(g, layer, tables):
+    kv = O.LayerKV(8, 256)
+    q = O.append(kv, 0, g[f"L{layer}_q_pre"], g[f"L{layer}_k_pre"], g[f"L{layer}_v_pre"],
+                 g[f"L{layer}_q_norm"], g[f"L{layer}_k_norm"], tables)
+    return kv, q
+
+
+def test_long_fixture_kv_rows_match_reference_oracle(golden200, tables):
+    T = golden200[f"L27_q_pre"].shape[0]
+    for layer in golden200["layers"]:
+        kv, _ = _oracle_layer200(golden200, layer, tables)
+        v_ref = golden200[f"L{layer}_v16"].astype(np.float16).view(np.uint16)
+        assert np.array_equal(kv.v[:, :T].transpose(1, 0, 2), v_ref)
+        # Within one FP16 ulp, as for the 40-token fixture, except where RoPE cancels to a small
+        # value: there the few-FP32-ulp difference of the two norms is a larger share of the
+        # result, and the bound is absolute (2.5e-7, two FP16 ulps at 1.2e-4).
+        mine = kv.k[:, :T].transpose(1, 0, 2)
+        k_ref = golden200[f"L{layer}_k16"].astype(np.float16)
+        diff = np.abs(mine.astype(np.int32) - k_ref.view(np.uint16).astype(np.int32))
+        absdiff = np.abs(mine.view(np.float16).astype(np.float64) - k_ref.astype(np.float64))
+        assert ((diff <= 1) | (absdiff <= 2.5e-7)).all()
+        assert (diff != 0).mean() < 1e-3
+
+
+def test_long_fixture_attention_past_row_128_matches_reference_oracle(golden200, tables):
+    rows = golden200["rows"]
+    T = int(rows[-1]) + 1
+    for layer in golden200["layers"]:
+        # identical inputs: the reference oracle's FP16 K/V and rotated query
+        kv = O.LayerKV(8, 256)
+        kv.k[:, :T] = golden200[f"L{layer}_k16"].astype(np.float16).view(np.uint16).transpose(1, 0, 2)
+        kv.v[:, :T] = golden200[f"L{layer}_v16"].astype(np.float16).view(np.uint16).transpose(1, 0, 2)
+        out = O.attention(kv, int(rows[0]), golden200[f"L{layer}_q_rot"], threads=4)
+        assert np.abs(out - golden200[f"L{layer}_out"]).max() < 5e-6
+        # the whole path from the pre-norm inputs
+        kv2, q = _oracle_layer200(golden200, layer, tables)
+        assert np.abs(q[rows] - golden200[f"L{layer}_q_rot"]).max() <= 4e-6 * max(1.0, np.abs(q).max())
+        out2 = O.attention(kv2, int(rows[0]), q[rows], threads=4)
+        assert np.abs(out2 - golden200[f"L{layer}_out"]).max() < 1e-3
