@@ -14,6 +14,16 @@
 // include/qattn.h: q and out [layers][n][q_heads][128], k and v [layers][n][kv_heads][128]
 // FP32, device memory or (Options::host_buffers) host memory.
 //
+// Two forms of the same passes:
+//   all layers at once  prefill / step / verify_two take every layer's rows in one call (a
+//                       caller whose layers are independent, such as a benchmark);
+//   layer by layer      begin_rows(n) / layer_rows(layer, ...) / end_rows(): the engine's own
+//                       loop (core.cpp:383-645), where layer l+1's q, k, v come from layer l's
+//                       attention output through o_proj and the MLP, so the rows of one layer
+//                       are appended and attended (core.cpp:395-406, :407-624) before the
+//                       next layer's projections run; the position advances once, after the
+//                       last layer (core.cpp:643), or the rows wait for commit_verified.
+//
 // Header-only; link libqattn.so. C++17.
 #pragma once
 
@@ -74,17 +84,20 @@ public:
     void reset() {
         check(qa_reset(ctx_, seq_), false);
         verification_pending_ = false;
+        pass_rows_ = 0;
     }
 
     void truncate(int position) {
         require(position >= 0 && position <= this->position(), "Rewind position out of range");
         check(qa_truncate(ctx_, seq_, position), false);
         verification_pending_ = false;
+        pass_rows_ = 0;
     }
 
     // Appends n rows at the current position and writes their attention outputs; q_rows
     // receives the normalised, rotated query rows (same layout as q).
     void prefill(int n, const float* q, const float* k, const float* v, float* q_rows, float* out) {
+        require(pass_rows_ == 0, "A layer pass is already open");
         if (verification_pending_) throw std::runtime_error("Commit or discard pending verification before inference");
         require(n > 0, "Empty token input");
         require(n <= context_ - position(), "Context capacity exceeded");
@@ -101,6 +114,7 @@ public:
 
     // One decode row through the fused step (append + attention in one launch).
     void step(const float* q, const float* k, const float* v, float* out) {
+        require(pass_rows_ == 0, "A layer pass is already open");
         if (verification_pending_) throw std::runtime_error("Commit or discard pending verification before inference");
         require(1 <= context_ - position(), "Context capacity exceeded");
         const int pos = position();
@@ -114,6 +128,7 @@ public:
     // Two rows evaluated at the current position without advancing it; returns that base
     // position. Their KV rows stay appended for commit_verified.
     int verify_two(const float* q, const float* k, const float* v, float* q_rows, float* out) {
+        require(pass_rows_ == 0, "A layer pass is already open");
         require(!verification_pending_, "Verification already pending");
         require(position() <= context_ - 2, "Context capacity exceeded");
         const int pos = position();
@@ -135,6 +150,60 @@ public:
 
     bool verification_pending() const { return verification_pending_; }
 
+    // ---- layer by layer ------------------------------------------------------------------
+    // Opens a pass of n new rows at the current position (n == 1: a decode step; verify: the
+    // two rows of verify_two). Returns the base position. The same checks as the all-layer
+    // calls, before anything runs.
+    int begin_rows(int n, bool verify = false) {
+        if (verification_pending_) throw std::runtime_error("Commit or discard pending verification before inference");
+        require(pass_rows_ == 0, "A layer pass is already open");
+        require(n > 0, "Empty token input");
+        if (verify) require(n == 2, "Verification takes two rows");
+        require(n <= context_ - position(), "Context capacity exceeded");
+        pass_rows_ = n;
+        pass_verify_ = verify;
+        pass_layer_ = 0;
+        pass_pos_ = position();
+        return pass_pos_;
+    }
+
+    // Appends the open pass's rows of `layer` (tensors of that one layer: q [n][q_heads][128],
+    // k and v [n][kv_heads][128]) and writes their attention outputs to out. Layers run in
+    // order 0, 1, ... . q_rows receives the normalised, rotated query rows; it may be null for
+    // a decode step, which runs as one fused launch.
+    void layer_rows(int layer, const float* q, const float* k, const float* v, float* q_rows, float* out) {
+        require(pass_rows_ > 0, "No layer pass is open");
+        require(layer == pass_layer_, "Layers must run in order");
+        const int n = pass_rows_, pos = pass_pos_;
+        require(n == 1 || q_rows != nullptr, "Query rows buffer required");
+        run([&] {
+            if (n == 1) return qa_decode_step(ctx_, seq_, layer, 1, pos, q, k, v, q_rows, out);
+            int st = qa_append(ctx_, seq_, layer, 1, pos, n, q, k, v, q_rows);
+            if (st == QA_OK)
+                st = pass_verify_ ? qa_attn_decode(ctx_, seq_, layer, 1, pos, n, q_rows, out)
+                                  : qa_attn_prefill(ctx_, seq_, layer, 1, pos, n, q_rows, out);
+            return st;
+        });
+        ++pass_layer_;
+    }
+
+    // Closes the pass after its last layer: prefill and step rows are committed; verify rows
+    // become pending for commit_verified.
+    void end_rows() {
+        require(pass_rows_ > 0, "No layer pass is open");
+        require(pass_layer_ == layers_, "Every layer must run before the pass ends");
+        const int n = pass_rows_;
+        const bool verify = pass_verify_;
+        pass_rows_ = 0;
+        if (verify) {
+            verification_pending_ = true;
+            return;
+        }
+        run([&] { return qa_commit(ctx_, seq_, n); });
+    }
+
+    bool layer_pass_open() const { return pass_rows_ > 0; }
+
     // Blocks until the queued work has finished; reports a device-side wait that expired.
     void sync() { run([&] { return qa_sync(ctx_); }); }
 
@@ -152,6 +221,7 @@ private:
         if (reset_on_failure && !validation) {
             qa_reset(ctx_, seq_);
             verification_pending_ = false;
+            pass_rows_ = 0;
         }
         throw std::runtime_error(msg);
     }
@@ -165,6 +235,8 @@ private:
     int layers_ = 0;
     int context_ = 0;
     bool verification_pending_ = false;
+    int pass_rows_ = 0, pass_layer_ = 0, pass_pos_ = 0;   // the open layer-by-layer pass
+    bool pass_verify_ = false;
 };
 
 }  // namespace qattn_host

@@ -8,6 +8,16 @@
 //                                   truncate, one more step. Writes the norm weights and
 //                                   every input and output (float32, in call order) for the
 //                                   test to replay.
+//   host_model_main engine <out.bin>
+//                                   the engine's own loop (engine/core.cpp:383-645) with a
+//                                   stand-in for the projections: per pass, every layer's q, k
+//                                   and v are computed from a residual that the previous
+//                                   layer's attention output updated, so layer l+1 depends on
+//                                   layer l. Passes: prefill 85 rows, 3 decode steps, a
+//                                   two-row verification committed by one; plus the refusals of
+//                                   a layer out of order and of an all-layer call while a pass
+//                                   is open. Writes the norm weights and, per pass, the
+//                                   residual in and, per layer, q, k, v and the output.
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -51,8 +61,71 @@ std::string refused(F&& f) {
 
 }  // namespace
 
+// Stand-in for the engine's projections around attention (not the reference's arithmetic,
+// only its data flow): q, k, v of layer l from the residual r [n][2048], and r += out / 2.
+void project_stand_in(int layer, int n, const std::vector<float>& r, std::vector<float>& q, std::vector<float>& k,
+                      std::vector<float>& v) {
+    const float a = 1.0f + 0.01f * (float)layer, b = 0.001f * (float)layer;
+    for (int i = 0; i < n * HQ * D; ++i) q[i] = r[i] * a + b;
+    for (int row = 0; row < n; ++row)
+        for (int i = 0; i < HKV * D; ++i) {
+            k[size_t(row) * HKV * D + i] = r[size_t(row) * HQ * D + i] * 0.9f;
+            v[size_t(row) * HKV * D + i] = r[size_t(row) * HQ * D + HKV * D + i] * 1.1f;
+        }
+}
+
+int engine_mode(const char* path) {
+    qattn_host::Options opt;
+    opt.layers = L;
+    opt.context = 512;
+    opt.host_buffers = true;
+    qattn_host::AttentionModel m(opt);
+    FILE* f = std::fopen(path, "wb");
+    if (!f) return 3;
+    Rng rng{0xD1B54A32D192ED03ull};
+    std::vector<float> qw(D), kw(D);
+    for (int l = 0; l < L; ++l) {
+        for (int j = 0; j < D; ++j) { qw[j] = 1.0f + 0.025f * rng.next(); kw[j] = 1.0f + 0.025f * rng.next(); }
+        m.set_norms(l, qw.data(), kw.data());
+        dump(f, qw); dump(f, kw);
+    }
+    std::string order_msg, open_msg;
+    auto pass = [&](int n, bool verify) {
+        std::vector<float> r(size_t(n) * HQ * D), q(r.size()), qn(r.size()), out(r.size());
+        std::vector<float> k(size_t(n) * HKV * D), v(k.size());
+        for (float& x : r) x = rng.next();
+        dump(f, r);
+        m.begin_rows(n, verify);
+        for (int l = 0; l < L; ++l) {
+            project_stand_in(l, n, r, q, k, v);
+            if (l == 1 && order_msg.empty())
+                order_msg = refused([&] { m.layer_rows(2, q.data(), k.data(), v.data(), qn.data(), out.data()); });
+            if (l == 2 && open_msg.empty())
+                open_msg = refused([&] { m.step(q.data(), k.data(), v.data(), out.data()); });
+            m.layer_rows(l, q.data(), k.data(), v.data(), n == 1 ? nullptr : qn.data(), out.data());
+            dump(f, q); dump(f, k); dump(f, v); dump(f, out);
+            for (size_t i = 0; i < r.size(); ++i) r[i] = r[i] + 0.5f * out[i];     // stand-in o_proj + residual
+        }
+        m.end_rows();
+    };
+    pass(85, false);
+    const int pos_prefill = m.position();
+    for (int s = 0; s < 3; ++s) pass(1, false);
+    const int pos_steps = m.position();
+    pass(2, true);
+    const bool pending = m.verification_pending();
+    m.commit_verified(1);
+    std::fclose(f);
+    m.sync();
+    std::printf("positions %d %d %d %d\n", pos_prefill, pos_steps, pending ? 1 : 0, m.position());
+    std::printf("order_msg %s\n", order_msg.c_str());
+    std::printf("open_msg %s\n", open_msg.c_str());
+    return 0;
+}
+
 int main(int argc, char** argv) {
     const std::string mode = argc > 1 ? argv[1] : "";
+    if (mode == "engine" && argc > 2) return engine_mode(argv[2]);
     if (mode == "nogpu") {
         try {
             qattn_host::AttentionModel m(qattn_host::Options{});

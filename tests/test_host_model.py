@@ -114,3 +114,62 @@ def test_host_model_matches_library(tmp_path):
     assert torch.equal(out, want)
     assert ctx.position(0) == 51
     ctx.close()
+
+
+@pytest.mark.gpu
+def test_engine_loop_layer_by_layer(tmp_path):
+    """The engine's own loop through the layer-by-layer form (begin_rows / layer_rows /
+    end_rows), host buffers: each layer's q, k, v come from a residual that the previous
+    layer's attention output updated (a stand-in for o_proj and the MLP), so the library must
+    serve layer l before layer l+1's inputs exist. The recorded inputs follow from the
+    recorded outputs exactly; every layer's outputs agree with the oracle replaying the same
+    rows; positions and refusals follow engine/core.cpp (the position advances after the last
+    layer; verification rows wait for commit_verified)."""
+    from oracle import oracle as O
+    from tests import helpers as H
+
+    exe = build(tmp_path)
+    out_file = tmp_path / "engine.bin"
+    res = subprocess.run([str(exe), "engine", str(out_file)], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout + res.stderr
+    lines = dict(line.split(" ", 1) for line in res.stdout.strip().splitlines())
+    assert lines["positions"].split() == ["85", "88", "1", "89"]
+    assert lines["order_msg"] == "Layers must run in order"
+    assert lines["open_msg"] == "A layer pass is already open"
+
+    a = np.fromfile(out_file, dtype=np.float32)
+    off = 0
+
+    def take(*shape):
+        nonlocal off
+        n = int(np.prod(shape))
+        x = a[off:off + n].reshape(shape)
+        off += n
+        return x
+
+    norms = [(take(D).copy(), take(D).copy()) for _ in range(L)]
+    passes = []                      # (pos0, n, [per layer (q, k, v, out)])
+    pos = 0
+    for n in (85, 1, 1, 1, 2):
+        r = take(n, HQ * D).copy()
+        layers = []
+        for layer in range(L):
+            q, k, v, out = take(n, HQ, D), take(n, HKV, D), take(n, HKV, D), take(n, HQ, D)
+            # the stand-in projection of this layer's residual, in the same FP32 operations
+            sa = np.float32(1.0) + np.float32(0.01) * np.float32(layer)
+            sb = np.float32(0.001) * np.float32(layer)
+            assert np.array_equal(q.reshape(n, -1), r * sa + sb)
+            assert np.array_equal(k.reshape(n, -1), r[:, :HKV * D] * np.float32(0.9))
+            assert np.array_equal(v.reshape(n, -1), r[:, HKV * D:] * np.float32(1.1))
+            layers.append((q, k, v, out))
+            r = r + np.float32(0.5) * out.reshape(n, -1)
+        passes.append((pos, n, layers))
+        pos += n
+    assert off == a.size
+    tables = O.rope_tables(512)
+    for layer in range(L):
+        kv = O.LayerKV(HKV, 512)
+        for pos0, n, layers in passes:
+            q, k, v, out = layers[layer]
+            qn = O.append(kv, pos0, q, k, v, norms[layer][0], norms[layer][1], tables)
+            H.check("engine loop layer by layer (host buffers)", out, O.attention(kv, pos0, qn, threads=4))
