@@ -57,6 +57,10 @@ struct qa_ctx {
     CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
     int* error = nullptr;                  // device error block (qattn_common.cuh: ERR_*), at io_dev
     int* prefill_tiles = nullptr;          // work-item counter of the persistent prefill kernel
+    // The FP32 rows below position 128 run on a second stream next to the persistent tensor-core
+    // kernel (fork: aux waits for the context stream; join: the context stream waits for aux).
+    cudaStream_t aux_stream = nullptr;
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     void* comm = nullptr;                  // NCCL communicator (multi-GPU)
     cudaStream_t comm_stream = nullptr;    // NCCL work runs here, ordered after/before the context stream
     cudaEvent_t comm_ev[2] = {nullptr, nullptr};
@@ -191,7 +195,7 @@ int check_appended(qa_ctx* ctx, int seq, int layer, int n_layers, int end) {
 // pinned mirror io_pin), one copy per tensor otherwise. Calls whose rows x layers exceed the
 // staging made at creation run in chunks of whole layers (every layer is independent). A bounded
 // wait that ran out during the call fails it with QA_ERR_TIMEOUT and resets the sequence.
-constexpr size_t IO_PACK_BYTES = size_t(4) << 20;
+constexpr size_t IO_PACK_BYTES = size_t(64) << 10;      // above this, one copy per tensor is faster
 
 struct IoCall {
     const float* in[3] = {};       // host inputs, [n_layers][...] layer-major
@@ -428,6 +432,10 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     ctx->error = reinterpret_cast<int*>(ctx->io_dev);
     ctx->staging = reinterpret_cast<float*>(ctx->io_dev + ERR_BLOCK_BYTES);
     if (cudaMalloc(&ctx->prefill_tiles, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaStreamCreateWithFlags(&ctx->aux_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->fork_ev, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->join_ev, cudaEventDisableTiming) != cudaSuccess)
+        return cleanup(QA_ERR_CUDA);
     // the device address of qa_attn_decode_noalloc's fixed scratch, looked up now (it loads that
     // module onto the GPU) rather than at its first call, when the host may own all free memory
     if (noalloc_prepare(c.device) != cudaSuccess) return cleanup(QA_ERR_CUDA);
@@ -448,6 +456,9 @@ void qa_destroy(qa_ctx* ctx) {
     cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
     cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->io_dev); cudaFreeHost(ctx->io_pin);
     cudaFree(ctx->prefill_tiles);
+    if (ctx->aux_stream) { cudaStreamSynchronize(ctx->aux_stream); cudaStreamDestroy(ctx->aux_stream); }
+    if (ctx->fork_ev) cudaEventDestroy(ctx->fork_ev);
+    if (ctx->join_ev) cudaEventDestroy(ctx->join_ev);
     cudaFree(ctx->gather_buf); cudaFree(ctx->kv_buf[0]); cudaFree(ctx->kv_buf[1]);
     for (cudaEvent_t e : ctx->kv_comm_done) if (e) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->kv_unpacked) if (e) cudaEventDestroy(e);
@@ -616,13 +627,24 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
             OutRows o{};
             if (gather) o = *gather;
             else { o.out = dout[0]; o.heads = ctx->hq; }
+            const bool both = tc_begin > 0 && tc_begin < n;
+            if (both) {
+                // the FP32 rows on the aux stream, submitted first, so their CTAs and the persistent
+                // kernel's share the GPU (the tensor-core CTAs start on the SMs they leave free)
+                QA_CUDA(cudaEventRecord(ctx->fork_ev, ctx->stream));
+                QA_CUDA(cudaStreamWaitEvent(ctx->aux_stream, ctx->fork_ev, 0));
+            }
             if (tc_begin > 0) {
                 r.row_end = tc_begin;
-                launch_attn_head_rows(r, o, ctx->stream);
+                launch_attn_head_rows(r, o, both ? ctx->aux_stream : ctx->stream);
             }
             if (launch_attn_prefill_sm100(ctx->kv_map, din[0], o, seq, l0, nl, pos0, n, ctx->hq, ctx->hkv,
                                           ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->error, ctx->stream))
                 return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel has an unexpected register allocation");
+            if (both) {
+                QA_CUDA(cudaEventRecord(ctx->join_ev, ctx->aux_stream));
+                QA_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->join_ev, 0));
+            }
         }
         return after_launch(ctx, seq, decode ? "attn_decode" : "attn_prefill");
     });
@@ -901,6 +923,84 @@ int qa_kv_slot_bytes(const qa_ctx* ctx, size_t* bytes) {
     if (!ctx || !bytes) return QA_ERR_INVALID;
     *bytes = ctx->kv.slot_elems() * sizeof(__half);
     return QA_OK;
+}
+
+// ---- decode projections (project.cu) ----------------------------------------------------------
+int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const int* rows, int cols, const float* x,
+                     int batch, float* const* y) {
+    if (!ctx) return QA_ERR_INVALID;
+    if (n_mats < 1 || n_mats > MAX_PROJECT_MATS || !w || !rows || !y)
+        return fail(ctx, QA_ERR_INVALID, "%d matrices (1..%d) or null arrays", n_mats, MAX_PROJECT_MATS);
+    if (cols < 8 || cols % 8) return fail(ctx, QA_ERR_INVALID, "columns %d: a positive multiple of 8", cols);
+    if (batch < 1 || batch > QA_MAX_BATCH) return fail(ctx, QA_ERR_INVALID, "batch %d outside 1..%d", batch, QA_MAX_BATCH);
+    if (!x) return fail(ctx, QA_ERR_INVALID, "null input");
+    size_t out_floats = 0;
+    ProjectArgs a{};
+    a.n_mats = n_mats; a.cols = cols; a.batch = batch;
+    for (int m = 0; m < n_mats; ++m) {
+        if (!w[m] || !y[m] || rows[m] < 1) return fail(ctx, QA_ERR_INVALID, "matrix %d: null pointer or %d rows", m, rows[m]);
+        if (reinterpret_cast<uintptr_t>(w[m]) & 15) return fail(ctx, QA_ERR_INVALID, "matrix %d is not 16-byte aligned", m);
+        a.w[m] = reinterpret_cast<const __half*>(w[m]);
+        a.rows[m] = rows[m];
+        out_floats += (size_t)rows[m] * batch;
+    }
+    QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    const size_t in_floats = (size_t)batch * cols;
+    if (!ctx->cfg.io_host) {
+        a.x = x;
+        for (int m = 0; m < n_mats; ++m) a.y[m] = y[m];
+        launch_project(a, ctx->stream);
+        return after_launch(ctx, -1, "project");
+    }
+    // host buffers: x into the staging inputs, every y from the staging outputs (one copy each
+    // way through the pinned mirror when they fit IO_PACK_BYTES)
+    if (in_floats > ctx->io_in_floats || out_floats > ctx->io_out_floats)
+        return fail(ctx, QA_ERR_CAPACITY, "projection of %zu outputs beyond the host-buffer staging", out_floats);
+    float* d_out = ctx->staging;
+    float* d_in = ctx->staging + ctx->io_out_floats;
+    int* h_err = reinterpret_cast<int*>(ctx->io_pin);
+    float* h_out = reinterpret_cast<float*>(ctx->io_pin + ERR_BLOCK_BYTES);
+    float* h_in = h_out + IO_PACK_BYTES / sizeof(float);
+    const bool pack_in = in_floats * sizeof(float) <= IO_PACK_BYTES, pack_out = out_floats * sizeof(float) <= IO_PACK_BYTES;
+    if (pack_in) {
+        std::memcpy(h_in, x, in_floats * sizeof(float));
+        QA_CUDA(cudaMemcpyAsync(d_in, h_in, in_floats * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+    } else {
+        QA_CUDA(cudaMemcpyAsync(d_in, x, in_floats * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+    }
+    a.x = d_in;
+    size_t off = 0;
+    for (int m = 0; m < n_mats; ++m) { a.y[m] = d_out + off; off += (size_t)rows[m] * batch; }
+    launch_project(a, ctx->stream);
+    int st;
+    if ((st = after_launch(ctx, -1, "project"))) return st;
+    if (pack_out) {
+        QA_CUDA(cudaMemcpyAsync(h_err, ctx->io_dev, ERR_BLOCK_BYTES + out_floats * sizeof(float), cudaMemcpyDeviceToHost,
+                                ctx->stream));
+    } else {
+        QA_CUDA(cudaMemcpyAsync(h_err, ctx->io_dev, ERR_BLOCK_BYTES, cudaMemcpyDeviceToHost, ctx->stream));
+        for (int m = 0; m < n_mats; ++m)
+            QA_CUDA(cudaMemcpyAsync(y[m], a.y[m], (size_t)rows[m] * batch * sizeof(float), cudaMemcpyDeviceToHost,
+                                    ctx->stream));
+    }
+    QA_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (pack_out) {
+        off = 0;
+        for (int m = 0; m < n_mats; ++m) {
+            std::memcpy(y[m], h_out + off, (size_t)rows[m] * batch * sizeof(float));
+            off += (size_t)rows[m] * batch;
+        }
+    }
+    if (const int code = h_err[ERR_CODE]) {
+        QA_CUDA(cudaMemsetAsync(ctx->error + ERR_CODE, 0, sizeof(int), ctx->stream));
+        QA_CUDA(cudaStreamSynchronize(ctx->stream));
+        return fail(ctx, QA_ERR_TIMEOUT, "a device-side wait expired (code %d); results of the last calls are invalid", code);
+    }
+    return QA_OK;
+}
+
+int qa_project(qa_ctx* ctx, const uint16_t* w, int rows, int cols, const float* x, int batch, float* y) {
+    return qa_project_group(ctx, 1, &w, &rows, cols, x, batch, &y);
 }
 
 int qa_synth_fill(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n, int head0,

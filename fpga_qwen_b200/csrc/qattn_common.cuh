@@ -171,6 +171,21 @@ void launch_pack_kv(const KVLayout& kv, int seq, int pos0, int ntok, void* buf, 
 // Partial record size (floats) of one split in RowsArgs::partial.
 constexpr int PARTIAL_FLOATS = 4 + GROUP * D;
 
+// Decode projections (project.cu): y[m][b][r] = eight-lane dot of x[b] and row r of the FP16
+// matrix w[m] ([rows[m]][cols], cols % 8 == 0, 16-byte aligned), for n_mats matrices sharing
+// one input x [batch][cols]. tile0 is filled by the launcher.
+constexpr int MAX_PROJECT_MATS = 8;
+struct ProjectArgs {
+    int n_mats = 0;
+    const __half* w[MAX_PROJECT_MATS] = {};
+    int rows[MAX_PROJECT_MATS] = {};
+    float* y[MAX_PROJECT_MATS] = {};
+    int tile0[MAX_PROJECT_MATS + 1] = {};
+    int cols = 0, batch = 0;
+    const float* x = nullptr;
+};
+void launch_project(ProjectArgs a, cudaStream_t s);
+
 // Looks up, for `device` and its current context, the device address of the fixed scratch array
 // behind qa_attn_decode_noalloc (attn_decode_noalloc.cu). Makes `device` current.
 cudaError_t noalloc_prepare(int device);

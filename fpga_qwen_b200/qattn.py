@@ -107,6 +107,10 @@ _SIGNATURES = {
     "qa_attn_decode_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                               ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                               ctypes.c_void_p, ctypes.c_void_p]),
+    "qa_project": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                  ctypes.c_int, ctypes.c_void_p]),
+    "qa_project_group": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                        ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "qa_synth_fill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                      ctypes.c_float, ctypes.c_void_p]),
@@ -318,6 +322,18 @@ class Context:
     def comm_join(self):
         """Makes the context stream wait for the communication queued so far."""
         self._check(lib().qa_comm_join(self._h))
+
+    def project(self, w_ptr: int, rows: int, cols: int, x_ptr: int, batch: int, y_ptr: int):
+        """y [batch][rows] = eight-lane dot of x [batch][cols] with each row of the FP16 matrix w."""
+        self._check(lib().qa_project(self._h, w_ptr, rows, cols, x_ptr, batch, y_ptr))
+
+    def project_group(self, w_ptrs, rows, cols: int, x_ptr: int, batch: int, y_ptrs):
+        """Several matrices sharing one input, one launch; y_ptrs[m] receives [batch][rows[m]]."""
+        n = len(w_ptrs)
+        ws = (ctypes.c_void_p * n)(*w_ptrs)
+        rs = (ctypes.c_int * n)(*rows)
+        ys = (ctypes.c_void_p * n)(*y_ptrs)
+        self._check(lib().qa_project_group(self._h, n, ws, rs, cols, x_ptr, batch, ys))
 
     def kv_slot_bytes(self) -> int:
         out = ctypes.c_size_t()

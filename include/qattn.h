@@ -210,6 +210,25 @@ int qa_read_kv(qa_ctx* ctx, int seq, int layer, int kv, int head, int pos0, int 
 int qa_kv_pointer(qa_ctx* ctx, int seq, int layer, int kv, int head, void** ptr);
 int qa_kv_slot_bytes(const qa_ctx* ctx, size_t* bytes);
 
+/* ---- Projections over FP16 matrices (the engine's GEMVs around attention) ------------------
+ * y[b][r] = dot(x[b], W[r]) for an FP16 matrix W [rows][cols] (cols a multiple of 8, W 16-byte
+ * aligned, DEVICE memory in every context: weights stay resident), FP32 x [batch][cols] and
+ * y [batch][rows] (device pointers, or host pointers in io_host contexts), 1 <= batch <=
+ * QA_MAX_BATCH. Every output follows the reference's eight-lane dot bit for bit: two 4-lane
+ * FP32 accumulators over channels j..j+3 and j+4..j+7, fused multiply-adds with j ascending by
+ * 8, then (s0+s1)+(s2+s3) of their lane-wise sums (core.cpp:119-147). That is the arithmetic
+ * of Model::Impl::project for one row (core.cpp:292-301), of the verification projections for
+ * two (project_verify, dot_verify_pair / dot_verify_two_rows, :182-206, :321-349) and of the
+ * FP16-only vocabulary head at any batch (:705, :713). (Batched prefill projections over the
+ * FP32 copies of the layer matrices, cblas_sgemm at :294, sum in an unpublished order; this
+ * call gives them within FP32 rounding.) Asynchronous on the context stream. */
+int qa_project(qa_ctx* ctx, const uint16_t* w, int rows, int cols, const float* x, int batch, float* y);
+/* The same for n_mats (1..8) matrices of equal width that share the input x, as one launch:
+ * q/k/v or gate/up (project_group / project_group_verify, core.cpp:302-320, :388-389, :629,
+ * :657, :693). y[m] receives [batch][rows[m]]. */
+int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const int* rows, int cols,
+                     const float* x, int batch, float* const* y);
+
 /* ---- Multi-GPU: KV-head sharding and prefill -> decode handoff (NCCL over NVLink) -------
  * No counterpart in the reference, a single-host CPU engine. One process per GPU; each
  * context holds KV heads [kv_head_begin, kv_head_begin + kv_head_count) with their GQA

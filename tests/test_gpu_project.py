@@ -1,0 +1,120 @@
+"""GPU projections (qa_project / qa_project_group) against the oracle's eight-lane dot.
+
+The reference computes every decode-time projection (one row), every verification projection
+(two rows) and the FP16-only vocabulary head with its eight-lane dot (engine/core.cpp:119-147,
+:182-206, :292-349, :705, :713); the library must reproduce it bit for bit. The oracle
+restatement (oracle.project, sgemm=False) is pinned to the reference's NumpyQwen through
+tests/golden/numpyqwen_proj_t3.npz (tests/test_oracle_projection.py).
+"""
+import os
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from fpga_qwen_b200 import qattn
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+THREADS = os.cpu_count() or 4
+SHAPES = {"q": (2048, 1024), "k": (1024, 1024), "v": (1024, 1024), "o": (1024, 2048),
+          "gate": (3072, 1024), "up": (3072, 1024), "down": (1024, 3072)}
+
+
+def _ctx(**kw):
+    ctx = qattn.Context(n_layers=1, context=256, **kw)
+    if not kw.get("io_host"):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    return ctx
+
+
+def _matrix(rng, rows, cols, scale=None):
+    scale = scale or 1.0 / np.sqrt(cols)
+    return (rng.standard_normal((rows, cols)) * scale).astype(np.float16).view(np.uint16)
+
+
+def _gpu_project(ctx, w16, x, batch):
+    w = torch.from_numpy(w16.view(np.int16)).cuda()
+    xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    y = torch.full((batch, w16.shape[0]), float("nan"), device="cuda")
+    ctx.project(w.data_ptr(), w16.shape[0], w16.shape[1], xd.data_ptr(), batch, y.data_ptr())
+    torch.cuda.synchronize()
+    ctx.sync()
+    return y.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", list(SHAPES))
+@pytest.mark.parametrize("batch", [1, 2])
+def test_layer_projections_bit_exact(name, batch):
+    rng = np.random.default_rng(10 * list(SHAPES).index(name) + batch)
+    rows, cols = SHAPES[name]
+    w = _matrix(rng, rows, cols)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    ctx = _ctx()
+    got = _gpu_project(ctx, w, x, batch)
+    assert np.array_equal(got, O.project(x, w, threads=THREADS)), name
+    ctx.close()
+
+
+def test_vocabulary_head_bit_exact():
+    rng = np.random.default_rng(7)
+    w = _matrix(rng, 151936, 1024, scale=0.05)
+    x = rng.standard_normal((1, 1024)).astype(np.float32)
+    ctx = _ctx()
+    got = _gpu_project(ctx, w, x, 1)
+    assert np.array_equal(got, O.project(x, w, threads=THREADS))
+    ctx.close()
+
+
+def test_group_ragged_shapes_and_batches_bit_exact():
+    """q/k/v as one launch; rows that are not a multiple of the 16-row tile, a width that is not
+    a multiple of the 256-column chunk, and batches that need several passes."""
+    rng = np.random.default_rng(8)
+    ctx = _ctx()
+    for rows, cols, batch in (((2048, 1024, 1024), 1024, 1), ((37, 5, 300), 776, 3), ((16, 17), 8, 5)):
+        ws = [_matrix(rng, r, cols) for r in rows]
+        x = rng.standard_normal((batch, cols)).astype(np.float32)
+        wd = [torch.from_numpy(w.view(np.int16)).cuda() for w in ws]
+        xd = torch.from_numpy(x).cuda()
+        ys = [torch.full((batch, r), float("nan"), device="cuda") for r in rows]
+        ctx.project_group([t.data_ptr() for t in wd], list(rows), cols, xd.data_ptr(), batch,
+                          [t.data_ptr() for t in ys])
+        torch.cuda.synchronize()
+        for w, y in zip(ws, ys):
+            assert np.array_equal(y.cpu().numpy(), O.project(x, w, threads=THREADS)), (rows, cols, batch)
+    ctx.close()
+
+
+def test_reference_fixture_through_the_gpu():
+    """The matrices and inputs NumpyQwen recorded: the GPU equals the restatement bit for bit
+    (and so lies within the restatement's pinned tolerance of the reference)."""
+    fix = np.load(Path(__file__).parent / "golden" / "numpyqwen_proj_t3.npz")
+    ctx = _ctx()
+    for kind in ("q", "k", "v", "o", "gate", "up", "down"):
+        x, w = fix[f"{kind}_in"], np.ascontiguousarray(fix[f"w_{kind}"])
+        got = _gpu_project(ctx, w, x, x.shape[0])
+        assert np.array_equal(got, O.project(x, w)), kind
+    logits = _gpu_project(ctx, np.ascontiguousarray(fix["embed"]), fix["final_hidden"][None], 1)
+    assert np.array_equal(logits, O.project(fix["final_hidden"][None], fix["embed"]))
+    ctx.close()
+
+
+def test_host_buffers_and_validation():
+    rng = np.random.default_rng(9)
+    rows, cols = 3072, 1024
+    w = _matrix(rng, rows, cols)
+    x = rng.standard_normal((2, cols)).astype(np.float32)
+    wd = torch.from_numpy(w.view(np.int16)).cuda()
+    host = _ctx(io_host=1)
+    y = np.full((2, rows), np.nan, np.float32)
+    host.project(wd.data_ptr(), rows, cols, x.ctypes.data, 2, y.ctypes.data)
+    assert np.array_equal(y, O.project(x, w, threads=THREADS))
+    with pytest.raises(qattn.QAttnError) as e:
+        host.project(wd.data_ptr(), rows, 1020, x.ctypes.data, 1, y.ctypes.data)
+    assert e.value.status == qattn.QA_ERR_INVALID
+    with pytest.raises(qattn.QAttnError) as e:
+        host.project(wd.data_ptr() + 2, rows, cols, x.ctypes.data, 1, y.ctypes.data)     # not 16-byte aligned
+    assert e.value.status == qattn.QA_ERR_INVALID
+    host.close()
