@@ -504,6 +504,8 @@ def run_ours(args):
             if sub:
                 line[key] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "decode_phase_ms", "prefill",
                                                  "roofline", "config", "handoff") if k in sub}
+        if world == 1 and not args.no_projections:
+            line["projections"] = projection_bench(args)
         if world == 1 and not args.no_e2e:
             line["e2e"] = e2e_decode(args, seed)
             line["e2e_per_layer"] = e2e_per_layer(args, seed)
@@ -635,6 +637,78 @@ def e2e_per_layer(args, seed):
             "h2d_bytes_per_step": (HQ + 2 * HKV) * D * 4 * L * DECODE, "d2h_bytes_per_step": HQ * D * 4 * L * DECODE,
             "note": "128 tokens x 28 qa_decode_step calls of one layer each (io_host, pageable host arrays) + "
                     "qa_commit per token; device_us = the 28 per-layer fused kernels (CUDA events)"}
+
+
+def projection_bench(args):
+    """Decode projections over the Qwen3-0.6B FP16 matrices (random weights; the checkpoint is
+    not available): per token, for each of the 28 layers q/k/v as one launch (qa_project_group),
+    o_proj, gate/up as one launch and down_proj, then the tied vocabulary head over the
+    151,936 x 1,024 embedding matrix, all at batch 1 and bit-exact with the reference's eight-lane
+    dot. Reports the weight bytes read per token over the device time (CUDA events), the
+    vocabulary head alone (its largest launch) against the measured HBM bandwidth, and the
+    launches per token."""
+    import torch
+    from fpga_qwen_b200 import qattn
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    H, QD, KD, F, VOCAB = 1024, HQ * D, HKV * D, 3072, 151936
+    g = torch.Generator(device=dev).manual_seed(11)
+
+    def mat(rows, cols):
+        return (torch.randn((rows, cols), device=dev, generator=g) * (cols ** -0.5)).half()
+
+    layers = [{"q": mat(QD, H), "k": mat(KD, H), "v": mat(KD, H), "o": mat(H, QD), "gate": mat(F, H),
+               "up": mat(F, H), "down": mat(H, F)} for _ in range(L)]
+    embed = mat(VOCAB, H)
+    x = torch.randn((1, max(H, QD, F)), device=dev, generator=g)
+    outs = {k: torch.empty((1, n), device=dev) for k, n in (("q", QD), ("k", KD), ("v", KD), ("o", H), ("gate", F),
+                                                            ("up", F), ("down", H), ("vocab", VOCAB))}
+    ctx = qattn.Context(n_layers=1, context=256)
+    ctx.set_stream(stream.cuda_stream)
+    p = lambda t: t.data_ptr()
+
+    def token():
+        for lw in layers:
+            ctx.project_group([p(lw["q"]), p(lw["k"]), p(lw["v"])], [QD, KD, KD], H, p(x), 1,
+                              [p(outs["q"]), p(outs["k"]), p(outs["v"])])
+            ctx.project(p(lw["o"]), H, QD, p(x), 1, p(outs["o"]))
+            ctx.project_group([p(lw["gate"]), p(lw["up"])], [F, F], H, p(x), 1, [p(outs["gate"]), p(outs["up"])])
+            ctx.project(p(lw["down"]), H, F, p(x), 1, p(outs["down"]))
+        ctx.project(p(embed), VOCAB, H, p(x), 1, p(outs["vocab"]))
+
+    tokens = 16
+    for _ in range(max(3, args.warmup)):
+        token()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(tokens):
+        token()
+    e1.record(stream)
+    v0, v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    v0.record(stream)
+    for _ in range(tokens):
+        ctx.project(p(embed), VOCAB, H, p(x), 1, p(outs["vocab"]))
+    v1.record(stream)
+    torch.cuda.synchronize()
+    ctx.sync()
+    ctx.close()
+    layer_bytes = 2 * H * (QD + 2 * KD) + 2 * QD * H + 2 * 2 * F * H + 2 * F * H
+    token_bytes = L * layer_bytes + 2 * VOCAB * H
+    tok_ms = e0.elapsed_time(e1) / tokens
+    vocab_us = v0.elapsed_time(v1) / tokens * 1e3
+    hbm_peak, _, peak_kind = load_peaks()
+    vocab_gbs = 2 * VOCAB * H / (vocab_us * 1e-6) / 1e9
+    return {"metric": "decode projections GB/s (weight bytes per token / device time)",
+            "value": round(token_bytes / (tok_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "us_per_token": round(tok_ms * 1e3, 1), "bytes_per_token": token_bytes, "launches_per_token": 4 * L + 1,
+            "roofline": {"bound": "hbm", "kernel": "project_kernel, vocabulary head (151936 x 1024 FP16)",
+                         "achieved": round(vocab_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(vocab_gbs / hbm_peak, 4), "kernel_us": round(vocab_us, 2),
+                         "peak_kind": peak_kind},
+            "config": {"workload": "one decode token of Qwen3-0.6B's projections: 28 x (q/k/v, o, gate/up, down) + "
+                                   "tied vocabulary head, batch 1, random FP16 weights",
+                       "arithmetic": "eight-lane dot of engine/core.cpp:119-147 (bit-exact)"}}
 
 
 def run_config5(args, nested=False, disagg=None, warmup=None, steps=None):
@@ -903,6 +977,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-projections", action="store_true", help="skip the nested decode-projection line")
     ap.add_argument("--no-config5", action="store_true",
                     help="skip the nested 64-request (request-sharded / disaggregated) lines")
     ap.add_argument("--workload", choices=["config4", "config5"], default="config4",
