@@ -6,6 +6,7 @@ Run where a checkout of tampajohn/fpga-qwen is available, with its directory in
     FPGA_QWEN_REF=<checkout> python tests/golden/make_golden.py                 # 40 tokens
     FPGA_QWEN_REF=<checkout> python tests/golden/make_golden.py --tokens 200    # 200 tokens
     FPGA_QWEN_REF=<checkout> python tests/golden/make_golden.py --projections   # projections
+    FPGA_QWEN_REF=<checkout> python tests/golden/make_golden.py --engine        # engine logits
 
 It imports ``NumpyQwen`` from the reference's ``tests/test_full_model.py`` (lines 14-80)
 unchanged and runs ``NumpyQwen.token`` on a synthetic checkpoint written in the
@@ -57,7 +58,8 @@ def bf16_bits(x: np.ndarray) -> np.ndarray:
     return u.astype(np.uint16)
 
 
-def write_checkpoint(path: Path, rng: np.random.Generator) -> None:
+def checkpoint_tensors(rng: np.random.Generator) -> dict:
+    """The synthetic checkpoint's tensors (float64, before BF16 rounding), in writing order."""
     tensors = {}
     tensors["model.embed_tokens.weight"] = rng.standard_normal((V, H))
     tensors["model.norm.weight"] = np.ones(H)
@@ -75,6 +77,16 @@ def write_checkpoint(path: Path, rng: np.random.Generator) -> None:
         tensors[p + "mlp.gate_proj.weight"] = rng.standard_normal((F, H)) * 0.1
         tensors[p + "mlp.up_proj.weight"] = rng.standard_normal((F, H)) * 0.1
         tensors[p + "mlp.down_proj.weight"] = rng.standard_normal((H, F)) * 0.1
+    return tensors
+
+
+def bf16_values(x: np.ndarray) -> np.ndarray:
+    """float -> the float32 value of its BF16 rounding (what NumpyQwen reads from the file)."""
+    return (bf16_bits(np.asarray(x, np.float32)).astype(np.uint32) << 16).view(np.float32)
+
+
+def write_checkpoint(path: Path, rng: np.random.Generator) -> None:
+    tensors = checkpoint_tensors(rng)
     header, blobs, offset = {}, [], 0
     for name, value in tensors.items():
         raw = bf16_bits(np.asarray(value, np.float32)).tobytes()
@@ -240,8 +252,36 @@ def projections() -> None:
     print(f"wrote {out} ({out.stat().st_size} bytes)")
 
 
+ENGINE_SEED = 20261203
+ENGINE_TOKENS = 13
+
+
+def engine() -> None:
+    """Engine fixture (numpyqwen_engine.npz): NumpyQwen with FP16 matrices and FP16 KV (the
+    engine's precision, weight_precision='f16', kv_precision='f16') on a third synthetic
+    checkpoint (seed ENGINE_SEED, regenerated by the test from checkpoint_tensors), fed
+    ENGINE_TOKENS token ids one at a time; records the logits after every token. A host engine
+    that prefills, decodes, verifies and rewinds over the same ids must reproduce the logits of
+    each prefix."""
+    sys.path.insert(0, str(reference_dir()))
+    from tests.test_full_model import NumpyQwen  # the reference's oracle, unchanged
+
+    rng = np.random.default_rng(ENGINE_SEED)
+    with tempfile.TemporaryDirectory() as tmp:
+        model = Path(tmp)
+        write_checkpoint(model / "model.safetensors", rng)
+        oracle = NumpyQwen(model, weight_precision="f16", kv_precision="f16")
+    ids = rng.integers(0, V, ENGINE_TOKENS)
+    logits = np.stack([np.asarray(oracle.token(int(t)), np.float32) for t in ids])
+    out = HERE / "numpyqwen_engine.npz"
+    np.savez_compressed(out, ids=ids.astype(np.int32), logits=logits)
+    print(f"wrote {out} ({out.stat().st_size} bytes)")
+
+
 if __name__ == "__main__":
-    if "--projections" in sys.argv:
+    if "--engine" in sys.argv:
+        engine()
+    elif "--projections" in sys.argv:
         projections()
     elif "--tokens" in sys.argv:
         main(int(sys.argv[sys.argv.index("--tokens") + 1]))
