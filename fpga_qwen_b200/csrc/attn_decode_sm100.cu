@@ -47,7 +47,8 @@ namespace {
 
 using namespace sm100;
 
-constexpr int THREADS = 128;
+constexpr int THREADS = 128;                  // four warps (the merge's reductions read red[][0..3])
+static_assert(THREADS == 128, "block reductions are written for four warps");
 constexpr int HALF_WARPS = THREADS / 16;
 constexpr int CH = 64;                        // keys per chunk
 constexpr int NST = 4;                        // ring stages
@@ -516,28 +517,64 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             if (tid == 0) is_last = (atomicAdd(&a.counters[unit], 1) == nrec - 1);
             __syncthreads();
             if (is_last) {
+                // Merge the unit's nrec records. The record loads are spread over the threads
+                // (max, then weights) and the per-output sums keep eight loads in flight, so the
+                // merge costs a few L2 round trips rather than one per record; a unit split over
+                // many CTAs (one layer per call) depends on that.
                 __threadfence();
                 const float* recs = a.partial + (size_t)unit * a.max_records * PARTIAL_FLOATS;
-                float mall[GROUP], lall[GROUP];
-                #pragma unroll
-                for (int gq = 0; gq < GROUP; ++gq) {
-                    float m = -INFINITY;
-                    for (int s = 0; s < nrec; ++s) m = fmaxf(m, __ldcg(recs + (size_t)s * PARTIAL_FLOATS + gq));
-                    mall[gq] = m;
-                    float lv = 0.f;
-                    for (int s = 0; s < nrec; ++s)
-                        lv += exp2f(__ldcg(recs + (size_t)s * PARTIAL_FLOATS + gq) - m) *
-                              __ldcg(recs + (size_t)s * PARTIAL_FLOATS + GROUP + gq);
-                    lall[gq] = lv;
+                // [GROUP][nrec] record weights in accbuf (free now): nrec <= max_records <= ctas + 2
+                // = 298 < 1024, the most accbuf's 2048 floats hold
+                float* wts = &accbuf[0][0][0];
+                float m0 = -INFINITY, m1 = -INFINITY;
+                for (int s = tid; s < nrec; s += THREADS) {
+                    m0 = fmaxf(m0, __ldcg(recs + (size_t)s * PARTIAL_FLOATS));
+                    m1 = fmaxf(m1, __ldcg(recs + (size_t)s * PARTIAL_FLOATS + 1));
                 }
+                #pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) {
+                    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+                    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+                }
+                if (lane == 0) { red[0][warp] = m0; red[1][warp] = m1; }
+                __syncthreads();
+                m0 = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+                m1 = fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3]));
+                float l0 = 0.f, l1 = 0.f;
+                for (int s = tid; s < nrec; s += THREADS) {
+                    const float* rs = recs + (size_t)s * PARTIAL_FLOATS;
+                    const float w0 = exp2f(__ldcg(rs) - m0), w1 = exp2f(__ldcg(rs + 1) - m1);
+                    wts[s] = w0;
+                    wts[nrec + s] = w1;
+                    l0 += w0 * __ldcg(rs + GROUP);
+                    l1 += w1 * __ldcg(rs + GROUP + 1);
+                }
+                #pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) {
+                    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+                    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+                }
+                __syncthreads();                       // red reuse; wts visible
+                if (lane == 0) { red[0][warp] = l0; red[1][warp] = l1; }
+                __syncthreads();
+                const float lall0 = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
+                const float lall1 = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
                 #pragma unroll
                 for (int i = 0; i < GROUP * D / THREADS; ++i) {
                     const int idx = tid + i * THREADS, gq = idx / D, jc = idx % D;
+                    const float* wq = wts + gq * nrec;
+                    const float* col = recs + 4 + idx;
                     float v = 0.f;
-                    for (int s = 0; s < nrec; ++s)
-                        v += exp2f(__ldcg(recs + (size_t)s * PARTIAL_FLOATS + gq) - mall[gq]) *
-                             __ldcg(recs + (size_t)s * PARTIAL_FLOATS + 4 + idx);
-                    store_out(u, gq, jc, v / lall[gq]);
+                    int s = 0;
+                    for (; s + 8 <= nrec; s += 8) {
+                        float x[8];
+                        #pragma unroll
+                        for (int e = 0; e < 8; ++e) x[e] = __ldcg(col + (size_t)(s + e) * PARTIAL_FLOATS);
+                        #pragma unroll
+                        for (int e = 0; e < 8; ++e) v += wq[s + e] * x[e];
+                    }
+                    for (; s < nrec; ++s) v += wq[s] * __ldcg(col + (size_t)s * PARTIAL_FLOATS);
+                    store_out(u, gq, jc, v / (gq ? lall1 : lall0));
                 }
                 if (tid == 0) a.counters[unit] = 0;    // ready for the next call on this stream
             }
