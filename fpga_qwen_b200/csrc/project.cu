@@ -8,17 +8,19 @@
 // The reference's dot keeps two 4-lane FP32 accumulators, a over channels j..j+3 and b over
 // j+4..j+7, fused multiply-adds with j ascending by 8, then vaddvq(a + b), whose pairwise
 // reduction is (s0 + s1) + (s2 + s3) with s_i = a_i + b_i. Every variant above keeps that
-// sequence per output, so one kernel reproduces all of them bit for bit: eight threads own
-// one output row, thread c the lane chain of channels c, c+8, c+16, ... (chain c < 4 is a_c,
-// chain c >= 4 is b_{c-4}); after the last column the eight chains combine with three
-// shuffles in the reference's order.
+// sequence per output, so one kernel reproduces all of them bit for bit: two threads own one
+// output row, thread 0 the four chains of a (channels j..j+3), thread 1 the four of b
+// (channels j+4..j+7), each step one 8-byte load of four FP16 weights and two packed FP32x2
+// fused multiply-adds (each lane rounded once, as vfmaq_f32); one shuffle then forms
+// s_i = a_i + b_i and each row's (s0 + s1) + (s2 + s3).
 //
-// The work is HBM-bound (2 bytes of matrix per multiply-add): a CTA of 128 threads owns 16
-// rows and streams their columns through a 4-stage cp.async ring of 256-column chunks
-// (16-byte copies, whole 512-byte row segments per warp, padded shared-memory rows so the
-// eight chains of four rows read without bank conflicts). The input row is read through the
-// read-only cache into registers a chunk at a time. Several matrices that share one input
-// (the reference's project_group) run as one launch over their concatenated row tiles.
+// The work is HBM-bound (2 bytes of matrix per multiply-add). The kernel is persistent (one
+// wave of CTAs): a CTA owns row tiles in turn and streams their columns through a cp.async
+// ring of 128-column chunks that runs on from one tile to the next (16-byte copies with
+// shift-only indexing; shared-memory rows padded by 16 bytes so a warp's 16 rows read without
+// bank conflicts); each stage also carries the chunk's input columns, so the multiply-add
+// chains read only shared memory. Several matrices that share one input (the reference's
+// project_group) run as one launch over their concatenated row tiles.
 #include <algorithm>
 
 #include "qattn_common.cuh"
@@ -26,14 +28,36 @@
 namespace qattn {
 namespace {
 
-constexpr int PR_ROWS = 16;                       // rows per CTA
-constexpr int PR_THREADS = PR_ROWS * 8;           // eight lane chains per row
-constexpr int PR_CHUNK = 256;                     // columns per ring stage
-constexpr int PR_STAGES = 4;
+constexpr int PR_CHUNK = 128;                     // columns per ring stage
 constexpr int PR_ROW_BYTES = PR_CHUNK * 2 + 16;   // padded: row r starts 4 banks after row r-1
-constexpr int PR_STAGE_BYTES = PR_ROWS * PR_ROW_BYTES;
-constexpr int PR_SMEM = PR_STAGES * PR_STAGE_BYTES;
-constexpr int PR_BATCH = 2;                       // batch rows per pass over the matrix
+constexpr int PR_BATCH = 2;                       // batch rows per pass over a tile
+constexpr int PR_PIECES = PR_CHUNK * 2 / 16;      // 16-byte pieces per row segment of a full chunk
+static_assert(PR_PIECES == 16, "shift-only copy indexing assumes 16 pieces per row segment");
+// Tiles of ROWS rows, two threads per row. Large matrices (the vocabulary head) use 64-row
+// tiles and a 4-stage ring; a launch with fewer 64-row tiles than half a wave uses 16-row tiles,
+// four times as many CTAs, and an 8-stage ring that holds a whole 1024-column tile in flight,
+// so that small per-layer matrices still spread over the GPU and wait for memory only once.
+template <int ROWS> struct Shape {
+    static constexpr int THREADS = 2 * ROWS;
+    static constexpr int STAGES = ROWS >= 64 ? 4 : 8;
+    static constexpr int W_BYTES = ROWS * PR_ROW_BYTES;
+    static constexpr int STAGE_BYTES = W_BYTES + PR_BATCH * PR_CHUNK * 4;   // + the input columns of the chunk
+    static constexpr int SMEM = STAGES * STAGE_BYTES;
+};
+
+// Position in a CTA's chunk sequence: column chunk k of pass `pass` (a pair of batch rows) of the
+// CTA's tile number `it`, advanced without divisions.
+struct Cursor {
+    int k = 0, pass = 0, it = 0;
+    __device__ __forceinline__ bool next(int nch, int passes) {     // true when a new tile starts
+        if (++k < nch) return false;
+        k = 0;
+        if (++pass < passes) return false;
+        pass = 0;
+        ++it;
+        return true;
+    }
+};
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
@@ -43,78 +67,160 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__global__ void __launch_bounds__(PR_THREADS) project_kernel(const ProjectArgs a) {
-    extern __shared__ __align__(16) uint8_t ring[];
-    // this CTA's matrix and first row
-    int m = 0;
-    while (m + 1 < a.n_mats && (int)blockIdx.x >= a.tile0[m + 1]) ++m;
-    const int r0 = ((int)blockIdx.x - a.tile0[m]) * PR_ROWS;
-    const int rows_here = min(PR_ROWS, a.rows[m] - r0);
-    const __half* W = a.w[m] + (size_t)r0 * a.cols;
-    const int tid = threadIdx.x, r = tid >> 3, c = tid & 7;
-    const int nch = (a.cols + PR_CHUNK - 1) / PR_CHUNK;
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long r, ua = *reinterpret_cast<unsigned long long*>(&a), ub = *reinterpret_cast<unsigned long long*>(&b),
+                          uc = *reinterpret_cast<unsigned long long*>(&c);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(ua), "l"(ub), "l"(uc));
+    return *reinterpret_cast<float2*>(&r);
+}
 
-    // chunk k of the CTA's rows into ring stage k % PR_STAGES: each row segment is
-    // (cols of the chunk) x 2 bytes, copied 16 bytes per thread-step
-    auto load = [&](int k) {
-        if (k < nch) {
+struct Tile { int m, r0, rows; const __half* w; };
+template <int ROWS>
+__device__ __forceinline__ Tile tile_at(const ProjectArgs& a, int t) {
+    Tile ti;
+    ti.m = 0;
+    while (ti.m + 1 < a.n_mats && t >= a.tile0[ti.m + 1]) ++ti.m;
+    ti.r0 = (t - a.tile0[ti.m]) * ROWS;
+    ti.rows = min(ROWS, a.rows[ti.m] - ti.r0);
+    ti.w = a.w[ti.m] + (size_t)ti.r0 * a.cols;
+    return ti;
+}
+
+// Persistent: CTA c takes tiles c, c + grid, c + 2*grid, ...; every tile is `passes` passes
+// (pairs of batch rows) of `nch` column chunks. The CTA's chunks form one sequence that the
+// ring streams without draining between tiles, so HBM sees a continuous read per CTA.
+template <int ROWS>
+__global__ void __launch_bounds__(Shape<ROWS>::THREADS) project_kernel(const ProjectArgs a) {
+    using S = Shape<ROWS>;
+    extern __shared__ __align__(16) uint8_t ring[];
+    const int tid = threadIdx.x, r = tid >> 1, hl = tid & 1;     // row of the tile, a (0) or b (1) lanes
+    const int ntiles = a.tile0[a.n_mats];
+    const int nch = (a.cols + PR_CHUNK - 1) / PR_CHUNK;
+    const int passes = (a.batch + PR_BATCH - 1) / PR_BATCH;
+    const int my_tiles = ((int)blockIdx.x < ntiles) ? (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    const int per_tile = passes * nch;
+    const int total = my_tiles * per_tile;
+
+    // chunk g of the sequence into ring stage g % STAGES: the tile's row segments and the
+    // pass's input columns (16-byte copies), so the multiply-add chains read only shared memory.
+    // The producer cursor runs STAGES - 1 chunks ahead of the consumers'.
+    Cursor pc;
+    Tile pt = tile_at<ROWS>(a, blockIdx.x);
+    int g_load = 0;
+    auto load = [&]() {
+        if (g_load < total) {
+            const int k = pc.k, b0 = pc.pass * PR_BATCH;
             const int cw = min(PR_CHUNK, a.cols - k * PR_CHUNK);     // columns in this chunk (multiple of 8)
-            const int per_row = cw / 8;                              // 16-byte pieces per row
-            uint8_t* st = ring + (k % PR_STAGES) * PR_STAGE_BYTES;
-            for (int i = tid; i < rows_here * per_row; i += PR_THREADS) {
-                const int rr = i / per_row, p = i - rr * per_row;
-                cp_async16(st + rr * PR_ROW_BYTES + p * 16, W + (size_t)rr * a.cols + (size_t)k * PR_CHUNK + p * 8);
+            uint8_t* st = ring + (g_load % S::STAGES) * S::STAGE_BYTES;
+            const __half* src = pt.w + (size_t)k * PR_CHUNK;
+            if (cw == PR_CHUNK) {
+                #pragma unroll
+                for (int i = 0; i < ROWS * PR_PIECES / S::THREADS; ++i) {   // 8 pieces per thread
+                    const int piece = tid + i * S::THREADS, rr = piece >> 4, p = piece & 15;
+                    if (rr < pt.rows) cp_async16(st + rr * PR_ROW_BYTES + p * 16, src + (size_t)rr * a.cols + p * 8);
+                }
+            } else {
+                const int per_row = cw / 8;                          // the ragged last chunk of a row
+                for (int i = tid; i < pt.rows * per_row; i += S::THREADS) {
+                    const int rr = i / per_row, p = i - rr * per_row;
+                    cp_async16(st + rr * PR_ROW_BYTES + p * 16, src + (size_t)rr * a.cols + p * 8);
+                }
             }
+            const int xq = cw / 4;                                   // 16-byte pieces per input row
+            const int nb = min(PR_BATCH, a.batch - b0);
+            for (int i = tid; i < nb * PR_CHUNK / 4; i += S::THREADS) {
+                const int bb = i >> 5, p = i & 31;                   // PR_CHUNK / 4 == 32 pieces per row
+                if (p < xq)
+                    cp_async16(st + S::W_BYTES + bb * PR_CHUNK * 4 + p * 16,
+                               a.x + (size_t)(b0 + bb) * a.cols + (size_t)k * PR_CHUNK + p * 4);
+            }
+            ++g_load;
+            if (pc.next(nch, passes) && g_load < total)
+                pt = tile_at<ROWS>(a, (int)blockIdx.x + pc.it * (int)gridDim.x);
         }
         cp_commit();
     };
 
-    for (int b0 = 0; b0 < a.batch; b0 += PR_BATCH) {
-        const int nb = min(PR_BATCH, a.batch - b0);
-        float acc[PR_BATCH] = {0.f, 0.f};
-        if (b0 > 0) __syncthreads();                         // the previous pass has read the ring
-        #pragma unroll
-        for (int s = 0; s < PR_STAGES - 1; ++s) load(s);
-        for (int k = 0; k < nch; ++k) {
-            cp_wait<PR_STAGES - 2>();                        // chunk k has landed (this thread's copies)
-            __syncthreads();                                 // ... everyone's; chunk k-1 fully read
-            load(k + PR_STAGES - 1);                         // into the stage chunk k-1 used
-            const int cw = min(PR_CHUNK, a.cols - k * PR_CHUNK);
-            const uint8_t* row = ring + (k % PR_STAGES) * PR_STAGE_BYTES + r * PR_ROW_BYTES + c * 2;
-            const float* xb = a.x + (size_t)b0 * a.cols + (size_t)k * PR_CHUNK + c;
+    #pragma unroll
+    for (int s = 0; s < S::STAGES - 1; ++s) load();
+    float2 acc[PR_BATCH][2];                         // this thread's four lane chains (two pairs) per batch row
+    #pragma unroll
+    for (int bb = 0; bb < PR_BATCH; ++bb) acc[bb][0] = acc[bb][1] = make_float2(0.f, 0.f);
+    Cursor cc;
+    Tile ti = tile_at<ROWS>(a, blockIdx.x);
+    for (int g = 0; g < total; ++g) {
+        cp_wait<S::STAGES - 2>();                        // chunk g has landed (this thread's copies)
+        __syncthreads();                                 // ... everyone's; chunk g-1 fully read
+        load();                                          // chunk g + STAGES - 1, into the stage chunk g-1 used
+        const int k = cc.k, b0 = cc.pass * PR_BATCH, nb = min(PR_BATCH, a.batch - b0);
+        const int cw = min(PR_CHUNK, a.cols - k * PR_CHUNK);
+        const uint8_t* st = ring + (g % S::STAGES) * S::STAGE_BYTES;
+        const uint8_t* row = st + r * PR_ROW_BYTES + hl * 8;
+        const float* xs = reinterpret_cast<const float*>(st + S::W_BYTES) + hl * 4;
+        #pragma unroll 4
+        for (int jj = 0; jj < cw / 8; ++jj) {
+            const uint2 wv = *reinterpret_cast<const uint2*>(row + jj * 16);      // 4 FP16 weights
+            const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+            const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+            const float4 x0 = *reinterpret_cast<const float4*>(xs + jj * 8);
+            acc[0][0] = ffma2(make_float2(x0.x, x0.y), w01, acc[0][0]);
+            acc[0][1] = ffma2(make_float2(x0.z, x0.w), w23, acc[0][1]);
             if (nb == PR_BATCH) {
-                #pragma unroll 8
-                for (int jj = 0; jj < cw / 8; ++jj) {
-                    const float wv = __half2float(*reinterpret_cast<const __half*>(row + jj * 16));
-                    acc[0] = fmaf(__ldg(xb + jj * 8), wv, acc[0]);
-                    acc[1] = fmaf(__ldg(xb + a.cols + jj * 8), wv, acc[1]);
-                }
-            } else {
-                #pragma unroll 8
-                for (int jj = 0; jj < cw / 8; ++jj) {
-                    const float wv = __half2float(*reinterpret_cast<const __half*>(row + jj * 16));
-                    acc[0] = fmaf(__ldg(xb + jj * 8), wv, acc[0]);
-                }
+                const float4 x1 = *reinterpret_cast<const float4*>(xs + PR_CHUNK + jj * 8);
+                acc[1][0] = ffma2(make_float2(x1.x, x1.y), w01, acc[1][0]);
+                acc[1][1] = ffma2(make_float2(x1.z, x1.w), w23, acc[1][1]);
             }
         }
-        cp_wait<0>();
-        // (s0 + s1) + (s2 + s3), s_i = a_i + b_i: chain c and chain c + 4, then pairs
-        #pragma unroll
-        for (int bb = 0; bb < PR_BATCH; ++bb) {
-            const float s = acc[bb] + __shfl_xor_sync(0xffffffffu, acc[bb], 4);
-            const float t = s + __shfl_xor_sync(0xffffffffu, s, 1);
-            const float y = t + __shfl_xor_sync(0xffffffffu, t, 2);
-            if (bb < nb && c == 0 && r < rows_here) a.y[m][(size_t)(b0 + bb) * a.rows[m] + r0 + r] = y;
+        if (k == nch - 1) {
+            // s_i = a_i + b_i (the partner thread holds b), then (s0 + s1) + (s2 + s3)
+            #pragma unroll
+            for (int bb = 0; bb < PR_BATCH; ++bb) {
+                float2 o0, o1;
+                o0.x = __shfl_xor_sync(0xffffffffu, acc[bb][0].x, 1); o0.y = __shfl_xor_sync(0xffffffffu, acc[bb][0].y, 1);
+                o1.x = __shfl_xor_sync(0xffffffffu, acc[bb][1].x, 1); o1.y = __shfl_xor_sync(0xffffffffu, acc[bb][1].y, 1);
+                const float s0 = acc[bb][0].x + o0.x, s1 = acc[bb][0].y + o0.y;
+                const float s2 = acc[bb][1].x + o1.x, s3 = acc[bb][1].y + o1.y;
+                const float y = (s0 + s1) + (s2 + s3);
+                if (bb < nb && hl == 0 && r < ti.rows) a.y[ti.m][(size_t)(b0 + bb) * a.rows[ti.m] + ti.r0 + r] = y;
+                acc[bb][0] = acc[bb][1] = make_float2(0.f, 0.f);
+            }
         }
+        if (cc.next(nch, passes) && g + 1 < total) ti = tile_at<ROWS>(a, (int)blockIdx.x + cc.it * (int)gridDim.x);
     }
+    cp_wait<0>();
+}
+
+template <int ROWS>
+int resident_ctas() {
+    // one wave of persistent CTAs: as many as fit on every SM at once
+    static int resident = 0;
+    if (!resident) {
+        int dev = 0, sms = NUM_SMS_B200, per_sm = 1;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaFuncSetAttribute(project_kernel<ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape<ROWS>::SMEM);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, project_kernel<ROWS>, Shape<ROWS>::THREADS,
+                                                          Shape<ROWS>::SMEM) != cudaSuccess || per_sm < 1)
+            per_sm = 1;
+        resident = sms * per_sm;
+    }
+    return resident;
+}
+
+template <int ROWS>
+void launch_rows(ProjectArgs a, cudaStream_t s) {
+    a.tile0[0] = 0;
+    for (int m = 0; m < a.n_mats; ++m) a.tile0[m + 1] = a.tile0[m] + (a.rows[m] + ROWS - 1) / ROWS;
+    const int grid = std::min(a.tile0[a.n_mats], resident_ctas<ROWS>());
+    project_kernel<ROWS><<<grid, Shape<ROWS>::THREADS, Shape<ROWS>::SMEM, s>>>(a);
 }
 
 }  // namespace
 
 void launch_project(ProjectArgs a, cudaStream_t s) {
-    a.tile0[0] = 0;
-    for (int m = 0; m < a.n_mats; ++m) a.tile0[m + 1] = a.tile0[m] + (a.rows[m] + PR_ROWS - 1) / PR_ROWS;
-    project_kernel<<<a.tile0[a.n_mats], PR_THREADS, PR_SMEM, s>>>(a);
+    int tiles64 = 0;
+    for (int m = 0; m < a.n_mats; ++m) tiles64 += (a.rows[m] + 63) / 64;
+    if (2 * tiles64 >= resident_ctas<64>()) launch_rows<64>(a, s);
+    else launch_rows<16>(a, s);
 }
 
 }  // namespace qattn

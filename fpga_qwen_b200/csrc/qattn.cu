@@ -934,6 +934,8 @@ int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const in
     if (cols < 8 || cols % 8) return fail(ctx, QA_ERR_INVALID, "columns %d: a positive multiple of 8", cols);
     if (batch < 1 || batch > QA_MAX_BATCH) return fail(ctx, QA_ERR_INVALID, "batch %d outside 1..%d", batch, QA_MAX_BATCH);
     if (!x) return fail(ctx, QA_ERR_INVALID, "null input");
+    if (!ctx->cfg.io_host && (reinterpret_cast<uintptr_t>(x) & 15))
+        return fail(ctx, QA_ERR_INVALID, "input rows must be 16-byte aligned");
     size_t out_floats = 0;
     ProjectArgs a{};
     a.n_mats = n_mats; a.cols = cols; a.batch = batch;

@@ -211,8 +211,8 @@ int qa_kv_pointer(qa_ctx* ctx, int seq, int layer, int kv, int head, void** ptr)
 int qa_kv_slot_bytes(const qa_ctx* ctx, size_t* bytes);
 
 /* ---- Projections over FP16 matrices (the engine's GEMVs around attention) ------------------
- * y[b][r] = dot(x[b], W[r]) for an FP16 matrix W [rows][cols] (cols a multiple of 8, W 16-byte
- * aligned, DEVICE memory in every context: weights stay resident), FP32 x [batch][cols] and
+ * y[b][r] = dot(x[b], W[r]) for an FP16 matrix W [rows][cols] (cols a multiple of 8, W and a
+ * device x 16-byte aligned, W DEVICE memory in every context: weights stay resident), FP32 x [batch][cols] and
  * y [batch][rows] (device pointers, or host pointers in io_host contexts), 1 <= batch <=
  * QA_MAX_BATCH. Every output follows the reference's eight-lane dot bit for bit: two 4-lane
  * FP32 accumulators over channels j..j+3 and j+4..j+7, fused multiply-adds with j ascending by
