@@ -54,6 +54,7 @@ constexpr int CH = 64;                        // keys per chunk
 constexpr int NST = 4;                        // ring stages
 constexpr uint32_t CHUNK_BYTES = CH * D * 2;  // 16 KB
 constexpr int MAX_UNIT_KEYS = 4096;           // longest unit (QA_MAX_CONTEXT): a segment's scores fit in 2 x 16 KB
+constexpr int FAST_MERGE = 4;                 // units split over at most this many CTAs merge in one load round
 
 struct DecodeArgs {
     const float* q; float* out;               // [n_layers][n][hq][128]
@@ -209,9 +210,10 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             for (int k = 0; k < i; ++k) next_unit(a, w);
             return w;
         };
-        // Inputs of unit i, staged in the last ring stage (primed only after this prologue):
+        // Inputs of unit i, staged in the score buffer (free until the first K chunk is scored,
+        // so every ring stage streams K/V meanwhile; the launch sizes it for the staging):
         // [q0 | q1 | k | v | cos | sin | q_norm | k_norm] = 896 floats at i * 1024.
-        float* stg = reinterpret_cast<float*>(ring + (NST - 1) * CHUNK_BYTES);
+        float* stg = scores;
         // tables (RoPE rows, norm weights: constant during a step) or the step's inputs
         auto stage_inputs = [&](bool tables) {
             for (int i = 0; i < QB; ++i) {
@@ -242,7 +244,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             // writing, then wait for its grid (and its memory) before touching this step's
             // inputs, records and rows, and let the next step launch.
             if (tid == 0)
-                for (int i = 0; i < NST - 1 && g_begin < g_end; ++i)
+                for (int i = 0; i < NST && g_begin < g_end; ++i)
                     if (!produce(true)) break;
             asm volatile("griddepcontrol.wait;" ::: "memory");
         }
@@ -251,7 +253,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         stage_inputs(false);
         if (tid == 0)                                  // K/V stream behind the small input copies
-            while ((int)issued < NST - 1 && produce(false)) {}
+            while ((int)issued < NST && produce(false)) {}
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();
         if (tid < 3 * QB) {                            // one lane per sequential FP64 chain
@@ -292,11 +294,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
                 }
             }
         }
-        __syncthreads();
-        if (tid == 0) {                                // the staging stage joins the copy ring
-            fence_proxy_async_smem();
-            produce(false);
-        }
+        __syncthreads();                               // the staging is read: the score buffer is free
         if (tid < QB * 32) {                          // store the new K and V rows, 16 B per lane
             const int i = tid >> 5, kv = (tid >> 4) & 1, c16 = tid & 15;
             const Unit w = unit_at(i);
@@ -516,7 +514,51 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
             __syncthreads();
             if (tid == 0) is_last = (atomicAdd(&a.counters[unit], 1) == nrec - 1);
             __syncthreads();
-            if (is_last) {
+            if (is_last && nrec <= FAST_MERGE) {
+                // Few records (a 28-layer step splits a unit over about 1.3 CTAs): every other
+                // record's statistics and this thread's two output columns are loaded at once, one
+                // L2 round trip; this CTA's own record is still in registers. The sum runs in
+                // record order, so the result does not depend on which CTA arrives last.
+                __threadfence();
+                const float* recs = a.partial + (size_t)unit * a.max_records * PARTIAL_FLOATS;
+                const int own = c - c_first;
+                float4 st4[FAST_MERGE];
+                float av[FAST_MERGE][GROUP * D / THREADS];
+                #pragma unroll
+                for (int sr = 0; sr < FAST_MERGE; ++sr) {
+                    if (sr < nrec && sr != own) {
+                        const float* rs = recs + (size_t)sr * PARTIAL_FLOATS;
+                        st4[sr] = __ldcg(reinterpret_cast<const float4*>(rs));
+                        #pragma unroll
+                        for (int i = 0; i < GROUP * D / THREADS; ++i) av[sr][i] = __ldcg(rs + 4 + tid + i * THREADS);
+                    } else {
+                        st4[sr] = make_float4(stat[0], stat[1], stat[GROUP], stat[GROUP + 1]);
+                        #pragma unroll
+                        for (int i = 0; i < GROUP * D / THREADS; ++i) av[sr][i] = o[i];
+                    }
+                }
+                float mm[GROUP] = {-INFINITY, -INFINITY};
+                #pragma unroll
+                for (int sr = 0; sr < FAST_MERGE; ++sr)
+                    if (sr < nrec) { mm[0] = fmaxf(mm[0], st4[sr].x); mm[1] = fmaxf(mm[1], st4[sr].y); }
+                float ll[GROUP] = {0.f, 0.f}, wt[FAST_MERGE][GROUP];
+                #pragma unroll
+                for (int sr = 0; sr < FAST_MERGE; ++sr) {
+                    wt[sr][0] = sr < nrec ? exp2f(st4[sr].x - mm[0]) : 0.f;
+                    wt[sr][1] = sr < nrec ? exp2f(st4[sr].y - mm[1]) : 0.f;
+                    if (sr < nrec) { ll[0] += wt[sr][0] * st4[sr].z; ll[1] += wt[sr][1] * st4[sr].w; }
+                }
+                #pragma unroll
+                for (int i = 0; i < GROUP * D / THREADS; ++i) {
+                    const int idx = tid + i * THREADS, gq = idx / D, jc = idx % D;
+                    float v = 0.f;
+                    #pragma unroll
+                    for (int sr = 0; sr < FAST_MERGE; ++sr)
+                        if (sr < nrec) v += wt[sr][gq] * av[sr][i];
+                    store_out(u, gq, jc, v / ll[gq]);
+                }
+                if (tid == 0) a.counters[unit] = 0;    // ready for the next call on this stream
+            } else if (is_last) {
                 // Merge the unit's nrec records. The record loads are spread over the threads
                 // (max, then weights) and the per-output sums keep eight loads in flight, so the
                 // merge costs a few L2 round trips rather than one per record; a unit split over
@@ -653,7 +695,10 @@ void launch_attn_decode_sm100(const DecodePlan& plan, const KVLayout& kv, const 
     a.total_keys = plan.total_keys; a.ctas = plan.ctas; a.max_keys = plan.max_keys;
     a.max_records = plan.max_records;
     a.partial = partial; a.counters = counters; a.error = error;
-    const size_t smem = (size_t)NST * CHUNK_BYTES + (size_t)GROUP * a.max_keys * sizeof(float);
+    // ring + score buffer; a fused step stages its inputs (1024 floats per unit) in the score buffer
+    const size_t score_bytes = std::max((size_t)GROUP * a.max_keys * sizeof(float),
+                                        step ? (size_t)FUSED_MAX_UNITS * 1024 * sizeof(float) : (size_t)0);
+    const size_t smem = (size_t)NST * CHUNK_BYTES + score_bytes;
     static bool attr = false;
     if (!attr) {
         const int max_smem = NST * CHUNK_BYTES + GROUP * MAX_UNIT_KEYS * (int)sizeof(float);
