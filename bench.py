@@ -644,7 +644,8 @@ def projection_bench(args):
     not available): per token, for each of the 28 layers q/k/v as one launch (qa_project_group),
     o_proj, gate/up as one launch and down_proj, then the tied vocabulary head over the
     151,936 x 1,024 embedding matrix, all at batch 1 and bit-exact with the reference's eight-lane
-    dot. Reports the weight bytes read per token over the device time (CUDA events), the
+    dot. Reports the weight bytes read per token over the device time of a CUDA-graph replay of
+    the token's launches (CUDA events), the same launches issued eagerly from Python, the
     vocabulary head alone (its largest launch) against the measured HBM bandwidth, and the
     launches per token."""
     import torch
@@ -680,10 +681,26 @@ def projection_bench(args):
     for _ in range(max(3, args.warmup)):
         token()
     torch.cuda.synchronize()
+    # eager: every launch issued from Python (the host, not the GPU, sets the pace)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(tokens):
         token()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    eager_ms = e0.elapsed_time(e1) / tokens
+    # one token's 113 launches captured in a CUDA graph and replayed: the device-side time
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        token()
+    ctx.set_stream(stream.cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(tokens):
+        graph.replay()
     e1.record(stream)
     v0, v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     v0.record(stream)
@@ -692,6 +709,7 @@ def projection_bench(args):
     v1.record(stream)
     torch.cuda.synchronize()
     ctx.sync()
+    del graph
     ctx.close()
     layer_bytes = 2 * H * (QD + 2 * KD) + 2 * QD * H + 2 * 2 * F * H + 2 * F * H
     token_bytes = L * layer_bytes + 2 * VOCAB * H
@@ -702,6 +720,8 @@ def projection_bench(args):
     return {"metric": "decode projections GB/s (weight bytes per token / device time)",
             "value": round(token_bytes / (tok_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "us_per_token": round(tok_ms * 1e3, 1), "bytes_per_token": token_bytes, "launches_per_token": 4 * L + 1,
+            "timing": "one token's launches replayed from a CUDA graph (CUDA events, 16 tokens)",
+            "eager_us_per_token": round(eager_ms * 1e3, 1),
             "roofline": {"bound": "hbm", "kernel": "project_kernel, vocabulary head (151936 x 1024 FP16)",
                          "achieved": round(vocab_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(vocab_gbs / hbm_peak, 4), "kernel_us": round(vocab_us, 2),
