@@ -923,11 +923,27 @@ def run_profile_case(args):
       prefill  4 layers, 3968-row prefill (append + attention) repeated 3 times
       append   28 layers x 1024-row append repeated 3 times
       decode_batch  8 sequences with the first 8 config-5 prompt lengths, then 3 batched fused
-               decode steps (each launch reads ~1.8 GB of KV)"""
+               decode steps (each launch reads ~1.8 GB of KV)
+      project  the vocabulary-head projection (151,936 x 1,024 FP16), 3 launches"""
     import torch
     from fpga_qwen_b200 import qattn
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
+    if args.profile_case == "project":
+        # the tied vocabulary head at batch 1, three launches (311 MB of FP16 matrix each)
+        g = torch.Generator(device=dev).manual_seed(1)
+        ctx = qattn.Context(n_layers=1, context=256)
+        ctx.set_stream(stream.cuda_stream)
+        w = (torch.randn((151936, 1024), device=dev, generator=g) * 0.03).half()
+        x = torch.randn((1, 1024), device=dev, generator=g)
+        y = torch.empty((1, 151936), device=dev)
+        for _ in range(3):
+            ctx.project(w.data_ptr(), 151936, 1024, x.data_ptr(), 1, y.data_ptr())
+        torch.cuda.synchronize()
+        ctx.sync()
+        ctx.close()
+        print(json.dumps({"profile_case": args.profile_case, "ok": True}))
+        return 0
     layers = 4 if args.profile_case == "prefill" else L
     nseq = 8 if args.profile_case == "decode_batch" else 1
     ctx = qattn.Context(n_layers=layers, context=4096, max_seqs=nseq)
@@ -1010,7 +1026,7 @@ def main():
                          "stores inside them")
     ap.add_argument("--split-decode", action="store_true",
                     help="decode with qa_append + qa_attn_decode (two launches) instead of the fused qa_decode_step")
-    ap.add_argument("--profile-case", choices=["decode", "prefill", "append", "decode_batch"], default=None,
+    ap.add_argument("--profile-case", choices=["decode", "prefill", "append", "decode_batch", "project"], default=None,
                     help="run a small single-kernel case for ncu instead of the benchmark")
     args = ap.parse_args()
     if args.profile_case:
