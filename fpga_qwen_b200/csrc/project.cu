@@ -190,6 +190,117 @@ __global__ void __launch_bounds__(Shape<ROWS>::THREADS) project_kernel(const Pro
     cp_wait<0>();
 }
 
+// ---- small launches: every row of the launch resident in shared memory at once ----------------
+// The per-layer matrices of one decode token (1,024 to 6,144 rows) are too small to keep a ring
+// busy: the persistent kernel's few CTAs would wait for memory once per chunk. Here each of
+// about one CTA per SM takes a slice of R consecutive rows (of the launch's concatenated
+// matrices), issues copies of the whole slice at once in four column groups and runs the
+// multiply-add chains over each group as it lands, so the launch costs about one memory latency
+// plus its bytes at full bandwidth. The chains, their order and the final reduction are the
+// persistent kernel's, so both give the same bits. Launched as a programmatic dependent: the
+// weight copies (constant data) start while the previous kernel finishes; the input is read
+// only after griddepcontrol.wait.
+constexpr int PS_THREADS = 256;
+constexpr int PS_GROUPS = 4;                       // column groups, one cp.async group each
+constexpr int PS_MAX_ROWS = PS_THREADS / 2;        // two threads per row
+constexpr int PS_MAX_SMEM = 200 * 1024;
+
+__device__ __forceinline__ int ps_stride(int cols) { return cols * 2 + 16; }   // padded row, bytes
+
+__global__ void __launch_bounds__(PS_THREADS) project_small_kernel(const ProjectArgs a, int rows_per_cta) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ const __half* rowptr[PS_MAX_ROWS];
+    __shared__ float* outptr[PS_MAX_ROWS];
+    __shared__ int outstride[PS_MAX_ROWS];
+    const int tid = threadIdx.x, cols = a.cols, pieces = cols / 8, stride = ps_stride(cols);
+    int total = 0;
+    for (int m = 0; m < a.n_mats; ++m) total += a.rows[m];
+    const int row0 = blockIdx.x * rows_per_cta, nrows = min(rows_per_cta, total - row0);
+    const int xbytes = a.batch * cols * 4;
+    uint8_t* wbase = sm + xbytes;
+    if (tid < nrows) {                             // the matrix and output of each row of the slice
+        int m = 0, r = row0 + tid;
+        while (m + 1 < a.n_mats && r >= a.rows[m]) r -= a.rows[m++];
+        rowptr[tid] = a.w[m] + (size_t)r * cols;
+        outptr[tid] = a.y[m] + r;
+        outstride[tid] = a.rows[m];
+    }
+    __syncthreads();
+    #pragma unroll
+    for (int g = 0; g < PS_GROUPS; ++g) {
+        const int p0 = pieces * g / PS_GROUPS, np = pieces * (g + 1) / PS_GROUPS - p0;
+        for (int i = tid; i < nrows * np; i += PS_THREADS) {
+            const int r = i / np, p = p0 + (i - r * np);
+            cp_async16(wbase + r * stride + p * 16, rowptr[r] + p * 8);
+        }
+        cp_commit();
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");        // the input is the previous kernel's
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    for (int i = tid; i < xbytes / 16; i += PS_THREADS)
+        reinterpret_cast<float4*>(sm)[i] = __ldcg(reinterpret_cast<const float4*>(a.x) + i);
+
+    // two threads per row as in project_kernel; the warps that hold no row only join the barriers
+    const int r = tid >> 1, hl = tid & 1;
+    const bool active_warp = (tid & ~31) < 2 * nrows;
+    const uint8_t* row = wbase + min(r, nrows - 1) * stride + hl * 8;
+    const float* xs = reinterpret_cast<const float*>(sm) + hl * 4;
+    float2 acc[PR_BATCH][2];
+    #pragma unroll
+    for (int bb = 0; bb < PR_BATCH; ++bb) acc[bb][0] = acc[bb][1] = make_float2(0.f, 0.f);
+    #pragma unroll
+    for (int g = 0; g < PS_GROUPS; ++g) {
+        if (g == 0) cp_wait<PS_GROUPS - 1>();
+        else if (g == 1) cp_wait<PS_GROUPS - 2>();
+        else if (g == 2) cp_wait<PS_GROUPS - 3>();
+        else cp_wait<0>();
+        __syncthreads();
+        if (!active_warp) continue;
+        const int j0 = pieces * g / PS_GROUPS, j1 = pieces * (g + 1) / PS_GROUPS;
+        #pragma unroll 4
+        for (int jj = j0; jj < j1; ++jj) {
+            const uint2 wv = *reinterpret_cast<const uint2*>(row + jj * 16);      // 4 FP16 weights
+            const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+            const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+            const float4 x0 = *reinterpret_cast<const float4*>(xs + jj * 8);
+            acc[0][0] = ffma2(make_float2(x0.x, x0.y), w01, acc[0][0]);
+            acc[0][1] = ffma2(make_float2(x0.z, x0.w), w23, acc[0][1]);
+            if (a.batch == PR_BATCH) {
+                const float4 x1 = *reinterpret_cast<const float4*>(xs + cols + jj * 8);
+                acc[1][0] = ffma2(make_float2(x1.x, x1.y), w01, acc[1][0]);
+                acc[1][1] = ffma2(make_float2(x1.z, x1.w), w23, acc[1][1]);
+            }
+        }
+    }
+    if (!active_warp) return;
+    #pragma unroll
+    for (int bb = 0; bb < PR_BATCH; ++bb) {
+        float2 o0, o1;
+        o0.x = __shfl_xor_sync(0xffffffffu, acc[bb][0].x, 1); o0.y = __shfl_xor_sync(0xffffffffu, acc[bb][0].y, 1);
+        o1.x = __shfl_xor_sync(0xffffffffu, acc[bb][1].x, 1); o1.y = __shfl_xor_sync(0xffffffffu, acc[bb][1].y, 1);
+        const float s0 = acc[bb][0].x + o0.x, s1 = acc[bb][0].y + o0.y;
+        const float s2 = acc[bb][1].x + o1.x, s3 = acc[bb][1].y + o1.y;
+        const float y = (s0 + s1) + (s2 + s3);
+        if (bb < a.batch && hl == 0 && r < nrows) outptr[r][(size_t)bb * outstride[r]] = y;
+    }
+}
+
+// The small-launch plan: rows per CTA and dynamic shared memory, or false when the launch
+// belongs to the persistent kernel (a batch beyond one pass, or a slice too large to hold).
+bool small_plan(const ProjectArgs& a, int sms, int* rows_per_cta, int* grid, size_t* smem) {
+    if (a.batch > PR_BATCH) return false;
+    int total = 0;
+    for (int m = 0; m < a.n_mats; ++m) total += a.rows[m];
+    const int r = (total + sms - 1) / sms;
+    if (r > PS_MAX_ROWS) return false;
+    const size_t bytes = (size_t)a.batch * a.cols * 4 + (size_t)r * (a.cols * 2 + 16);
+    if (bytes > PS_MAX_SMEM) return false;
+    *rows_per_cta = r;
+    *grid = (total + r - 1) / r;
+    *smem = bytes;
+    return true;
+}
+
 template <int ROWS>
 int resident_ctas() {
     // one wave of persistent CTAs: as many as fit on every SM at once
@@ -217,6 +328,25 @@ void launch_rows(ProjectArgs a, cudaStream_t s) {
 }  // namespace
 
 void launch_project(ProjectArgs a, cudaStream_t s) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        sms = NUM_SMS_B200;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaFuncSetAttribute(project_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PS_MAX_SMEM);
+    }
+    int rows_per_cta = 0, grid = 0;
+    size_t smem = 0;
+    if (small_plan(a, sms, &rows_per_cta, &grid, &smem)) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(grid); cfg.blockDim = dim3(PS_THREADS); cfg.dynamicSmemBytes = smem; cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr; cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, project_small_kernel, a, rows_per_cta);
+        return;
+    }
     int tiles64 = 0;
     for (int m = 0; m < a.n_mats; ++m) tiles64 += (a.rows[m] + 63) / 64;
     if (2 * tiles64 >= resident_ctas<64>()) launch_rows<64>(a, s);

@@ -70,10 +70,15 @@ def test_vocabulary_head_bit_exact():
 
 def test_group_ragged_shapes_and_batches_bit_exact():
     """q/k/v as one launch; rows that are not a multiple of the 16-row tile, a width that is not
-    a multiple of the 256-column chunk, and batches that need several passes."""
+    a multiple of the 128-column chunk, and batches that need several passes (the persistent
+    kernel); at batch 1 and 2 the same shapes take the small-launch kernel, whose row slices
+    cross matrix boundaries, and a 4096-column case whose slice is too large for it."""
     rng = np.random.default_rng(8)
     ctx = _ctx()
-    for rows, cols, batch in (((2048, 1024, 1024), 1024, 1), ((37, 5, 300), 776, 3), ((16, 17), 8, 5)):
+    for rows, cols, batch in (((2048, 1024, 1024), 1024, 1), ((2048, 1024, 1024), 1024, 2),
+                              ((37, 5, 300), 776, 3), ((37, 5, 300), 776, 2), ((37, 5, 300), 776, 1),
+                              ((16, 17), 8, 5), ((16, 17), 8, 1), ((3000, 3000), 4096, 2),
+                              ((1,), 3072, 2)):
         ws = [_matrix(rng, r, cols) for r in rows]
         x = rng.standard_normal((batch, cols)).astype(np.float32)
         wd = [torch.from_numpy(w.view(np.int16)).cuda() for w in ws]
