@@ -195,7 +195,26 @@ int check_appended(qa_ctx* ctx, int seq, int layer, int n_layers, int end) {
 // pinned mirror io_pin), one copy per tensor otherwise. Calls whose rows x layers exceed the
 // staging made at creation run in chunks of whole layers (every layer is independent). A bounded
 // wait that ran out during the call fails it with QA_ERR_TIMEOUT and resets the sequence.
+// Pinned host buffers (cudaHostAlloc, cudaHostRegister, torch's pin_memory) are reachable from the
+// device: when every host buffer of a call is pinned, 16-byte aligned, and the call moves at most
+// IO_DIRECT_BYTES, the kernels read the inputs and write the outputs over PCIe themselves and
+// only the error block is copied back, which saves the staging copies and their latency on
+// decode-sized calls.
 constexpr size_t IO_PACK_BYTES = size_t(64) << 10;      // above this, one copy per tensor is faster
+constexpr size_t IO_DIRECT_BYTES = size_t(8) << 20;
+
+// The device address of pinned host memory at p, or null (pageable, device memory, misaligned).
+const void* pinned_device_address(const void* p) {
+    cudaPointerAttributes at{};
+    if (!p || (reinterpret_cast<uintptr_t>(p) & 15)) return nullptr;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (at.type != cudaMemoryTypeHost || !at.devicePointer || (reinterpret_cast<uintptr_t>(at.devicePointer) & 15))
+        return nullptr;
+    return at.devicePointer;
+}
 
 struct IoCall {
     const float* in[3] = {};       // host inputs, [n_layers][...] layer-major
@@ -213,11 +232,40 @@ int io_host_call(qa_ctx* ctx, int seq, int layer, int n_layers, const IoCall& c,
     size_t fit = (size_t)n_layers;
     if (in_pl) fit = std::min(fit, ctx->io_in_floats / in_pl);
     if (out_pl) fit = std::min(fit, ctx->io_out_floats / out_pl);
+    int* const h_err = reinterpret_cast<int*>(ctx->io_pin);
+    // the error block came back with the call's outputs: a wait that ran out fails the call
+    auto check_error = [&]() -> int {
+        if (const int code = h_err[ERR_CODE]) {
+            QA_CUDA(cudaMemsetAsync(ctx->error + ERR_CODE, 0, sizeof(int), ctx->stream));
+            QA_CUDA(cudaStreamSynchronize(ctx->stream));
+            if (seq >= 0 && seq < (int)ctx->pos.size()) {
+                ctx->pos[seq] = 0;
+                std::fill(ctx->appended[seq].begin(), ctx->appended[seq].end(), 0);
+            }
+            return fail(ctx, QA_ERR_TIMEOUT, "a device-side wait expired (code %d); the call's results are invalid", code);
+        }
+        return QA_OK;
+    };
+    if ((in_pl + out_pl) * n_layers * sizeof(float) <= IO_DIRECT_BYTES) {
+        const float* din[3] = {};
+        float* dout[2] = {};
+        bool direct = true;
+        for (int i = 0; i < 3; ++i)
+            if (c.in_floats[i]) direct = direct && (din[i] = static_cast<const float*>(pinned_device_address(c.in[i])));
+        for (int j = 0; j < 2; ++j)
+            if (c.out[j]) direct = direct && (dout[j] = static_cast<float*>(const_cast<void*>(pinned_device_address(c.out[j]))));
+        if (direct) {
+            int st = launch(layer, n_layers, din, dout);
+            if (st) return st;
+            QA_CUDA(cudaMemcpyAsync(h_err, ctx->io_dev, ERR_BLOCK_BYTES, cudaMemcpyDeviceToHost, ctx->stream));
+            QA_CUDA(cudaStreamSynchronize(ctx->stream));
+            return check_error();
+        }
+    }
     if (fit < 1) return fail(ctx, QA_ERR_CAPACITY, "one layer of this call exceeds the host-buffer staging");
     const int chunk = (int)fit;
     float* const d_out = ctx->staging;
     float* const d_in = ctx->staging + ctx->io_out_floats;
-    int* const h_err = reinterpret_cast<int*>(ctx->io_pin);
     float* const h_out = reinterpret_cast<float*>(ctx->io_pin + ERR_BLOCK_BYTES);
     float* const h_in = h_out + IO_PACK_BYTES / sizeof(float);
     for (int l0 = layer; l0 < layer + n_layers; l0 += chunk) {
@@ -267,15 +315,7 @@ int io_host_call(qa_ctx* ctx, int seq, int layer, int n_layers, const IoCall& c,
                     o += c.out_floats[j] * nl;
                 }
         }
-        if (const int code = h_err[ERR_CODE]) {
-            QA_CUDA(cudaMemsetAsync(ctx->error + ERR_CODE, 0, sizeof(int), ctx->stream));
-            QA_CUDA(cudaStreamSynchronize(ctx->stream));
-            if (seq >= 0 && seq < (int)ctx->pos.size()) {
-                ctx->pos[seq] = 0;
-                std::fill(ctx->appended[seq].begin(), ctx->appended[seq].end(), 0);
-            }
-            return fail(ctx, QA_ERR_TIMEOUT, "a device-side wait expired (code %d); the call's results are invalid", code);
-        }
+        if ((st = check_error())) return st;
     }
     return QA_OK;
 }

@@ -633,6 +633,65 @@ def test_fused_decode_step_host_buffers():
     dev.close(); host.close()
 
 
+def test_pinned_host_buffers_go_direct():
+    """io_host calls whose host buffers are all pinned (here torch's pin_memory) let the kernels
+    read inputs and write outputs over PCIe with no staging copy: fused decode steps with and
+    without q_out, an attention-only decode and a one-row append give the device-pointer
+    context's results bit for bit; a misaligned pinned buffer falls back to the staging copies
+    with the same results."""
+    L, P = 28, 300
+    dev = make_ctx(L, context=1024)
+    host = qattn.Context(n_layers=L, context=1024, io_host=1)
+    qw, kw = H.norms(94, L)
+    q, k, v = H.inputs(94, L, 0, P + 3)
+    for c in (dev, host):
+        H.set_norms(c, qw, kw)
+    gpu_append(dev, 0, 0, *(t[:, :P].contiguous() for t in (q, k, v)))
+    dev.commit(0, P)
+    qh, kh, vh = (np.ascontiguousarray(t[:, :P].cpu().numpy()) for t in (q, k, v))
+    qo = np.empty_like(qh)
+    host.append(0, 0, L, 0, P, qh.ctypes.data, kh.ctypes.data, vh.ctypes.data, qo.ctypes.data)
+    host.commit(0, P)
+
+    def pinned(t):
+        return t.cpu().pin_memory()
+
+    for s, with_q in ((0, True), (1, False)):
+        q1, k1, v1 = (t[:, P + s:P + s + 1].contiguous() for t in (q, k, v))
+        qn_d, out_d = torch.empty_like(q1), torch.empty_like(q1)
+        dev.decode_step(0, 0, L, P + s, q1.data_ptr(), k1.data_ptr(), v1.data_ptr(), qn_d.data_ptr(), out_d.data_ptr())
+        dev.commit(0, 1)
+        torch.cuda.synchronize()
+        qp, kp, vp = (pinned(t) for t in (q1, k1, v1))
+        qn_h, out_h = torch.full_like(qp, float("nan")).pin_memory(), torch.full_like(qp, float("nan")).pin_memory()
+        host.decode_step(0, 0, L, P + s, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(),
+                         qn_h.data_ptr() if with_q else 0, out_h.data_ptr())
+        host.commit(0, 1)
+        assert torch.equal(out_h, out_d.cpu())
+        if with_q:
+            assert torch.equal(qn_h, qn_d.cpu())
+    # attention-only decode of the committed rows at P + 2 after a one-row append, both pinned
+    q1, k1, v1 = (t[:, P + 2:P + 3].contiguous() for t in (q, k, v))
+    qn_d = gpu_append(dev, 0, P + 2, q1, k1, v1)
+    out_d = gpu_attend(dev, 0, P + 2, qn_d, decode=True)
+    torch.cuda.synchronize()
+    qp, kp, vp = (pinned(t) for t in (q1, k1, v1))
+    qn_h = torch.empty_like(qp).pin_memory()
+    host.append(0, 0, L, P + 2, 1, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), qn_h.data_ptr())
+    assert torch.equal(qn_h, qn_d.cpu())
+    out_h = torch.empty_like(qp).pin_memory()
+    host.attn_decode(0, 0, L, P + 2, 1, qn_h.data_ptr(), out_h.data_ptr())
+    assert torch.equal(out_h, out_d.cpu())
+    # a pinned buffer 4 bytes off a 16-byte boundary takes the staging copies
+    big = torch.empty(qn_h.numel() + 4).pin_memory()
+    shifted = big[1:1 + qn_h.numel()].view_as(qn_h)
+    shifted.copy_(qn_h)
+    out_s = torch.empty(out_h.numel() + 4).pin_memory()[1:1 + out_h.numel()].view_as(out_h)
+    host.attn_decode(0, 0, L, P + 2, 1, shifted.data_ptr(), out_s.data_ptr())
+    assert torch.equal(out_s, out_d.cpu())
+    dev.close(); host.close()
+
+
 def test_host_buffer_calls_in_layer_chunks_and_per_layer():
     """io_host calls whose rows x layers exceed the staging made at creation (one layer of the
     context's rows) run in layer chunks; per-layer decode steps, the shape an engine that
