@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
     __shared__ __align__(8) uint64_t full[NST];
     __shared__ float red[GROUP][THREADS / 32];
     __shared__ float stat[2 * GROUP];
-    __shared__ float accbuf[HALF_WARPS][GROUP][D];
+    __shared__ __align__(16) float accbuf[HALF_WARPS][GROUP][D];
     __shared__ int is_last, abort_flag, never_abort;
     constexpr int QB = FUSED ? FUSED_MAX_UNITS : 1;
     __shared__ __align__(16) float s_q[QB][GROUP][D];      // fused: normalised query rows of unit i
@@ -559,64 +559,65 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
                 }
                 if (tid == 0) a.counters[unit] = 0;    // ready for the next call on this stream
             } else if (is_last) {
-                // Merge the unit's nrec records. The record loads are spread over the threads
-                // (max, then weights) and the per-output sums keep eight loads in flight, so the
-                // merge costs a few L2 round trips rather than one per record; a unit split over
-                // many CTAs (one layer per call) depends on that.
+                // Merge the unit's nrec records (a unit split over many CTAs: one layer per call)
+                // in rounds of `cap` records: a round copies its records into shared memory with
+                // every copy in flight at once (one L2 round trip), then each thread folds its two
+                // output columns over the round in record order, rescaling across rounds. The
+                // ring holds 63 records when this is the range's last segment (nothing is left to
+                // stream into it); otherwise the score buffer (this segment's scores are spent) or
+                // accbuf holds a round.
                 __threadfence();
                 const float* recs = a.partial + (size_t)unit * a.max_records * PARTIAL_FLOATS;
-                // [GROUP][nrec] record weights in accbuf (free now): nrec <= max_records <= ctas + 2
-                // = 298 < 1024, the most accbuf's 2048 floats hold
-                float* wts = &accbuf[0][0][0];
-                float m0 = -INFINITY, m1 = -INFINITY;
-                for (int s = tid; s < nrec; s += THREADS) {
-                    m0 = fmaxf(m0, __ldcg(recs + (size_t)s * PARTIAL_FLOATS));
-                    m1 = fmaxf(m1, __ldcg(recs + (size_t)s * PARTIAL_FLOATS + 1));
+                const int score_floats = FUSED ? max(GROUP * a.max_keys, FUSED_MAX_UNITS * 1024) : GROUP * a.max_keys;
+                float* buf = &accbuf[0][0][0];
+                int cap = HALF_WARPS * GROUP * D / PARTIAL_FLOATS;
+                if (g >= g_end) {
+                    buf = reinterpret_cast<float*>(ring);
+                    cap = NST * (int)CHUNK_BYTES / (PARTIAL_FLOATS * 4);
+                } else if (score_floats / PARTIAL_FLOATS > cap) {
+                    buf = scores;
+                    cap = score_floats / PARTIAL_FLOATS;
                 }
+                float M[GROUP] = {-INFINITY, -INFINITY}, Ls[GROUP] = {0.f, 0.f};
+                float V[GROUP * D / THREADS];
                 #pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) {
-                    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
-                    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+                for (int i = 0; i < GROUP * D / THREADS; ++i) V[i] = 0.f;
+                for (int r0 = 0; r0 < nrec; r0 += cap) {
+                    const int nr = min(cap, nrec - r0);
+                    __syncthreads();                   // the previous round (or accbuf's last use) is read
+                    const float* src = recs + (size_t)r0 * PARTIAL_FLOATS;
+                    for (int i = tid; i < nr * PARTIAL_FLOATS / 4; i += THREADS)
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                     ::"r"(smem_u32(buf + 4 * i)), "l"(src + 4 * i) : "memory");
+                    asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+                    __syncthreads();
+                    #pragma unroll
+                    for (int gq = 0; gq < GROUP; ++gq) {
+                        float mr = M[gq];
+                        for (int sr = 0; sr < nr; ++sr) mr = fmaxf(mr, buf[sr * PARTIAL_FLOATS + gq]);
+                        const float sc = M[gq] == -INFINITY ? 0.f : exp2f(M[gq] - mr);
+                        Ls[gq] *= sc;
+                        #pragma unroll
+                        for (int i = 0; i < GROUP * D / THREADS; ++i)
+                            if ((tid + i * THREADS) / D == gq) V[i] *= sc;
+                        M[gq] = mr;
+                    }
+                    for (int sr = 0; sr < nr; ++sr) {
+                        const float* rb = buf + sr * PARTIAL_FLOATS;
+                        const float w0 = exp2f(rb[0] - M[0]), w1 = exp2f(rb[1] - M[1]);
+                        Ls[0] += w0 * rb[GROUP];
+                        Ls[1] += w1 * rb[GROUP + 1];
+                        #pragma unroll
+                        for (int i = 0; i < GROUP * D / THREADS; ++i) {
+                            const int idx = tid + i * THREADS;
+                            V[i] += (idx / D ? w1 : w0) * rb[4 + idx];
+                        }
+                    }
                 }
-                if (lane == 0) { red[0][warp] = m0; red[1][warp] = m1; }
-                __syncthreads();
-                m0 = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
-                m1 = fmaxf(fmaxf(red[1][0], red[1][1]), fmaxf(red[1][2], red[1][3]));
-                float l0 = 0.f, l1 = 0.f;
-                for (int s = tid; s < nrec; s += THREADS) {
-                    const float* rs = recs + (size_t)s * PARTIAL_FLOATS;
-                    const float w0 = exp2f(__ldcg(rs) - m0), w1 = exp2f(__ldcg(rs + 1) - m1);
-                    wts[s] = w0;
-                    wts[nrec + s] = w1;
-                    l0 += w0 * __ldcg(rs + GROUP);
-                    l1 += w1 * __ldcg(rs + GROUP + 1);
-                }
-                #pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) {
-                    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-                    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-                }
-                __syncthreads();                       // red reuse; wts visible
-                if (lane == 0) { red[0][warp] = l0; red[1][warp] = l1; }
-                __syncthreads();
-                const float lall0 = (red[0][0] + red[0][1]) + (red[0][2] + red[0][3]);
-                const float lall1 = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
                 #pragma unroll
                 for (int i = 0; i < GROUP * D / THREADS; ++i) {
                     const int idx = tid + i * THREADS, gq = idx / D, jc = idx % D;
-                    const float* wq = wts + gq * nrec;
-                    const float* col = recs + 4 + idx;
-                    float v = 0.f;
-                    int s = 0;
-                    for (; s + 8 <= nrec; s += 8) {
-                        float x[8];
-                        #pragma unroll
-                        for (int e = 0; e < 8; ++e) x[e] = __ldcg(col + (size_t)(s + e) * PARTIAL_FLOATS);
-                        #pragma unroll
-                        for (int e = 0; e < 8; ++e) v += wq[s + e] * x[e];
-                    }
-                    for (; s < nrec; ++s) v += wq[s] * __ldcg(col + (size_t)s * PARTIAL_FLOATS);
-                    store_out(u, gq, jc, v / (gq ? lall1 : lall0));
+                    store_out(u, gq, jc, V[i] / Ls[gq]);
                 }
                 if (tid == 0) a.counters[unit] = 0;    // ready for the next call on this stream
             }
