@@ -203,6 +203,11 @@ int check_appended(qa_ctx* ctx, int seq, int layer, int n_layers, int end) {
 constexpr size_t IO_PACK_BYTES = size_t(64) << 10;      // above this, one copy per tensor is faster
 constexpr size_t IO_DIRECT_BYTES = size_t(8) << 20;
 
+// A decode launch splits the keys of its n_layers x n x hkv units evenly over 2 CTAs per SM, and
+// every CTA that covers part of a unit reads the unit's input rows: with at least one unit per
+// SM the rows are read about once or twice; a one-layer call splits each unit over ~37 CTAs.
+bool decode_inputs_read_once(int n_layers, int n, int hkv) { return (long long)n_layers * n * hkv >= NUM_SMS_B200; }
+
 // The device address of pinned host memory at p, or null (pageable, device memory, misaligned).
 const void* pinned_device_address(const void* p) {
     cudaPointerAttributes at{};
@@ -221,6 +226,9 @@ struct IoCall {
     size_t in_floats[3] = {};      // floats per layer of each input (0: unused)
     float* out[2] = {};            // host outputs: out[0] always, out[1] optional (may be null)
     size_t out_floats[2] = {};     // floats per layer (device room for out[1] is kept even when null)
+    // the kernels read each input row about once, so pinned inputs may be read over PCIe in
+    // place; false where many CTAs read the same rows (a decode whose units are split many ways)
+    bool inputs_read_once = true;
 };
 
 // launch(l0, nl, din, dout) enqueues the work of layers [l0, l0 + nl) on device pointers and
@@ -247,14 +255,33 @@ int io_host_call(qa_ctx* ctx, int seq, int layer, int n_layers, const IoCall& c,
         return QA_OK;
     };
     if ((in_pl + out_pl) * n_layers * sizeof(float) <= IO_DIRECT_BYTES) {
+        // pinned outputs are written in place; pinned inputs are read in place when each row is
+        // read about once, otherwise they go through the staging like pageable ones
         const float* din[3] = {};
         float* dout[2] = {};
-        bool direct = true;
-        for (int i = 0; i < 3; ++i)
-            if (c.in_floats[i]) direct = direct && (din[i] = static_cast<const float*>(pinned_device_address(c.in[i])));
+        bool out_direct = true, in_direct = c.inputs_read_once;
         for (int j = 0; j < 2; ++j)
-            if (c.out[j]) direct = direct && (dout[j] = static_cast<float*>(const_cast<void*>(pinned_device_address(c.out[j]))));
-        if (direct) {
+            if (c.out[j]) out_direct = out_direct && (dout[j] = static_cast<float*>(const_cast<void*>(pinned_device_address(c.out[j]))));
+        for (int i = 0; i < 3 && in_direct; ++i)
+            if (c.in_floats[i]) in_direct = (din[i] = static_cast<const float*>(pinned_device_address(c.in[i]))) != nullptr;
+        const size_t in_total = in_pl * n_layers;
+        if (out_direct && !in_direct && in_total <= ctx->io_in_floats) {
+            float* const d_in = ctx->staging + ctx->io_out_floats;
+            float* const h_in = reinterpret_cast<float*>(ctx->io_pin + ERR_BLOCK_BYTES) + IO_PACK_BYTES / sizeof(float);
+            const bool pack = in_total * sizeof(float) <= IO_PACK_BYTES;
+            size_t o = 0;
+            for (int i = 0; i < 3; ++i)
+                if (c.in_floats[i]) {
+                    const size_t nf = c.in_floats[i] * n_layers;
+                    if (pack) std::memcpy(h_in + o, c.in[i], nf * sizeof(float));
+                    else QA_CUDA(cudaMemcpyAsync(d_in + o, c.in[i], nf * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+                    din[i] = d_in + o;
+                    o += nf;
+                }
+            if (pack && in_total) QA_CUDA(cudaMemcpyAsync(d_in, h_in, in_total * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
+            in_direct = true;
+        }
+        if (out_direct && in_direct) {
             int st = launch(layer, n_layers, din, dout);
             if (st) return st;
             QA_CUDA(cudaMemcpyAsync(h_err, ctx->io_dev, ERR_BLOCK_BYTES, cudaMemcpyDeviceToHost, ctx->stream));
@@ -649,6 +676,7 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
     IoCall c;
     c.in[0] = q; c.in_floats[0] = qn;
     c.out[0] = out; c.out_floats[0] = qn;
+    c.inputs_read_once = !decode || decode_inputs_read_once(n_layers, n, ctx->hkv);
     return run_call(ctx, seq, layer, n_layers, c, [&](int l0, int nl, const float* const* din, float* const* dout) {
         int s2;
         if (decode) {
@@ -759,6 +787,7 @@ int qa_attn_decode_batch(qa_ctx* ctx, const int* seqs, int n, int layer, int n_l
     IoCall c;
     c.in[0] = q; c.in_floats[0] = qn;
     c.out[0] = out; c.out_floats[0] = qn;
+    c.inputs_read_once = decode_inputs_read_once(n_layers, n, ctx->hkv);
     return run_call(ctx, -1, layer, n_layers, c, [&](int l0, int nl, const float* const* din, float* const* dout) {
         const DecodePlan plan = plan_attn_decode(nl, ctx->hkv, n, pos);
         int s2;
@@ -781,6 +810,7 @@ static int decode_step(qa_ctx* ctx, const int* seqs, const int* pos, int n, int 
     c.in[0] = q_pre; c.in[1] = k_pre; c.in[2] = v; c.in_floats[0] = qn; c.in_floats[1] = kn; c.in_floats[2] = kn;
     c.out[0] = out; c.out_floats[0] = qn;
     c.out[1] = q_out; c.out_floats[1] = qn;
+    c.inputs_read_once = decode_inputs_read_once(n_layers, n, ctx->hkv);
     bool fused = false;
     const int seq1 = n == 1 ? seqs[0] : -1;
     st = run_call(ctx, seq1, layer, n_layers, c, [&](int l0, int nl, const float* const* din, float* const* dout) {

@@ -643,7 +643,7 @@ def test_pinned_host_buffers_go_direct():
     dev = make_ctx(L, context=1024)
     host = qattn.Context(n_layers=L, context=1024, io_host=1)
     qw, kw = H.norms(94, L)
-    q, k, v = H.inputs(94, L, 0, P + 3)
+    q, k, v = H.inputs(94, L, 0, P + 4)
     for c in (dev, host):
         H.set_norms(c, qw, kw)
     gpu_append(dev, 0, 0, *(t[:, :P].contiguous() for t in (q, k, v)))
@@ -670,24 +670,40 @@ def test_pinned_host_buffers_go_direct():
         assert torch.equal(out_h, out_d.cpu())
         if with_q:
             assert torch.equal(qn_h, qn_d.cpu())
-    # attention-only decode of the committed rows at P + 2 after a one-row append, both pinned
+    # one layer per call, as an engine that runs its projections between the layers calls it:
+    # each unit is split over many CTAs, so the pinned inputs are staged and only the outputs
+    # are written in place
     q1, k1, v1 = (t[:, P + 2:P + 3].contiguous() for t in (q, k, v))
-    qn_d = gpu_append(dev, 0, P + 2, q1, k1, v1)
-    out_d = gpu_attend(dev, 0, P + 2, qn_d, decode=True)
+    qp, kp, vp = (pinned(t) for t in (q1, k1, v1))
+    out_d = torch.empty_like(q1)
+    out_h = torch.full_like(qp, float("nan")).pin_memory()
+    for layer in range(L):
+        dev.decode_step(0, layer, 1, P + 2, q1[layer].data_ptr(), k1[layer].data_ptr(), v1[layer].data_ptr(), 0,
+                        out_d[layer].data_ptr())
+        host.decode_step(0, layer, 1, P + 2, qp[layer].data_ptr(), kp[layer].data_ptr(), vp[layer].data_ptr(), 0,
+                         out_h[layer].data_ptr())
+    dev.commit(0, 1)
+    host.commit(0, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(out_h, out_d.cpu())
+    # attention-only decode of the committed rows at P + 3 after a one-row append, both pinned
+    q1, k1, v1 = (t[:, P + 3:P + 4].contiguous() for t in (q, k, v))
+    qn_d = gpu_append(dev, 0, P + 3, q1, k1, v1)
+    out_d = gpu_attend(dev, 0, P + 3, qn_d, decode=True)
     torch.cuda.synchronize()
     qp, kp, vp = (pinned(t) for t in (q1, k1, v1))
     qn_h = torch.empty_like(qp).pin_memory()
-    host.append(0, 0, L, P + 2, 1, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), qn_h.data_ptr())
+    host.append(0, 0, L, P + 3, 1, qp.data_ptr(), kp.data_ptr(), vp.data_ptr(), qn_h.data_ptr())
     assert torch.equal(qn_h, qn_d.cpu())
     out_h = torch.empty_like(qp).pin_memory()
-    host.attn_decode(0, 0, L, P + 2, 1, qn_h.data_ptr(), out_h.data_ptr())
+    host.attn_decode(0, 0, L, P + 3, 1, qn_h.data_ptr(), out_h.data_ptr())
     assert torch.equal(out_h, out_d.cpu())
     # a pinned buffer 4 bytes off a 16-byte boundary takes the staging copies
     big = torch.empty(qn_h.numel() + 4).pin_memory()
     shifted = big[1:1 + qn_h.numel()].view_as(qn_h)
     shifted.copy_(qn_h)
     out_s = torch.empty(out_h.numel() + 4).pin_memory()[1:1 + out_h.numel()].view_as(out_h)
-    host.attn_decode(0, 0, L, P + 2, 1, shifted.data_ptr(), out_s.data_ptr())
+    host.attn_decode(0, 0, L, P + 3, 1, shifted.data_ptr(), out_s.data_ptr())
     assert torch.equal(out_s, out_d.cpu())
     dev.close(); host.close()
 
