@@ -449,7 +449,14 @@ def run_ours(args):
     value = dec_bytes / (decode_phase * 1e-3) / 1e9
     line = None
     if rank == 0:
-        dec_kernel_gbs = kern_bytes / world / (dattn * 1e-3) / 1e9    # this GPU's kernel bytes / kernel time
+        # The decode kernel's average launch duration over the timed region: with one fused launch per
+        # step on one GPU the 128 launches fill the decode phase back to back (consecutive steps
+        # overlap by programmatic dependent launch), so the phase time / 128 is that average. The
+        # two-launch forms (split decode; the gather's wait/copy at N > 1) use the probe step's
+        # events around each decode launch instead, which also serve as the isolated figure.
+        steady = world == 1 and not args.split_decode
+        dkern = decode_phase if steady else dattn
+        dec_kernel_gbs = kern_bytes / world / (dkern * 1e-3) / 1e9    # this GPU's kernel bytes / kernel time
         pre_kernel_tfs = pre_flops / world / (pattn * 1e-3) / 1e12
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -481,7 +488,10 @@ def run_ours(args):
                          "kernel": ("attn_decode (28 layers per launch)" if args.split_decode else
                                     "fused decode step: append of the new row + attn_decode, 28 layers per launch")
                                    + (" + head gather" if world > 1 else ""),
-                         "kernel_us": round(dattn / DECODE * 1e3, 2)},
+                         "kernel_us": round(dkern / DECODE * 1e3, 2),
+                         "kernel_us_isolated": round(dattn / DECODE * 1e3, 2),
+                         "timing": ("decode phase of the timed steps / 128 launches (back to back, overlapped)"
+                                    if steady else "CUDA events around each decode launch of a probe step")},
             "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
         }

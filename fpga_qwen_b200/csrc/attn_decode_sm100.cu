@@ -578,6 +578,8 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
                     buf = scores;
                     cap = score_floats / PARTIAL_FLOATS;
                 }
+                // per round: the two heads' maxima (warp 0), one weight per (record, head) into the
+                // record's max slot, then every thread's columns and the sums over the weights
                 float M[GROUP] = {-INFINITY, -INFINITY}, Ls[GROUP] = {0.f, 0.f};
                 float V[GROUP * D / THREADS];
                 #pragma unroll
@@ -591,20 +593,35 @@ __global__ void __launch_bounds__(THREADS, 2) attn_decode_sm100_kernel(const Dec
                                      ::"r"(smem_u32(buf + 4 * i)), "l"(src + 4 * i) : "memory");
                     asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
                     __syncthreads();
-                    #pragma unroll
-                    for (int gq = 0; gq < GROUP; ++gq) {
-                        float mr = M[gq];
-                        for (int sr = 0; sr < nr; ++sr) mr = fmaxf(mr, buf[sr * PARTIAL_FLOATS + gq]);
-                        const float sc = M[gq] == -INFINITY ? 0.f : exp2f(M[gq] - mr);
-                        Ls[gq] *= sc;
+                    if (warp == 0) {
+                        float m0 = M[0], m1 = M[1];
+                        for (int sr = lane; sr < nr; sr += 32) {
+                            m0 = fmaxf(m0, buf[sr * PARTIAL_FLOATS]);
+                            m1 = fmaxf(m1, buf[sr * PARTIAL_FLOATS + 1]);
+                        }
                         #pragma unroll
-                        for (int i = 0; i < GROUP * D / THREADS; ++i)
-                            if ((tid + i * THREADS) / D == gq) V[i] *= sc;
-                        M[gq] = mr;
+                        for (int off = 16; off >= 1; off >>= 1) {
+                            m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+                            m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+                        }
+                        if (lane == 0) { stat[0] = m0; stat[1] = m1; }
                     }
+                    __syncthreads();
+                    const float n0 = stat[0], n1 = stat[1];
+                    for (int k = tid; k < GROUP * nr; k += THREADS) {      // weight of record k / 2, head k % 2
+                        float* slot = buf + (k >> 1) * PARTIAL_FLOATS + (k & 1);
+                        *slot = exp2f(*slot - ((k & 1) ? n1 : n0));
+                    }
+                    const float sc0 = M[0] == -INFINITY ? 0.f : exp2f(M[0] - n0);
+                    const float sc1 = M[1] == -INFINITY ? 0.f : exp2f(M[1] - n1);
+                    M[0] = n0; M[1] = n1;
+                    Ls[0] *= sc0; Ls[1] *= sc1;
+                    #pragma unroll
+                    for (int i = 0; i < GROUP * D / THREADS; ++i) V[i] *= ((tid + i * THREADS) / D) ? sc1 : sc0;
+                    __syncthreads();                   // weights in place
                     for (int sr = 0; sr < nr; ++sr) {
                         const float* rb = buf + sr * PARTIAL_FLOATS;
-                        const float w0 = exp2f(rb[0] - M[0]), w1 = exp2f(rb[1] - M[1]);
+                        const float w0 = rb[0], w1 = rb[1];
                         Ls[0] += w0 * rb[GROUP];
                         Ls[1] += w1 * rb[GROUP + 1];
                         #pragma unroll
@@ -668,6 +685,9 @@ DecodePlan plan_attn_decode(int n_layers, int hkv, int n, const int* pos) {
     int max_len = 0;
     for (int b = 0; b < n; ++b) { row_keys += pos[b] + 1; max_len = std::max(max_len, pos[b] + 1); }
     p.total_keys = (long long)n_layers * hkv * row_keys;
+    // Two CTAs per SM with at least 64 keys each. (One CTA per SM for launches under 512 keys
+    // per CTA, halving the records of a one-layer call, measured slower: 461 against 374 us per
+    // token of 28 one-layer steps, the longer per-CTA streams cost more than the merges save.)
     long long ctas = (long long)NUM_SMS_B200 * 2;
     ctas = std::min<long long>(ctas, std::max<long long>(1, p.total_keys / 64));
     p.ctas = (int)ctas;

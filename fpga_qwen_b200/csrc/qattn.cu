@@ -226,8 +226,9 @@ struct IoCall {
     size_t in_floats[3] = {};      // floats per layer of each input (0: unused)
     float* out[2] = {};            // host outputs: out[0] always, out[1] optional (may be null)
     size_t out_floats[2] = {};     // floats per layer (device room for out[1] is kept even when null)
-    // the kernels read each input row about once, so pinned inputs may be read over PCIe in
-    // place; false where many CTAs read the same rows (a decode whose units are split many ways)
+    // the kernels read each input row about once, so pinned buffers may be used in place over
+    // PCIe; false where many CTAs read the same rows (a decode whose units are split many ways),
+    // which then goes through the staging copies (measured faster for one-layer decode calls)
     bool inputs_read_once = true;
 };
 
@@ -254,34 +255,15 @@ int io_host_call(qa_ctx* ctx, int seq, int layer, int n_layers, const IoCall& c,
         }
         return QA_OK;
     };
-    if ((in_pl + out_pl) * n_layers * sizeof(float) <= IO_DIRECT_BYTES) {
-        // pinned outputs are written in place; pinned inputs are read in place when each row is
-        // read about once, otherwise they go through the staging like pageable ones
+    if (c.inputs_read_once && (in_pl + out_pl) * n_layers * sizeof(float) <= IO_DIRECT_BYTES) {
         const float* din[3] = {};
         float* dout[2] = {};
-        bool out_direct = true, in_direct = c.inputs_read_once;
+        bool direct = true;
+        for (int i = 0; i < 3; ++i)
+            if (c.in_floats[i]) direct = direct && (din[i] = static_cast<const float*>(pinned_device_address(c.in[i])));
         for (int j = 0; j < 2; ++j)
-            if (c.out[j]) out_direct = out_direct && (dout[j] = static_cast<float*>(const_cast<void*>(pinned_device_address(c.out[j]))));
-        for (int i = 0; i < 3 && in_direct; ++i)
-            if (c.in_floats[i]) in_direct = (din[i] = static_cast<const float*>(pinned_device_address(c.in[i]))) != nullptr;
-        const size_t in_total = in_pl * n_layers;
-        if (out_direct && !in_direct && in_total <= ctx->io_in_floats) {
-            float* const d_in = ctx->staging + ctx->io_out_floats;
-            float* const h_in = reinterpret_cast<float*>(ctx->io_pin + ERR_BLOCK_BYTES) + IO_PACK_BYTES / sizeof(float);
-            const bool pack = in_total * sizeof(float) <= IO_PACK_BYTES;
-            size_t o = 0;
-            for (int i = 0; i < 3; ++i)
-                if (c.in_floats[i]) {
-                    const size_t nf = c.in_floats[i] * n_layers;
-                    if (pack) std::memcpy(h_in + o, c.in[i], nf * sizeof(float));
-                    else QA_CUDA(cudaMemcpyAsync(d_in + o, c.in[i], nf * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-                    din[i] = d_in + o;
-                    o += nf;
-                }
-            if (pack && in_total) QA_CUDA(cudaMemcpyAsync(d_in, h_in, in_total * sizeof(float), cudaMemcpyHostToDevice, ctx->stream));
-            in_direct = true;
-        }
-        if (out_direct && in_direct) {
+            if (c.out[j]) direct = direct && (dout[j] = static_cast<float*>(const_cast<void*>(pinned_device_address(c.out[j]))));
+        if (direct) {
             int st = launch(layer, n_layers, din, dout);
             if (st) return st;
             QA_CUDA(cudaMemcpyAsync(h_err, ctx->io_dev, ERR_BLOCK_BYTES, cudaMemcpyDeviceToHost, ctx->stream));

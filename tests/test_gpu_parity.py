@@ -671,8 +671,7 @@ def test_pinned_host_buffers_go_direct():
         if with_q:
             assert torch.equal(qn_h, qn_d.cpu())
     # one layer per call, as an engine that runs its projections between the layers calls it:
-    # each unit is split over many CTAs, so the pinned inputs are staged and only the outputs
-    # are written in place
+    # each unit is split over many CTAs, so the pinned buffers go through the staging copies
     q1, k1, v1 = (t[:, P + 2:P + 3].contiguous() for t in (q, k, v))
     qp, kp, vp = (pinned(t) for t in (q1, k1, v1))
     out_d = torch.empty_like(q1)
