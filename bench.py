@@ -519,10 +519,37 @@ def run_ours(args):
         if world == 1 and not args.no_e2e:
             line["e2e"] = e2e_decode(args, seed)
             line["e2e_per_layer"] = e2e_per_layer(args, seed)
+            cpp = cpp_decode_loop()
+            if cpp:
+                line["e2e_per_layer"]["cpp"] = cpp
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline_report(CpuBaseline())
         print(json.dumps(line), flush=True)
     return 0
+
+
+def cpp_decode_loop():
+    """The same two decode call patterns timed from C++ (fpga_qwen_b200/host/decode_loop_bench.cpp:
+    28 one-layer qa_decode_step calls per token, and one 28-layer call per token, both with
+    pageable host buffers), as an x86 engine linking libqattn.so sees them without Python's call
+    overhead. Built with g++ here; returns None (and says why on stderr) if that fails."""
+    pkg = ROOT / "fpga_qwen_b200"
+    with tempfile.TemporaryDirectory() as tmp:
+        exe = Path(tmp) / "decode_loop_bench"
+        cmd = ["g++", "-O2", "-std=c++17", f"-I{ROOT / 'include'}", str(pkg / "host" / "decode_loop_bench.cpp"),
+               f"-L{pkg}", "-lqattn", f"-Wl,-rpath,{pkg}", "-o", str(exe)]
+        built = subprocess.run(cmd, capture_output=True, text=True)
+        if built.returncode != 0:
+            print(f"decode_loop_bench: build failed: {built.stderr[-500:]}", file=sys.stderr)
+            return None
+        ran = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600)
+        if ran.returncode != 0:
+            print(f"decode_loop_bench: {ran.stderr[-500:]}", file=sys.stderr)
+            return None
+        res = json.loads(ran.stdout.strip().splitlines()[-1])
+        res["note"] = ("C++ through the C ABI with pageable host buffers, steady_clock around 128 tokens; "
+                       "per layer = 28 one-layer qa_decode_step calls + qa_commit per token")
+        return res
 
 
 def e2e_decode(args, seed):
