@@ -2,8 +2,9 @@
 
 The launches rely on them: the tensor-core prefill moves registers between warpgroups with
 setmaxnreg and refuses to launch unless it was built with exactly 168 registers per thread;
-the decode kernels run two 256-thread CTAs per SM and the FP32 head-rows kernel one
-512-thread CTA, so both need <= 128 registers; and no kernel may spill to local memory.
+the decode kernels run two 128-thread CTAs per SM (65,536 registers / 256 threads: at most 255
+per thread, the architectural limit) and the FP32 head-rows kernel one 512-thread CTA (at most
+128); and no kernel may spill to local memory.
 """
 import re
 
@@ -55,7 +56,7 @@ def test_prefill_register_split_is_consistent(resources):
     assert all(regs == 168 for regs, _ in found.values()), found
 
 
-@pytest.mark.parametrize("name", ["attn_decode_sm100_kernel", "attn_head_rows_kernel"])
-def test_occupancy_register_budgets(resources, name):
+@pytest.mark.parametrize("name,budget", [("attn_decode_sm100_kernel", 255), ("attn_head_rows_kernel", 128)])
+def test_occupancy_register_budgets(resources, name, budget):
     found = _pick(resources, name)
-    assert all(regs <= 128 for regs, _ in found.values()), found
+    assert all(regs <= budget for regs, _ in found.values()), found
