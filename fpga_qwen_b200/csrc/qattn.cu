@@ -43,6 +43,7 @@ struct qa_ctx {
     float* sines = nullptr;
     std::vector<int> pos;                  // committed position per sequence
     std::vector<std::vector<int>> appended;  // per sequence, per layer: rows written through
+    void* proj_scratch = nullptr;          // the tensor-core projections' split input rows (project_mma.cu)
     float* partial = nullptr;              // split-context records, sized at creation for any call
     size_t partial_floats = 0;
     int* counters = nullptr;
@@ -481,6 +482,7 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     ctx->error = reinterpret_cast<int*>(ctx->io_dev);
     ctx->staging = reinterpret_cast<float*>(ctx->io_dev + ERR_BLOCK_BYTES);
     if (cudaMalloc(&ctx->prefill_tiles, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMalloc(&ctx->proj_scratch, project_gemm_scratch_bytes()) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaStreamCreateWithFlags(&ctx->aux_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->fork_ev, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->join_ev, cudaEventDisableTiming) != cudaSuccess)
@@ -504,7 +506,7 @@ void qa_destroy(qa_ctx* ctx) {
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
     cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->io_dev); cudaFreeHost(ctx->io_pin);
-    cudaFree(ctx->prefill_tiles);
+    cudaFree(ctx->prefill_tiles); cudaFree(ctx->proj_scratch);
     if (ctx->aux_stream) { cudaStreamSynchronize(ctx->aux_stream); cudaStreamDestroy(ctx->aux_stream); }
     if (ctx->fork_ev) cudaEventDestroy(ctx->fork_ev);
     if (ctx->join_ev) cudaEventDestroy(ctx->join_ev);
@@ -977,14 +979,18 @@ int qa_kv_slot_bytes(const qa_ctx* ctx, size_t* bytes) {
     return QA_OK;
 }
 
-// ---- decode projections (project.cu) ----------------------------------------------------------
-int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const int* rows, int cols, const float* x,
-                     int batch, float* const* y) {
+}  // extern "C"
+
+// ---- projections: decode GEMVs (project.cu) and batched prompt rows (project_mma.cu) -------------
+namespace {
+int project_call(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const int* rows, int cols, const float* x,
+                 int batch, float* const* y, bool gemm) {
     if (!ctx) return QA_ERR_INVALID;
     if (n_mats < 1 || n_mats > MAX_PROJECT_MATS || !w || !rows || !y)
         return fail(ctx, QA_ERR_INVALID, "%d matrices (1..%d) or null arrays", n_mats, MAX_PROJECT_MATS);
     if (cols < 8 || cols % 8) return fail(ctx, QA_ERR_INVALID, "columns %d: a positive multiple of 8", cols);
-    if (batch < 1 || batch > QA_MAX_BATCH) return fail(ctx, QA_ERR_INVALID, "batch %d outside 1..%d", batch, QA_MAX_BATCH);
+    if (batch < 1 || (!gemm && batch > QA_MAX_BATCH))
+        return fail(ctx, QA_ERR_INVALID, "batch %d outside 1..%d", batch, gemm ? INT32_MAX : QA_MAX_BATCH);
     if (!x) return fail(ctx, QA_ERR_INVALID, "null input");
     if (!ctx->cfg.io_host && (reinterpret_cast<uintptr_t>(x) & 15))
         return fail(ctx, QA_ERR_INVALID, "input rows must be 16-byte aligned");
@@ -999,11 +1005,16 @@ int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const in
         out_floats += (size_t)rows[m] * batch;
     }
     QA_CUDA(cudaSetDevice(ctx->cfg.device));
+    // the tensor-core path where the shape allows it; otherwise the CUDA-core kernels, whose
+    // eight-lane sums are one of the FP32 summation orders the batched form admits
+    auto launch = [&]() {
+        if (!gemm || launch_project_gemm(a, ctx->proj_scratch, ctx->error, ctx->stream) < 0) launch_project(a, ctx->stream);
+    };
     const size_t in_floats = (size_t)batch * cols;
     if (!ctx->cfg.io_host) {
         a.x = x;
         for (int m = 0; m < n_mats; ++m) a.y[m] = y[m];
-        launch_project(a, ctx->stream);
+        launch();
         return after_launch(ctx, -1, "project");
     }
     // host buffers: x into the staging inputs, every y from the staging outputs (one copy each
@@ -1025,7 +1036,7 @@ int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const in
     a.x = d_in;
     size_t off = 0;
     for (int m = 0; m < n_mats; ++m) { a.y[m] = d_out + off; off += (size_t)rows[m] * batch; }
-    launch_project(a, ctx->stream);
+    launch();
     int st;
     if ((st = after_launch(ctx, -1, "project"))) return st;
     if (pack_out) {
@@ -1053,8 +1064,23 @@ int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const in
     return QA_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const int* rows, int cols, const float* x,
+                     int batch, float* const* y) {
+    return project_call(ctx, n_mats, w, rows, cols, x, batch, y, false);
+}
 int qa_project(qa_ctx* ctx, const uint16_t* w, int rows, int cols, const float* x, int batch, float* y) {
-    return qa_project_group(ctx, 1, &w, &rows, cols, x, batch, &y);
+    return project_call(ctx, 1, &w, &rows, cols, x, batch, &y, false);
+}
+int qa_project_group_gemm(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const int* rows, int cols, const float* x,
+                          int batch, float* const* y) {
+    return project_call(ctx, n_mats, w, rows, cols, x, batch, y, true);
+}
+int qa_project_gemm(qa_ctx* ctx, const uint16_t* w, int rows, int cols, const float* x, int batch, float* y) {
+    return project_call(ctx, 1, &w, &rows, cols, x, batch, &y, true);
 }
 
 int qa_synth_fill(float* dst, uint64_t seed, int kind, int layer0, int n_layers, int pos0, int n, int head0,

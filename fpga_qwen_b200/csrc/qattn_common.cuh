@@ -185,6 +185,13 @@ struct ProjectArgs {
     const float* x = nullptr;
 };
 void launch_project(ProjectArgs a, cudaStream_t s);
+// Batched projections on the tensor cores (project_mma.cu): the rows are split into FP16 halves
+// in a scratch area of project_gemm_scratch_bytes() (made at context creation), GEMM_CHUNK_ROWS
+// input rows at a time. Returns 0, or < 0 when the shape does not fit (cols > GEMM_MAX_COLS) or
+// a tensor map cannot be made. Bounded-wait expiry codes go to *error.
+constexpr int GEMM_CHUNK_ROWS = 512, GEMM_MAX_COLS = 8192;
+size_t project_gemm_scratch_bytes();
+int launch_project_gemm(const ProjectArgs& a, void* scratch, int* error, cudaStream_t s);
 
 // Looks up, for `device` and its current context, the device address of the fixed scratch array
 // behind qa_attn_decode_noalloc (attn_decode_noalloc.cu). Makes `device` current.

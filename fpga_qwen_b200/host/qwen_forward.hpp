@@ -8,7 +8,9 @@
 //          g * (0.5 + 0.5 tanh(g/2)) * up (:636-639; std::tanh for Accelerate's vvtanhf);
 //   GPU    every projection (qa_project / qa_project_group: q/k/v and gate/up grouped as at
 //          :388-389, :629; the eight-lane dot per output, bit-exact with the reference's for one
-//          row, for verification and for the FP16-only vocabulary head), QK-RMSNorm + RoPE +
+//          row, for verification and for the FP16-only vocabulary head; prompt chunks of more
+//          than one row take qa_project_gemm / qa_project_group_gemm on the tensor cores, where
+//          the reference uses cblas_sgemm, :294), QK-RMSNorm + RoPE +
 //          FP16 KV write and attention (AttentionModel's layer-by-layer pass: qa_append +
 //          qa_attn_prefill / qa_attn_decode, or the fused qa_decode_step for one row).
 // Layer l+1's projections consume layer l's attention output, exactly the engine's order; the
@@ -127,7 +129,7 @@ private:
         qa_ctx* ctx = attn_.context();
         attn_.begin_rows(n, verify);
         try {
-            layers(ctx, n, H, F, L);
+            layers(ctx, n, H, F, L, n > 1 && !verify);
         } catch (...) {
             attn_.reset();                 // as Model::verify_two / commit_verified do (core.cpp:740, :751)
             throw;
@@ -139,7 +141,16 @@ private:
         return hidden;
     }
 
-    void layers(qa_ctx* ctx, int n, int H, int F, int L) {
+    // batched: a prompt chunk (core.cpp:294's sgemm); otherwise one row or a verification pair
+    void layers(qa_ctx* ctx, int n, int H, int F, int L, bool batched) {
+        auto project = [&](const uint16_t* w, int rows, int cols, const float* x, float* y) {
+            run(batched ? qa_project_gemm(ctx, w, rows, cols, x, n, y) : qa_project(ctx, w, rows, cols, x, n, y));
+        };
+        auto project_group = [&](int k, const uint16_t* const* ws, const int* rows, int cols, const float* x,
+                                 float* const* ys) {
+            run(batched ? qa_project_group_gemm(ctx, k, ws, rows, cols, x, n, ys)
+                        : qa_project_group(ctx, k, ws, rows, cols, x, n, ys));
+        };
         for (int l = 0; l < L; ++l) {
             const LayerWeights& lw = w_.layers[l];
             for (int b = 0; b < n; ++b) norm(&x_[(size_t)b * H], lw.input_norm, &h_[(size_t)b * H], H);
@@ -147,23 +158,23 @@ private:
                 const uint16_t* ws[3] = {lw.q, lw.k, lw.v};
                 const int rows[3] = {qd_, kd_, kd_};
                 float* ys[3] = {q_.data(), k_.data(), v_.data()};
-                run(qa_project_group(ctx, 3, ws, rows, H, h_.data(), n, ys));
+                project_group(3, ws, rows, H, h_.data(), ys);
             }
             attn_.layer_rows(l, q_.data(), k_.data(), v_.data(), n == 1 ? nullptr : qrows_.data(), att_.data());
-            run(qa_project(ctx, lw.o, H, qd_, att_.data(), n, res_.data()));
+            project(lw.o, H, qd_, att_.data(), res_.data());
             for (size_t j = 0; j < x_.size(); ++j) x_[j] += res_[j];
             for (int b = 0; b < n; ++b) norm(&x_[(size_t)b * H], lw.post_norm, &h_[(size_t)b * H], H);
             {
                 const uint16_t* ws[2] = {lw.gate, lw.up};
                 const int rows[2] = {F, F};
                 float* ys[2] = {gate_.data(), up_.data()};
-                run(qa_project_group(ctx, 2, ws, rows, H, h_.data(), n, ys));
+                project_group(2, ws, rows, H, h_.data(), ys);
             }
             for (size_t j = 0; j < gate_.size(); ++j) {
                 const float t = std::tanh(gate_[j] * 0.5f);
                 gate_[j] = gate_[j] * (0.5f + 0.5f * t) * up_[j];
             }
-            run(qa_project(ctx, lw.down, H, F, gate_.data(), n, res_.data()));
+            project(lw.down, H, F, gate_.data(), res_.data());
             for (size_t j = 0; j < x_.size(); ++j) x_[j] += res_[j];
         }
     }

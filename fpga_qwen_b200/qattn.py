@@ -111,6 +111,10 @@ _SIGNATURES = {
                                   ctypes.c_int, ctypes.c_void_p]),
     "qa_project_group": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "qa_project_gemm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                       ctypes.c_int, ctypes.c_void_p]),
+    "qa_project_group_gemm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "qa_synth_fill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                      ctypes.c_float, ctypes.c_void_p]),
@@ -334,6 +338,18 @@ class Context:
         rs = (ctypes.c_int * n)(*rows)
         ys = (ctypes.c_void_p * n)(*y_ptrs)
         self._check(lib().qa_project_group(self._h, n, ws, rs, cols, x_ptr, batch, ys))
+
+    def project_gemm(self, w_ptr: int, rows: int, cols: int, x_ptr: int, batch: int, y_ptr: int):
+        """Batched prompt rows on the tensor cores (FP32 products within accumulation rounding)."""
+        self._check(lib().qa_project_gemm(self._h, w_ptr, rows, cols, x_ptr, batch, y_ptr))
+
+    def project_group_gemm(self, w_ptrs, rows, cols: int, x_ptr: int, batch: int, y_ptrs):
+        """project_group on the tensor cores; y_ptrs[m] receives [batch][rows[m]]."""
+        n = len(w_ptrs)
+        ws = (ctypes.c_void_p * n)(*w_ptrs)
+        rs = (ctypes.c_int * n)(*rows)
+        ys = (ctypes.c_void_p * n)(*y_ptrs)
+        self._check(lib().qa_project_group_gemm(self._h, n, ws, rs, cols, x_ptr, batch, ys))
 
     def kv_slot_bytes(self) -> int:
         out = ctypes.c_size_t()

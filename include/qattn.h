@@ -228,6 +228,18 @@ int qa_project(qa_ctx* ctx, const uint16_t* w, int rows, int cols, const float* 
  * :657, :693). y[m] receives [batch][rows[m]]. */
 int qa_project_group(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const int* rows, int cols,
                      const float* x, int batch, float* const* y);
+/* Batched projections of prompt rows on the tensor cores: Model::Impl::project and
+ * project_group with more than one row (core.cpp:292-320, the cblas_sgemm at :294 over the FP32
+ * widening of the FP16 matrices; :387-394, :625-641 for a prompt chunk). Each input row is split
+ * into two FP16 halves (22 bits of its significand, after an exact power-of-two scale) and both
+ * are multiplied by W with FP32 accumulation, so y lies within FP32 accumulation rounding of the
+ * exact product, as sgemm's does (no bit-exact claim: sgemm's summation order is unpublished).
+ * Same arguments and alignment rules as qa_project / qa_project_group; any batch >= 1 (host
+ * buffers: up to the staging made at creation). Widths above 8192 columns run on the CUDA-core
+ * kernels instead. Asynchronous on the context stream. */
+int qa_project_gemm(qa_ctx* ctx, const uint16_t* w, int rows, int cols, const float* x, int batch, float* y);
+int qa_project_group_gemm(qa_ctx* ctx, int n_mats, const uint16_t* const* w, const int* rows, int cols,
+                          const float* x, int batch, float* const* y);
 
 /* ---- Multi-GPU: KV-head sharding and prefill -> decode handoff (NCCL over NVLink) -------
  * No counterpart in the reference, a single-host CPU engine. One process per GPU; each

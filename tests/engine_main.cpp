@@ -9,10 +9,14 @@
 // verify_two(ids[10], ids[11]) + commit_verified(2), step ids[12], truncate(5), prefill
 // ids[5..9), step ids[9]. logits.bin: FP32 [8][vocab], the logits after each of those rows
 // in order (a verification gives two rows). Prints the final position.
+//   engine_main <weights.bin> <ids.bin> <logits.bin> long
+// A long prompt: ids.bin holds n ids (n <= 255); prefill ids[0..n-1) as one chunk (its
+// projections on the tensor cores), then step ids[n-1]; logits.bin: FP32 [2][vocab].
 #include <cuda_runtime.h>
 
 #include <cstdint>
 #include <cstdio>
+#include <string>
 #include <vector>
 
 #include "qwen_forward.hpp"
@@ -73,18 +77,36 @@ int main(int argc, char** argv) {
         w.layers.push_back(lw);
     }
     std::fclose(wf);
+    const bool long_prompt = argc > 4 && std::string(argv[4]) == "long";
     FILE* idf = std::fopen(argv[2], "rb");
     if (!idf) return 4;
-    std::vector<int32_t> ids(13);
-    if (std::fread(ids.data(), 4, ids.size(), idf) != ids.size()) return 5;
+    std::vector<int32_t> ids(long_prompt ? 255 : 13);
+    const size_t got = std::fread(ids.data(), 4, ids.size(), idf);
     std::fclose(idf);
+    if (long_prompt) {
+        if (got < 2) return 5;
+        ids.resize(got);
+    } else if (got != ids.size()) {
+        return 5;
+    }
 
     qattn_host::Options opt;
     opt.layers = L;
-    opt.context = 64;
+    opt.context = long_prompt ? 256 : 64;
     qattn_host::QwenForward model(w, opt);
     std::vector<float> out;
     auto keep = [&](const std::vector<float>& lg) { out.insert(out.end(), lg.begin(), lg.end()); };
+    if (long_prompt) {
+        keep(model.prefill(std::vector<int>(ids.begin(), ids.end() - 1)));
+        keep(model.step(ids.back()));
+        FILE* of = std::fopen(argv[3], "wb");
+        if (!of) return 6;
+        std::fwrite(out.data(), sizeof(float), out.size(), of);
+        std::fclose(of);
+        std::printf("position %d\n", model.position());
+        for (void* d : g_device) cudaFree(d);
+        return 0;
+    }
     keep(model.prefill(std::vector<int>(ids.begin(), ids.begin() + 8)));
     keep(model.step(ids[8]));
     keep(model.step(ids[9]));

@@ -98,3 +98,37 @@ def test_gpu_engine_forward_matches_numpyqwen(tmp_path):
     d = np.abs(got.astype(np.float64) - ref)
     H.record("engine forward logits vs NumpyQwen", mx, 0.0, len(SCENARIO_ROWS))
     assert d.max() < 0.01, d.max()
+
+
+@pytest.mark.gpu
+def test_gpu_engine_long_prompt_chunk_on_tensor_cores(tmp_path):
+    """A 150-token prompt in one chunk: its projections run batched on the tensor cores
+    (qa_project_gemm, where the reference uses cblas_sgemm, engine/core.cpp:294), then one
+    decode step on the eight-lane GEMVs. Both rows' logits against the CPU restatement of the
+    forward pass (which sums the batched products in FP32, as sgemm does) within the
+    reference's full-logit gate, with the same top token."""
+    from oracle.engine_oracle import EngineOracle
+    from tests import helpers as H
+    if shutil.which("g++") is None:
+        pytest.skip("g++ not available")
+    lib = ROOT / "fpga_qwen_b200" / "libqattn.so"
+    exe = tmp_path / "engine_main"
+    subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-Werror", f"-I{ROOT / 'include'}",
+                    f"-I{ROOT / 'fpga_qwen_b200' / 'host'}", "-I/usr/local/cuda/include",
+                    str(ROOT / "tests" / "engine_main.cpp"), f"-L{lib.parent}", "-lqattn", "-L/usr/local/cuda/lib64",
+                    "-lcudart", f"-Wl,-rpath,{lib.parent}", "-o", str(exe)], check=True, capture_output=True, text=True)
+    V = _write_inputs(tmp_path)
+    ids = np.random.default_rng(150).integers(0, V, 150).astype(np.int32)
+    (tmp_path / "long_ids.bin").write_bytes(ids.tobytes())
+    res = subprocess.run([str(exe), str(tmp_path / "weights.bin"), str(tmp_path / "long_ids.bin"),
+                          str(tmp_path / "long_out.bin"), "long"], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert res.stdout.split() == ["position", "150"]
+    got = np.fromfile(tmp_path / "long_out.bin", dtype=np.float32).reshape(2, V)
+    w, *_ = engine_weights()
+    e = EngineOracle(w, context=256)
+    ref = np.concatenate([e.chunk([int(t) for t in ids[:-1]]), e.chunk([int(ids[-1])])]).astype(np.float64)
+    d = np.abs(got.astype(np.float64) - ref)
+    H.record("engine 150-token prompt (tensor-core projections)", float(d.max()), float(np.sqrt((d * d).mean())), 2)
+    assert d.max() < MAX_ABS and np.sqrt((d * d).mean()) < RMS, (d.max(), np.sqrt((d * d).mean()))
+    assert (np.argmax(got, axis=-1) == np.argmax(ref, axis=-1)).all()

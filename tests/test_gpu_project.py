@@ -123,3 +123,65 @@ def test_host_buffers_and_validation():
         host.project(wd.data_ptr() + 2, rows, cols, x.ctypes.data, 1, y.ctypes.data)     # not 16-byte aligned
     assert e.value.status == qattn.QA_ERR_INVALID
     host.close()
+
+
+def _gemm_check(got, x, ws):
+    """Each matrix's batched product within FP32 accumulation rounding of the exact product: the
+    split FP16 input keeps 22 bits, the sums run in FP32 (as sgemm's, in another order)."""
+    for y, w in zip(got, ws):
+        exact = x.astype(np.float64) @ w.view(np.float16).astype(np.float64).T
+        scale = np.abs(x).astype(np.float64) @ np.abs(w.view(np.float16).astype(np.float64)).T
+        err = np.abs(y.astype(np.float64) - exact)
+        assert (err <= 1e-5 * scale + 1e-30).all(), (err / np.maximum(scale, 1e-30)).max()
+
+
+@pytest.mark.parametrize("rows,cols,batch", [((2048, 1024, 1024), 1024, 512), ((3072, 3072), 1024, 129),
+                                             ((1024,), 3072, 37), ((1024,), 2048, 600), ((37, 5, 300), 776, 3),
+                                             ((3000,), 8200, 5)])
+def test_gemm_batched_prompt_rows(rows, cols, batch):
+    """qa_project_group_gemm (tensor cores; batches over one or several 512-row chunks, ragged
+    rows, widths that are not a multiple of the 64-column K step, and a width beyond the tensor
+    path's 8192 that runs on the CUDA cores) against the exact product, and against the CPU
+    restatement of the reference's batched sgemm form."""
+    rng = np.random.default_rng(sum(rows) + cols + batch)
+    ws = [_matrix(rng, r, cols) for r in rows]
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    ctx = _ctx()
+    wd = [torch.from_numpy(w.view(np.int16)).cuda() for w in ws]
+    xd = torch.from_numpy(x).cuda()
+    ys = [torch.full((batch, r), float("nan"), device="cuda") for r in rows]
+    ctx.project_group_gemm([t.data_ptr() for t in wd], list(rows), cols, xd.data_ptr(), batch, [t.data_ptr() for t in ys])
+    torch.cuda.synchronize()
+    ctx.sync()
+    got = [y.cpu().numpy() for y in ys]
+    _gemm_check(got, x, ws)
+    if batch <= 129:
+        for y, w in zip(got, ws):
+            ref = O.project(x, w, sgemm=True, threads=THREADS)
+            assert np.abs(y - ref).max() <= 1e-5 * max(1.0, float(np.abs(ref).max()))
+    ctx.close()
+
+
+def test_gemm_rows_of_extreme_magnitude_and_host_buffers():
+    """Input rows scaled by 1e-20 and 1e20 keep full relative precision (each row is brought to a
+    fixed range by an exact power of two before the FP16 split); the host-buffer form gives the
+    device form's results."""
+    rng = np.random.default_rng(12)
+    w = _matrix(rng, 1024, 1024)
+    x = rng.standard_normal((40, 1024)).astype(np.float32)
+    x[3] *= 1e-20
+    x[7] *= 1e20
+    x[11] = 0.0
+    wd = torch.from_numpy(w.view(np.int16)).cuda()
+    dev = _ctx()
+    y = torch.empty((40, 1024), device="cuda")
+    dev.project_gemm(wd.data_ptr(), 1024, 1024, torch.from_numpy(x).cuda().data_ptr(), 40, y.data_ptr())
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    _gemm_check([got], x, [w])
+    assert (got[11] == 0).all()
+    host = _ctx(io_host=1)
+    yh = np.full((40, 1024), np.nan, np.float32)
+    host.project_gemm(wd.data_ptr(), 1024, 1024, x.ctypes.data, 40, yh.ctypes.data)
+    assert np.array_equal(yh, got)
+    dev.close(); host.close()
