@@ -781,7 +781,45 @@ def projection_bench(args):
     torch.cuda.synchronize()
     ctx.sync()
     del graph
+    # a 512-row prompt chunk through the 28 layers' projections on the tensor cores
+    # (qa_project_group_gemm / qa_project_gemm), replayed from a CUDA graph
+    B = 512
+    xb = torch.randn((B, max(H, QD, F)), device=dev, generator=g)
+    ob = {k: torch.empty((B, n), device=dev) for k, n in (("q", QD), ("k", KD), ("v", KD), ("o", H), ("gate", F),
+                                                          ("up", F), ("down", H))}
+
+    def chunk():
+        for lw in layers:
+            ctx.project_group_gemm([p(lw["q"]), p(lw["k"]), p(lw["v"])], [QD, KD, KD], H, p(xb), B,
+                                   [p(ob["q"]), p(ob["k"]), p(ob["v"])])
+            ctx.project_gemm(p(lw["o"]), H, QD, p(xb), B, p(ob["o"]))
+            ctx.project_group_gemm([p(lw["gate"]), p(lw["up"])], [F, F], H, p(xb), B, [p(ob["gate"]), p(ob["up"])])
+            ctx.project_gemm(p(lw["down"]), H, F, p(xb), B, p(ob["down"]))
+
+    for _ in range(2):
+        chunk()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        chunk()
+    ctx.set_stream(stream.cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 4
+    c0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    c1.record(stream)
+    torch.cuda.synchronize()
+    ctx.sync()
+    del graph
     ctx.close()
+    chunk_ms = c0.elapsed_time(c1) / reps
+    chunk_flops = 2 * B * L * (H * (QD + 2 * KD) + QD * H + 2 * F * H + F * H)
+    _, tf_peak, tf_kind = load_peaks()
+    chunk_tfs = chunk_flops / (chunk_ms * 1e-3) / 1e12
     layer_bytes = 2 * H * (QD + 2 * KD) + 2 * QD * H + 2 * 2 * F * H + 2 * F * H
     token_bytes = L * layer_bytes + 2 * VOCAB * H
     tok_ms = e0.elapsed_time(e1) / tokens
@@ -799,7 +837,17 @@ def projection_bench(args):
                          "peak_kind": peak_kind},
             "config": {"workload": "one decode token of Qwen3-0.6B's projections: 28 x (q/k/v, o, gate/up, down) + "
                                    "tied vocabulary head, batch 1, random FP16 weights",
-                       "arithmetic": "eight-lane dot of engine/core.cpp:119-147 (bit-exact)"}}
+                       "arithmetic": "eight-lane dot of engine/core.cpp:119-147 (bit-exact)"},
+            "prompt_chunk": {"metric": "prompt-chunk projections TFLOP/s (FP32-product FLOPs / device time)",
+                             "value": round(chunk_tfs, 1), "unit": "TFLOP/s", "ms_per_chunk": round(chunk_ms, 3),
+                             "rows": B, "launches_per_chunk": 8 * L,
+                             "timing": "one 512-row chunk's launches (split + GEMM per call) replayed from a CUDA graph",
+                             "roofline": {"bound": "tensor", "achieved": round(chunk_tfs, 1), "peak": tf_peak,
+                                          "unit": "TFLOP/s", "frac": round(chunk_tfs / tf_peak, 4),
+                                          "peak_kind": f"{tf_kind} bf16 burst; each product runs as two FP16 MMAs "
+                                                       "(input split in halves), so the tensor pipe does twice this"},
+                             "arithmetic": "tcgen05.mma FP16 x (FP16 hi + lo of the input), FP32 accumulation "
+                                           "(cblas_sgemm's role, engine/core.cpp:294)"}}
 
 
 def run_config5(args, nested=False, disagg=None, warmup=None, steps=None):

@@ -17,8 +17,11 @@
 // thread issuing the MMAs (M = 128 weight rows, N = 128 batch rows, K = 16 per instruction),
 // the accumulator in 128 TMEM columns, and an epilogue of all four warps (each its TMEM lane
 // quarter: 32 weight rows) that stores y with one coalesced 128-byte row segment per column.
-// Rows past a matrix's end, batch rows past the chunk and K past cols read as zero (TMA out of
-// bounds fill). Every wait is bounded (globaltimer, 2 s); on expiry the kernel records an error
+// Launches with fewer tiles than SMs (o_proj, down_proj: 1,024 rows) split K over blockIdx.z
+// and add the splits' partial sums in order in a second kernel. Rows past a matrix's end, batch
+// rows past the chunk and K past cols read as zero (TMA out of bounds fill). Each K step moves
+// 48 KB for 4.2 MFLOP of MMA (the split doubles both the input tiles and the MMAs), so the
+// kernel is bound by the operand traffic through L2, not by the tensor pipe. Every wait is bounded (globaltimer, 2 s); on expiry the kernel records an error
 // code, drains what it issued and frees its TMEM.
 #include <algorithm>
 
@@ -49,6 +52,10 @@ struct GemmArgs {
     float* y[MAX_PROJECT_MATS];       // [batch][rows[m]]
     int cols, b0, nb;                 // this chunk: batch rows [b0, b0 + nb)
     const float* inv_scale;           // [nb]: 2^-e of each split row
+    int ksplit;                       // K split over blockIdx.z (1: the tile writes y directly)
+    int total_rows;                   // sum of rows: the row pitch of `partial`
+    int row0_of[MAX_PROJECT_MATS];    // first row of each matrix in that concatenation
+    float* partial;                   // ksplit > 1: [ksplit][nb][total_rows] tile sums, summed in order
     int* error;
 };
 
@@ -98,7 +105,9 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
     while (m + 1 < a.n_mats && t >= a.tile0[m + 1]) ++m;
     const int r0 = (t - a.tile0[m]) * GM;                  // first weight row of the tile
     const int bt0 = blockIdx.y * GN;                       // first batch row of the tile (in the chunk)
-    const int KT = (a.cols + GK - 1) / GK;
+    const int KT_all = (a.cols + GK - 1) / GK;
+    const int kt_begin = (int)((long long)KT_all * blockIdx.z / a.ksplit);
+    const int KT = (int)((long long)KT_all * (blockIdx.z + 1) / a.ksplit) - kt_begin;   // this split's K steps
 
     if (tid == 0) {
         abort_flag = 0;
@@ -129,9 +138,10 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
             if (kt >= GSTAGES && !mbar_wait(&empty[s], ((kt / GSTAGES) - 1) & 1, abortp)) { fail(61); ok = false; break; }
             uint8_t* st = smem + s * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_3d(st, &maps.w[m], kt * GK, r0, 0, &full[s]);
-            tma_load_3d(st + W_TILE, &maps.xhi, kt * GK, bt0, 0, &full[s]);
-            tma_load_3d(st + W_TILE + X_TILE, &maps.xlo, kt * GK, bt0, 0, &full[s]);
+            const int kx = (kt_begin + kt) * GK;
+            tma_load_3d(st, &maps.w[m], kx, r0, 0, &full[s]);
+            tma_load_3d(st + W_TILE, &maps.xhi, kx, bt0, 0, &full[s]);
+            tma_load_3d(st + W_TILE + X_TILE, &maps.xlo, kx, bt0, 0, &full[s]);
             ++issued;
         }
         if (!ok) {                                         // drain this thread's copies (bounded)
@@ -164,6 +174,8 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
     const int r = r0 + warp * 32 + lane;
     const int rows_m = a.rows[m];
     float* y = a.y[m];
+    // split K: this split's sum goes to partial[z][b][row offset of m + r]
+    float* part = a.ksplit > 1 ? a.partial + (size_t)blockIdx.z * a.nb * a.total_rows : nullptr;
     #pragma unroll 1
     for (int c0 = 0; c0 < GN; c0 += 32) {
         uint32_t v[32];
@@ -173,7 +185,11 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
             #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const int b = bt0 + c0 + j;
-                if (b < a.nb) y[(size_t)(a.b0 + b) * rows_m + r] = __uint_as_float(v[j]) * a.inv_scale[b];
+                if (b < a.nb) {
+                    const float val = __uint_as_float(v[j]) * a.inv_scale[b];
+                    if (part) part[(size_t)b * a.total_rows + a.row0_of[m] + r] = val;
+                    else y[(size_t)(a.b0 + b) * rows_m + r] = val;
+                }
             }
         }
     }
@@ -182,6 +198,19 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, GN);
+    }
+}
+
+// y of a split-K launch: the splits' sums added in split order (deterministic).
+__global__ void __launch_bounds__(256) sum_splits_kernel(const GemmArgs a) {
+    const size_t n = (size_t)a.nb * a.total_rows;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v = a.partial[i];
+        for (int z = 1; z < a.ksplit; ++z) v += a.partial[(size_t)z * n + i];
+        const int b = (int)(i / a.total_rows), row = (int)(i - (size_t)b * a.total_rows);
+        int m = 0;
+        while (m + 1 < a.n_mats && row >= a.row0_of[m + 1]) ++m;
+        a.y[m][(size_t)(a.b0 + b) * a.rows[m] + (row - a.row0_of[m])] = v;
     }
 }
 
@@ -215,8 +244,12 @@ bool encode_rows(CUtensorMap* map, const void* base, int rows, int cols) {
 
 }  // namespace
 
+// Split-K partial sums share the scratch: room for 4 splits of a 512 x 2048 output.
+constexpr size_t PARTIAL_FLOATS_MAX = (size_t)4 * GEMM_CHUNK_ROWS * 2048;
+
 size_t project_gemm_scratch_bytes() {
-    return (size_t)GEMM_CHUNK_ROWS * GEMM_MAX_COLS * 2 * sizeof(__half) + GEMM_CHUNK_ROWS * sizeof(float) + 512;
+    return (size_t)GEMM_CHUNK_ROWS * GEMM_MAX_COLS * 2 * sizeof(__half) + GEMM_CHUNK_ROWS * sizeof(float) + 512 +
+           PARTIAL_FLOATS_MAX * sizeof(float);
 }
 
 int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStream_t s) {
@@ -233,7 +266,10 @@ int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStr
     a.cols = p.cols;
     a.error = error;
     a.tile0[0] = 0;
+    a.total_rows = 0;
     for (int m = 0; m < p.n_mats; ++m) {
+        a.row0_of[m] = a.total_rows;
+        a.total_rows += p.rows[m];
         a.rows[m] = p.rows[m];
         a.y[m] = p.y[m];
         a.tile0[m + 1] = a.tile0[m] + (p.rows[m] + GM - 1) / GM;
@@ -249,7 +285,21 @@ int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStr
         a.b0 = b0;
         a.nb = nb;
         a.inv_scale = inv;
-        project_gemm_kernel<<<dim3(a.tile0[p.n_mats], (nb + GN - 1) / GN), GTHREADS, GSMEM, s>>>(maps, a);
+        // Launches with fewer tiles than SMs split K (at least four K steps per split) so that
+        // more SMs stream the matrix; the partial sums are then added in split order.
+        const int tiles = a.tile0[p.n_mats] * ((nb + GN - 1) / GN), KT = (p.cols + GK - 1) / GK;
+        int sms = NUM_SMS_B200, dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        a.ksplit = std::max(1, std::min({4, sms / std::max(1, tiles), KT / 4}));
+        a.partial = reinterpret_cast<float*>(
+            reinterpret_cast<char*>(scratch) + (size_t)GEMM_CHUNK_ROWS * GEMM_MAX_COLS * 2 * sizeof(__half) +
+            GEMM_CHUNK_ROWS * sizeof(float) + 512);
+        if ((size_t)a.ksplit * nb * a.total_rows > PARTIAL_FLOATS_MAX) a.ksplit = 1;
+        project_gemm_kernel<<<dim3(a.tile0[p.n_mats], (nb + GN - 1) / GN, a.ksplit), GTHREADS, GSMEM, s>>>(maps, a);
+        if (a.ksplit > 1) {
+            const size_t n = (size_t)nb * a.total_rows;
+            sum_splits_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, (size_t)sms * 8), 256, 0, s>>>(a);
+        }
     }
     return 0;
 }
