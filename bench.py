@@ -1043,11 +1043,30 @@ def run_profile_case(args):
       append   28 layers x 1024-row append repeated 3 times
       decode_batch  8 sequences with the first 8 config-5 prompt lengths, then 3 batched fused
                decode steps (each launch reads ~1.8 GB of KV)
-      project  the vocabulary-head projection (151,936 x 1,024 FP16), 3 launches"""
+      project  the vocabulary-head projection (151,936 x 1,024 FP16), 3 launches
+      gemm     a 512-row prompt chunk's q/k/v group and down_proj on the tensor cores, twice"""
     import torch
     from fpga_qwen_b200 import qattn
     dev = torch.device("cuda", 0)
     stream = torch.cuda.current_stream(dev)
+    if args.profile_case == "gemm":
+        # a 512-row prompt chunk's q/k/v group and down_proj on the tensor cores, twice each
+        g = torch.Generator(device=dev).manual_seed(1)
+        ctx = qattn.Context(n_layers=1, context=256)
+        ctx.set_stream(stream.cuda_stream)
+        mats = [(torch.randn((r, c), device=dev, generator=g) * c ** -0.5).half()
+                for r, c in ((2048, 1024), (1024, 1024), (1024, 1024), (1024, 3072))]
+        x = torch.randn((512, 3072), device=dev, generator=g)
+        ys = [torch.empty((512, r), device=dev) for r in (2048, 1024, 1024, 1024)]
+        for _ in range(2):
+            ctx.project_group_gemm([m.data_ptr() for m in mats[:3]], [2048, 1024, 1024], 1024, x.data_ptr(), 512,
+                                   [y.data_ptr() for y in ys[:3]])
+            ctx.project_gemm(mats[3].data_ptr(), 1024, 3072, x.data_ptr(), 512, ys[3].data_ptr())
+        torch.cuda.synchronize()
+        ctx.sync()
+        ctx.close()
+        print(json.dumps({"profile_case": args.profile_case, "ok": True}))
+        return 0
     if args.profile_case == "project":
         # the tied vocabulary head at batch 1, three launches (311 MB of FP16 matrix each)
         g = torch.Generator(device=dev).manual_seed(1)
@@ -1145,7 +1164,8 @@ def main():
                          "stores inside them")
     ap.add_argument("--split-decode", action="store_true",
                     help="decode with qa_append + qa_attn_decode (two launches) instead of the fused qa_decode_step")
-    ap.add_argument("--profile-case", choices=["decode", "prefill", "append", "decode_batch", "project"], default=None,
+    ap.add_argument("--profile-case", choices=["decode", "prefill", "append", "decode_batch", "project", "gemm"],
+                    default=None,
                     help="run a small single-kernel case for ncu instead of the benchmark")
     args = ap.parse_args()
     if args.profile_case:

@@ -7,22 +7,28 @@
 // tcgen05.mma multiplies FP16 operands, so each input row is first split (split_rows_kernel):
 // scaled by a power of two 2^e that brings its largest magnitude to [2^13, 2^14) (exact), then
 // x_hi = fp16(x * 2^e) and x_lo = fp16(x * 2^e - x_hi), 22 bits of the row's significand in
-// two FP16 halves. Two MMAs per K step accumulate W x_hi + W x_lo in FP32 in TMEM and the
-// epilogue multiplies by 2^-e (exact). The products of FP16 weights with the 22-bit input are
+// two FP16 halves. W x_hi and W x_lo accumulate in FP32 in two TMEM column ranges and the
+// epilogue adds them and multiplies by 2^-e (exact). The products of FP16 weights with the 22-bit input are
 // exact; the result lies within FP32 accumulation rounding of the exact product, as sgemm's
 // does (its summation order is unpublished, so no sum order can be bit-identical to it).
 //
-// project_gemm_kernel: one CTA per 128-row x 128-batch output tile, full K: a 4-stage TMA ring
-// of 64-column K steps (W tile 16 KB, x_hi and x_lo tiles 16 KB each, 128-byte swizzle), one
-// thread issuing the MMAs (M = 128 weight rows, N = 128 batch rows, K = 16 per instruction),
-// the accumulator in 128 TMEM columns, and an epilogue of all four warps (each its TMEM lane
-// quarter: 32 weight rows) that stores y with one coalesced 128-byte row segment per column.
-// Launches with fewer tiles than SMs (o_proj, down_proj: 1,024 rows) split K over blockIdx.z
-// and add the splits' partial sums in order in a second kernel. Rows past a matrix's end, batch
-// rows past the chunk and K past cols read as zero (TMA out of bounds fill). Each K step moves
-// 48 KB for 4.2 MFLOP of MMA (the split doubles both the input tiles and the MMAs), so the
-// kernel is bound by the operand traffic through L2, not by the tensor pipe. Every wait is bounded (globaltimer, 2 s); on expiry the kernel records an error
-// code, drains what it issued and frees its TMEM.
+// project_gemm_kernel: persistent, one CTA per SM; work units are 128-row x 128-batch output
+// tiles (times the K splits), taken in an order where the units that share a weight tile run at
+// the same time, so each weight byte comes from HBM once. Warp 0 runs a 4-stage TMA ring of
+// 64-column K steps (W tile 16 KB, x_hi and x_lo tiles 16 KB each, 128-byte swizzle) across
+// units; warp 1 issues the MMAs (M = 128 weight rows, N = 256: the unit's 128 batch rows of
+// x_hi then of x_lo, K = 16 per instruction) into one of two 256-column TMEM accumulators;
+// warps 2-5 (each its TMEM lane quarter: 32 weight rows) empty the other accumulator at the
+// same time, so a unit's epilogue overlaps the next unit's K loop. Each epilogue warp stages
+// 32 x 32 sub-tiles in shared memory and writes them with TMA stores (ragged row counts take
+// plain coalesced stores). Launched as a programmatic dependent of the split kernel: set-up and
+// the first weight tiles overlap it.
+// Launches with fewer tiles than SMs (o_proj, down_proj: 1,024 rows) split K and add the
+// splits' partial sums in order in a second kernel. Rows past a matrix's end, batch rows past
+// the chunk and K past cols read as zero (TMA out of bounds fill). Each K step moves 48 KB
+// into shared memory for four 128 x 256 x 16 MMAs (512 tensor-pipe cycles). Every wait is
+// bounded (globaltimer, 2 s); on expiry the kernel records an error code, drains what it
+// issued and frees its TMEM.
 #include <algorithm>
 
 #include "qattn_common.cuh"
@@ -33,16 +39,21 @@ namespace {
 
 using namespace sm100;
 
-constexpr int GM = 128, GN = 128, GK = 64, GSTAGES = 4, GTHREADS = 128;
+constexpr int GM = 128, GN = 128, GK = 64, GSTAGES = 4;
+constexpr int EPI_WARP0 = 2, EPI_WARPS = 4, GTHREADS = 32 * (EPI_WARP0 + EPI_WARPS);
+constexpr int SUB = 32;                                  // epilogue sub-tile: 32 rows x 32 batch rows
 constexpr uint32_t W_TILE = GM * GK * 2;                 // 16 KB
 constexpr uint32_t X_TILE = GN * GK * 2;                 // 16 KB
 constexpr uint32_t STAGE_BYTES = W_TILE + 2 * X_TILE;    // 48 KB
-constexpr int GSMEM = GSTAGES * STAGE_BYTES + 1024 + 128;  // + alignment slack + barriers
+constexpr uint32_t STAGING_BYTES = EPI_WARPS * 2 * SUB * SUB * 4;   // two 4 KB sub-tiles per warp
+constexpr int GSMEM = GSTAGES * STAGE_BYTES + STAGING_BYTES + 1024 + 256;  // + alignment slack + barriers
 static_assert(GSMEM <= 232448, "shared memory per CTA");
 
 struct GemmMaps {
     CUtensorMap w[MAX_PROJECT_MATS];
     CUtensorMap xhi, xlo;
+    CUtensorMap y[MAX_PROJECT_MATS];  // FP32 [batch][rows[m]], boxes of 32 rows x 32 batch rows
+    CUtensorMap partial;              // FP32 [ksplit][nb][total_rows], boxes of 32 x 32 x 1
 };
 
 struct GemmArgs {
@@ -56,12 +67,14 @@ struct GemmArgs {
     int total_rows;                   // sum of rows: the row pitch of `partial`
     int row0_of[MAX_PROJECT_MATS];    // first row of each matrix in that concatenation
     float* partial;                   // ksplit > 1: [ksplit][nb][total_rows] tile sums, summed in order
+    int tma_store;                    // 1: sub-tiles leave through shared memory and TMA stores
     int* error;
 };
 
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ x, int cols, __half* hi, __half* lo,
                                                         float* inv_scale) {
     __shared__ float red[8];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // the GEMM may start its set-up
     const float* xr = x + (size_t)blockIdx.x * cols;
     float m = 0.f;
     for (int c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, fabsf(xr[c]));
@@ -89,36 +102,56 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
     if (threadIdx.x == 0) inv_scale[blockIdx.x] = ldexpf(1.f, -e);
 }
 
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
+// A work unit: matrix m, weight rows [r0, r0 + 128), batch rows [bt0, bt0 + 128) of the chunk,
+// K steps [kt0, kt0 + kt_n) of split z. Units sharing a weight tile are consecutive.
+struct Unit {
+    int m, r0, bt0, z, kt0, kt_n;
+};
+__device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u, int n_bt, int kt_all) {
+    Unit w;
+    const int by = u % n_bt, rest = u / n_bt;
+    w.z = rest % a.ksplit;
+    const int t = rest / a.ksplit;
+    w.m = 0;
+    while (w.m + 1 < a.n_mats && t >= a.tile0[w.m + 1]) ++w.m;
+    w.r0 = (t - a.tile0[w.m]) * GM;
+    w.bt0 = by * GN;
+    w.kt0 = (int)((long long)kt_all * w.z / a.ksplit);
+    w.kt_n = (int)((long long)kt_all * (w.z + 1) / a.ksplit) - w.kt0;
+    return w;
+}
+
 __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_constant__ GemmMaps maps,
                                                                   const GemmArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + GSTAGES * STAGE_BYTES);
+    float* staging = reinterpret_cast<float*>(smem + GSTAGES * STAGE_BYTES);   // [warp][2][SUB batch][SUB rows]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + GSTAGES * STAGE_BYTES + STAGING_BYTES);
     uint64_t* empty = full + GSTAGES;
-    uint64_t* done = empty + GSTAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* acc_full = empty + GSTAGES;                  // accumulator b holds a finished unit
+    uint64_t* acc_empty = acc_full + 2;                    // the epilogue has read accumulator b
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     __shared__ int abort_flag, never_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-    int m = 0;
-    const int t = blockIdx.x;
-    while (m + 1 < a.n_mats && t >= a.tile0[m + 1]) ++m;
-    const int r0 = (t - a.tile0[m]) * GM;                  // first weight row of the tile
-    const int bt0 = blockIdx.y * GN;                       // first batch row of the tile (in the chunk)
-    const int KT_all = (a.cols + GK - 1) / GK;
-    const int kt_begin = (int)((long long)KT_all * blockIdx.z / a.ksplit);
-    const int KT = (int)((long long)KT_all * (blockIdx.z + 1) / a.ksplit) - kt_begin;   // this split's K steps
+    const int n_bt = (a.nb + GN - 1) / GN;
+    const int units = a.tile0[a.n_mats] * n_bt * a.ksplit;
+    const int kt_all = (a.cols + GK - 1) / GK;
 
     if (tid == 0) {
         abort_flag = 0;
         never_abort = 0;
         for (int s = 0; s < GSTAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        mbar_init(done, 1);
+        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], 1); mbar_init(&acc_empty[b], EPI_WARPS); }
+        mbar_init(drain, 1);
         fence_mbar_init();
     }
-    if (warp == 1) { tmem_alloc(tmem_slot, GN); tmem_relinquish(); }
+    if (warp == 1) { tmem_alloc(tmem_slot, 4 * GN); tmem_relinquish(); }   // two accumulators of 2 x 128 columns
     if (warp == 0 && lane == 0) {
-        prefetch_tmap(&maps.w[m]);
+        for (int m = 0; m < a.n_mats; ++m) prefetch_tmap(&maps.w[m]);
         prefetch_tmap(&maps.xhi);
         prefetch_tmap(&maps.xlo);
     }
@@ -129,75 +162,153 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
     volatile int* abortp = &abort_flag;
     auto fail = [&](int code) { *abortp = 1; atomicCAS(a.error, 0, code); };
 
-    if (warp == 0 && lane == 0) {
-        // ---- TMA producer: K step kt into stage kt % GSTAGES ----
-        int issued = 0;
-        bool ok = true;
-        for (int kt = 0; kt < KT; ++kt) {
-            const int s = kt % GSTAGES;
-            if (kt >= GSTAGES && !mbar_wait(&empty[s], ((kt / GSTAGES) - 1) & 1, abortp)) { fail(61); ok = false; break; }
-            uint8_t* st = smem + s * STAGE_BYTES;
-            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            const int kx = (kt_begin + kt) * GK;
-            tma_load_3d(st, &maps.w[m], kx, r0, 0, &full[s]);
-            tma_load_3d(st + W_TILE, &maps.xhi, kx, bt0, 0, &full[s]);
-            tma_load_3d(st + W_TILE + X_TILE, &maps.xlo, kx, bt0, 0, &full[s]);
-            ++issued;
-        }
-        if (!ok) {                                         // drain this thread's copies (bounded)
-            for (int it = std::max(0, issued - GSTAGES); it < issued; ++it)
-                mbar_wait(&full[it % GSTAGES], (it / GSTAGES) & 1, &never_abort, 500000000ull);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // ---- MMA issuer: D (+)= W x_hi^T + W x_lo^T per 16-column K slice ----
-        const uint32_t idesc = idesc_f16_f32(GM, GN, false);
-        for (int kt = 0; kt < KT; ++kt) {
-            const int s = kt % GSTAGES;
-            if (!mbar_wait(&full[s], (kt / GSTAGES) & 1, abortp)) { fail(62); break; }
-            tc_fence_after();
-            const uint32_t wb = smem_u32(smem + s * STAGE_BYTES), hb = wb + W_TILE, lb = hb + X_TILE;
-            #pragma unroll
-            for (int ks = 0; ks < GK / 16; ++ks) {
-                mma_f16_ss(tmem, sw128_desc(wb + ks * 32, 16, 1024), sw128_desc(hb + ks * 32, 16, 1024), idesc,
-                           (kt > 0 || ks > 0) ? 1u : 0u);
-                mma_f16_ss(tmem, sw128_desc(wb + ks * 32, 16, 1024), sw128_desc(lb + ks * 32, 16, 1024), idesc, 1u);
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer: K step g (counted across units) into stage g % GSTAGES ----
+            // The first unit's first weight tiles are requested before waiting for the split
+            // kernel (the weights do not depend on it); its x halves after.
+            int pre = 0;
+            if ((int)blockIdx.x < units) {
+                const Unit w = unit_of(a, blockIdx.x, n_bt, kt_all);
+                pre = min(GSTAGES, w.kt_n);
+                for (int kt = 0; kt < pre; ++kt) {
+                    mbar_arrive_expect_tx(&full[kt], STAGE_BYTES);
+                    tma_load_3d(smem + kt * STAGE_BYTES, &maps.w[w.m], (w.kt0 + kt) * GK, w.r0, 0, &full[kt]);
+                }
             }
-            mma_commit(&empty[s]);                         // the stage is free once these MMAs complete
+            griddep_wait();
+            uint32_t g = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const Unit w = unit_of(a, u, n_bt, kt_all);
+                for (int kt = 0; kt < w.kt_n; ++kt, ++g) {
+                    const int s = g % GSTAGES;
+                    uint8_t* st = smem + s * STAGE_BYTES;
+                    const int kx = (w.kt0 + kt) * GK;
+                    if ((int)g >= pre) {
+                        if (g >= GSTAGES && !mbar_wait(&empty[s], ((g / GSTAGES) - 1) & 1, abortp)) {
+                            fail(61);
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                        tma_load_3d(st, &maps.w[w.m], kx, w.r0, 0, &full[s]);
+                    }
+                    tma_load_3d(st + W_TILE, &maps.xhi, kx, w.bt0, 0, &full[s]);
+                    tma_load_3d(st + W_TILE + X_TILE, &maps.xlo, kx, w.bt0, 0, &full[s]);
+                }
+            }
+            if (!ok) {                                     // drain this thread's copies (bounded)
+                const uint32_t issued = max(g, (uint32_t)pre);
+                for (uint32_t it = issued > GSTAGES ? issued - GSTAGES : 0; it < issued; ++it)
+                    mbar_wait(&full[it % GSTAGES], (it / GSTAGES) & 1, &never_abort, 500000000ull);
+            }
         }
-        mma_commit(done);                                  // every MMA issued: the accumulator is final
-    }
-    __syncwarp();
-
-    // ---- epilogue: warp w holds weight rows r0 + 32 w + lane; 32 batch columns per TMEM load ----
-    if (!mbar_wait(done, 0, &never_abort)) atomicCAS(a.error, 0, 63);
-    tc_fence_after();
-    const int r = r0 + warp * 32 + lane;
-    const int rows_m = a.rows[m];
-    float* y = a.y[m];
-    // split K: this split's sum goes to partial[z][b][row offset of m + r]
-    float* part = a.ksplit > 1 ? a.partial + (size_t)blockIdx.z * a.nb * a.total_rows : nullptr;
-    #pragma unroll 1
-    for (int c0 = 0; c0 < GN; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-        tmem_wait_ld();
-        if (r < rows_m) {
-            #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int b = bt0 + c0 + j;
-                if (b < a.nb) {
-                    const float val = __uint_as_float(v[j]) * a.inv_scale[b];
-                    if (part) part[(size_t)b * a.total_rows + a.row0_of[m] + r] = val;
-                    else y[(size_t)(a.b0 + b) * rows_m + r] = val;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer: [D_hi | D_lo] (+)= W [x_hi; x_lo]^T per 16-column K slice ----
+            // The x_lo tile follows the x_hi tile in the stage, so one N = 256 MMA takes both as
+            // a 256-row operand (128-row MMAs cannot be issued fast enough by one thread to keep
+            // the tensor pipe busy; 256-row ones can).
+            const uint32_t idesc = idesc_f16_f32(GM, 2 * GN, false);
+            uint32_t g = 0;
+            bool ok = true;
+            int i = 0;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++i) {
+                const Unit w = unit_of(a, u, n_bt, kt_all);
+                const int b = i & 1;
+                if (i >= 2 && !mbar_wait(&acc_empty[b], ((i >> 1) - 1) & 1, abortp)) { fail(64); break; }
+                tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(b * 2 * GN);
+                for (int kt = 0; kt < w.kt_n; ++kt, ++g) {
+                    const int s = g % GSTAGES;
+                    if (!mbar_wait(&full[s], (g / GSTAGES) & 1, abortp)) { fail(62); ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t wb = smem_u32(smem + s * STAGE_BYTES), xb = wb + W_TILE;
+                    #pragma unroll
+                    for (int ks = 0; ks < GK / 16; ++ks)
+                        mma_f16_ss(acc, sw128_desc(wb + ks * 32, 16, 1024), sw128_desc(xb + ks * 32, 16, 1024), idesc,
+                                   (kt > 0 || ks > 0) ? 1u : 0u);
+                    mma_commit(&empty[s]);                 // the stage is free once these MMAs complete
+                }
+                if (ok) mma_commit(&acc_full[b]);          // the unit's accumulator is final
+            }
+            mma_commit(drain);                             // every MMA issued has completed
+            mbar_wait(drain, 0, &never_abort);
+        }
+    } else {
+        // ---- epilogue: warp holds weight rows r0 + 32 q + lane (its TMEM lane quarter q) ----
+        const int q = warp & 3, ew = warp - EPI_WARP0;
+        float* stage_w = staging + ew * 2 * SUB * SUB;
+        bool waited = false;
+        uint32_t sub = 0;                                  // sub-tiles stored by this warp
+        int i = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
+            const Unit w = unit_of(a, u, n_bt, kt_all);
+            const int b = i & 1;
+            if (!mbar_wait(&acc_full[b], (i >> 1) & 1, abortp)) { fail(63); break; }
+            tc_fence_after();
+            if (!waited) { griddep_wait(); waited = true; }   // inv_scale is the split kernel's output
+            const int nb = a.nb, rows_m = a.rows[w.m], r = w.r0 + 32 * q + lane;
+            const bool row_ok = r < rows_m;
+            // plain-store path: y[b0 + b][r], or with split K partial[z][b][row offset of m + r]
+            float* out;
+            size_t pitch;
+            if (a.ksplit > 1) {
+                pitch = a.total_rows;
+                out = a.partial + (size_t)w.z * nb * pitch + a.row0_of[w.m] + r;
+            } else {
+                pitch = rows_m;
+                out = a.y[w.m] + (size_t)a.b0 * pitch + r;
+            }
+            const uint32_t acc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * 2 * GN);
+            #pragma unroll 1
+            for (int c0 = 0; c0 < GN; c0 += SUB, ++sub) {
+                uint32_t v[32], x[32];
+                tmem_ld32(acc + c0, v);
+                tmem_ld32(acc + GN + c0, x);
+                // each lane loads one batch row's 2^-e; the loop broadcasts it (a load per element
+                // would wait behind the stores, which the compiler cannot prove do not alias it)
+                const int bl = w.bt0 + c0 + lane;
+                const float my_inv = bl < nb ? a.inv_scale[bl] : 0.f;
+                tmem_wait_ld();
+                if (c0 + SUB == GN) {                      // the accumulator is read: the MMA warp may reuse it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[b]);
+                }
+                if (a.tma_store) {
+                    float* sb = stage_w + (sub & 1) * SUB * SUB;
+                    if (lane == 0 && sub >= 2) bulk_wait_read_1();   // this buffer's previous store has read it
+                    __syncwarp();
+                    #pragma unroll
+                    for (int j = 0; j < SUB; ++j)
+                        sb[j * SUB + lane] = (__uint_as_float(v[j]) + __uint_as_float(x[j])) * __shfl_sync(0xffffffffu, my_inv, j);
+                    fence_proxy_async_smem();              // the sub-tile is visible to the TMA unit
+                    __syncwarp();
+                    if (lane == 0) {                       // rows and batch rows outside the extent are clipped
+                        if (a.ksplit > 1) tma_store_3d(&maps.partial, sb, a.row0_of[w.m] + w.r0 + 32 * q, w.bt0 + c0, w.z);
+                        else tma_store_3d(&maps.y[w.m], sb, w.r0 + 32 * q, a.b0 + w.bt0 + c0, 0);
+                        bulk_commit();
+                    }
+                } else {
+                    #pragma unroll
+                    for (int j = 0; j < SUB; ++j) {
+                        const float sc = __shfl_sync(0xffffffffu, my_inv, j);
+                        const int bb = w.bt0 + c0 + j;
+                        if (row_ok && bb < nb) out[(size_t)bb * pitch] = (__uint_as_float(v[j]) + __uint_as_float(x[j])) * sc;
+                    }
                 }
             }
         }
+        if (lane == 0) bulk_wait_read_all();               // shared memory outlives this warp's stores
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, GN);
+        tmem_dealloc(tmem, 4 * GN);
     }
 }
 
@@ -229,6 +340,18 @@ EncodeTiledFn encoder() {
     return fn;
 }
 
+// FP32 output [d2][d1][d0] (innermost d0), boxes of 32 x 32 x 1, no swizzle.
+bool encode_out(CUtensorMap* map, void* base, int d0, int d1, int d2) {
+    EncodeTiledFn enc = encoder();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+    cuuint64_t strides[2] = {(cuuint64_t)d0 * 4, (cuuint64_t)d0 * 4 * d1};
+    cuuint32_t box[3] = {SUB, SUB, 1}, elem[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // FP16 matrix [rows][cols] (row stride cols): boxes of 64 columns x 128 rows, 128-byte swizzle,
 // zero fill outside.
 bool encode_rows(CUtensorMap* map, const void* base, int rows, int cols) {
@@ -255,9 +378,12 @@ size_t project_gemm_scratch_bytes() {
 int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStream_t s) {
     if (p.cols > GEMM_MAX_COLS || !scratch) return -1;
     static bool attr = false;
+    static int sms = NUM_SMS_B200;
     if (!attr) {
         if (cudaFuncSetAttribute(project_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GSMEM) != cudaSuccess)
             return -2;
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         attr = true;
     }
     GemmMaps maps;
@@ -267,6 +393,9 @@ int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStr
     a.error = error;
     a.tile0[0] = 0;
     a.total_rows = 0;
+    // TMA stores need 16-byte row pitches and aligned bases, and (for the split-K partial
+    // rows, where the matrices sit side by side) tiles that end at their matrix's end
+    bool tma_store = true;
     for (int m = 0; m < p.n_mats; ++m) {
         a.row0_of[m] = a.total_rows;
         a.total_rows += p.rows[m];
@@ -274,6 +403,8 @@ int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStr
         a.y[m] = p.y[m];
         a.tile0[m + 1] = a.tile0[m] + (p.rows[m] + GM - 1) / GM;
         if (!encode_rows(&maps.w[m], p.w[m], p.rows[m], p.cols)) return -3;
+        tma_store = tma_store && p.rows[m] % GM == 0 && reinterpret_cast<uintptr_t>(p.y[m]) % 16 == 0 &&
+                    encode_out(&maps.y[m], p.y[m], p.rows[m], p.batch, 1);
     }
     for (int b0 = 0; b0 < p.batch; b0 += GEMM_CHUNK_ROWS) {
         const int nb = std::min(GEMM_CHUNK_ROWS, p.batch - b0);
@@ -288,14 +419,24 @@ int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStr
         // Launches with fewer tiles than SMs split K (at least four K steps per split) so that
         // more SMs stream the matrix; the partial sums are then added in split order.
         const int tiles = a.tile0[p.n_mats] * ((nb + GN - 1) / GN), KT = (p.cols + GK - 1) / GK;
-        int sms = NUM_SMS_B200, dev = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         a.ksplit = std::max(1, std::min({4, sms / std::max(1, tiles), KT / 4}));
         a.partial = reinterpret_cast<float*>(
             reinterpret_cast<char*>(scratch) + (size_t)GEMM_CHUNK_ROWS * GEMM_MAX_COLS * 2 * sizeof(__half) +
             GEMM_CHUNK_ROWS * sizeof(float) + 512);
         if ((size_t)a.ksplit * nb * a.total_rows > PARTIAL_FLOATS_MAX) a.ksplit = 1;
-        project_gemm_kernel<<<dim3(a.tile0[p.n_mats], (nb + GN - 1) / GN, a.ksplit), GTHREADS, GSMEM, s>>>(maps, a);
+        a.tma_store = tma_store && (a.ksplit == 1 || encode_out(&maps.partial, a.partial, a.total_rows, nb, a.ksplit));
+        // persistent: one CTA per SM at most, launched as a programmatic dependent of the split
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)std::min(tiles * a.ksplit, sms));
+        cfg.blockDim = dim3(GTHREADS);
+        cfg.dynamicSmemBytes = GSMEM;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, project_gemm_kernel, maps, a) != cudaSuccess) return -4;
         if (a.ksplit > 1) {
             const size_t n = (size_t)nb * a.total_rows;
             sum_splits_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, (size_t)sms * 8), 256, 0, s>>>(a);
