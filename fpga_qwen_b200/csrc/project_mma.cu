@@ -23,8 +23,10 @@
 // 32 x 32 sub-tiles in shared memory and writes them with TMA stores (ragged row counts take
 // plain coalesced stores). Launched as a programmatic dependent of the split kernel: set-up and
 // the first weight tiles overlap it.
-// Launches with fewer tiles than SMs (o_proj, down_proj: 1,024 rows) split K and add the
-// splits' partial sums in order in a second kernel. Rows past a matrix's end, batch rows past
+// Launches with fewer tiles than SMs (o_proj, down_proj: 1,024 rows) split K: the splits of a
+// tile form one thread-block cluster, each leaves its scaled partial tile in its shared memory,
+// and after a cluster barrier each CTA adds a share of the tile's batch rows over the peers'
+// shared memory in split order (deterministic) and stores y. Rows past a matrix's end, batch rows past
 // the chunk and K past cols read as zero (TMA out of bounds fill). Each K step moves 48 KB
 // into shared memory for four 128 x 256 x 16 MMAs (512 tensor-pipe cycles). Every wait is
 // bounded (globaltimer, 2 s); on expiry the kernel records an error code, drains what it
@@ -53,7 +55,6 @@ struct GemmMaps {
     CUtensorMap w[MAX_PROJECT_MATS];
     CUtensorMap xhi, xlo;
     CUtensorMap y[MAX_PROJECT_MATS];  // FP32 [batch][rows[m]], boxes of 32 rows x 32 batch rows
-    CUtensorMap partial;              // FP32 [ksplit][nb][total_rows], boxes of 32 x 32 x 1
 };
 
 struct GemmArgs {
@@ -63,10 +64,7 @@ struct GemmArgs {
     float* y[MAX_PROJECT_MATS];       // [batch][rows[m]]
     int cols, b0, nb;                 // this chunk: batch rows [b0, b0 + nb)
     const float* inv_scale;           // [nb]: 2^-e of each split row
-    int ksplit;                       // K split over blockIdx.z (1: the tile writes y directly)
-    int total_rows;                   // sum of rows: the row pitch of `partial`
-    int row0_of[MAX_PROJECT_MATS];    // first row of each matrix in that concatenation
-    float* partial;                   // ksplit > 1: [ksplit][nb][total_rows] tile sums, summed in order
+    int ksplit;                       // K splits per tile, one cluster of ksplit CTAs per tile when > 1
     int tma_store;                    // 1: sub-tiles leave through shared memory and TMA stores
     int* error;
 };
@@ -104,17 +102,37 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Every thread of every CTA of the cluster arrives; shared-memory writes before it are visible
+// to the peers' reads after it.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_peer(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
 
 // A work unit: matrix m, weight rows [r0, r0 + 128), batch rows [bt0, bt0 + 128) of the chunk,
-// K steps [kt0, kt0 + kt_n) of split z. Units sharing a weight tile are consecutive.
+// K steps [kt0, kt0 + kt_n) of split z. Units sharing a weight tile are consecutive, the splits
+// of one output tile first (they form a cluster: split z is cluster rank z).
 struct Unit {
     int m, r0, bt0, z, kt0, kt_n;
 };
 __device__ __forceinline__ Unit unit_of(const GemmArgs& a, int u, int n_bt, int kt_all) {
     Unit w;
-    const int by = u % n_bt, rest = u / n_bt;
-    w.z = rest % a.ksplit;
-    const int t = rest / a.ksplit;
+    w.z = u % a.ksplit;
+    const int rest = u / a.ksplit, by = rest % n_bt, t = rest / n_bt;
     w.m = 0;
     while (w.m + 1 < a.n_mats && t >= a.tile0[w.m + 1]) ++w.m;
     w.r0 = (t - a.tile0[w.m]) * GM;
@@ -240,44 +258,49 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
         // ---- epilogue: warp holds weight rows r0 + 32 q + lane (its TMEM lane quarter q) ----
         const int q = warp & 3, ew = warp - EPI_WARP0;
         float* stage_w = staging + ew * 2 * SUB * SUB;
-        bool waited = false;
+        griddep_wait();                                    // inv_scale is the split kernel's output
         uint32_t sub = 0;                                  // sub-tiles stored by this warp
         int i = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
             const Unit w = unit_of(a, u, n_bt, kt_all);
             const int b = i & 1;
+            // the unit's 2^-e of batch row bt0 + 32 k + lane, loaded while the K loop runs
+            float inv[GN / SUB];
+            #pragma unroll
+            for (int k = 0; k < GN / SUB; ++k) {
+                const int bl = w.bt0 + SUB * k + lane;
+                inv[k] = bl < a.nb ? a.inv_scale[bl] : 0.f;
+            }
             if (!mbar_wait(&acc_full[b], (i >> 1) & 1, abortp)) { fail(63); break; }
             tc_fence_after();
-            if (!waited) { griddep_wait(); waited = true; }   // inv_scale is the split kernel's output
             const int nb = a.nb, rows_m = a.rows[w.m], r = w.r0 + 32 * q + lane;
             const bool row_ok = r < rows_m;
-            // plain-store path: y[b0 + b][r], or with split K partial[z][b][row offset of m + r]
-            float* out;
-            size_t pitch;
-            if (a.ksplit > 1) {
-                pitch = a.total_rows;
-                out = a.partial + (size_t)w.z * nb * pitch + a.row0_of[w.m] + r;
-            } else {
-                pitch = rows_m;
-                out = a.y[w.m] + (size_t)a.b0 * pitch + r;
-            }
+            // plain-store path: y[b0 + b][r]
+            const size_t pitch = rows_m;
+            float* out = a.y[w.m] + (size_t)a.b0 * pitch + r;
+            // split K: this split's tile [128 batch rows][128 weight rows] in shared memory (the
+            // stage buffers: the unit's MMAs, the last readers, have completed)
+            float* part = reinterpret_cast<float*>(smem);
             const uint32_t acc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * 2 * GN);
-            #pragma unroll 1
-            for (int c0 = 0; c0 < GN; c0 += SUB, ++sub) {
+            #pragma unroll
+            for (int k = 0; k < GN / SUB; ++k, ++sub) {
+                const int c0 = k * SUB;
                 uint32_t v[32], x[32];
                 tmem_ld32(acc + c0, v);
                 tmem_ld32(acc + GN + c0, x);
-                // each lane loads one batch row's 2^-e; the loop broadcasts it (a load per element
-                // would wait behind the stores, which the compiler cannot prove do not alias it)
-                const int bl = w.bt0 + c0 + lane;
-                const float my_inv = bl < nb ? a.inv_scale[bl] : 0.f;
+                const float my_inv = inv[k];                // broadcast below, one batch row per j
                 tmem_wait_ld();
                 if (c0 + SUB == GN) {                      // the accumulator is read: the MMA warp may reuse it
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[b]);
                 }
-                if (a.tma_store) {
+                if (a.ksplit > 1) {
+                    #pragma unroll
+                    for (int j = 0; j < SUB; ++j)
+                        part[(c0 + j) * GM + 32 * q + lane] =
+                            (__uint_as_float(v[j]) + __uint_as_float(x[j])) * __shfl_sync(0xffffffffu, my_inv, j);
+                } else if (a.tma_store) {
                     float* sb = stage_w + (sub & 1) * SUB * SUB;
                     if (lane == 0 && sub >= 2) bulk_wait_read_1();   // this buffer's previous store has read it
                     __syncwarp();
@@ -287,8 +310,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
                     fence_proxy_async_smem();              // the sub-tile is visible to the TMA unit
                     __syncwarp();
                     if (lane == 0) {                       // rows and batch rows outside the extent are clipped
-                        if (a.ksplit > 1) tma_store_3d(&maps.partial, sb, a.row0_of[w.m] + w.r0 + 32 * q, w.bt0 + c0, w.z);
-                        else tma_store_3d(&maps.y[w.m], sb, w.r0 + 32 * q, a.b0 + w.bt0 + c0, 0);
+                        tma_store_3d(&maps.y[w.m], sb, w.r0 + 32 * q, a.b0 + w.bt0 + c0, 0);
                         bulk_commit();
                     }
                 } else {
@@ -304,24 +326,35 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
         if (lane == 0) bulk_wait_read_all();               // shared memory outlives this warp's stores
         __syncwarp();
     }
+    if (a.ksplit > 1) {
+        // one unit per CTA (the launch has one CTA per unit): sum the splits' tiles in split
+        // order over the cluster's shared memory; this CTA takes batch rows [z per, (z + 1) per)
+        __syncwarp();
+        cluster_sync_all();
+        const Unit w = unit_of(a, blockIdx.x, n_bt, kt_all);
+        const uint32_t z = cluster_rank();
+        const int per = (GN + a.ksplit - 1) / a.ksplit, bb0 = (int)z * per, bb1 = min(GN, bb0 + per);
+        const int rows_m = a.rows[w.m];
+        uint32_t peer[4];
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) peer[k] = peer_addr(smem, (uint32_t)min(k, a.ksplit - 1));
+        for (int e = tid; e < (bb1 - bb0) * GM; e += GTHREADS) {
+            const int bl = bb0 + e / GM, row = e % GM;
+            const uint32_t off = (uint32_t)(bl * GM + row) * 4u;
+            float sum = ld_peer(peer[0] + off);
+            #pragma unroll
+            for (int k = 1; k < 4; ++k)
+                if (k < a.ksplit) sum += ld_peer(peer[k] + off);
+            const int bg = w.bt0 + bl, r = w.r0 + row;
+            if (bg < a.nb && r < rows_m) a.y[w.m][(size_t)(a.b0 + bg) * rows_m + r] = sum;
+        }
+        cluster_sync_all();                                // no CTA leaves while a peer reads its tile
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 4 * GN);
-    }
-}
-
-// y of a split-K launch: the splits' sums added in split order (deterministic).
-__global__ void __launch_bounds__(256) sum_splits_kernel(const GemmArgs a) {
-    const size_t n = (size_t)a.nb * a.total_rows;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        float v = a.partial[i];
-        for (int z = 1; z < a.ksplit; ++z) v += a.partial[(size_t)z * n + i];
-        const int b = (int)(i / a.total_rows), row = (int)(i - (size_t)b * a.total_rows);
-        int m = 0;
-        while (m + 1 < a.n_mats && row >= a.row0_of[m + 1]) ++m;
-        a.y[m][(size_t)(a.b0 + b) * a.rows[m] + (row - a.row0_of[m])] = v;
     }
 }
 
@@ -367,12 +400,8 @@ bool encode_rows(CUtensorMap* map, const void* base, int rows, int cols) {
 
 }  // namespace
 
-// Split-K partial sums share the scratch: room for 4 splits of a 512 x 2048 output.
-constexpr size_t PARTIAL_FLOATS_MAX = (size_t)4 * GEMM_CHUNK_ROWS * 2048;
-
 size_t project_gemm_scratch_bytes() {
-    return (size_t)GEMM_CHUNK_ROWS * GEMM_MAX_COLS * 2 * sizeof(__half) + GEMM_CHUNK_ROWS * sizeof(float) + 512 +
-           PARTIAL_FLOATS_MAX * sizeof(float);
+    return (size_t)GEMM_CHUNK_ROWS * GEMM_MAX_COLS * 2 * sizeof(__half) + GEMM_CHUNK_ROWS * sizeof(float) + 512;
 }
 
 int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStream_t s) {
@@ -392,13 +421,9 @@ int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStr
     a.cols = p.cols;
     a.error = error;
     a.tile0[0] = 0;
-    a.total_rows = 0;
-    // TMA stores need 16-byte row pitches and aligned bases, and (for the split-K partial
-    // rows, where the matrices sit side by side) tiles that end at their matrix's end
+    // TMA stores need 16-byte row pitches, aligned bases and tiles that end at their matrix's end
     bool tma_store = true;
     for (int m = 0; m < p.n_mats; ++m) {
-        a.row0_of[m] = a.total_rows;
-        a.total_rows += p.rows[m];
         a.rows[m] = p.rows[m];
         a.y[m] = p.y[m];
         a.tile0[m + 1] = a.tile0[m] + (p.rows[m] + GM - 1) / GM;
@@ -417,30 +442,26 @@ int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStr
         a.nb = nb;
         a.inv_scale = inv;
         // Launches with fewer tiles than SMs split K (at least four K steps per split) so that
-        // more SMs stream the matrix; the partial sums are then added in split order.
+        // more SMs stream the matrix; then every CTA has one unit and each tile's splits form a
+        // cluster that adds them. Otherwise persistent: one CTA per SM at most.
         const int tiles = a.tile0[p.n_mats] * ((nb + GN - 1) / GN), KT = (p.cols + GK - 1) / GK;
         a.ksplit = std::max(1, std::min({4, sms / std::max(1, tiles), KT / 4}));
-        a.partial = reinterpret_cast<float*>(
-            reinterpret_cast<char*>(scratch) + (size_t)GEMM_CHUNK_ROWS * GEMM_MAX_COLS * 2 * sizeof(__half) +
-            GEMM_CHUNK_ROWS * sizeof(float) + 512);
-        if ((size_t)a.ksplit * nb * a.total_rows > PARTIAL_FLOATS_MAX) a.ksplit = 1;
-        a.tma_store = tma_store && (a.ksplit == 1 || encode_out(&maps.partial, a.partial, a.total_rows, nb, a.ksplit));
-        // persistent: one CTA per SM at most, launched as a programmatic dependent of the split
+        a.tma_store = tma_store ? 1 : 0;
         cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3((unsigned)std::min(tiles * a.ksplit, sms));
+        cfg.gridDim = dim3((unsigned)(a.ksplit > 1 ? tiles * a.ksplit : std::min(tiles, sms)));
         cfg.blockDim = dim3(GTHREADS);
         cfg.dynamicSmemBytes = GSMEM;
         cfg.stream = s;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // overlaps the split kernel
         attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = (unsigned)a.ksplit;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = a.ksplit > 1 ? 2 : 1;
         if (cudaLaunchKernelEx(&cfg, project_gemm_kernel, maps, a) != cudaSuccess) return -4;
-        if (a.ksplit > 1) {
-            const size_t n = (size_t)nb * a.total_rows;
-            sum_splits_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, (size_t)sms * 8), 256, 0, s>>>(a);
-        }
     }
     return 0;
 }
