@@ -69,33 +69,48 @@ struct GemmArgs {
     int* error;
 };
 
+// One CTA per input row; the row stays in registers (PER elements per thread, cols <= 256 PER)
+// between the max and the split. Rows whose largest magnitude is below 2^-112 take e = 126 (the
+// largest exponent whose 2^-e is a normal float): they keep fewer than 22 bits.
+template <int PER>
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ x, int cols, __half* hi, __half* lo,
                                                         float* inv_scale) {
     __shared__ float red[8];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // the GEMM may start its set-up
     const float* xr = x + (size_t)blockIdx.x * cols;
+    float v[PER];
     float m = 0.f;
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, fabsf(xr[c]));
+    #pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        v[i] = c < cols ? __ldg(xr + c) : 0.f;
+        m = fmaxf(m, fabsf(v[i]));
+    }
     #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
     __syncthreads();
     m = red[0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+    #pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
     int e = 0;
     if (m > 0.f && m <= 3.0e38f) {                       // finite, non-zero: bring the max to [2^13, 2^14)
         int ex;
         frexpf(m, &ex);                                   // m = f * 2^ex, f in [0.5, 1)
-        e = 14 - ex;
+        e = min(14 - ex, 126);
     }
     const float s = ldexpf(1.f, e);
     __half* h = hi + (size_t)blockIdx.x * cols;
     __half* l = lo + (size_t)blockIdx.x * cols;
-    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-        const float v = xr[c] * s;
-        const __half vh = __float2half_rn(v);
-        h[c] = vh;
-        l[c] = __float2half_rn(v - __half2float(vh));
+    #pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        if (c < cols) {
+            const float t = v[i] * s;
+            const __half th = __float2half_rn(t);
+            h[c] = th;
+            l[c] = __float2half_rn(t - __half2float(th));
+        }
     }
     if (threadIdx.x == 0) inv_scale[blockIdx.x] = ldexpf(1.f, -e);
 }
@@ -117,9 +132,12 @@ __device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
     return r;
 }
-__device__ __forceinline__ float ld_peer(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+// No memory clobber: the loads may overlap one another and the global stores between them;
+// volatile keeps them after the cluster barrier.
+__device__ __forceinline__ float4 ld_peer4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
     return v;
 }
 
@@ -338,15 +356,41 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
         uint32_t peer[4];
         #pragma unroll
         for (int k = 0; k < 4; ++k) peer[k] = peer_addr(smem, (uint32_t)min(k, a.ksplit - 1));
-        for (int e = tid; e < (bb1 - bb0) * GM; e += GTHREADS) {
-            const int bl = bb0 + e / GM, row = e % GM;
-            const uint32_t off = (uint32_t)(bl * GM + row) * 4u;
-            float sum = ld_peer(peer[0] + off);
+        // four consecutive weight rows per thread and step, three steps' loads in flight
+        const int n4 = (bb1 - bb0) * (GM / 4);
+        float* ym = a.y[w.m];
+        for (int e0 = tid; e0 < n4; e0 += 3 * GTHREADS) {
+            float4 sum[3];
             #pragma unroll
-            for (int k = 1; k < 4; ++k)
-                if (k < a.ksplit) sum += ld_peer(peer[k] + off);
-            const int bg = w.bt0 + bl, r = w.r0 + row;
-            if (bg < a.nb && r < rows_m) a.y[w.m][(size_t)(a.b0 + bg) * rows_m + r] = sum;
+            for (int h = 0; h < 3; ++h) {
+                const int e = e0 + h * GTHREADS;
+                if (e < n4) {
+                    const uint32_t off = (uint32_t)((bb0 + e / (GM / 4)) * GM + 4 * (e % (GM / 4))) * 4u;
+                    sum[h] = ld_peer4(peer[0] + off);
+                    #pragma unroll
+                    for (int k = 1; k < 4; ++k)
+                        if (k < a.ksplit) {
+                            const float4 t = ld_peer4(peer[k] + off);
+                            sum[h].x += t.x; sum[h].y += t.y; sum[h].z += t.z; sum[h].w += t.w;
+                        }
+                }
+            }
+            #pragma unroll
+            for (int h = 0; h < 3; ++h) {
+                const int e = e0 + h * GTHREADS;
+                if (e >= n4) continue;
+                const int bg = w.bt0 + bb0 + e / (GM / 4), r = w.r0 + 4 * (e % (GM / 4));
+                if (bg >= a.nb) continue;
+                float* yr = ym + (size_t)(a.b0 + bg) * rows_m + r;
+                if (a.tma_store) {                         // rows_m % 128 == 0, 16-byte aligned y
+                    *reinterpret_cast<float4*>(yr) = sum[h];
+                } else {
+                    const float t[4] = {sum[h].x, sum[h].y, sum[h].z, sum[h].w};
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (r + i < rows_m) yr[i] = t[i];
+                }
+            }
         }
         cluster_sync_all();                                // no CTA leaves while a peer reads its tile
     }
@@ -437,7 +481,11 @@ int launch_project_gemm(const ProjectArgs& p, void* scratch, int* error, cudaStr
         __half* lo = hi + (((size_t)nb * p.cols + 127) & ~size_t(127));
         float* inv = reinterpret_cast<float*>(lo + (((size_t)nb * p.cols + 127) & ~size_t(127)));
         if (!encode_rows(&maps.xhi, hi, nb, p.cols) || !encode_rows(&maps.xlo, lo, nb, p.cols)) return -3;
-        split_rows_kernel<<<nb, 256, 0, s>>>(p.x + (size_t)b0 * p.cols, p.cols, hi, lo, inv);
+        const float* xc = p.x + (size_t)b0 * p.cols;
+        if (p.cols <= 1024) split_rows_kernel<4><<<nb, 256, 0, s>>>(xc, p.cols, hi, lo, inv);
+        else if (p.cols <= 2048) split_rows_kernel<8><<<nb, 256, 0, s>>>(xc, p.cols, hi, lo, inv);
+        else if (p.cols <= 4096) split_rows_kernel<16><<<nb, 256, 0, s>>>(xc, p.cols, hi, lo, inv);
+        else split_rows_kernel<32><<<nb, 256, 0, s>>>(xc, p.cols, hi, lo, inv);
         a.b0 = b0;
         a.nb = nb;
         a.inv_scale = inv;

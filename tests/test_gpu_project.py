@@ -164,14 +164,16 @@ def test_gemm_batched_prompt_rows(rows, cols, batch):
 
 def test_gemm_rows_of_extreme_magnitude_and_host_buffers():
     """Input rows scaled by 1e-20 and 1e20 keep full relative precision (each row is brought to a
-    fixed range by an exact power of two before the FP16 split); the host-buffer form gives the
-    device form's results."""
+    fixed range by an exact power of two before the FP16 split); a row of FP32 subnormals (whose
+    power of two would overflow) stays finite; the host-buffer form gives the device form's
+    results."""
     rng = np.random.default_rng(12)
     w = _matrix(rng, 1024, 1024)
     x = rng.standard_normal((40, 1024)).astype(np.float32)
     x[3] *= 1e-20
     x[7] *= 1e20
     x[11] = 0.0
+    x[15] *= np.float32(1e-39)
     wd = torch.from_numpy(w.view(np.int16)).cuda()
     dev = _ctx()
     y = torch.empty((40, 1024), device="cuda")
@@ -179,7 +181,7 @@ def test_gemm_rows_of_extreme_magnitude_and_host_buffers():
     torch.cuda.synchronize()
     got = y.cpu().numpy()
     _gemm_check([got], x, [w])
-    assert (got[11] == 0).all()
+    assert (got[11] == 0).all() and np.isfinite(got).all()
     host = _ctx(io_host=1)
     yh = np.full((40, 1024), np.nan, np.float32)
     host.project_gemm(wd.data_ptr(), 1024, 1024, x.ctypes.data, 40, yh.ctypes.data)
