@@ -368,6 +368,12 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         const uint32_t idesc_qk = idesc_f16_f32(BM, BN, false);
         const uint32_t idesc_pv = idesc_f16_f32(BM, D, true);
         const uint32_t q_addr = smem_u32(smem + OFF_Q), ring_addr = smem_u32(smem + OFF_RING);
+        // Descriptors as a fixed high word (stride offset, version, swizzle) and a low word
+        // stepped by 32-bit adds (start address >> 4 in bits 0-13: shared addresses stay below
+        // 256 KB, so the field never carries): cheaper to issue than rebuilding both words.
+        const uint64_t dq = sw128_desc(q_addr, 16, 1024);
+        const uint32_t d_hi = (uint32_t)(dq >> 32), lo_q = (uint32_t)dq;
+        const uint32_t lo_k = (uint32_t)sw128_desc(ring_addr, 16, 1024), lo_v = (uint32_t)sw128_desc(ring_addr, 16384, 1024);
         bool ok = true;
         auto wait_item = [&](int it) {                   // ring item it has landed
             return mbar_wait(&bar[B_FULL0 + it % RING], (it / RING) & 1, abortp);
@@ -377,23 +383,23 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             __syncwarp();
         };
         auto issue_qk = [&](int it, int h) {
-            const uint32_t kb = ring_addr + (it % RING) * TILE_BYTES, qb = q_addr + h * 32768;
+            const uint32_t kb = lo_k + (uint32_t)((it % RING) * TILE_BYTES >> 4), qb = lo_q + (uint32_t)(h * 32768 >> 4);
             if (lane == 0) {
                 #pragma unroll
                 for (int s = 0; s < 8; ++s) {
-                    const uint32_t off = (s >> 2) * 16384 + (s & 3) * 32;
-                    mma_f16_ss(tmem + h * 128, sw128_desc(qb + off, 16, 1024), sw128_desc(kb + off, 16, 1024), idesc_qk, s > 0);
+                    const uint32_t off = ((s >> 2) * 16384 + (s & 3) * 32) >> 4;
+                    mma_f16_ss(tmem + h * 128, desc_of(qb + off, d_hi), desc_of(kb + off, d_hi), idesc_qk, s > 0);
                 }
                 mma_commit(&bar[B_SF0 + h]);
             }
             __syncwarp();
         };
         auto issue_pv = [&](int it, int h, bool first, bool last) {   // A = P_h in TMEM: 8 columns per 16 keys
-            const uint32_t vb = ring_addr + (it % RING) * TILE_BYTES;
+            const uint32_t vb = lo_v + (uint32_t)((it % RING) * TILE_BYTES >> 4);
             if (lane == 0) {
                 #pragma unroll
                 for (int s = 0; s < 8; ++s)
-                    mma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + s * 8, sw128_desc(vb + s * 2048, 16384, 1024),
+                    mma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + s * 8, desc_of(vb + (s * 2048 >> 4), d_hi),
                                idesc_pv, (!first || s > 0) ? 1u : 0u);
                 if (last) mma_commit(&bar[B_OD0 + h]);   // O_h final for the tile
             }

@@ -171,6 +171,14 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uin
     return d;
 }
 
+// A descriptor from its two 32-bit words (low: start address >> 4 and leading offset; high:
+// stride offset, version, layout).
+__device__ __forceinline__ uint64_t desc_of(uint32_t lo, uint32_t hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+
 // Instruction descriptor of kind::f16 with FP16 A/B and FP32 D.
 //   bits 4-5 D format (1 = F32)   bits 7-9 A format (0 = F16)   bits 10-12 B format (0 = F16)
 //   bit 15 A major (0 = K)        bit 16 B major (1 = MN)       bits 17-22 N >> 3   bits 24-28 M >> 4
