@@ -38,8 +38,12 @@
 // K/V tiles come from the HBM KV store through one 3-D tensor map
 // {128 channels, ctx positions, planes} with 64x128 boxes and 128-byte swizzle; loads run
 // up to 2.5 tiles ahead of the tensor pipe.
-// Q rows are read with coalesced 512-byte row loads; the output rows leave through the
-// head's Q buffer (free once the last MMA of the head has completed) as coalesced stores.
+// Q rows are read with coalesced 512-byte row loads. At an item boundary the softmax warps
+// first store the next item's Q (the head's Q buffer is free once the last QK of the item has
+// completed), so its first QK runs on the tensor pipe while they write this item's output rows
+// straight from TMEM (16x256b loads: every store writes whole 32-byte sectors). The peer-store
+// instantiation instead stages rows in the Q buffer for 128-byte writes over NVLink and stores
+// the next Q after its epilogue.
 //
 // Every wait is bounded (globaltimer, 2 s): on expiry the CTA raises an abort flag, writes
 // an error code to the host-visible flag, drains what it issued and frees its TMEM.
@@ -136,20 +140,14 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 }
 
 // Rows [r_off, r_off + 16) of one warp's 32-row quarter of head h: lane i reads channels
-// 4i..4i+3 of each row (coalesced 512-byte rows), all 16 rows in flight. With prefetch_only,
-// the rows are only pulled into L2 (no registers held).
+// 4i..4i+3 of each row (coalesced 512-byte rows), all 16 rows in flight.
 __device__ __forceinline__ void q_load_rows(const PrefillArgs& a, const TileInfo& ti, int h, int wq, int lane,
-                                            int r_off, float4 (&xr)[16], bool prefetch_only) {
+                                            int r_off, float4 (&xr)[16]) {
     const float* base = a.q + (((size_t)ti.l * a.n) * a.hq + (size_t)ti.kh * 2 + h) * D + lane * 4;
     #pragma unroll
     for (int rr = 0; rr < 16; ++rr) {
         const int r = ti.r0 + wq * 32 + r_off + rr;
-        const float* p = base + (size_t)r * a.hq * D;
-        if (prefetch_only) {
-            if (r < a.n) asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-        } else {
-            xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(base + (size_t)r * a.hq * D)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 }
 // ... as FP16 in the swizzled K-major layout of the head's Q buffer.
@@ -221,9 +219,9 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         // FP16 into this warp's own rows of the head's Q buffer when that is free.
         float4 xr[16];
         auto store_q = [&](const TileInfo& tn) {
-            q_load_rows(a, tn, h, wq, lane, 0, xr, false);
+            q_load_rows(a, tn, h, wq, lane, 0, xr);
             q_store_rows(Qs, wq, lane, 0, xr);
-            q_load_rows(a, tn, h, wq, lane, 16, xr, false);
+            q_load_rows(a, tn, h, wq, lane, 16, xr);
             q_store_rows(Qs, wq, lane, 16, xr);
             fence_proxy_async_smem();
             mbar_arrive(&bar[B_Q0 + h]);
@@ -308,60 +306,87 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 mbar_arrive(&bar[B_PF0 + h]);
             }
             if (!ok) break;
-            // the next work item's Q rows start loading now and land during the epilogue
+            // the next work item (its Q rows were pulled into L2 by the producer when it took it)
             const int next = read_tile(i + 1);
-            if (next >= 0) {                                 // pulled into L2 while the epilogue runs
-                const TileInfo tn = tile_info(a, next);
-                q_load_rows(a, tn, h, wq, lane, 0, xr, true);
-                q_load_rows(a, tn, h, wq, lane, 16, xr, true);
+            if constexpr (!PEERS) {
+                // Q_h is free (QK_h of the last key tile completed before its S was announced):
+                // the next item's Q rows go in now, so its first QK_h runs on the tensor pipe
+                // while this item's epilogue runs
+                if (next >= 0) store_q(tile_info(a, next));
             }
             // ---- epilogue: O_h of this tile (all its MMAs, QK_h included, have completed) ----
             if (!mbar_wait(&bar[B_OD0 + h], i & 1, abortp)) { fail(13); break; }
             tc_fence_after();
-            // Output rows leave through the 4 KB piece of this head's Q buffer that holds the
-            // first 64 channels of this warp's own Q rows, 32 columns at a time: each thread
-            // writes its normalised 128-byte row segment (8 chunks, XOR-swizzled by row), then
-            // the warp stores four rows per instruction as coalesced 128-byte segments.
             const float inv = 1.f / lsum;
-            uint8_t* stage = Qs + wq * 4096;
-            #pragma unroll
-            for (int part = 0; part < 4; ++part) {
-                uint32_t ro[32];
-                tmem_ld32(o_col + part * 32, ro);
+            if constexpr (!PEERS) {
+                // Rows straight from TMEM in the 16x256b shape: a thread holds two adjacent
+                // columns of rows t/4 and t/4 + 8 of a 16-row half, so each store instruction
+                // writes eight rows x 32 contiguous bytes (whole sectors) and no shared memory
+                // is involved. Row sums come from the thread that owns the row.
+                uint32_t ro[2][64];
+                tmem_ld_16x256b_x16(o_col, ro[0]);
+                tmem_ld_16x256b_x16(o_col + (16u << 16), ro[1]);
                 tmem_wait_ld();
-                if (part == 3) {                              // O_h fully read: the next tile may overwrite it
-                    tc_fence_before();
-                    mbar_arrive(&bar[B_OF0 + h]);
+                tc_fence_before();
+                mbar_arrive(&bar[B_OF0 + h]);                // O_h read: the next item may overwrite it
+                #pragma unroll
+                for (int rh = 0; rh < 2; ++rh) {
+                    const int ra = rh * 16 + (lane >> 2);    // rows ra and ra + 8 of the warp's quarter
+                    const float ia = __shfl_sync(0xffffffffu, inv, ra), ib = __shfl_sync(0xffffffffu, inv, ra + 8);
+                    const int r = ti.r0 + wq * 32 + ra;
+                    float* pa = a.o.out + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D + 2 * (lane & 3);
+                    float* pb = pa + (size_t)8 * a.hq * D;
+                    #pragma unroll
+                    for (int g = 0; g < 16; ++g) {
+                        if (r < a.n)
+                            *reinterpret_cast<float2*>(pa + 8 * g) =
+                                make_float2(__uint_as_float(ro[rh][4 * g]) * ia, __uint_as_float(ro[rh][4 * g + 1]) * ia);
+                        if (r + 8 < a.n)
+                            *reinterpret_cast<float2*>(pb + 8 * g) =
+                                make_float2(__uint_as_float(ro[rh][4 * g + 2]) * ib, __uint_as_float(ro[rh][4 * g + 3]) * ib);
+                    }
                 }
+            } else {
+                // Output rows leave through the 4 KB piece of this head's Q buffer that holds
+                // the first 64 channels of this warp's own Q rows, 32 columns at a time: each
+                // thread writes its normalised 128-byte row segment (8 chunks, XOR-swizzled by
+                // row), then the warp stores four rows per instruction as 128-byte segments, the
+                // peers' copies included (whole 128-byte writes over NVLink).
+                uint8_t* stage = Qs + wq * 4096;
                 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<float4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-                        make_float4(__uint_as_float(ro[4 * c]) * inv, __uint_as_float(ro[4 * c + 1]) * inv,
-                                    __uint_as_float(ro[4 * c + 2]) * inv, __uint_as_float(ro[4 * c + 3]) * inv);
-                __syncwarp();
-                #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int rr = 4 * k + (lane >> 3), c = lane & 7;
-                    const float4 val = *reinterpret_cast<const float4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
-                    const int r = ti.r0 + wq * 32 + rr;
-                    if (r < a.n) {
-                        if constexpr (PEERS) {
+                for (int part = 0; part < 4; ++part) {
+                    uint32_t ro[32];
+                    tmem_ld32(o_col + part * 32, ro);
+                    tmem_wait_ld();
+                    if (part == 3) {                          // O_h fully read: the next tile may overwrite it
+                        tc_fence_before();
+                        mbar_arrive(&bar[B_OF0 + h]);
+                    }
+                    #pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        *reinterpret_cast<float4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                            make_float4(__uint_as_float(ro[4 * c]) * inv, __uint_as_float(ro[4 * c + 1]) * inv,
+                                        __uint_as_float(ro[4 * c + 2]) * inv, __uint_as_float(ro[4 * c + 3]) * inv);
+                    __syncwarp();
+                    #pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int rr = 4 * k + (lane >> 3), c = lane & 7;
+                        const float4 val = *reinterpret_cast<const float4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+                        const int r = ti.r0 + wq * 32 + rr;
+                        if (r < a.n) {
                             const size_t off = (((size_t)ti.l * a.n + r) * a.o.heads + a.o.head0 + ti.kh * 2 + h) * D +
                                                part * 32 + c * 4;
                             *reinterpret_cast<float4*>(a.o.out + off) = val;
                             #pragma unroll
                             for (int p = 0; p < MAX_RANKS - 1; ++p)
                                 if (p < a.o.n_peers) *reinterpret_cast<float4*>(a.o.peers[p] + off) = val;
-                        } else {
-                            *reinterpret_cast<float4*>(a.o.out + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D +
-                                                       part * 32 + c * 4) = val;
                         }
                     }
+                    __syncwarp();
                 }
-                __syncwarp();
+                if (next >= 0) store_q(tile_info(a, next));  // this warp's own Q rows, after its staging
             }
             tt = next;
-            if (tt >= 0) store_q(tile_info(a, tt));                          // this warp's own Q rows, after its staging
         }
     } else if (warp == 8) {
         // ================================== MMA issuer ==================================
@@ -481,6 +506,10 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             mbar_arrive(&bar[B_TF0 + slot]);                 // the slot's value is visible to the waiters
             if (tt < 0) break;
             const TileInfo ti = tile_info(a, tt);
+            // the item's query rows (both heads of the pair: 1 KB per row) into L2, well before
+            // the softmax warps load them
+            for (int r = ti.r0; r < min(ti.r0 + BM, a.n); ++r)
+                bulk_prefetch_l2(a.q + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2) * D, 2 * D * sizeof(float));
             for (int j2 = 0; j2 < 2 * ti.nk; ++j2) {
                 const int st = issued % RING;
                 if (issued >= RING && !mbar_wait(&bar[B_EMPTY0 + st], ((issued / RING) - 1) & 1, abortp)) {
