@@ -139,22 +139,22 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Rows [r_off, r_off + 16) of one warp's 32-row quarter of head h: lane i reads channels
-// 4i..4i+3 of each row (coalesced 512-byte rows), all 16 rows in flight.
+// The 32 rows of one warp's quarter of head h: lane i reads channels 4i..4i+3 of each row
+// (coalesced 512-byte rows), all 32 rows in flight (one L2 round trip).
 __device__ __forceinline__ void q_load_rows(const PrefillArgs& a, const TileInfo& ti, int h, int wq, int lane,
-                                            int r_off, float4 (&xr)[16]) {
+                                            float4 (&xr)[32]) {
     const float* base = a.q + (((size_t)ti.l * a.n) * a.hq + (size_t)ti.kh * 2 + h) * D + lane * 4;
     #pragma unroll
-    for (int rr = 0; rr < 16; ++rr) {
-        const int r = ti.r0 + wq * 32 + r_off + rr;
+    for (int rr = 0; rr < 32; ++rr) {
+        const int r = ti.r0 + wq * 32 + rr;
         xr[rr] = r < a.n ? __ldg(reinterpret_cast<const float4*>(base + (size_t)r * a.hq * D)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 }
 // ... as FP16 in the swizzled K-major layout of the head's Q buffer.
-__device__ __forceinline__ void q_store_rows(uint8_t* Qs, int wq, int lane, int r_off, const float4 (&xr)[16]) {
+__device__ __forceinline__ void q_store_rows(uint8_t* Qs, int wq, int lane, const float4 (&xr)[32]) {
     #pragma unroll
-    for (int rr = 0; rr < 16; ++rr)
-        *reinterpret_cast<uint2*>(Qs + swz(wq * 32 + r_off + rr, lane >> 1) + (lane & 1) * 8) =
+    for (int rr = 0; rr < 32; ++rr)
+        *reinterpret_cast<uint2*>(Qs + swz(wq * 32 + rr, lane >> 1) + (lane & 1) * 8) =
             make_uint2(pack_half2(xr[rr].x, xr[rr].y), pack_half2(xr[rr].z, xr[rr].w));
 }
 
@@ -215,14 +215,12 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             mbar_arrive(&bar[B_TE0 + slot]);
             return tt;
         };
-        // Q rows of this warp's quarter (q_load_rows / q_store_rows): loaded early, stored as
-        // FP16 into this warp's own rows of the head's Q buffer when that is free.
-        float4 xr[16];
+        // Q rows of this warp's quarter (q_load_rows / q_store_rows): all 32 loaded at once, then
+        // stored as FP16 into this warp's own rows of the head's Q buffer (free when called).
         auto store_q = [&](const TileInfo& tn) {
-            q_load_rows(a, tn, h, wq, lane, 0, xr);
-            q_store_rows(Qs, wq, lane, 0, xr);
-            q_load_rows(a, tn, h, wq, lane, 16, xr);
-            q_store_rows(Qs, wq, lane, 16, xr);
+            float4 xr[32];
+            q_load_rows(a, tn, h, wq, lane, xr);
+            q_store_rows(Qs, wq, lane, xr);
             fence_proxy_async_smem();
             mbar_arrive(&bar[B_Q0 + h]);
         };

@@ -692,7 +692,7 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
             }
             if (launch_attn_prefill_sm100(ctx->kv_map, din[0], o, seq, l0, nl, pos0, n, ctx->hq, ctx->hkv,
                                           ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->error, ctx->stream))
-                return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel has an unexpected register allocation");
+                return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel cannot launch (unexpected register allocation or shared-memory limit)");
             if (both) {
                 QA_CUDA(cudaEventRecord(ctx->join_ev, ctx->aux_stream));
                 QA_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->join_ev, 0));
