@@ -16,7 +16,8 @@
 // Warp roles (384 threads, three warpgroups):
 //   warps 0-3  softmax group for query head 0 (thread t owns query row t of the tile)
 //   warps 4-7  softmax group for query head 1
-//   warp  8    MMA issuer (one elected thread issues tcgen05.mma, the warp zeroes stale V rows)
+//   warp  8    MMA issuer (the warp runs the issue sequences, one elected lane issues
+//              tcgen05.mma; the warp zeroes stale V rows)
 //   warp  9    TMA producer (one thread); warps 10-11 idle
 // setmaxnreg moves registers from the control warpgroup to the softmax warpgroups so each
 // softmax thread holds its 128-column S row in registers.
@@ -401,32 +402,27 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         auto wait_item = [&](int it) {                   // ring item it has landed
             return mbar_wait(&bar[B_FULL0 + it % RING], (it / RING) & 1, abortp);
         };
+        // The whole warp runs the issue sequences; the elected lane issues (sm100.cuh).
+        const uint32_t leader = elect_one();
         auto release_item = [&](int it) {                // stage of item it free once prior MMAs finish
-            if (lane == 0) mma_commit(&bar[B_EMPTY0 + it % RING]);
-            __syncwarp();
+            mma_commit_warp(&bar[B_EMPTY0 + it % RING], leader);
         };
-        auto issue_qk = [&](int it, int h) {
+        auto issue_qk = [&](int it, int h) {             // 8 K-steps of 16 channels (32-byte column pairs)
             const uint32_t kb = lo_k + (uint32_t)((it % RING) * TILE_BYTES >> 4), qb = lo_q + (uint32_t)(h * 32768 >> 4);
-            if (lane == 0) {
-                #pragma unroll
-                for (int s = 0; s < 8; ++s) {
-                    const uint32_t off = ((s >> 2) * 16384 + (s & 3) * 32) >> 4;
-                    mma_f16_ss(tmem + h * 128, desc_of(qb + off, d_hi), desc_of(kb + off, d_hi), idesc_qk, s > 0);
-                }
-                mma_commit(&bar[B_SF0 + h]);
-            }
-            __syncwarp();
+            const uint32_t d = tmem + h * 128;
+#define QK_STEP(S) mma_f16_ss_warp<(((S >> 2) * 16384 + (S & 3) * 32) >> 4), (((S >> 2) * 16384 + (S & 3) * 32) >> 4)>( \
+        d, qb, kb, d_hi, idesc_qk, (S > 0), leader)
+            QK_STEP(0); QK_STEP(1); QK_STEP(2); QK_STEP(3); QK_STEP(4); QK_STEP(5); QK_STEP(6); QK_STEP(7);
+#undef QK_STEP
+            mma_commit_warp(&bar[B_SF0 + h], leader);
         };
         auto issue_pv = [&](int it, int h, bool first, bool last) {   // A = P_h in TMEM: 8 columns per 16 keys
             const uint32_t vb = lo_v + (uint32_t)((it % RING) * TILE_BYTES >> 4);
-            if (lane == 0) {
-                #pragma unroll
-                for (int s = 0; s < 8; ++s)
-                    mma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + s * 8, desc_of(vb + (s * 2048 >> 4), d_hi),
-                               idesc_pv, (!first || s > 0) ? 1u : 0u);
-                if (last) mma_commit(&bar[B_OD0 + h]);   // O_h final for the tile
-            }
-            __syncwarp();
+            const uint32_t d = tmem + 256 + h * 128, p = tmem + h * 128, acc0 = first ? 0u : 1u;
+#define PV_STEP(S) mma_f16_ts_warp<(S * 8), ((S * 2048) >> 4)>(d, p, vb, d_hi, idesc_pv, (S > 0 ? 1u : acc0), leader)
+            PV_STEP(0); PV_STEP(1); PV_STEP(2); PV_STEP(3); PV_STEP(4); PV_STEP(5); PV_STEP(6); PV_STEP(7);
+#undef PV_STEP
+            if (last) mma_commit_warp(&bar[B_OD0 + h], leader);   // O_h final for the tile
         };
         int base = 0;                                    // ring item of the tile's K_0
         uint32_t kt = 0;                                 // key tiles processed (S, P phases)

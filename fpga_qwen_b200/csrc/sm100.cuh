@@ -174,6 +174,46 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
         ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// Warp-converged issue: the whole warp executes these (no divergent branch around them), and
+// only the lane whose `issue` is non-zero (elect_one) issues the MMA or commit. Issued this
+// way the operands stay warp-uniform; issuing from inside `if (lane == 0)` measured about 2%
+// slower in the prefill kernel, whose single issuing thread is on the tensor pipe's critical
+// path. Descriptors are a shared high word and low words base + an immediate offset (start
+// address >> 4), added inside the instruction sequence.
+__device__ __forceinline__ uint32_t elect_one() {
+    uint32_t e;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(e));
+    return e;
+}
+template <uint32_t OFF_A, uint32_t OFF_B>
+__device__ __forceinline__ void mma_f16_ss_warp(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                                uint32_t accumulate, uint32_t issue) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 al, bl;\n\t.reg .b64 ad, bd;\n\t"
+        "add.u32 al, %1, %7;\n\tadd.u32 bl, %2, %8;\n\tmov.b64 ad, {al, %3};\n\tmov.b64 bd, {bl, %3};\n\t"
+        "setp.ne.b32 e, %6, 0;\n\tsetp.ne.b32 p, %5, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %4, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate), "r"(issue), "n"(OFF_A), "n"(OFF_B)
+        : "memory");
+}
+// A from TMEM at column a_tmem + A_COL (two 16-bit K elements per 32-bit column).
+template <uint32_t A_COL, uint32_t OFF_B>
+__device__ __forceinline__ void mma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                                uint32_t accumulate, uint32_t issue) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 at, bl;\n\t.reg .b64 bd;\n\t"
+        "add.u32 at, %1, %7;\n\tadd.u32 bl, %2, %8;\n\tmov.b64 bd, {bl, %3};\n\t"
+        "setp.ne.b32 e, %6, 0;\n\tsetp.ne.b32 p, %5, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [at], bd, %4, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate), "r"(issue), "n"(A_COL), "n"(OFF_B)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit_warp(uint64_t* bar, uint32_t issue) {
+    asm volatile("{\n\t.reg .pred e;\n\tsetp.ne.b32 e, %1, 0;\n\t"
+                 "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+                 ::"r"(smem_u32(bar)), "r"(issue) : "memory");
+}
+
 // Arrives once on `bar` when all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
