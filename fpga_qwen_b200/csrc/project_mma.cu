@@ -241,37 +241,40 @@ __global__ void __launch_bounds__(GTHREADS, 1) project_gemm_kernel(const __grid_
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---- MMA issuer: [D_hi | D_lo] (+)= W [x_hi; x_lo]^T per 16-column K slice ----
-            // The x_lo tile follows the x_hi tile in the stage, so one N = 256 MMA takes both as
-            // a 256-row operand (128-row MMAs cannot be issued fast enough by one thread to keep
-            // the tensor pipe busy; 256-row ones can).
-            const uint32_t idesc = idesc_f16_f32(GM, 2 * GN, false);
-            uint32_t g = 0;
-            bool ok = true;
-            int i = 0;
-            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++i) {
-                const Unit w = unit_of(a, u, n_bt, kt_all);
-                const int b = i & 1;
-                if (i >= 2 && !mbar_wait(&acc_empty[b], ((i >> 1) - 1) & 1, abortp)) { fail(64); break; }
+        // ---- MMA issuer: [D_hi | D_lo] (+)= W [x_hi; x_lo]^T per 16-column K slice ----
+        // The x_lo tile follows the x_hi tile in the stage, so one N = 256 MMA takes both as a
+        // 256-row operand (128-row MMAs cannot be issued fast enough by one thread to keep the
+        // tensor pipe busy; 256-row ones can). The whole warp runs the loop and the elected lane
+        // issues (warp-converged issue, sm100.cuh); descriptors step by their low words.
+        const uint32_t leader = elect_one();
+        const uint32_t idesc = idesc_f16_f32(GM, 2 * GN, false);
+        const uint32_t d_hi = (uint32_t)(sw128_desc(0, 16, 1024) >> 32);
+        uint32_t g = 0;
+        bool ok = true;
+        int i = 0;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++i) {
+            const Unit w = unit_of(a, u, n_bt, kt_all);
+            const int b = i & 1;
+            if (i >= 2 && !mbar_wait(&acc_empty[b], ((i >> 1) - 1) & 1, abortp)) { fail(64); break; }
+            tc_fence_after();
+            const uint32_t acc = tmem + (uint32_t)(b * 2 * GN);
+            for (int kt = 0; kt < w.kt_n; ++kt, ++g) {
+                const int s = g % GSTAGES;
+                if (!mbar_wait(&full[s], (g / GSTAGES) & 1, abortp)) { fail(62); ok = false; break; }
                 tc_fence_after();
-                const uint32_t acc = tmem + (uint32_t)(b * 2 * GN);
-                for (int kt = 0; kt < w.kt_n; ++kt, ++g) {
-                    const int s = g % GSTAGES;
-                    if (!mbar_wait(&full[s], (g / GSTAGES) & 1, abortp)) { fail(62); ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t wb = smem_u32(smem + s * STAGE_BYTES), xb = wb + W_TILE;
-                    #pragma unroll
-                    for (int ks = 0; ks < GK / 16; ++ks)
-                        mma_f16_ss(acc, sw128_desc(wb + ks * 32, 16, 1024), sw128_desc(xb + ks * 32, 16, 1024), idesc,
-                                   (kt > 0 || ks > 0) ? 1u : 0u);
-                    mma_commit(&empty[s]);                 // the stage is free once these MMAs complete
-                }
-                if (ok) mma_commit(&acc_full[b]);          // the unit's accumulator is final
+                const uint32_t wl = (uint32_t)sw128_desc(smem_u32(smem + s * STAGE_BYTES), 16, 1024);
+                const uint32_t xl = wl + (uint32_t)(W_TILE >> 4);
+                static_assert(GK / 16 == 4, "four 16-column K slices per stage");
+                mma_f16_ss_warp<0, 0>(acc, wl, xl, d_hi, idesc, kt > 0 ? 1u : 0u, leader);
+                mma_f16_ss_warp<2, 2>(acc, wl, xl, d_hi, idesc, 1u, leader);   // +32 bytes per slice
+                mma_f16_ss_warp<4, 4>(acc, wl, xl, d_hi, idesc, 1u, leader);
+                mma_f16_ss_warp<6, 6>(acc, wl, xl, d_hi, idesc, 1u, leader);
+                mma_commit_warp(&empty[s], leader);        // the stage is free once these MMAs complete
             }
-            mma_commit(drain);                             // every MMA issued has completed
-            mbar_wait(drain, 0, &never_abort);
+            if (ok) mma_commit_warp(&acc_full[b], leader); // the unit's accumulator is final
         }
+        mma_commit_warp(drain, leader);                    // every MMA issued has completed
+        mbar_wait(drain, 0, &never_abort);
     } else {
         // ---- epilogue: warp holds weight rows r0 + 32 q + lane (its TMEM lane quarter q) ----
         const int q = warp & 3, ew = warp - EPI_WARP0;
