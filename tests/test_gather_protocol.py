@@ -97,7 +97,7 @@ def run_protocol(nranks, calls, gate=True, slow_copy_rank=-1, seed=0):
     return list(errors)
 
 
-@pytest.mark.parametrize("nranks", [2, 4])
+@pytest.mark.parametrize("nranks", [2, 4, 8])
 def test_every_copy_reads_its_own_call(nranks):
     assert run_protocol(nranks, calls=12, seed=nranks) == [0] * nranks
 
@@ -155,7 +155,7 @@ def run_decode_protocol(nranks, steps, buffers=2, slow_copy_rank=-1, seed=0):
     return list(errors)
 
 
-@pytest.mark.parametrize("nranks", [2, 4])
+@pytest.mark.parametrize("nranks", [2, 4, 8])
 def test_decode_gather_alternating_buffers(nranks):
     assert run_decode_protocol(nranks, steps=16, seed=nranks) == [0] * nranks
     assert run_decode_protocol(nranks, steps=4, slow_copy_rank=nranks - 1) == [0] * nranks
