@@ -202,12 +202,19 @@ __global__ void __launch_bounds__(Shape<ROWS>::THREADS) project_kernel(const Pro
 // only after griddepcontrol.wait.
 constexpr int PS_THREADS = 256;
 constexpr int PS_GROUPS = 4;                       // column groups, one cp.async group each
-constexpr int PS_MAX_ROWS = PS_THREADS / 2;        // two threads per row
+constexpr int PS_MAX_ROWS = PS_THREADS / 2;        // at least two threads per row
 constexpr int PS_MAX_SMEM = 200 * 1024;
 
 __device__ __forceinline__ int ps_stride(int cols) { return cols * 2 + 16; }   // padded row, bytes
 
+// TPR threads per row, each owning 8 / TPR of the dot's eight lanes (a0..a3 = channels j..j+3,
+// b0..b3 = channels j+4..j+7 of every 8-channel step): every lane is still one chain of fused
+// multiply-adds in ascending j, so the bits do not depend on TPR. Slices of few rows (o_proj,
+// down_proj: about 7 rows per SM) use 8 threads per row, so that a CTA runs more than one
+// warp of chains; TPR = 2 reproduces the persistent kernel's thread layout.
+template <int TPR>
 __global__ void __launch_bounds__(PS_THREADS) project_small_kernel(const ProjectArgs a, int rows_per_cta) {
+    constexpr int LANES = 8 / TPR;                 // lanes (channels of each 8-channel step) per thread
     extern __shared__ __align__(16) uint8_t sm[];
     __shared__ const __half* rowptr[PS_MAX_ROWS];
     __shared__ float* outptr[PS_MAX_ROWS];
@@ -240,14 +247,16 @@ __global__ void __launch_bounds__(PS_THREADS) project_small_kernel(const Project
     for (int i = tid; i < xbytes / 16; i += PS_THREADS)
         reinterpret_cast<float4*>(sm)[i] = __ldcg(reinterpret_cast<const float4*>(a.x) + i);
 
-    // two threads per row as in project_kernel; the warps that hold no row only join the barriers
-    const int r = tid >> 1, hl = tid & 1;
-    const bool active_warp = (tid & ~31) < 2 * nrows;
-    const uint8_t* row = wbase + min(r, nrows - 1) * stride + hl * 8;
-    const float* xs = reinterpret_cast<const float*>(sm) + hl * 4;
-    float2 acc[PR_BATCH][2];
+    // TPR threads per row; the warps that hold no row only join the barriers
+    const int r = tid / TPR, q = tid % TPR;
+    const bool active_warp = (tid & ~31) < TPR * nrows;
+    const uint8_t* row = wbase + min(r, nrows - 1) * stride + q * LANES * 2;
+    const float* xs = reinterpret_cast<const float*>(sm) + q * LANES;
+    float acc[PR_BATCH][LANES];
     #pragma unroll
-    for (int bb = 0; bb < PR_BATCH; ++bb) acc[bb][0] = acc[bb][1] = make_float2(0.f, 0.f);
+    for (int bb = 0; bb < PR_BATCH; ++bb)
+        #pragma unroll
+        for (int l = 0; l < LANES; ++l) acc[bb][l] = 0.f;
     #pragma unroll
     for (int g = 0; g < PS_GROUPS; ++g) {
         if (g == 0) cp_wait<PS_GROUPS - 1>();
@@ -259,35 +268,60 @@ __global__ void __launch_bounds__(PS_THREADS) project_small_kernel(const Project
         const int j0 = pieces * g / PS_GROUPS, j1 = pieces * (g + 1) / PS_GROUPS;
         #pragma unroll 4
         for (int jj = j0; jj < j1; ++jj) {
-            const uint2 wv = *reinterpret_cast<const uint2*>(row + jj * 16);      // 4 FP16 weights
-            const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
-            const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
-            const float4 x0 = *reinterpret_cast<const float4*>(xs + jj * 8);
-            acc[0][0] = ffma2(make_float2(x0.x, x0.y), w01, acc[0][0]);
-            acc[0][1] = ffma2(make_float2(x0.z, x0.w), w23, acc[0][1]);
+            float w[LANES], x0[LANES], x1[LANES];
+            if constexpr (LANES == 4) {
+                const uint2 wv = *reinterpret_cast<const uint2*>(row + jj * 16);
+                const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv.x));
+                const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv.y));
+                w[0] = w01.x; w[1] = w01.y; w[2] = w23.x; w[3] = w23.y;
+                const float4 v = *reinterpret_cast<const float4*>(xs + jj * 8);
+                x0[0] = v.x; x0[1] = v.y; x0[2] = v.z; x0[3] = v.w;
+            } else if constexpr (LANES == 2) {
+                const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(row + jj * 16));
+                w[0] = w01.x; w[1] = w01.y;
+                const float2 v = *reinterpret_cast<const float2*>(xs + jj * 8);
+                x0[0] = v.x; x0[1] = v.y;
+            } else {
+                w[0] = __half2float(*reinterpret_cast<const __half*>(row + jj * 16));
+                x0[0] = xs[jj * 8];
+            }
+            #pragma unroll
+            for (int l = 0; l < LANES; ++l) acc[0][l] = fmaf(x0[l], w[l], acc[0][l]);
             if (a.batch == PR_BATCH) {
-                const float4 x1 = *reinterpret_cast<const float4*>(xs + cols + jj * 8);
-                acc[1][0] = ffma2(make_float2(x1.x, x1.y), w01, acc[1][0]);
-                acc[1][1] = ffma2(make_float2(x1.z, x1.w), w23, acc[1][1]);
+                #pragma unroll
+                for (int l = 0; l < LANES; ++l) x1[l] = xs[cols + jj * 8 + l];
+                #pragma unroll
+                for (int l = 0; l < LANES; ++l) acc[1][l] = fmaf(x1[l], w[l], acc[1][l]);
             }
         }
     }
     if (!active_warp) return;
     #pragma unroll
     for (int bb = 0; bb < PR_BATCH; ++bb) {
-        float2 o0, o1;
-        o0.x = __shfl_xor_sync(0xffffffffu, acc[bb][0].x, 1); o0.y = __shfl_xor_sync(0xffffffffu, acc[bb][0].y, 1);
-        o1.x = __shfl_xor_sync(0xffffffffu, acc[bb][1].x, 1); o1.y = __shfl_xor_sync(0xffffffffu, acc[bb][1].y, 1);
-        const float s0 = acc[bb][0].x + o0.x, s1 = acc[bb][0].y + o0.y;
-        const float s2 = acc[bb][1].x + o1.x, s3 = acc[bb][1].y + o1.y;
-        const float y = (s0 + s1) + (s2 + s3);
-        if (bb < a.batch && hl == 0 && r < nrows) outptr[r][(size_t)bb * outstride[r]] = y;
+        // s_i = a_i + b_i, then (s0 + s1) + (s2 + s3), with the reference's association
+        float y;
+        if constexpr (TPR == 2) {                  // q = 0: a0..a3, q = 1: b0..b3
+            float s[4];
+            #pragma unroll
+            for (int l = 0; l < 4; ++l) s[l] = acc[bb][l] + __shfl_xor_sync(0xffffffffu, acc[bb][l], 1);
+            y = (s[0] + s[1]) + (s[2] + s[3]);
+        } else if constexpr (TPR == 4) {           // q: lanes 2q, 2q+1 (q = 0, 1: a; 2, 3: b)
+            const float s0 = acc[bb][0] + __shfl_xor_sync(0xffffffffu, acc[bb][0], 2);
+            const float s1 = acc[bb][1] + __shfl_xor_sync(0xffffffffu, acc[bb][1], 2);
+            const float h = s0 + s1;               // q = 0: s0 + s1, q = 1: s2 + s3
+            y = h + __shfl_xor_sync(0xffffffffu, h, 1);
+        } else {                                   // q: lane q (0..3: a_q, 4..7: b_(q-4))
+            const float s = acc[bb][0] + __shfl_xor_sync(0xffffffffu, acc[bb][0], 4);
+            const float h = s + __shfl_xor_sync(0xffffffffu, s, 1);     // q = 0: s0 + s1, q = 2: s2 + s3
+            y = h + __shfl_xor_sync(0xffffffffu, h, 2);
+        }
+        if (bb < a.batch && q == 0 && r < nrows) outptr[r][(size_t)bb * outstride[r]] = y;
     }
 }
 
-// The small-launch plan: rows per CTA and dynamic shared memory, or false when the launch
-// belongs to the persistent kernel (a batch beyond one pass, or a slice too large to hold).
-bool small_plan(const ProjectArgs& a, int sms, int* rows_per_cta, int* grid, size_t* smem) {
+// The small-launch plan: rows per CTA, threads per row and dynamic shared memory, or false when
+// the launch belongs to the persistent kernel (a batch beyond one pass, or a slice too large).
+bool small_plan(const ProjectArgs& a, int sms, int* rows_per_cta, int* tpr, int* grid, size_t* smem) {
     if (a.batch > PR_BATCH) return false;
     int total = 0;
     for (int m = 0; m < a.n_mats; ++m) total += a.rows[m];
@@ -296,6 +330,7 @@ bool small_plan(const ProjectArgs& a, int sms, int* rows_per_cta, int* grid, siz
     const size_t bytes = (size_t)a.batch * a.cols * 4 + (size_t)r * (a.cols * 2 + 16);
     if (bytes > PS_MAX_SMEM) return false;
     *rows_per_cta = r;
+    *tpr = 8 * r <= PS_THREADS ? 8 : 4 * r <= PS_THREADS ? 4 : 2;
     *grid = (total + r - 1) / r;
     *smem = bytes;
     return true;
@@ -333,18 +368,22 @@ void launch_project(ProjectArgs a, cudaStream_t s) {
         int dev = 0;
         sms = NUM_SMS_B200;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaFuncSetAttribute(project_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PS_MAX_SMEM);
+        cudaFuncSetAttribute(project_small_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, PS_MAX_SMEM);
+        cudaFuncSetAttribute(project_small_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, PS_MAX_SMEM);
+        cudaFuncSetAttribute(project_small_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, PS_MAX_SMEM);
     }
-    int rows_per_cta = 0, grid = 0;
+    int rows_per_cta = 0, tpr = 2, grid = 0;
     size_t smem = 0;
-    if (small_plan(a, sms, &rows_per_cta, &grid, &smem)) {
+    if (small_plan(a, sms, &rows_per_cta, &tpr, &grid, &smem)) {
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(grid); cfg.blockDim = dim3(PS_THREADS); cfg.dynamicSmemBytes = smem; cfg.stream = s;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr; cfg.numAttrs = 1;
-        cudaLaunchKernelEx(&cfg, project_small_kernel, a, rows_per_cta);
+        if (tpr == 8) cudaLaunchKernelEx(&cfg, project_small_kernel<8>, a, rows_per_cta);
+        else if (tpr == 4) cudaLaunchKernelEx(&cfg, project_small_kernel<4>, a, rows_per_cta);
+        else cudaLaunchKernelEx(&cfg, project_small_kernel<2>, a, rows_per_cta);
         return;
     }
     int tiles64 = 0;
