@@ -72,13 +72,16 @@ def test_group_ragged_shapes_and_batches_bit_exact():
     """q/k/v as one launch; rows that are not a multiple of the 16-row tile, a width that is not
     a multiple of the 128-column chunk, and batches that need several passes (the persistent
     kernel); at batch 1 and 2 the same shapes take the small-launch kernel, whose row slices
-    cross matrix boundaries, and a 4096-column case whose slice is too large for it."""
+    cross matrix boundaries, and a 4096-column case whose slice is too large for it. The
+    small-launch kernel gives each row 8, 4 or 2 threads by the rows a slice holds: q/k/v
+    (28 rows per SM) takes 8, gate/up (42) takes 4 and a 10,000-row group (68) takes 2."""
     rng = np.random.default_rng(8)
     ctx = _ctx()
     for rows, cols, batch in (((2048, 1024, 1024), 1024, 1), ((2048, 1024, 1024), 1024, 2),
                               ((37, 5, 300), 776, 3), ((37, 5, 300), 776, 2), ((37, 5, 300), 776, 1),
                               ((16, 17), 8, 5), ((16, 17), 8, 1), ((3000, 3000), 4096, 2),
-                              ((1,), 3072, 2)):
+                              ((1,), 3072, 2), ((3072, 3072), 1024, 1), ((3072, 3072), 1024, 2),
+                              ((5000, 5000), 520, 1), ((5000, 4999), 512, 2)):
         ws = [_matrix(rng, r, cols) for r in rows]
         x = rng.standard_normal((batch, cols)).astype(np.float32)
         wd = [torch.from_numpy(w.view(np.int16)).cuda() for w in ws]
