@@ -519,6 +519,7 @@ def run_ours(args):
         if world == 1 and not args.no_e2e:
             line["e2e"] = e2e_decode(args, seed)
             line["e2e_per_layer"] = e2e_per_layer(args, seed)
+            line["prefill_per_layer"] = prefill_per_layer(args, seed)
             cpp = cpp_decode_loop()
             if cpp:
                 line["e2e_per_layer"]["cpp"] = cpp
@@ -595,6 +596,71 @@ def e2e_decode(args, seed):
             "d2h_bytes_per_step": per_step_out * DECODE, "us_per_token": round(t / DECODE * 1e6, 2),
             "note": "128 fused decode steps (qa_decode_step, io_host, all 28 layers per call) per step, host "
                     "wall clock around the C-ABI calls with host buffers"}
+
+
+def prefill_per_layer(args, seed):
+    """The prefill as an engine whose projections run between the layers calls it (engine/core.cpp
+    :383-645): per layer one qa_append and one qa_attn_prefill of the 3968 prompt rows (device
+    pointers), against the same work as one 28-layer call of each. CUDA events on the context's
+    stream around each form, launched back to back; medians over the timed repetitions."""
+    import torch
+    from fpga_qwen_b200 import qattn
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+
+    def gen(kind, heads):
+        t = torch.empty((L, PREFILL, heads, D), dtype=torch.float32, device=dev)
+        qattn.synth_fill(t.data_ptr(), seed, kind, 0, L, 0, PREFILL, 0, heads, 0.0, 1.0, stream.cuda_stream)
+        return t
+
+    pq, pk, pv = gen(0, HQ), gen(1, HKV), gen(2, HKV)
+    qn, out = torch.empty_like(pq), torch.empty_like(pq)
+    ctx = qattn.Context(n_layers=L, context=4096, max_seqs=1)
+    ctx.set_stream(stream.cuda_stream)
+    lq, lk, lo = PREFILL * HQ * D * 4, PREFILL * HKV * D * 4, PREFILL * HQ * D * 4   # bytes per layer
+
+    def run(per_layer, evs):
+        ctx.reset(0)
+        evs[0].record(stream)
+        if per_layer:
+            for layer in range(L):
+                ctx.append(0, layer, 1, 0, PREFILL, pq.data_ptr() + layer * lq, pk.data_ptr() + layer * lk,
+                           pv.data_ptr() + layer * lk, qn.data_ptr() + layer * lq)
+                ctx.attn_prefill(0, layer, 1, 0, PREFILL, qn.data_ptr() + layer * lq, out.data_ptr() + layer * lo)
+        else:
+            ctx.append(0, 0, L, 0, PREFILL, pq.data_ptr(), pk.data_ptr(), pv.data_ptr(), qn.data_ptr())
+            ctx.attn_prefill(0, 0, L, 0, PREFILL, qn.data_ptr(), out.data_ptr())
+        evs[1].record(stream)
+        # attention alone, once more over the same rows (not committed yet: the K/V and q_out of
+        # every layer are in place)
+        evs[2].record(stream)
+        if per_layer:
+            for layer in range(L):
+                ctx.attn_prefill(0, layer, 1, 0, PREFILL, qn.data_ptr() + layer * lq, out.data_ptr() + layer * lo)
+        else:
+            ctx.attn_prefill(0, 0, L, 0, PREFILL, qn.data_ptr(), out.data_ptr())
+        evs[3].record(stream)
+        ctx.commit(0, PREFILL)
+
+    res = {}
+    for per_layer in (False, True):
+        phase, attn = [], []
+        for it in range(max(3, args.warmup) + args.steps):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            run(per_layer, evs)
+            torch.cuda.synchronize()
+            if it >= max(3, args.warmup):
+                phase.append(evs[0].elapsed_time(evs[1]))
+                attn.append(evs[2].elapsed_time(evs[3]))
+        res[per_layer] = (statistics.median(phase), statistics.median(attn))
+    ctx.close()
+    flops = prefill_flops(0, PREFILL)
+    (ph1, at1), (phl, atl) = res[False], res[True]
+    return {"metric": "prefill-attn TFLOP/s, 28 one-layer calls", "value": round(flops / (atl * 1e-3) / 1e12, 1),
+            "unit": "TFLOP/s", "attn_ms": round(atl, 3), "phase_ms": round(phl, 3),
+            "attn_ms_one_call": round(at1, 3), "phase_ms_one_call": round(ph1, 3),
+            "note": "per layer: qa_append + qa_attn_prefill of 3968 rows (device pointers), as the engine's layer "
+                    "loop calls them; *_one_call: the same work as one 28-layer call of each; CUDA events"}
 
 
 def e2e_per_layer(args, seed):

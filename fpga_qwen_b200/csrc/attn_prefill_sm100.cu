@@ -88,17 +88,21 @@ struct PrefillArgs {
     OutRows o;                        // output rows: local layout, or full-head layout here and on peers
     int seq, layer0, n_layers, pos0, n, hq, hkv, layers_total;
     int row_begin, n_qtiles, n_tiles;
+    int size_major;                   // 1: items ordered by size across all (layer, KV head) groups
     int* tile_counter;                // next tile to hand out; zero before the launch
     int* error;
 };
 
-// Tile t of the launch: the query tiles of one (layer, KV head) are consecutive, heaviest first,
-// so CTAs running at the same time read the same K/V planes and hit in L2.
+// Tile t of the launch. Launches whose K/V exceed a share of L2: the query tiles of one (layer,
+// KV head) are consecutive, heaviest first, so CTAs running at the same time read the same K/V
+// planes and hit in L2. Launches whose K/V fit in L2 (a layer or two, as an engine calls it):
+// heaviest first across all groups (the longest items start first, so the launch ends evenly).
 struct TileInfo { int l, kh, r0, nk, valid_keys, plane_k; };
 __device__ __forceinline__ TileInfo tile_info(const PrefillArgs& a, int t) {
     TileInfo ti;
-    const int lh = t / a.n_qtiles;
-    const int tile = a.n_qtiles - 1 - t % a.n_qtiles;
+    const int groups = a.hkv * a.n_layers;
+    const int lh = a.size_major ? t % groups : t / a.n_qtiles;
+    const int tile = a.n_qtiles - 1 - (a.size_major ? t / groups : t % a.n_qtiles);
     ti.kh = lh % a.hkv;
     ti.l = lh / a.hkv;
     ti.r0 = a.row_begin + tile * BM;                          // first query row of the tile
@@ -560,6 +564,9 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
     a.hq = hq; a.hkv = hkv; a.layers_total = layers_total; a.row_begin = row_begin;
     a.n_qtiles = (n - row_begin + BM - 1) / BM; a.error = error;
     a.n_tiles = a.n_qtiles * hkv * n_layers;
+    // K/V the launch reads (FP16 K and V rows of every (layer, head) up to the last row), against
+    // a third of the 126 MB L2
+    a.size_major = (double)n_layers * hkv * 2.0 * (pos0 + n) * D * 2 <= 42.0e6 ? 1 : 0;
     a.tile_counter = tile_counter;
     // persistent: one CTA per SM (225 KB of shared memory each) pulls tiles from the counter
     int dev = 0, sms = NUM_SMS_B200;
