@@ -642,6 +642,31 @@ def prefill_per_layer(args, seed):
         evs[3].record(stream)
         ctx.commit(0, PREFILL)
 
+    # the engine's own chunking (core.cpp:712): 512-row chunks (the last one 384 rows), each
+    # appended for all layers, then attended one layer per call: 224 launches, each with fewer
+    # work items than SMs (the kernel splits their key ranges); the attention calls are timed
+    chunks = [(p0, 512) for p0 in range(0, PREFILL - 384, 512)] + [(PREFILL - 384, 384)]
+    # each chunk's rows of every layer, contiguous [L][n][heads][128] as the calls take them
+    cin = [tuple(t[:, p0:p0 + n].contiguous() for t in (pq, pk, pv)) for p0, n in chunks]
+    cqn = [torch.empty_like(c[0]) for c in cin]
+    cout = [torch.empty_like(c[0]) for c in cin]
+
+    def run_chunked():
+        ctx.reset(0)
+        total = 0.0
+        for ci, (p0, n) in enumerate(chunks):
+            q_, k_, v_ = cin[ci]
+            ctx.append(0, 0, L, p0, n, q_.data_ptr(), k_.data_ptr(), v_.data_ptr(), cqn[ci].data_ptr())
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for layer in range(L):
+                ctx.attn_prefill(0, layer, 1, p0, n, cqn[ci][layer].data_ptr(), cout[ci][layer].data_ptr())
+            e1.record(stream)
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+            ctx.commit(0, n)
+        return total
+
     res = {}
     for per_layer in (False, True):
         phase, attn = [], []
@@ -653,14 +678,17 @@ def prefill_per_layer(args, seed):
                 phase.append(evs[0].elapsed_time(evs[1]))
                 attn.append(evs[2].elapsed_time(evs[3]))
         res[per_layer] = (statistics.median(phase), statistics.median(attn))
+    chunked = statistics.median([run_chunked() for _ in range(max(3, args.warmup) + args.steps)][max(3, args.warmup):])
     ctx.close()
     flops = prefill_flops(0, PREFILL)
     (ph1, at1), (phl, atl) = res[False], res[True]
     return {"metric": "prefill-attn TFLOP/s, 28 one-layer calls", "value": round(flops / (atl * 1e-3) / 1e12, 1),
             "unit": "TFLOP/s", "attn_ms": round(atl, 3), "phase_ms": round(phl, 3),
             "attn_ms_one_call": round(at1, 3), "phase_ms_one_call": round(ph1, 3),
+            "attn_ms_chunked": round(chunked, 3), "tflops_chunked": round(flops / (chunked * 1e-3) / 1e12, 1),
             "note": "per layer: qa_append + qa_attn_prefill of 3968 rows (device pointers), as the engine's layer "
-                    "loop calls them; *_one_call: the same work as one 28-layer call of each; CUDA events"}
+                    "loop calls them; *_one_call: the same work as one 28-layer call of each; *_chunked: the engine's "
+                    "512-row chunks, 224 one-layer attention calls; CUDA events"}
 
 
 def e2e_per_layer(args, seed):

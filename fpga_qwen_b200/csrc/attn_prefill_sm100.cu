@@ -89,6 +89,9 @@ struct PrefillArgs {
     int seq, layer0, n_layers, pos0, n, hq, hkv, layers_total;
     int row_begin, n_qtiles, n_tiles;
     int size_major;                   // 1: items ordered by size across all (layer, KV head) groups
+    int kseg;                         // key segments per item (work units = items x kseg); 1: no split
+    float* part;                      // kseg > 1: [unit][2 heads][128 rows][128] unnormalised O rows
+    float* part_ml;                   // kseg > 1: [unit][2 heads][128 rows] (running max, sum)
     int* tile_counter;                // next tile to hand out; zero before the launch
     int* error;
 };
@@ -97,18 +100,23 @@ struct PrefillArgs {
 // KV head) are consecutive, heaviest first, so CTAs running at the same time read the same K/V
 // planes and hit in L2. Launches whose K/V fit in L2 (a layer or two, as an engine calls it):
 // heaviest first across all groups (the longest items start first, so the launch ends evenly).
-struct TileInfo { int l, kh, r0, nk, valid_keys, plane_k; };
+// With kseg > 1 (launches with fewer items than SMs) unit t is segment t % kseg of item
+// t / kseg: key tiles [j0, j0 + nj) of the item's nk, an even share.
+struct TileInfo { int l, kh, r0, nk, valid_keys, plane_k, j0, nj; };
 __device__ __forceinline__ TileInfo tile_info(const PrefillArgs& a, int t) {
     TileInfo ti;
+    const int item = t / a.kseg, seg = t - item * a.kseg;
     const int groups = a.hkv * a.n_layers;
-    const int lh = a.size_major ? t % groups : t / a.n_qtiles;
-    const int tile = a.n_qtiles - 1 - (a.size_major ? t / groups : t % a.n_qtiles);
+    const int lh = a.size_major ? item % groups : item / a.n_qtiles;
+    const int tile = a.n_qtiles - 1 - (a.size_major ? item / groups : item % a.n_qtiles);
     ti.kh = lh % a.hkv;
     ti.l = lh / a.hkv;
     ti.r0 = a.row_begin + tile * BM;                          // first query row of the tile
     ti.valid_keys = a.pos0 + min(ti.r0 + BM, a.n);            // keys visible to the tile's last row
     ti.nk = (ti.valid_keys + BN - 1) / BN;                    // causal key tiles
     ti.plane_k = ((a.seq * a.layers_total + a.layer0 + ti.l) * 2 + 0) * a.hkv + ti.kh;
+    ti.j0 = seg * ti.nk / a.kseg;
+    ti.nj = (seg + 1) * ti.nk / a.kseg - ti.j0;
     return ti;
 }
 
@@ -236,7 +244,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             const int row_pos = a.pos0 + ti.r0 + trow;
             float m = -INFINITY, lsum = 0.f;
             bool ok = true;
-            for (int j = 0; j < ti.nk; ++j, ++kt) {
+            for (int j = 0; j < ti.nj; ++j, ++kt) {
                 if (!mbar_wait(&bar[B_SF0 + h], kt & 1, abortp)) { fail(11); ok = false; break; }
                 tc_fence_after();
                 // S row -> registers: four 32-column loads in flight, one wait; the empty asm pins
@@ -250,7 +258,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     #pragma unroll
                     for (int e = 0; e < 32; ++e) asm volatile("" : "+r"(sr[c][e]));
                 float* v = reinterpret_cast<float*>(&sr[0][0]);
-                const int k0 = j * BN;
+                const int k0 = (ti.j0 + j) * BN;
                 const int lim = row_pos - k0;                   // keys c > lim are in the future
                 if (lim < BN - 1) {                             // tile crosses the diagonal
                     #pragma unroll
@@ -320,7 +328,15 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             // ---- epilogue: O_h of this tile (all its MMAs, QK_h included, have completed) ----
             if (!mbar_wait(&bar[B_OD0 + h], i & 1, abortp)) { fail(13); break; }
             tc_fence_after();
-            const float inv = 1.f / lsum;
+            // a key segment of a split item leaves its rows unnormalised (weight 1) in the scratch,
+            // with the row's running max and sum beside them, for prefill_merge_kernel
+            const bool split = !PEERS && a.kseg > 1;
+            const float inv = split ? 1.f : 1.f / lsum;
+            if (split) {
+                float* ml = a.part_ml + (((size_t)tt * 2 + h) * BM + trow) * 2;
+                ml[0] = m;
+                ml[1] = lsum;
+            }
             if constexpr (!PEERS) {
                 // Rows straight from TMEM in the 16x256b shape: a thread holds two adjacent
                 // columns of rows t/4 and t/4 + 8 of a 16-row half, so each store instruction
@@ -337,14 +353,16 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     const int ra = rh * 16 + (lane >> 2);    // rows ra and ra + 8 of the warp's quarter
                     const float ia = __shfl_sync(0xffffffffu, inv, ra), ib = __shfl_sync(0xffffffffu, inv, ra + 8);
                     const int r = ti.r0 + wq * 32 + ra;
-                    float* pa = a.o.out + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D + 2 * (lane & 3);
-                    float* pb = pa + (size_t)8 * a.hq * D;
+                    const bool sa = split || r < a.n, sb = split || r + 8 < a.n;   // split: all 128 scratch rows
+                    float* pa = split ? a.part + (((size_t)tt * 2 + h) * BM + wq * 32 + ra) * D + 2 * (lane & 3)
+                                      : a.o.out + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D + 2 * (lane & 3);
+                    float* pb = pa + (size_t)8 * (split ? D : a.hq * D);
                     #pragma unroll
                     for (int g = 0; g < 16; ++g) {
-                        if (r < a.n)
+                        if (sa)
                             *reinterpret_cast<float2*>(pa + 8 * g) =
                                 make_float2(__uint_as_float(ro[rh][4 * g]) * ia, __uint_as_float(ro[rh][4 * g + 1]) * ia);
-                        if (r + 8 < a.n)
+                        if (sb)
                             *reinterpret_cast<float2*>(pb + 8 * g) =
                                 make_float2(__uint_as_float(ro[rh][4 * g + 2]) * ib, __uint_as_float(ro[rh][4 * g + 3]) * ib);
                     }
@@ -449,14 +467,14 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             // Per key tile j and head h: O_h += P_h(j) V_j as soon as P_h(j) is written, then
             // S_h(j+1) = Q_h K_{j+1}^T over P_h(j) (ordered after PV_h(j), issued just before);
             // the tensor pipe works on one head while the other head's softmax runs.
-            for (int j = 0; j < ti.nk && ok; ++j, ++kt) {
+            for (int j = 0; j < ti.nj && ok; ++j, ++kt) {
                 const int iv = base + 2 * j + 1;
                 if (!wait_item(iv)) { fail(22); ok = false; break; }
-                if (j == ti.nk - 1 && ti.valid_keys < (j + 1) * BN) {
+                if (ti.j0 + j == ti.nk - 1 && ti.valid_keys < (ti.j0 + j + 1) * BN) {
                     // Rows of the last V tile past the causal end hold stale data: zero them so
                     // that a zero probability never meets a non-finite value.
                     uint8_t* Vs = smem + OFF_RING + (iv % RING) * TILE_BYTES;
-                    const int first = ti.valid_keys - j * BN;
+                    const int first = ti.valid_keys - (ti.j0 + j) * BN;
                     for (int idx = first * 16 + lane; idx < BN * 16; idx += 32) {
                         const int row = idx >> 4, c = idx & 15;    // c: 16-byte chunk of the 256-byte row
                         const int half_sel = c >> 3, cc = c & 7;
@@ -472,9 +490,9 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     // the first PV of a tile overwrites O_h: the previous tile's epilogue has read it
                     if (j == 0 && i > 0 && !mbar_wait(&bar[B_OF0 + h], (i - 1) & 1, abortp)) { fail(27); ok = false; break; }
                     tc_fence_after();
-                    issue_pv(iv, h, j == 0, j == ti.nk - 1);
+                    issue_pv(iv, h, j == 0, j == ti.nj - 1);
                     if (h == 1) release_item(iv);                  // V_j free when PV_1(j) completes
-                    if (j + 1 < ti.nk) {
+                    if (j + 1 < ti.nj) {
                         const int ik = base + 2 * j + 2;
                         if (h == 0 && !wait_item(ik)) { fail(24); ok = false; break; }
                         tc_fence_after();
@@ -483,7 +501,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     }
                 }
             }
-            base += 2 * ti.nk;
+            base += 2 * ti.nj;
         }
         // drain: every MMA this thread issued has completed before TMEM is released
         if (lane == 0) {
@@ -508,13 +526,13 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             // the softmax warps load them
             for (int r = ti.r0; r < min(ti.r0 + BM, a.n); ++r)
                 bulk_prefetch_l2(a.q + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2) * D, 2 * D * sizeof(float));
-            for (int j2 = 0; j2 < 2 * ti.nk; ++j2) {
+            for (int j2 = 0; j2 < 2 * ti.nj; ++j2) {
                 const int st = issued % RING;
                 if (issued >= RING && !mbar_wait(&bar[B_EMPTY0 + st], ((issued / RING) - 1) & 1, abortp)) {
                     fail(31); ok = false; break;
                 }
                 uint8_t* dst = smem + OFF_RING + st * TILE_BYTES;
-                const int plane = (j2 & 1) ? ti.plane_k + a.hkv : ti.plane_k, key0 = (j2 >> 1) * BN;
+                const int plane = (j2 & 1) ? ti.plane_k + a.hkv : ti.plane_k, key0 = (ti.j0 + (j2 >> 1)) * BN;
                 mbar_arrive_expect_tx(&bar[B_FULL0 + st], TILE_BYTES);
                 tma_load_3d(dst, &kv_map, 0, key0, plane, &bar[B_FULL0 + st]);
                 tma_load_3d(dst + 16384, &kv_map, 64, key0, plane, &bar[B_FULL0 + st]);
@@ -537,12 +555,56 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
     if (PEERS && a.o.n_peers && tid == 0) __threadfence_system();   // rows stored to peers: visible system-wide at exit
 }
 
+// Key-segment merge of split items: one warp per output row (item, head, row), lane l holding
+// columns 4l..4l+3. Every segment's running max and sum and its piece of the row are loaded at
+// once; the segments then combine in segment order with weights 2^(m_s - M) (the same log2
+// domain as the kernel's softmax): out = sum_s w_s O_s / sum_s w_s l_s.
+constexpr int MAX_KSEG = 16;
+constexpr int SPLIT_UNITS = NUM_SMS_B200;     // scratch: at most one wave of units
+__global__ void __launch_bounds__(256) prefill_merge_kernel(const PrefillArgs a) {
+    const int w = (int)((blockIdx.x * 256u + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    const int n_items = a.n_tiles / a.kseg;
+    if (w >= n_items * 2 * BM) return;
+    const int item = w / (2 * BM), h = (w / BM) & 1, row = w % BM;
+    const TileInfo ti = tile_info(a, item * a.kseg);
+    const int r = ti.r0 + row;
+    if (r >= a.n) return;
+    float m[MAX_KSEG], l[MAX_KSEG];
+    float4 o[MAX_KSEG];
+    #pragma unroll
+    for (int sg = 0; sg < MAX_KSEG; ++sg)
+        if (sg < a.kseg) {
+            const size_t u = ((size_t)(item * a.kseg + sg) * 2 + h) * BM + row;
+            m[sg] = __ldcg(a.part_ml + 2 * u);
+            l[sg] = __ldcg(a.part_ml + 2 * u + 1);
+            o[sg] = __ldcg(reinterpret_cast<const float4*>(a.part + u * D) + lane);
+        }
+    float M = -INFINITY;
+    #pragma unroll
+    for (int sg = 0; sg < MAX_KSEG; ++sg)
+        if (sg < a.kseg) M = fmaxf(M, m[sg]);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    #pragma unroll
+    for (int sg = 0; sg < MAX_KSEG; ++sg)
+        if (sg < a.kseg) {
+            const float wt = ex2_approx(m[sg] - M);
+            L += wt * l[sg];
+            acc.x += wt * o[sg].x; acc.y += wt * o[sg].y; acc.z += wt * o[sg].z; acc.w += wt * o[sg].w;
+        }
+    const float inv = 1.f / L;
+    *reinterpret_cast<float4*>(a.o.out + (((size_t)ti.l * a.n + r) * a.hq + (size_t)ti.kh * 2 + h) * D + lane * 4) =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
+
 }  // namespace
+
+size_t prefill_split_scratch_bytes() { return (size_t)SPLIT_UNITS * 2 * BM * (D + 2) * sizeof(float); }
 
 // Host side --------------------------------------------------------------------------------------
 int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutRows& o, int seq, int layer0,
                               int n_layers, int pos0, int n, int hq, int hkv, int layers_total, int row_begin,
-                              int* tile_counter, int* error, cudaStream_t s) {
+                              int* tile_counter, float* split_scratch, int* error, cudaStream_t s) {
     if (row_begin >= n) return 0;
     const bool peers = o.n_peers > 0 || o.heads != hq || o.head0 != 0;
     static int checked[2] = {0, 0};              // per instantiation: 1 ready, -1 refused
@@ -563,7 +625,7 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
     a.q = q; a.o = o; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
     a.hq = hq; a.hkv = hkv; a.layers_total = layers_total; a.row_begin = row_begin;
     a.n_qtiles = (n - row_begin + BM - 1) / BM; a.error = error;
-    a.n_tiles = a.n_qtiles * hkv * n_layers;
+    const int n_items = a.n_qtiles * hkv * n_layers;
     // K/V the launch reads (FP16 K and V rows of every (layer, head) up to the last row), against
     // a third of the 126 MB L2
     a.size_major = (double)n_layers * hkv * 2.0 * (pos0 + n) * D * 2 <= 42.0e6 ? 1 : 0;
@@ -571,10 +633,25 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
     // persistent: one CTA per SM (225 KB of shared memory each) pulls tiles from the counter
     int dev = 0, sms = NUM_SMS_B200;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // Fewer items than SMs (a prompt chunk of a few hundred rows at an offset, one layer per call):
+    // each item's key tiles split into kseg segments of at least two tiles, one unit per SM at
+    // most, merged by prefill_merge_kernel.
+    a.kseg = 1;
+    if (!peers && split_scratch && n_items < sms) {
+        const int nk_min = (pos0 + std::min(row_begin + BM, n) + BN - 1) / BN;   // the first row tile's key tiles
+        const int k = std::min({sms / n_items, nk_min / 2, MAX_KSEG, SPLIT_UNITS / n_items});
+        if (k >= 2) {
+            a.kseg = k;
+            a.part = split_scratch;
+            a.part_ml = split_scratch + (size_t)SPLIT_UNITS * 2 * BM * D;
+        }
+    }
+    a.n_tiles = n_items * a.kseg;
     const unsigned blocks = (unsigned)std::min(a.n_tiles, sms);
     if (cudaMemsetAsync(tile_counter, 0, sizeof(int), s) != cudaSuccess) return -2;
     if (peers) attn_prefill_sm100_kernel<true><<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
     else attn_prefill_sm100_kernel<false><<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
+    if (a.kseg > 1) prefill_merge_kernel<<<(unsigned)(n_items * 2 * BM / 8), 256, 0, s>>>(a);
     return 0;
 }
 

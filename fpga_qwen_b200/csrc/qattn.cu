@@ -58,6 +58,7 @@ struct qa_ctx {
     CUtensorMap kv_map{};                  // 3-D view {128 ch, ctx, planes} of the KV store, 64x128 boxes
     int* error = nullptr;                  // device error block (qattn_common.cuh: ERR_*), at io_dev
     int* prefill_tiles = nullptr;          // work-item counter of the persistent prefill kernel
+    float* prefill_split = nullptr;        // partial rows of prefill items split over key segments
     // The FP32 rows below position 128 run on a second stream next to the persistent tensor-core
     // kernel (fork: aux waits for the context stream; join: the context stream waits for aux).
     cudaStream_t aux_stream = nullptr;
@@ -482,6 +483,7 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     ctx->error = reinterpret_cast<int*>(ctx->io_dev);
     ctx->staging = reinterpret_cast<float*>(ctx->io_dev + ERR_BLOCK_BYTES);
     if (cudaMalloc(&ctx->prefill_tiles, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMalloc(&ctx->prefill_split, prefill_split_scratch_bytes()) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMalloc(&ctx->proj_scratch, project_gemm_scratch_bytes()) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaStreamCreateWithFlags(&ctx->aux_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->fork_ev, cudaEventDisableTiming) != cudaSuccess ||
@@ -506,7 +508,7 @@ void qa_destroy(qa_ctx* ctx) {
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->kv.base); cudaFree(ctx->cosines); cudaFree(ctx->sines); cudaFree(ctx->norms);
     cudaFree(ctx->partial); cudaFree(ctx->counters); cudaFree(ctx->io_dev); cudaFreeHost(ctx->io_pin);
-    cudaFree(ctx->prefill_tiles); cudaFree(ctx->proj_scratch);
+    cudaFree(ctx->prefill_tiles); cudaFree(ctx->prefill_split); cudaFree(ctx->proj_scratch);
     if (ctx->aux_stream) { cudaStreamSynchronize(ctx->aux_stream); cudaStreamDestroy(ctx->aux_stream); }
     if (ctx->fork_ev) cudaEventDestroy(ctx->fork_ev);
     if (ctx->join_ev) cudaEventDestroy(ctx->join_ev);
@@ -691,7 +693,8 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
                 launch_attn_head_rows(r, o, both ? ctx->aux_stream : ctx->stream);
             }
             if (launch_attn_prefill_sm100(ctx->kv_map, din[0], o, seq, l0, nl, pos0, n, ctx->hq, ctx->hkv,
-                                          ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->error, ctx->stream))
+                                          ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->prefill_split,
+                                          ctx->error, ctx->stream))
                 return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel cannot launch (unexpected register allocation or shared-memory limit)");
             if (both) {
                 QA_CUDA(cudaEventRecord(ctx->join_ev, ctx->aux_stream));

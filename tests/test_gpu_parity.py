@@ -126,6 +126,34 @@ def test_prefill_attention_parity(pos0, n):
     ctx.close()
 
 
+@pytest.mark.parametrize("chunks", [[(p, 512) for p in range(0, 3584, 512)] + [(3584, 384)], [(0, 3000), (3000, 700)]])
+def test_chunked_prefill_one_layer_calls(chunks):
+    """The engine's prefill pattern: a prompt in chunks (512 rows like core.cpp:712, or an
+    unaligned offset), each chunk appended for both layers and then attended one layer per
+    call. These launches hold fewer work items than SMs, so each item's key tiles are split
+    over several CTAs and merged; every chunk's rows are compared with the oracle."""
+    L = 2
+    ctx = make_ctx(L, context=4096)
+    qw, kw = H.norms(7, L)
+    H.set_norms(ctx, qw, kw)
+    for ci, (pos0, n) in enumerate(chunks):
+        q, k, v = H.inputs(300 + ci, L, pos0, n)
+        qn = gpu_append(ctx, 0, pos0, q, k, v)
+        out = torch.empty_like(qn)
+        for layer in range(L):
+            ctx.attn_prefill(0, layer, 1, pos0, n, qn[layer].data_ptr(), out[layer].data_ptr())
+        torch.cuda.synchronize()
+        outh, qnh = out.cpu().numpy(), qn.cpu().numpy()
+        for layer in range(L):
+            kv = H.read_layer_kv(ctx, 0, layer, pos0 + n, 4096)
+            ref = O.attention(kv, pos0, qnh[layer], threads=8)
+            mx, rms = H.err_stats(outh[layer], ref)
+            H.record("chunked prefill, one-layer calls (split key ranges)", mx, rms, n)
+            assert mx < H.MAX_ABS and rms < H.RMS, (pos0, n, layer, mx, rms)
+        ctx.commit(0, n)
+    ctx.close()
+
+
 def test_config1_prefill_then_32_decode_steps():
     """85-row prefill + 32 decode steps (the odd final row), 28 layers, vs the oracle."""
     L, n, steps = 28, 85, 32
