@@ -102,10 +102,12 @@ struct PrefillArgs {
 // heaviest first across all groups (the longest items start first, so the launch ends evenly).
 // With kseg > 1 (launches with fewer items than SMs) unit t is segment t % kseg of item
 // t / kseg: key tiles [j0, j0 + nj) of the item's nk, an even share.
+// SPLIT is the kernel instantiation for such launches (the others compile without the division).
 struct TileInfo { int l, kh, r0, nk, valid_keys, plane_k, j0, nj; };
+template <bool SPLIT>
 __device__ __forceinline__ TileInfo tile_info(const PrefillArgs& a, int t) {
     TileInfo ti;
-    const int item = t / a.kseg, seg = t - item * a.kseg;
+    const int item = SPLIT ? t / a.kseg : t, seg = SPLIT ? t - item * a.kseg : 0;
     const int groups = a.hkv * a.n_layers;
     const int lh = a.size_major ? item % groups : item / a.n_qtiles;
     const int tile = a.n_qtiles - 1 - (a.size_major ? item / groups : item % a.n_qtiles);
@@ -115,8 +117,8 @@ __device__ __forceinline__ TileInfo tile_info(const PrefillArgs& a, int t) {
     ti.valid_keys = a.pos0 + min(ti.r0 + BM, a.n);            // keys visible to the tile's last row
     ti.nk = (ti.valid_keys + BN - 1) / BN;                    // causal key tiles
     ti.plane_k = ((a.seq * a.layers_total + a.layer0 + ti.l) * 2 + 0) * a.hkv + ti.kh;
-    ti.j0 = seg * ti.nk / a.kseg;
-    ti.nj = (seg + 1) * ti.nk / a.kseg - ti.j0;
+    ti.j0 = SPLIT ? seg * ti.nk / a.kseg : 0;
+    ti.nj = SPLIT ? (seg + 1) * ti.nk / a.kseg - ti.j0 : ti.nk;
     return ti;
 }
 
@@ -172,8 +174,9 @@ __device__ __forceinline__ void q_store_rows(uint8_t* Qs, int wq, int lane, cons
 }
 
 // PEERS: rows go where a.o says, peers included; otherwise the local layout {out, hq, 0}
-// (the single-GPU path carries no peer-store code).
-template <bool PEERS>
+// (the single-GPU path carries no peer-store code). SPLIT (single-GPU only): units are key
+// segments of items, whose rows go unnormalised to the scratch for prefill_merge_kernel.
+template <bool PEERS, bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -238,9 +241,9 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             mbar_arrive(&bar[B_Q0 + h]);
         };
         int tt = read_tile(0);
-        if (tt >= 0) store_q(tile_info(a, tt));
+        if (tt >= 0) store_q(tile_info<SPLIT>(a, tt));
         for (int i = 0; tt >= 0; ++i) {
-            const TileInfo ti = tile_info(a, tt);
+            const TileInfo ti = tile_info<SPLIT>(a, tt);
             const int row_pos = a.pos0 + ti.r0 + trow;
             float m = -INFINITY, lsum = 0.f;
             bool ok = true;
@@ -323,14 +326,14 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                 // Q_h is free (QK_h of the last key tile completed before its S was announced):
                 // the next item's Q rows go in now, so its first QK_h runs on the tensor pipe
                 // while this item's epilogue runs
-                if (next >= 0) store_q(tile_info(a, next));
+                if (next >= 0) store_q(tile_info<SPLIT>(a, next));
             }
             // ---- epilogue: O_h of this tile (all its MMAs, QK_h included, have completed) ----
             if (!mbar_wait(&bar[B_OD0 + h], i & 1, abortp)) { fail(13); break; }
             tc_fence_after();
             // a key segment of a split item leaves its rows unnormalised (weight 1) in the scratch,
             // with the row's running max and sum beside them, for prefill_merge_kernel
-            const bool split = !PEERS && a.kseg > 1;
+            constexpr bool split = SPLIT && !PEERS;
             const float inv = split ? 1.f : 1.f / lsum;
             if (split) {
                 float* ml = a.part_ml + (((size_t)tt * 2 + h) * BM + trow) * 2;
@@ -405,7 +408,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
                     }
                     __syncwarp();
                 }
-                if (next >= 0) store_q(tile_info(a, next));  // this warp's own Q rows, after its staging
+                if (next >= 0) store_q(tile_info<SPLIT>(a, next));  // this warp's own Q rows, after its staging
             }
             tt = next;
         }
@@ -455,7 +458,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar[B_TE0 + slot]);
             if (tt < 0) break;
-            const TileInfo ti = tile_info(a, tt);
+            const TileInfo ti = tile_info<SPLIT>(a, tt);
             // tile prologue: S_0(0) as soon as Q_0 is in place, then S_1(0)
             if (!wait_item(base) || !mbar_wait(&bar[B_Q0], i & 1, abortp)) { fail(21); ok = false; break; }
             tc_fence_after();
@@ -521,7 +524,7 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
             tq[slot] = tt;
             mbar_arrive(&bar[B_TF0 + slot]);                 // the slot's value is visible to the waiters
             if (tt < 0) break;
-            const TileInfo ti = tile_info(a, tt);
+            const TileInfo ti = tile_info<SPLIT>(a, tt);
             // the item's query rows (both heads of the pair: 1 KB per row) into L2, well before
             // the softmax warps load them
             for (int r = ti.r0; r < min(ti.r0 + BM, a.n); ++r)
@@ -566,7 +569,7 @@ __global__ void __launch_bounds__(256) prefill_merge_kernel(const PrefillArgs a)
     const int n_items = a.n_tiles / a.kseg;
     if (w >= n_items * 2 * BM) return;
     const int item = w / (2 * BM), h = (w / BM) & 1, row = w % BM;
-    const TileInfo ti = tile_info(a, item * a.kseg);
+    const TileInfo ti = tile_info<true>(a, item * a.kseg);
     const int r = ti.r0 + row;
     if (r >= a.n) return;
     float m[MAX_KSEG], l[MAX_KSEG];
@@ -607,20 +610,6 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
                               int* tile_counter, float* split_scratch, int* error, cudaStream_t s) {
     if (row_begin >= n) return 0;
     const bool peers = o.n_peers > 0 || o.heads != hq || o.head0 != 0;
-    static int checked[2] = {0, 0};              // per instantiation: 1 ready, -1 refused
-    int& ck = checked[peers ? 1 : 0];
-    if (!ck) {
-        // setmaxnreg.inc waits for registers the control warpgroup releases; the split is
-        // only consistent with a launch at exactly REGS_LAUNCH registers per thread.
-        const void* fn = peers ? (const void*)attn_prefill_sm100_kernel<true> : (const void*)attn_prefill_sm100_kernel<false>;
-        cudaFuncAttributes fa{};
-        if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess || fa.numRegs != REGS_LAUNCH ||
-            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
-            ck = -1;
-        else
-            ck = 1;
-    }
-    if (ck < 0) return -1;
     PrefillArgs a{};
     a.q = q; a.o = o; a.seq = seq; a.layer0 = layer0; a.n_layers = n_layers; a.pos0 = pos0; a.n = n;
     a.hq = hq; a.hkv = hkv; a.layers_total = layers_total; a.row_begin = row_begin;
@@ -647,10 +636,27 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
         }
     }
     a.n_tiles = n_items * a.kseg;
+    const int which = peers ? 2 : a.kseg > 1 ? 1 : 0;
+    void (*const kernels[3])(const CUtensorMap, const PrefillArgs) = {
+        attn_prefill_sm100_kernel<false, false>, attn_prefill_sm100_kernel<false, true>,
+        attn_prefill_sm100_kernel<true, false>};
+    static int checked[3] = {0, 0, 0};           // per instantiation: 1 ready, -1 refused
+    int& ck = checked[which];
+    if (!ck) {
+        // setmaxnreg.inc waits for registers the control warpgroup releases; the split is
+        // only consistent with a launch at exactly REGS_LAUNCH registers per thread.
+        const void* fn = (const void*)kernels[which];
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess || fa.numRegs != REGS_LAUNCH ||
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+            ck = -1;
+        else
+            ck = 1;
+    }
+    if (ck < 0) return -1;
     const unsigned blocks = (unsigned)std::min(a.n_tiles, sms);
     if (cudaMemsetAsync(tile_counter, 0, sizeof(int), s) != cudaSuccess) return -2;
-    if (peers) attn_prefill_sm100_kernel<true><<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
-    else attn_prefill_sm100_kernel<false><<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
+    kernels[which]<<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
     if (a.kseg > 1) prefill_merge_kernel<<<(unsigned)(n_items * 2 * BM / 8), 256, 0, s>>>(a);
     return 0;
 }

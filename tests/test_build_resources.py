@@ -52,7 +52,7 @@ def test_no_kernel_spills(resources):
 
 def test_prefill_register_split_is_consistent(resources):
     found = _pick(resources, "attn_prefill_sm100_kernel")
-    assert len(found) == 2                          # single-GPU and peer-store instantiations
+    assert len(found) == 3                          # single-GPU, key-segment split and peer-store instantiations
     assert all(regs == 168 for regs, _ in found.values()), found
 
 
