@@ -92,7 +92,7 @@ struct PrefillArgs {
     int kseg;                         // key segments per item (work units = items x kseg); 1: no split
     float* part;                      // kseg > 1: [unit][2 heads][128 rows][128] unnormalised O rows
     float* part_ml;                   // kseg > 1: [unit][2 heads][128 rows] (running max, sum)
-    int* tile_counter;                // next tile to hand out; zero before the launch
+    int* tile_counter;                // [0] next unit to hand out, [1] CTAs finished; zero between launches
     int* error;
 };
 
@@ -207,6 +207,11 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Single-GPU launches are programmatic dependents: the set-up above overlaps the previous
+    // kernel, and nothing that kernel writes (q, K/V, the work counter, the split scratch) is
+    // read before this wait.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     volatile int* abortp = &abort_flag;
     if (warp < 8) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
     else asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CONTROL));
@@ -555,6 +560,14 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
+    if (tid == 0) {
+        // this CTA takes no more items (on every path): the last CTA out resets the work counter
+        // and this count for the next launch
+        if (atomicAdd(a.tile_counter + 1, 1) == (int)gridDim.x - 1) {
+            a.tile_counter[0] = 0;
+            a.tile_counter[1] = 0;
+        }
+    }
     if (PEERS && a.o.n_peers && tid == 0) __threadfence_system();   // rows stored to peers: visible system-wide at exit
 }
 
@@ -565,6 +578,8 @@ attn_prefill_sm100_kernel(const __grid_constant__ CUtensorMap kv_map, const Pref
 constexpr int MAX_KSEG = 16;
 constexpr int SPLIT_UNITS = NUM_SMS_B200;     // scratch: at most one wave of units
 __global__ void __launch_bounds__(256) prefill_merge_kernel(const PrefillArgs a) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");          // the partials are the prefill's output
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int w = (int)((blockIdx.x * 256u + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     const int n_items = a.n_tiles / a.kseg;
     if (w >= n_items * 2 * BM) return;
@@ -655,9 +670,20 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
     }
     if (ck < 0) return -1;
     const unsigned blocks = (unsigned)std::min(a.n_tiles, sms);
-    if (cudaMemsetAsync(tile_counter, 0, sizeof(int), s) != cudaSuccess) return -2;
-    kernels[which]<<<blocks, THREADS, SMEM_BYTES, s>>>(map, a);
-    if (a.kseg > 1) prefill_merge_kernel<<<(unsigned)(n_items * 2 * BM / 8), 256, 0, s>>>(a);
+    // single-GPU launches (and the merge after a split one) as programmatic dependents
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(blocks); cfg.blockDim = dim3(THREADS); cfg.dynamicSmemBytes = SMEM_BYTES; cfg.stream = s;
+    cfg.attrs = attr; cfg.numAttrs = peers ? 0 : 1;
+    if (cudaLaunchKernelEx(&cfg, kernels[which], map, a) != cudaSuccess) return -2;
+    if (a.kseg > 1) {
+        cudaLaunchConfig_t mc{};
+        mc.gridDim = dim3((unsigned)(n_items * 2 * BM / 8)); mc.blockDim = dim3(256); mc.stream = s;
+        mc.attrs = attr; mc.numAttrs = 1;
+        if (cudaLaunchKernelEx(&mc, prefill_merge_kernel, a) != cudaSuccess) return -2;
+    }
     return 0;
 }
 

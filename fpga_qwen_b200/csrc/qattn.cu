@@ -482,7 +482,9 @@ int qa_create(const qa_config* cfg, qa_ctx** out) {
     if (cudaMemset(ctx->io_dev, 0, ERR_BLOCK_BYTES) != cudaSuccess) return cleanup(QA_ERR_CUDA);
     ctx->error = reinterpret_cast<int*>(ctx->io_dev);
     ctx->staging = reinterpret_cast<float*>(ctx->io_dev + ERR_BLOCK_BYTES);
-    if (cudaMalloc(&ctx->prefill_tiles, sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    // the prefill's work counter and finished-CTA count: zero here, reset by each launch's last CTA
+    if (cudaMalloc(&ctx->prefill_tiles, 2 * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_OOM);
+    if (cudaMemset(ctx->prefill_tiles, 0, 2 * sizeof(int)) != cudaSuccess) return cleanup(QA_ERR_CUDA);
     if (cudaMalloc(&ctx->prefill_split, prefill_split_scratch_bytes()) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaMalloc(&ctx->proj_scratch, project_gemm_scratch_bytes()) != cudaSuccess) return cleanup(QA_ERR_OOM);
     if (cudaStreamCreateWithFlags(&ctx->aux_stream, cudaStreamNonBlocking) != cudaSuccess ||
@@ -692,10 +694,12 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
                 r.row_end = tc_begin;
                 launch_attn_head_rows(r, o, both ? ctx->aux_stream : ctx->stream);
             }
-            if (launch_attn_prefill_sm100(ctx->kv_map, din[0], o, seq, l0, nl, pos0, n, ctx->hq, ctx->hkv,
-                                          ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles, ctx->prefill_split,
-                                          ctx->error, ctx->stream))
+            const int lr = launch_attn_prefill_sm100(ctx->kv_map, din[0], o, seq, l0, nl, pos0, n, ctx->hq, ctx->hkv,
+                                                     ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles,
+                                                     ctx->prefill_split, ctx->error, ctx->stream);
+            if (lr == -1)
                 return fail(ctx, QA_ERR_UNSUPPORTED, "tensor-core prefill kernel cannot launch (unexpected register allocation or shared-memory limit)");
+            if (lr) return fail(ctx, QA_ERR_CUDA, "tensor-core prefill launch failed: %s", cudaGetErrorString(cudaGetLastError()));
             if (both) {
                 QA_CUDA(cudaEventRecord(ctx->join_ev, ctx->aux_stream));
                 QA_CUDA(cudaStreamWaitEvent(ctx->stream, ctx->join_ev, 0));
