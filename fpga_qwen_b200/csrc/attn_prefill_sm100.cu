@@ -46,6 +46,13 @@
 // instantiation instead stages rows in the Q buffer for 128-byte writes over NVLink and stores
 // the next Q after its epilogue.
 //
+// Launches with fewer items than SMs (a prompt chunk of a few hundred rows attended one layer
+// per call) split every item's key tiles into segments (the <false, true> instantiation): each
+// segment leaves unnormalised rows and their running max and sum in a scratch, and
+// prefill_merge_kernel combines them. Single-GPU launches are programmatic dependents of the
+// previous kernel (set-up overlaps it; griddepcontrol.wait precedes every read of its output),
+// and the last CTA of each launch resets the work counter for the next one.
+//
 // Every wait is bounded (globaltimer, 2 s): on expiry the CTA raises an abort flag, writes
 // an error code to the host-visible flag, drains what it issued and frees its TMEM.
 #include <algorithm>
