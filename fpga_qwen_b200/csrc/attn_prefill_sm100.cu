@@ -629,7 +629,8 @@ size_t prefill_split_scratch_bytes() { return (size_t)SPLIT_UNITS * 2 * BM * (D 
 // Host side --------------------------------------------------------------------------------------
 int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutRows& o, int seq, int layer0,
                               int n_layers, int pos0, int n, int hq, int hkv, int layers_total, int row_begin,
-                              int* tile_counter, float* split_scratch, int* error, cudaStream_t s) {
+                              int* tile_counter, float* split_scratch, int reserve_sms, int* error,
+                              cudaStream_t s) {
     if (row_begin >= n) return 0;
     const bool peers = o.n_peers > 0 || o.heads != hq || o.head0 != 0;
     PrefillArgs a{};
@@ -644,6 +645,9 @@ int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutR
     // persistent: one CTA per SM (225 KB of shared memory each) pulls tiles from the counter
     int dev = 0, sms = NUM_SMS_B200;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // SMs left to a kernel that runs beside this one (the FP32 head rows of a short launch), so
+    // that its CTAs start at once instead of after the persistent CTAs
+    sms = std::max(1, sms - std::max(0, reserve_sms));
     // Fewer items than SMs (a prompt chunk of a few hundred rows at an offset, one layer per call):
     // each item's key tiles split into kseg segments of at least two tiles, one unit per SM at
     // most, merged by prefill_merge_kernel.

@@ -96,7 +96,8 @@ void launch_kv_copy(const KVLayout& kv, int src_seq, int dst_seq, int ntok, cuda
 // Returns non-zero (and launches nothing) if the kernel was not built with the expected registers.
 int launch_attn_prefill_sm100(const CUtensorMap& map, const float* q, const OutRows& o, int seq, int layer0,
                               int n_layers, int pos0, int n, int hq, int hkv, int layers_total, int row_begin,
-                              int* tile_counter, float* split_scratch, int* error, cudaStream_t s);
+                              int* tile_counter, float* split_scratch, int reserve_sms, int* error,
+                              cudaStream_t s);
 // Device scratch for launches whose items are split over key segments (sized at context creation).
 size_t prefill_split_scratch_bytes();
 // TMA-streamed split-context decode. Row b of the call is sequence rows.seq[b] at position
