@@ -694,9 +694,10 @@ static int attend(qa_ctx* ctx, int seq, int layer, int n_layers, int pos0, int n
                 r.row_end = tc_begin;
                 launch_attn_head_rows(r, o, both ? ctx->aux_stream : ctx->stream);
             }
-            // a short head-rows launch beside it (one CTA per layer and KV head) keeps its SMs, so
-            // that it runs alongside the persistent kernel rather than after it
-            const int head_ctas = both ? nl * ctx->hkv : 0;
+            // beside a short persistent launch (one or two layers, as an engine's layer loop makes
+            // them) the head-rows launch (one CTA per layer and KV head) keeps its SMs, so that it
+            // runs alongside rather than after it; longer launches leave it their tail
+            const int head_ctas = both && nl <= 2 ? nl * ctx->hkv : 0;
             const int lr = launch_attn_prefill_sm100(ctx->kv_map, din[0], o, seq, l0, nl, pos0, n, ctx->hq, ctx->hkv,
                                                      ctx->cfg.n_layers, tc_begin, ctx->prefill_tiles,
                                                      ctx->prefill_split, head_ctas <= NUM_SMS_B200 / 4 ? head_ctas : 0,
